@@ -1,0 +1,365 @@
+#!/usr/bin/env python
+"""Benchmark of the Qwen3-TTS per-frame decode on B200.
+
+Workload ("C3"): batch-1 frame loop of Qwen3-TTS-12Hz-0.6B with
+random-init bf16 weights (seed 0 backbone / seed 1 code predictor), a 200-token N(0,1) prefill
+context, 64 trailing-text rows, greedy decoding with EOS disabled. One step = one frame =
+code-predictor chain (15 weight sweeps) + 16-embedding combine + 28-layer backbone step +
+codec head + group-0 sampling, i.e. one launch of the persistent sm_100a kernel.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank decoding its own utterance (replicas,
+weak scaling, no collective on the decode path; codes are gathered to rank 0 afterwards).
+Rank 0 prints one JSON line. ``--impl reference`` times the reference algorithm on the host
+CPU cores (the oracle port of the reference's PyTorch path) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "codec_frames_per_s"
+UNIT = "frames/s"
+CTX = 200
+N_TRAILING = 64
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_config(args):
+    return {
+        "workload": "C3: bs1 frame loop (15-step code predictor + combine + 28-layer backbone step + codec head "
+                    "+ sampling), 200-token context, 64 trailing rows, greedy, EOS disabled",
+        "model": "Qwen3-TTS-12Hz-0.6B (random-init bf16)",
+        "global_batch": args.gpus,
+        "batch_per_gpu": 1,
+        "ctx": CTX,
+        "seq_len": CTX + args.warmup + args.steps,
+        "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU",
+        "l2": "inputs larger than L2: 3.31 GB of weights streamed per frame (L2 126 MB)",
+    }
+
+
+# ------------------------------------------------------------------------------------------
+# clocks sampled with nvidia-smi during the timed region
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: int):
+        self.samples = []
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            sel = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                self.samples.append((time.time(), float(parts[0]), float(parts[1]),
+                                     [n for n, v in zip(self.NAMES, parts[3:7]) if v.lower() == "active"]))
+            except ValueError:
+                pass
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        win = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not win:  # short timed region: take the samples closest to it
+            win = sorted(self.samples, key=lambda s: min(abs(s[0] - t0), abs(s[0] - t1)))[:3]
+        reasons = sorted({r for s in win for r in s[3]})
+        return {"sm_mhz": statistics.median(s[1] for s in win), "sm_max_mhz": max(s[2] for s in win),
+                "reasons": reasons, "samples": len(win)}
+
+
+# ------------------------------------------------------------------------------------------
+def measured_hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic_per_frame():
+    """DRAM bytes per frame launch from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "qtt_decode_kernel_frame_c3.txt")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_frame:"):
+                    return int(float(line.split(":", 1)[1].split()[0]))
+    except OSError:
+        pass
+    return None
+
+
+def cpu_frames_per_s(seconds: float, warmup: int = 1, max_frames: int | None = None, seed: int = 4):
+    """Oracle (CPU port of the reference path) frames/s on the C3 workload, all host threads."""
+    from oracle.qtt_oracle import Qwen3TTSOracle
+    from qwentts_turbo_b200.weights import synthetic_weights
+    from qwentts_turbo_b200.workloads import c3_inputs
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    w = synthetic_weights()
+    embeds, trailing, pad = c3_inputs(CTX, N_TRAILING, seed)
+    orc = Qwen3TTSOracle(w, max_seq=CTX + 2048)
+    del w
+    # the oracle's generate() loop, frame by frame, with a time budget
+    from oracle import qtt_oracle as O
+    eos = orc.d.eos_token_id
+    sup = orc.suppress_mask(eos)
+    h = orc.prefill(embeds)
+    logits = orc.head_logits(orc.codec_head, h)
+    logits[sup] = float("-inf")
+    g0 = O.sample_token(logits, False, 0.9, 50, 1.0, eos)
+    t_start = None
+    timed = 0
+    step = 0
+    while True:
+        if step == warmup:
+            t_start = time.perf_counter()
+        toks, _ = orc.cp_chain(h, g0)
+        groups = [g0] + toks
+        extra = trailing[step] if step < trailing.shape[0] else pad
+        h = orc.backbone_step(orc.combine(groups, extra))
+        logits = orc.head_logits(orc.codec_head, h)
+        logits[sup] = float("-inf")
+        g0 = O.sample_token(logits, False, 0.9, 50, 1.0, None)
+        step += 1
+        if t_start is not None:
+            timed += 1
+            el = time.perf_counter() - t_start
+            if el >= seconds or (max_frames is not None and timed >= max_frames):
+                break
+    el = time.perf_counter() - t_start
+    return timed / el, cores, timed, el
+
+
+# ------------------------------------------------------------------------------------------
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    budget = 60.0
+    fps, cores, timed, el = cpu_frames_per_s(budget, warmup=min(args.warmup, 2), max_frames=args.steps)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus, "steps": timed,
+        "warmup": min(args.warmup, 2), "ms_per_step": 1000.0 * el / timed, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{timed} frames of the C3 loop after a 200-token prefill ({el:.1f} s, "
+                                   f"fp32 torch on {cores} host threads)"},
+        "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch.distributed as dist
+
+    from qwentts_turbo_b200 import _lib
+    from qwentts_turbo_b200.config import frame_weight_bytes, kv_read_bytes_per_frame
+    from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
+    from qwentts_turbo_b200.weights import synthetic_weights
+    from qwentts_turbo_b200.workloads import c3_inputs
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    K, W = args.steps, args.warmup
+    max_seq = CTX + W + K + 8
+    weights = synthetic_weights()
+    dm = DeviceModel(weights, rope_rows=max_seq)
+    del weights
+    eng = Engine(dm, max_streams=1, max_seq=max_seq, max_frames=W + K + 1)
+    embeds, trailing, pad = c3_inputs(CTX, N_TRAILING, seed=4 + rank)
+    embeds_d, trailing_d, pad_d = embeds.cuda(), trailing.cuda(), pad.cuda()
+    sp = sampling_struct(do_sample=False, min_new_tokens=1 << 30)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident run: inputs already in HBM --------------------------------------
+    eng.prefill(0, embeds_d, sp)
+    eng.frames(0, W, trailing_d, pad_d, sp)
+    eng.check()
+    clocks = ClockSampler(dev)
+    time.sleep(0.3)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(stream)
+    eng.frames(0, K, trailing_d, pad_d, sp)
+    e1.record(stream)
+    barrier()
+    t1 = time.time()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks.stop()
+    eng.check()
+    st = eng.state(0)
+    assert st["frames"] == W + K and st["done"] == 0, st
+    codes = eng.codes(0)[: W + K].clone()
+
+    # ---- end to end through the C-ABI with host buffers ---------------------------------
+    lib = _lib.load()
+    trailing_h = trailing.pin_memory()
+    pad_h = pad.pin_memory()
+    row_d = torch.empty(1024, dtype=torch.bfloat16, device="cuda")
+    codes_dev = eng.codes(0)
+    codes_h = torch.empty(K, 16, dtype=torch.int32).pin_memory()
+    sh = stream.cuda_stream
+    spb = ctypes.byref(sp)
+
+    def e2e_frame(step, out_row):
+        src = trailing_h[step] if step < N_TRAILING else pad_h
+        row_d.copy_(src, non_blocking=True)
+        rc = lib.qtt_frames(eng.h, 0, 1, None, 0, row_d.data_ptr(), spb, sh)
+        if rc != 0:
+            raise _lib.QTTError(rc, "qtt_frames")
+        if out_row is not None:
+            out_row.copy_(codes_dev[step], non_blocking=True)
+
+    eng.prefill(0, embeds_d, sp)
+    for s in range(W):
+        e2e_frame(s, None)
+    eng.check()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for f in range(K):
+        e2e_frame(W + f, codes_h[f])
+    e3.record(stream)
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    eng.check()
+    assert torch.equal(codes_h, codes[W:].cpu()), "e2e path produced different codes"
+
+    # ---- gather codes to rank 0 (after timing; NCCL over NVLink) ---------------------------
+    if world > 1:
+        gathered = [torch.empty_like(codes) for _ in range(world)]
+        dist.all_gather(gathered, codes)
+        n_codes = sum(g.shape[0] for g in gathered)
+    else:
+        n_codes = codes.shape[0]
+
+    if rank != 0:
+        eng.close()
+        return
+
+    # ---- roofline -------------------------------------------------------------------------
+    wbytes = frame_weight_bytes()
+    kvb = [kv_read_bytes_per_frame(CTX + W + f) for f in range(K)]
+    bytes_per_frame = wbytes + sum(kvb) / K
+    frame_s = ms / 1000.0 / K
+    achieved = bytes_per_frame / frame_s / 1e9
+    peak, peak_src = measured_hbm_peak()
+    traffic = ncu_traffic_per_frame()
+    value = world * K / (ms / 1000.0)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random-init weights, seeded N(0,1) inputs)",
+        "config": workload_config(args),
+        "frame_latency_us": 1000.0 * ms / K,
+        "rtf": (ms / K) / (1000.0 / 12.0),
+        "hbm_gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": bytes_per_frame,
+                     "kernel": "qtt_decode_kernel (1 launch per frame)"},
+        "e2e": {"value": world * K / (ms_e2e / 1000.0), "unit": UNIT, "h2d_bytes_per_step": 2048,
+                "d2h_bytes_per_step": 64,
+                "path": "qtt_frames C-ABI per frame: pinned H2D of the frame's text row, D2H of its 16 codes"},
+        "gpu_launches": K,
+        "clocks": clocks.summary(t0, t1),
+        "codes_gathered": n_codes,
+    }
+    eng.close()
+    if world == 1 and not args.no_cpu_baseline:
+        fps, cores, timed, el = cpu_frames_per_s(args.cpu_seconds)
+        line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": f"{timed} frames of the C3 loop after a 200-token prefill ({el:.1f} s, "
+                                          f"fp32 torch oracle on {cores} host threads)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    args.gpus = world
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank)
+        else:
+            run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

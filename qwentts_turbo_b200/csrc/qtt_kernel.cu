@@ -1,0 +1,1100 @@
+// Persistent decode kernel for Qwen3-TTS on B200 (sm_100a).
+//
+// One cooperative launch runs one "program": a whole 12 Hz frame (code-predictor chain of
+// 15 weight sweeps + 16-embedding combine + 28-layer backbone step + codec head + group-0
+// sampling), or a single backbone / code-predictor decode step (the reference's launchers,
+// fused_decode_tts.cu:834-890 and fused_decode_code_predictor.cu:674-730).
+//
+// Grid: one CTA per SM. Each CTA has
+//   * 1 producer warp: walks the same stage schedule as the consumers and streams this CTA's
+//     rows of every weight matrix into a 7-slot shared-memory ring with 1-D TMA bulk copies
+//     (cp.async.bulk, no multicast). Weights do not depend on activations, so the producer
+//     runs ahead across grid barriers and keeps HBM busy while the consumers wait.
+//   * 12 consumer warps: GEMV dot products from shared memory (fp32 accumulate), the
+//     split-K attention, RMSNorms, sampling, and the grid barriers between dependent stages.
+// Row partition: every matrix is split over the CTAs in contiguous row ranges, so a CTA's
+// share of a matrix is one contiguous stretch of HBM.
+//
+// Numerics follow the reference kernels: fp32 accumulation, bf16 backbone hidden between
+// layers (fused_decode_tts.cu:541), bf16 backbone KV, fp32 code-predictor hidden and KV
+// (fused_decode_code_predictor.cu:553,287-289), bf16 head logits (generator.py:158,351).
+#include "qtt_kernel.cuh"
+#include "qtt_device.cuh"
+
+namespace qtt {
+
+enum StageKind : int { SK_QKV = 0, SK_O = 1, SK_GU = 2, SK_D = 3, SK_HEAD = 4 };
+
+struct __align__(128) Smem {
+  uint8_t ring[NSLOTS][SLOT_BYTES];
+  float xs[NTMAX * INTER];           // stage input vector; attention / sampler scratch
+  float part[MAXPART * NTMAX];       // per-unit partial dot products of the current stage
+  float red[4 * NCW];
+  unsigned long long ured[NCW + 1];
+  int hist[256];
+  uint64_t full[NSLOTS];
+  uint64_t empty[NSLOTS];
+  int abort;
+  int bcast[4];
+};
+
+size_t work_bytes() {
+  size_t n = 0;
+  n += 256;                                             // bar, err, att_cnt
+  n += sizeof(float) * 2 * NTMAX * HID;                 // hbuf
+  n += sizeof(float) * NTMAX * QKV_ROWS;                // qkv
+  n += sizeof(float) * NTMAX * QSZ;                     // attn
+  n += sizeof(float) * NTMAX * NQH * MAX_ATT_CHUNKS * PRT_STRIDE;  // prt
+  n += sizeof(float) * NTMAX * HID;                     // hmid
+  n += sizeof(float) * NTMAX * INTER;                   // mlp
+  n += sizeof(float) * VMAX;                            // logits
+  return n;
+}
+
+void work_carve(void* base, Work* w) {
+  char* c = static_cast<char*>(base);
+  w->bar = reinterpret_cast<uint32_t*>(c);
+  w->err = reinterpret_cast<int*>(c + 64);
+  w->att_cnt = reinterpret_cast<uint32_t*>(c + 128);
+  c += 256;
+  w->hbuf = reinterpret_cast<float*>(c); c += sizeof(float) * 2 * NTMAX * HID;
+  w->qkv = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * QKV_ROWS;
+  w->attn = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * QSZ;
+  w->prt = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * NQH * MAX_ATT_CHUNKS * PRT_STRIDE;
+  w->hmid = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * HID;
+  w->mlp = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * INTER;
+  w->logits = reinterpret_cast<float*>(c);
+}
+
+// ------------------------------------------------------------------------------------------
+// Stage plans: which rows of which matrix this CTA streams and reduces.
+// ------------------------------------------------------------------------------------------
+struct Plan {
+  int P;            // units per row (K / 1024)
+  int nseg;
+  int units;        // total units of this CTA in the stage
+  int r0, r1;       // logical row range (QKV: of the 4096 fused rows; GU: of the 3072 j)
+  const bf16* ptr[3];
+  int nun[3];
+};
+
+__device__ __forceinline__ int split_lo(int n, int G, int c) {
+  return static_cast<int>((static_cast<long long>(n) * c) / G);
+}
+
+__device__ __forceinline__ void plan_add(Plan& pl, const bf16* base, int rows) {
+  pl.ptr[pl.nseg] = base;
+  pl.nun[pl.nseg] = rows * pl.P;
+  pl.units += rows * pl.P;
+  pl.nseg++;
+}
+
+__device__ Plan make_plan(int kind, const LayerW* lw, const bf16* head, int head_rows, int cta, int G) {
+  Plan pl;
+  pl.nseg = 0;
+  pl.units = 0;
+  pl.P = 1;
+  if (kind == SK_QKV) {
+    pl.r0 = split_lo(QKV_ROWS, G, cta);
+    pl.r1 = split_lo(QKV_ROWS, G, cta + 1);
+    const bf16* mats[3] = {lw->wq, lw->wk, lw->wv};
+    const int lo[3] = {0, QSZ, QSZ + KVSZ};
+    const int hi[3] = {QSZ, QSZ + KVSZ, QKV_ROWS};
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+      const int a = max(pl.r0, lo[m]), b = min(pl.r1, hi[m]);
+      if (a < b) plan_add(pl, mats[m] + static_cast<size_t>(a - lo[m]) * HID, b - a);
+    }
+  } else if (kind == SK_O) {
+    pl.P = QSZ / UNIT;
+    pl.r0 = split_lo(HID, G, cta);
+    pl.r1 = split_lo(HID, G, cta + 1);
+    if (pl.r1 > pl.r0) plan_add(pl, lw->wo + static_cast<size_t>(pl.r0) * QSZ, pl.r1 - pl.r0);
+  } else if (kind == SK_GU) {
+    pl.r0 = split_lo(INTER, G, cta);
+    pl.r1 = split_lo(INTER, G, cta + 1);
+    if (pl.r1 > pl.r0) {
+      plan_add(pl, lw->wg + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
+      plan_add(pl, lw->wu + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
+    }
+  } else if (kind == SK_D) {
+    pl.P = INTER / UNIT;
+    pl.r0 = split_lo(HID, G, cta);
+    pl.r1 = split_lo(HID, G, cta + 1);
+    if (pl.r1 > pl.r0) plan_add(pl, lw->wd + static_cast<size_t>(pl.r0) * INTER, pl.r1 - pl.r0);
+  } else {  // SK_HEAD
+    pl.r0 = split_lo(head_rows, G, cta);
+    pl.r1 = split_lo(head_rows, G, cta + 1);
+    if (pl.r1 > pl.r0) plan_add(pl, head + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
+  }
+  return pl;
+}
+
+// ------------------------------------------------------------------------------------------
+// Producer
+// ------------------------------------------------------------------------------------------
+struct Prod {
+  uint32_t slot, round, issued;
+  bool ok;
+};
+
+__device__ void prod_stage(Smem& sm, Prod& pr, const Plan& pl, int* err) {
+  for (int u = 0; u < pl.units && pr.ok; u += SLOT_UNITS) {
+    const int n = min(SLOT_UNITS, pl.units - u);
+    if (!mbar_wait(&sm.empty[pr.slot], (pr.round & 1u) ^ 1u, &sm.abort)) {
+      if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+      pr.ok = false;
+      return;
+    }
+    mbar_arrive_expect_tx(&sm.full[pr.slot], static_cast<uint32_t>(n * UNIT_BYTES));
+    int base = 0;
+    for (int s = 0; s < pl.nseg; ++s) {
+      const int a = max(u, base), b = min(u + n, base + pl.nun[s]);
+      if (a < b)
+        bulk_g2s(sm.ring[pr.slot] + (a - u) * UNIT_BYTES, pl.ptr[s] + static_cast<size_t>(a - base) * UNIT,
+                 static_cast<uint32_t>((b - a) * UNIT_BYTES), &sm.full[pr.slot]);
+      base += pl.nun[s];
+    }
+    pr.issued++;
+    if (++pr.slot == NSLOTS) {
+      pr.slot = 0;
+      pr.round++;
+    }
+  }
+}
+
+__device__ void prod_layers(Smem& sm, Prod& pr, const LayerW* L, int n, int cta, int G, int* err) {
+  for (int l = 0; l < n && pr.ok; ++l) {
+    prod_stage(sm, pr, make_plan(SK_QKV, L + l, nullptr, 0, cta, G), err);
+    prod_stage(sm, pr, make_plan(SK_O, L + l, nullptr, 0, cta, G), err);
+    prod_stage(sm, pr, make_plan(SK_GU, L + l, nullptr, 0, cta, G), err);
+    prod_stage(sm, pr, make_plan(SK_D, L + l, nullptr, 0, cta, G), err);
+  }
+}
+
+__device__ bool frame_skipped(const Params& p) {
+  const StreamState* st = p.st;
+  const int done = ld_volatile_i32(&st->done);
+  const int g0 = ld_volatile_i32(&st->g0);
+  return done != 0 || g0 == p.sp.eos;
+}
+
+__device__ void producer_main(const Params& p, Smem& sm, int cta, int G) {
+  Prod pr{0u, 0u, 0u, true};
+  int* err = p.w.err;
+  if (p.mode == MODE_FRAME) {
+    if (!frame_skipped(p)) {
+      for (int pass = 0; pass < NCPHEADS && pr.ok; ++pass) {
+        prod_layers(sm, pr, p.cp_layers, p.n_cp, cta, G, err);
+        prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.cp_head[pass], p.cp_vocab, cta, G), err);
+      }
+      prod_layers(sm, pr, p.bb_layers, p.n_bb, cta, G, err);
+      prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err);
+    }
+  } else if (p.mode == MODE_BB_STEP) {
+    prod_layers(sm, pr, p.bb_layers, p.n_bb, cta, G, err);
+    if (p.flags & FLAG_HEAD_SAMPLE) prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err);
+  } else {
+    prod_layers(sm, pr, p.cp_layers, p.n_cp, cta, G, err);
+  }
+  // Drain: wait (bounded) for the copies of the last ring's worth of fills so that no bulk
+  // copy is still writing shared memory when this CTA exits early.
+  const uint32_t inflight = pr.issued < NSLOTS ? pr.issued : NSLOTS;
+  uint32_t slot = pr.slot, round = pr.round;
+  int zero = 0;
+  for (uint32_t i = 0; i < inflight; ++i) {
+    if (slot == 0) {
+      slot = NSLOTS - 1;
+      round--;
+    } else {
+      slot--;
+    }
+    mbar_wait(&sm.full[slot], round & 1u, &zero);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Consumers
+// ------------------------------------------------------------------------------------------
+struct Cons {
+  uint32_t slot, round, bar_target;
+  int cta, G, tid, warp, lane;
+};
+
+__device__ __forceinline__ bool aborted(Smem& sm) { return *reinterpret_cast<volatile int*>(&sm.abort) != 0; }
+
+__device__ __forceinline__ void fail(const Params& p, Smem& sm, int code) {
+  set_error(p.w.err, code);
+  *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+}
+
+// Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded).
+__device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
+  named_sync(1, NCT);
+  cs.bar_target += static_cast<uint32_t>(cs.G);
+  if (cs.tid == 0 && !aborted(sm)) {
+    __threadfence();
+    red_release_gpu_add(p.w.bar, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      const uint32_t v = ld_acquire_gpu(p.w.bar);
+      if (static_cast<int>(v - cs.bar_target) >= 0) break;
+      if ((it & 31u) == 31u) {
+        if (ld_volatile_i32(p.w.err) != 0) {
+          *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+          break;
+        }
+        if (globaltimer_ns() - t0 > QTT_WAIT_NS) {
+          fail(p, sm, DEV_ERR_GRID_TIMEOUT);
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  named_sync(1, NCT);
+  return !aborted(sm);
+}
+
+// Sum of NT per-thread values over the consumer threads; every thread gets the same totals.
+template <int NT>
+__device__ __forceinline__ void block_sum(Smem& sm, Cons& cs, float (&v)[NT]) {
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const float s = warp_sum(v[t]);
+    if (cs.lane == 0) sm.red[t * NCW + cs.warp] = s;
+  }
+  named_sync(1, NCT);
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) s += sm.red[t * NCW + w];
+    v[t] = s;
+  }
+  named_sync(1, NCT);
+}
+
+// In-place RMSNorm of NT vectors of HID floats in shared memory: x * rsqrt(mean(x^2)+eps) * w.
+template <int NT>
+__device__ void rmsnorm_smem(Smem& sm, Cons& cs, float* x, const bf16* w, float eps) {
+  float ss[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    float a = 0.f;
+    for (int i = cs.tid; i < HID; i += NCT) a = fmaf(x[t * HID + i], x[t * HID + i], a);
+    ss[t] = a;
+  }
+  block_sum<NT>(sm, cs, ss);
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const float rstd = rsqrtf(ss[t] / static_cast<float>(HID) + eps);
+    for (int i = cs.tid; i < HID; i += NCT) x[t * HID + i] = x[t * HID + i] * rstd * __bfloat162float(w[i]);
+  }
+  named_sync(1, NCT);
+}
+
+// Copy NT vectors of n floats from global (L2, written by other CTAs) into shared memory.
+__device__ __forceinline__ void load_vec(Cons& cs, float* dst, const float* src, int n_total) {
+  for (int i = cs.tid * 4; i < n_total; i += NCT * 4)
+    *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(src + i));
+}
+
+// GEMV over this CTA's units of one stage: part[u * NT + t] = dot(unit u, x part of u).
+template <int NT>
+__device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const float* xsrc, int xstride) {
+  const int part = cs.warp % pl.P;
+  float xr[NT][32];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const float* xp = xsrc + t * xstride + part * UNIT + 8 * cs.lane;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 a = *reinterpret_cast<const float4*>(xp + 256 * i);
+      const float4 b = *reinterpret_cast<const float4*>(xp + 256 * i + 4);
+      xr[t][8 * i + 0] = a.x; xr[t][8 * i + 1] = a.y; xr[t][8 * i + 2] = a.z; xr[t][8 * i + 3] = a.w;
+      xr[t][8 * i + 4] = b.x; xr[t][8 * i + 5] = b.y; xr[t][8 * i + 6] = b.z; xr[t][8 * i + 7] = b.w;
+    }
+  }
+  for (int u0 = 0; u0 < pl.units; u0 += SLOT_UNITS) {
+    const int n = min(SLOT_UNITS, pl.units - u0);
+    if (!mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort)) {
+      if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
+    } else if (cs.warp < n) {
+      const uint4* src = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + cs.warp * UNIT_BYTES);
+      float acc[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = src[cs.lane + 32 * i];
+        const float w[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
+                            bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[t] = fmaf(w[j], xr[t][8 * i + j], acc[t]);
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] = warp_sum(acc[t]);
+      if (cs.lane == 0) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) sm.part[(u0 + cs.warp) * NT + t] = acc[t];
+      }
+    }
+    __syncwarp();
+    if (cs.lane == 0) mbar_arrive(&sm.empty[cs.slot]);
+    if (++cs.slot == NSLOTS) {
+      cs.slot = 0;
+      cs.round++;
+    }
+  }
+  named_sync(1, NCT);
+  return !aborted(sm);
+}
+
+// ------------------------------------------------------------------------------------------
+// Attention: split over (KV head, chunk of positions) work items; the last item of a head to
+// finish combines the partial softmaxes (flash-decoding style), so no extra grid barrier.
+// ------------------------------------------------------------------------------------------
+template <int NT, bool CP>
+__device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0) {
+  const int S = p0 + NT;
+  int nch = (S + ATT_TARGET - 1) / ATT_TARGET;
+  const int maxch = min(MAX_ATT_CHUNKS, max(1, cs.G / NKVH));
+  nch = min(max(nch, 1), maxch);
+  const int chunk = (S + nch - 1) / nch;
+  nch = (S + chunk - 1) / chunk;
+  if (chunk > ATT_CHMAX) {
+    fail(p, sm, DEV_ERR_BAD_POSITION);
+    return false;
+  }
+  const int max_seq = CP ? p.cp_max_seq : p.bb_max_seq;
+  const size_t layer_off = static_cast<size_t>(li) * NKVH * max_seq * HD;
+  const LayerW* L = lw;
+
+  // shared scratch inside xs
+  float* qr = sm.xs;                         // [NT][2][HD]
+  float* kn = qr + NT * 2 * HD;              // [NT][HD]
+  float* vn = kn + NT * HD;                  // [NT][HD]
+  float* sc = vn + NT * HD;                  // [NT][2][ATT_CHMAX]
+  float* accg = sc + NT * 2 * ATT_CHMAX;     // [3][NT*2][HD]
+  float* ml = accg + 3 * NT * 2 * HD;        // [NT*2][2]
+
+  for (int item = cs.cta; item < NKVH * nch; item += cs.G) {
+    const int h = item / nch, c = item - h * nch;
+    const int s0 = c * chunk, s1 = min(S, s0 + chunk), len = s1 - s0;
+
+    // 1. q/k RMSNorm (per head, fused_decode_tts.cu:183-197) + RoPE; v copy. Warp j handles
+    //    vector j%4 (q head 2h, q head 2h+1, k, v) of token j/4; lane holds d = lane + 32 i,
+    //    so each rotation pair (d, d+64) lives in one lane.
+    if (cs.warp < NT * 4) {
+      const int t = cs.warp >> 2, vec = cs.warp & 3;
+      const int pos = p0 + t;
+      const float* src = p.w.qkv + t * QKV_ROWS +
+                         (vec < 2 ? (2 * h + vec) * HD : (vec == 2 ? QSZ + h * HD : QSZ + KVSZ + h * HD));
+      float x[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = __ldcg(src + cs.lane + 32 * i);
+      if (vec < 3) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ss = fmaf(x[i], x[i], ss);
+        ss = warp_sum(ss);
+        const float rstd = rsqrtf(ss / static_cast<float>(HD) + p.eps);
+        const bf16* nw = vec < 2 ? L->q_norm : L->k_norm;
+        float y[4], cv[4], sv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int d = cs.lane + 32 * i;
+          y[i] = x[i] * rstd * __bfloat162float(nw[d]);
+          cv[i] = __bfloat162float(p.cos_tab[static_cast<size_t>(pos) * HD + d]);
+          sv[i] = __bfloat162float(p.sin_tab[static_cast<size_t>(pos) * HD + d]);
+        }
+        float o[4];
+        o[0] = y[0] * cv[0] - y[2] * sv[0];
+        o[1] = y[1] * cv[1] - y[3] * sv[1];
+        o[2] = y[2] * cv[2] + y[0] * sv[2];
+        o[3] = y[3] * cv[3] + y[1] * sv[3];
+        float* dst = vec < 2 ? qr + (t * 2 + vec) * HD : kn + t * HD;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[cs.lane + 32 * i] = (vec == 2 && !CP) ? round_bf16(o[i]) : o[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) vn[t * HD + cs.lane + 32 * i] = CP ? x[i] : round_bf16(x[i]);
+      }
+    }
+    named_sync(1, NCT);
+
+    // 2. item 0 of each head stores the new K/V rows into the cache.
+    if (c == 0) {
+      for (int e = cs.tid; e < NT * HD; e += NCT) {
+        const int t = e / HD, d = e - t * HD;
+        const size_t off = layer_off + (static_cast<size_t>(h) * max_seq + p0 + t) * HD + d;
+        if (CP) {
+          p.cp_k[off] = kn[e];
+          p.cp_v[off] = vn[e];
+        } else {
+          p.bb_k[off] = __float2bfloat16_rn(kn[e]);
+          p.bb_v[off] = __float2bfloat16_rn(vn[e]);
+        }
+      }
+    }
+
+    // 3. scores: one warp per position, lane holds d = 4 lane .. 4 lane + 3.
+    for (int s = s0 + cs.warp; s < s1; s += NCW) {
+      float k4[4];
+      if (s < p0) {
+        const size_t off = layer_off + (static_cast<size_t>(h) * max_seq + s) * HD + 4 * cs.lane;
+        if (CP) {
+          const float4 kk = __ldcg(reinterpret_cast<const float4*>(p.cp_k + off));
+          k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+        } else {
+          const uint2 kk = __ldcg(reinterpret_cast<const uint2*>(p.bb_k + off));
+          k4[0] = bf16_lo(kk.x); k4[1] = bf16_hi(kk.x); k4[2] = bf16_lo(kk.y); k4[3] = bf16_hi(kk.y);
+        }
+      } else {
+        const float4 kk = *reinterpret_cast<const float4*>(kn + (s - p0) * HD + 4 * cs.lane);
+        k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float4 q = *reinterpret_cast<const float4*>(qr + (t * 2 + hh) * HD + 4 * cs.lane);
+          float d = q.x * k4[0];
+          d = fmaf(q.y, k4[1], d);
+          d = fmaf(q.z, k4[2], d);
+          d = fmaf(q.w, k4[3], d);
+          d = warp_sum(d) * p.attn_scale;
+          if (cs.lane == 0) sc[(t * 2 + hh) * ATT_CHMAX + (s - s0)] = (s <= p0 + t) ? d : -INFINITY;
+        }
+      }
+    }
+    named_sync(1, NCT);
+
+    // 4. chunk-local softmax statistics: warp j handles (token, head) j.
+    if (cs.warp < NT * 2) {
+      float* row = sc + cs.warp * ATT_CHMAX;
+      float m = -INFINITY;
+      for (int i = cs.lane; i < len; i += 32) m = fmaxf(m, row[i]);
+      m = warp_max(m);
+      float l = 0.f;
+      for (int i = cs.lane; i < len; i += 32) {
+        const float e = (m == -INFINITY) ? 0.f : expf(row[i] - m);
+        row[i] = e;
+        l += e;
+      }
+      l = warp_sum(l);
+      if (cs.lane == 0) {
+        ml[cs.warp * 2 + 0] = m;
+        ml[cs.warp * 2 + 1] = l;
+      }
+    }
+    named_sync(1, NCT);
+
+    // 5. P.V: thread -> (d, position residue g mod 3).
+    {
+      const int d = cs.tid & (HD - 1), g = cs.tid >> 7;
+      float acc[NT * 2];
+#pragma unroll
+      for (int j = 0; j < NT * 2; ++j) acc[j] = 0.f;
+      for (int s = s0 + g; s < s1; s += 3) {
+        float v;
+        if (s < p0) {
+          const size_t off = layer_off + (static_cast<size_t>(h) * max_seq + s) * HD + d;
+          v = CP ? __ldcg(p.cp_v + off) : __bfloat162float(__ldcg(p.bb_v + off));
+        } else {
+          v = vn[(s - p0) * HD + d];
+        }
+#pragma unroll
+        for (int j = 0; j < NT * 2; ++j) acc[j] = fmaf(sc[j * ATT_CHMAX + (s - s0)], v, acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < NT * 2; ++j) accg[(g * NT * 2 + j) * HD + d] = acc[j];
+    }
+    named_sync(1, NCT);
+
+    // 6. publish (or finish directly when the head has a single item).
+    if (nch == 1) {
+      for (int e = cs.tid; e < NT * 2 * HD; e += NCT) {
+        const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
+        const float a = (accg[(0 * NT * 2 + j) * HD + d] + accg[(1 * NT * 2 + j) * HD + d]) +
+                        accg[(2 * NT * 2 + j) * HD + d];
+        p.w.attn[t * QSZ + (2 * h + hh) * HD + d] = a / ml[j * 2 + 1];
+      }
+      named_sync(1, NCT);
+      continue;
+    }
+    for (int e = cs.tid; e < NT * 2 * PRT_STRIDE; e += NCT) {
+      const int j = e / PRT_STRIDE, k = e - j * PRT_STRIDE, t = j >> 1, hh = j & 1;
+      float val;
+      if (k < 2) {
+        val = ml[j * 2 + k];
+      } else {
+        const int d = k - 2;
+        val = (accg[(0 * NT * 2 + j) * HD + d] + accg[(1 * NT * 2 + j) * HD + d]) + accg[(2 * NT * 2 + j) * HD + d];
+      }
+      p.w.prt[((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + c) * PRT_STRIDE + k] = val;
+    }
+    named_sync(1, NCT);
+    if (cs.tid == 0) {
+      __threadfence();
+      const uint32_t old = atomicAdd(p.w.att_cnt + h, 1u);
+      sm.bcast[0] = (old == static_cast<uint32_t>(nch - 1)) ? 1 : 0;
+      __threadfence();
+    }
+    named_sync(1, NCT);
+    if (sm.bcast[0]) {
+      // combine the nch partials of KV head h in chunk order
+      for (int e = cs.tid; e < NT * 2 * HD; e += NCT) {
+        const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
+        const float* rec = p.w.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE;
+        float M = -INFINITY;
+        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(rec + cc * PRT_STRIDE));
+        float Ls = 0.f, O = 0.f;
+        for (int cc = 0; cc < nch; ++cc) {
+          const float mc = __ldcg(rec + cc * PRT_STRIDE);
+          if (mc == -INFINITY) continue;
+          const float wgt = expf(mc - M);
+          Ls = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 1), Ls);
+          O = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 2 + d), O);
+        }
+        p.w.attn[t * QSZ + (2 * h + hh) * HD + d] = O / Ls;
+      }
+      if (cs.tid == 0) atomicExch(p.w.att_cnt + h, 0u);
+    }
+    named_sync(1, NCT);
+  }
+  return !aborted(sm);
+}
+
+// ------------------------------------------------------------------------------------------
+// One decoder layer (fused_decode_tts.cu:764-794 / fused_decode_code_predictor.cu:601-631).
+// On entry sm.xs holds the raw layer input of the NT tokens and hin (global) holds the same
+// values (written by the previous stage or by CTA 0 before the first barrier).
+// ------------------------------------------------------------------------------------------
+template <int NT, bool CP>
+__device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const float* hin,
+                      float* hout) {
+  // ---- input RMSNorm + QKV
+  rmsnorm_smem<NT>(sm, cs, sm.xs, lw->in_norm, p.eps);
+  {
+    const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+    const int nr = pl.r1 - pl.r0;
+    for (int e = cs.tid; e < NT * nr; e += NCT) {
+      const int t = e / nr, r = e - t * nr;
+      __stcg(p.w.qkv + t * QKV_ROWS + pl.r0 + r, sm.part[r * NT + t]);
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return false;
+
+  // ---- q/k norm + RoPE + KV write + attention
+  if (!attention<NT, CP>(p, sm, cs, lw, li, p0)) return false;
+  if (!grid_sync(p, sm, cs)) return false;
+
+  // ---- o_proj + residual
+  load_vec(cs, sm.xs, p.w.attn, NT * QSZ);
+  named_sync(1, NCT);
+  {
+    const Plan pl = make_plan(SK_O, lw, nullptr, 0, cs.cta, cs.G);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, QSZ)) return false;
+    const int nr = pl.r1 - pl.r0;
+    for (int e = cs.tid; e < NT * nr; e += NCT) {
+      const int t = e / nr, r = e - t * nr;
+      const float v = (sm.part[(2 * r) * NT + t] + sm.part[(2 * r + 1) * NT + t]) + __ldcg(hin + t * HID + pl.r0 + r);
+      __stcg(p.w.hmid + t * HID + pl.r0 + r, v);
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return false;
+
+  // ---- post-attention RMSNorm + gate/up + SiLU
+  load_vec(cs, sm.xs, p.w.hmid, NT * HID);
+  named_sync(1, NCT);
+  rmsnorm_smem<NT>(sm, cs, sm.xs, lw->post_norm, p.eps);
+  {
+    const Plan pl = make_plan(SK_GU, lw, nullptr, 0, cs.cta, cs.G);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+    const int nj = pl.r1 - pl.r0;
+    for (int e = cs.tid; e < NT * nj; e += NCT) {
+      const int t = e / nj, j = e - t * nj;
+      const float g = sm.part[j * NT + t], u = sm.part[(nj + j) * NT + t];
+      __stcg(p.w.mlp + t * INTER + pl.r0 + j, (g / (1.0f + expf(-g))) * u);
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return false;
+
+  // ---- down_proj + residual
+  load_vec(cs, sm.xs, p.w.mlp, NT * INTER);
+  named_sync(1, NCT);
+  {
+    const Plan pl = make_plan(SK_D, lw, nullptr, 0, cs.cta, cs.G);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, INTER)) return false;
+    const int nr = pl.r1 - pl.r0;
+    for (int e = cs.tid; e < NT * nr; e += NCT) {
+      const int t = e / nr, r = e - t * nr;
+      float v = ((sm.part[(3 * r) * NT + t] + sm.part[(3 * r + 1) * NT + t]) + sm.part[(3 * r + 2) * NT + t]) +
+                __ldcg(p.w.hmid + t * HID + pl.r0 + r);
+      if (!CP) v = round_bf16(v);
+      __stcg(hout + t * HID + pl.r0 + r, v);
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return false;
+  load_vec(cs, sm.xs, hout, NT * HID);
+  named_sync(1, NCT);
+  return true;
+}
+
+// Runs a stack of layers; on return sm.xs holds the final-normed hidden (fp32) of NT tokens.
+template <int NT, bool CP>
+__device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0) {
+  const LayerW* L = CP ? p.cp_layers : p.bb_layers;
+  const int n = CP ? p.n_cp : p.n_bb;
+  // layer input already in sm.xs; CTA 0 publishes it for the o_proj residual.
+  float* hb0 = p.w.hbuf;
+  float* hb1 = p.w.hbuf + NTMAX * HID;
+  if (cs.cta == 0)
+    for (int i = cs.tid; i < NT * HID; i += NCT) __stcg(hb0 + i, sm.xs[i]);
+  for (int l = 0; l < n; ++l) {
+    const float* hin = (l & 1) ? hb1 : hb0;
+    float* hout = (l & 1) ? hb0 : hb1;
+    if (!layer<NT, CP>(p, sm, cs, L + l, l, p0, hin, hout)) return false;
+  }
+  rmsnorm_smem<NT>(sm, cs, sm.xs, CP ? p.cp_norm : p.bb_norm, p.eps);
+  return true;
+}
+
+// Head GEMV on token t of sm.xs (bf16-cast hidden, generator.py:158,351) -> bf16 logits in
+// global, followed by a grid barrier.
+__device__ bool head(const Params& p, Smem& sm, Cons& cs, const bf16* W, int rows, int t) {
+  float* x = sm.xs + t * HID;
+  for (int i = cs.tid; i < HID; i += NCT) x[i] = round_bf16(x[i]);
+  named_sync(1, NCT);
+  const Plan pl = make_plan(SK_HEAD, nullptr, W, rows, cs.cta, cs.G);
+  if (!gemv<1>(p, pl, sm, cs, x, HID)) return false;
+  for (int r = cs.tid; r < pl.r1 - pl.r0; r += NCT) __stcg(p.w.logits + pl.r0 + r, round_bf16(sm.part[r]));
+  return grid_sync(p, sm, cs);
+}
+
+// ------------------------------------------------------------------------------------------
+// Sampler (generator.py:158-172,178-207), computed redundantly by every CTA so that the
+// token is known grid-wide without another barrier. Each consumer thread owns 8 contiguous
+// vocabulary entries.
+// ------------------------------------------------------------------------------------------
+struct SampleCfg {
+  int V;
+  int do_sample;
+  float temperature;
+  int top_k;
+  int suppress_from;   // ids >= suppress_from are masked, except eos (V = none)
+  int eos;
+  int mask_eos;
+  float penalty;
+  const uint8_t* seen; // nullptr = no repetition penalty
+  uint32_t u24;
+};
+
+constexpr int SPT = VMAX / NCT;  // 8 entries per thread
+
+__device__ __forceinline__ uint32_t bf16_key(float v) {
+  uint32_t b = __float_as_uint(v) >> 16;
+  if (b == 0x8000u) b = 0u;  // -0 == +0
+  return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+}
+
+// Find the top-k threshold key: largest key K with count(key >= K) >= k.
+__device__ uint32_t radix_threshold(Smem& sm, Cons& cs, const uint32_t (&key)[SPT], int k) {
+  uint32_t prefix = 0;
+  int need = k;
+#pragma unroll 1
+  for (int pass = 0; pass < 2; ++pass) {
+    const int shift = pass == 0 ? 8 : 0;
+    for (int i = cs.tid; i < 256; i += NCT) sm.hist[i] = 0;
+    named_sync(1, NCT);
+#pragma unroll
+    for (int j = 0; j < SPT; ++j) {
+      if (pass == 0 || (key[j] >> 8) == (prefix >> 8)) atomicAdd(&sm.hist[(key[j] >> shift) & 0xffu], 1);
+    }
+    named_sync(1, NCT);
+    if (cs.warp == 0) {
+      // lane l owns bins [8l, 8l+8); find the bin where the count from the top reaches need
+      int c8 = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) c8 += sm.hist[8 * cs.lane + b];
+      int above = 0;  // count in bins strictly above this lane's range
+      int s = c8;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_down_sync(0xffffffffu, s, o);
+        if (cs.lane + o < 32) s += v;
+      }
+      above = s - c8;  // inclusive suffix minus own
+      const bool mine = (above < need) && (s >= need);
+      const unsigned ballot = __ballot_sync(0xffffffffu, mine);
+      const int src = __ffs(ballot) - 1;
+      if (cs.lane == src) {
+        int cnt = above;
+        int bin = 8 * cs.lane + 7;
+        for (; bin > 8 * cs.lane; --bin) {
+          if (cnt + sm.hist[bin] >= need) break;
+          cnt += sm.hist[bin];
+        }
+        sm.bcast[1] = bin;
+        sm.bcast[2] = need - cnt;
+      }
+    }
+    named_sync(1, NCT);
+    const int bin = sm.bcast[1];
+    need = sm.bcast[2];
+    prefix |= static_cast<uint32_t>(bin) << shift;
+    named_sync(1, NCT);
+  }
+  return prefix;
+}
+
+__device__ int sample(const Params& p, Smem& sm, Cons& cs, const SampleCfg& c) {
+  float v[SPT];
+  const int base = cs.tid * SPT;
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) {
+    const int i = base + j;
+    float x = -INFINITY;
+    if (i < c.V) {
+      x = __ldcg(p.w.logits + i);
+      if (i >= c.suppress_from && i != c.eos) x = -INFINITY;
+      if (c.seen != nullptr && __ldcg(c.seen + i)) x = round_bf16(x > 0.f ? __fdiv_rn(x, c.penalty) : x * c.penalty);
+      if (c.mask_eos && i == c.eos) x = -INFINITY;
+    }
+    v[j] = x;
+  }
+  if (!c.do_sample) {
+    // argmax, first index on ties (torch.argmax)
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < SPT; ++j) {
+      if (base + j < c.V && (bi == 0x7fffffff || v[j] > bv)) {
+        bv = v[j];
+        bi = base + j;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (cs.lane == 0) {
+      sm.red[cs.warp] = bv;
+      sm.red[NCW + cs.warp] = __int_as_float(bi);
+    }
+    named_sync(1, NCT);
+    float best = sm.red[0];
+    int besti = __float_as_int(sm.red[NCW]);
+    for (int w = 1; w < NCW; ++w) {
+      const float ov = sm.red[w];
+      const int oi = __float_as_int(sm.red[NCW + w]);
+      if (ov > best || (ov == best && oi < besti)) {
+        best = ov;
+        besti = oi;
+      }
+    }
+    named_sync(1, NCT);
+    return besti;
+  }
+  // scaled = bf16(l / T)
+  uint32_t key[SPT];
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) {
+    v[j] = round_bf16(__fdiv_rn(v[j], c.temperature));
+    key[j] = (base + j < c.V) ? bf16_key(v[j]) : 0u;
+  }
+  uint32_t thr = 0;
+  if (c.top_k > 0 && c.top_k < c.V) thr = radix_threshold(sm, cs, key, c.top_k);
+  // softmax over kept entries (probabilities rounded to bf16 as torch.softmax on bf16)
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SPT; ++j)
+    if (base + j < c.V && key[j] >= thr) mx = fmaxf(mx, v[j]);
+  mx = warp_max(mx);
+  if (cs.lane == 0) sm.red[cs.warp] = mx;
+  named_sync(1, NCT);
+  mx = sm.red[0];
+  for (int w = 1; w < NCW; ++w) mx = fmaxf(mx, sm.red[w]);
+  named_sync(1, NCT);
+  float e[SPT];
+  float es[1] = {0.f};
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) {
+    e[j] = (base + j < c.V && key[j] >= thr && v[j] != -INFINITY) ? expf(v[j] - mx) : 0.f;
+    es[0] += e[j];
+  }
+  block_sum<1>(sm, cs, es);
+  // exact fixed-point inverse CDF over the bf16 probabilities in vocabulary order
+  unsigned long long f[SPT];
+  unsigned long long tsum = 0;
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) {
+    const float pr = round_bf16(__fdiv_rn(e[j], es[0]));
+    f[j] = pr > 0.f ? static_cast<unsigned long long>(ldexp(static_cast<double>(pr), 60)) : 0ull;
+    tsum += f[j];
+  }
+  // block exclusive scan of tsum
+  unsigned long long incl = tsum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (cs.lane >= o) incl += n;
+  }
+  if (cs.lane == 31) sm.ured[cs.warp] = incl;
+  named_sync(1, NCT);
+  unsigned long long wpre = 0, total = 0;
+  for (int w = 0; w < NCW; ++w) {
+    if (w < cs.warp) wpre += sm.ured[w];
+    total += sm.ured[w];
+  }
+  named_sync(1, NCT);
+  const unsigned long long hi = __umul64hi(static_cast<unsigned long long>(c.u24), total);
+  const unsigned long long lo = static_cast<unsigned long long>(c.u24) * total;
+  const unsigned long long target = (hi << 40) | (lo >> 24);
+  unsigned long long cum = wpre + (incl - tsum);
+  float cnt[1] = {0.f};
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) {
+    cum += f[j];
+    if (base + j < c.V && cum <= target) cnt[0] += 1.f;
+  }
+  block_sum<1>(sm, cs, cnt);
+  const int pick = static_cast<int>(cnt[0]);
+  return pick < c.V ? pick : c.V - 1;
+}
+
+__device__ __forceinline__ uint32_t draw_u24(const Sampling& sp, int frame, int group) {
+  const uint4 r = philox4x32_10(make_uint4(static_cast<uint32_t>(frame), static_cast<uint32_t>(group),
+                                           static_cast<uint32_t>(sp.philox_stream), 0u),
+                                make_uint2(static_cast<uint32_t>(sp.seed), static_cast<uint32_t>(sp.seed >> 32)));
+  return r.x >> 8;
+}
+
+// Write a bf16 row (as fp32) into NT slot t of sm.xs.
+__device__ __forceinline__ void xs_from_bf16(Cons& cs, float* dst, const bf16* src) {
+  for (int i = cs.tid; i < HID; i += NCT) dst[i] = __bfloat162float(src[i]);
+}
+
+// ------------------------------------------------------------------------------------------
+// Programs
+// ------------------------------------------------------------------------------------------
+__device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
+  StreamState* st = p.st;
+  const int done = ld_volatile_i32(&st->done);
+  const int g0 = ld_volatile_i32(&st->g0);
+  const int pos = ld_volatile_i32(&st->position);
+  const int step = ld_volatile_i32(&st->step);
+  if (done) return true;
+  if (g0 == p.sp.eos) {  // generator.py:126
+    if (cs.cta == 0 && cs.tid == 0) st->done = 1;
+    return true;
+  }
+  if (g0 < 0 || g0 >= p.vocab) {
+    fail(p, sm, DEV_ERR_BAD_TOKEN);
+    return false;
+  }
+  if (pos < 0 || pos >= p.bb_max_seq || pos >= p.rope_rows || step >= p.max_frames) {
+    fail(p, sm, DEV_ERR_BAD_POSITION);
+    return false;
+  }
+  if (cs.cta == 0 && cs.tid == 0) st->seen[g0] = 1;  // generated_g0.append (generator.py:129)
+
+  int toks[NGROUPS];
+  toks[0] = g0;
+  // ---- code-predictor pass 0: [bf16(h), codec_embedding[g0]] at positions 0, 1
+  for (int i = cs.tid; i < HID; i += NCT) {
+    sm.xs[i] = round_bf16(__ldcg(st->h + i));
+    sm.xs[HID + i] = __bfloat162float(p.codec_emb[static_cast<size_t>(g0) * HID + i]);
+  }
+  named_sync(1, NCT);
+  if (!run_stack<2, true>(p, sm, cs, 0)) return false;
+  for (int g = 0; g < NCPHEADS; ++g) {
+    if (g > 0) {
+      // pass g: codec embedding g-1 of token g at position g+1 (generator.py:347-352)
+      const bf16* row = p.cp_emb[g - 1] + static_cast<size_t>(toks[g]) * HID;
+      xs_from_bf16(cs, sm.xs, row);
+      named_sync(1, NCT);
+      if (!run_stack<1, true>(p, sm, cs, g + 1)) return false;
+    }
+    if (!head(p, sm, cs, p.cp_head[g], p.cp_vocab, g == 0 ? 1 : 0)) return false;
+    if (p.dbg_cp_logits && cs.cta == 0)
+      for (int i = cs.tid; i < p.cp_vocab; i += NCT) p.dbg_cp_logits[g * p.cp_vocab + i] = __ldcg(p.w.logits + i);
+    SampleCfg c;
+    c.V = p.cp_vocab;
+    c.do_sample = p.sp.cp_do_sample;
+    c.temperature = p.sp.cp_temperature;
+    c.top_k = p.sp.cp_top_k;
+    c.suppress_from = p.cp_vocab;
+    c.eos = -1;
+    c.mask_eos = 0;
+    c.penalty = 1.f;
+    c.seen = nullptr;
+    c.u24 = c.do_sample ? draw_u24(p.sp, step, g + 1) : 0u;
+    toks[g + 1] = sample(p, sm, cs, c);
+  }
+  // ---- combine (generator.py:143-149,356-362): sequential bf16 adds
+  {
+    const bf16* extra = step < p.n_trailing ? p.trailing + static_cast<size_t>(step) * HID : p.pad;
+    for (int i = cs.tid; i < HID; i += NCT) {
+      float a = __bfloat162float(p.codec_emb[static_cast<size_t>(g0) * HID + i]);
+#pragma unroll 1
+      for (int q = 0; q < NCPHEADS; ++q)
+        a = round_bf16(a + __bfloat162float(p.cp_emb[q][static_cast<size_t>(toks[q + 1]) * HID + i]));
+      sm.xs[i] = round_bf16(a + __bfloat162float(extra[i]));
+    }
+    named_sync(1, NCT);
+  }
+  // ---- backbone step at position pos
+  if (!run_stack<1, false>(p, sm, cs, pos)) return false;
+  if (cs.cta == 0)
+    for (int i = cs.tid; i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
+  if (!head(p, sm, cs, p.codec_head, p.vocab, 0)) return false;
+  if (p.dbg_g0_logits && cs.cta == 0)
+    for (int i = cs.tid; i < p.vocab; i += NCT) p.dbg_g0_logits[i] = __ldcg(p.w.logits + i);
+  SampleCfg c;
+  c.V = p.vocab;
+  c.do_sample = p.sp.do_sample;
+  c.temperature = p.sp.temperature;
+  c.top_k = p.sp.top_k;
+  c.suppress_from = p.vocab - 1024;
+  c.eos = p.sp.eos;
+  c.mask_eos = (step + 1 < p.sp.min_new_tokens) ? 1 : 0;
+  c.penalty = p.sp.repetition_penalty;
+  c.seen = (p.sp.repetition_penalty != 1.f) ? st->seen : nullptr;
+  c.u24 = c.do_sample ? draw_u24(p.sp, step + 1, 0) : 0u;
+  const int g0n = sample(p, sm, cs, c);
+  if (cs.cta == 0 && cs.tid == 0) {
+    int32_t* out = p.codes + static_cast<size_t>(step) * NGROUPS;
+    for (int g = 0; g < NGROUPS; ++g) out[g] = toks[g];
+    st->g0 = g0n;
+    st->position = pos + 1;
+    st->step = step + 1;
+  }
+  return true;
+}
+
+__device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
+  const int pos = p.position;
+  const int max_seq = cp ? p.cp_max_seq : p.bb_max_seq;
+  if (pos < 0 || pos >= max_seq || pos >= p.rope_rows) {
+    fail(p, sm, DEV_ERR_BAD_POSITION);
+    return false;
+  }
+  xs_from_bf16(cs, sm.xs, p.in_emb);
+  named_sync(1, NCT);
+  const bool ok = cp ? run_stack<1, true>(p, sm, cs, pos) : run_stack<1, false>(p, sm, cs, pos);
+  if (!ok) return false;
+  if (cs.cta == 0) {
+    for (int i = cs.tid; i < HID; i += NCT) {
+      if (p.out_hidden) p.out_hidden[i] = sm.xs[i];
+      if (p.out_raw_hidden) {
+        const float* last = p.w.hbuf + ((cp ? p.n_cp : p.n_bb) & 1 ? NTMAX * HID : 0);
+        p.out_raw_hidden[i] = __float2bfloat16_rn(__ldcg(last + i));
+      }
+    }
+  }
+  if (!cp && (p.flags & FLAG_HEAD_SAMPLE)) {
+    // end of prefill: first group-0 token (generator.py:115-120), no repetition history
+    StreamState* st = p.st;
+    if (cs.cta == 0)
+      for (int i = cs.tid; i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
+    if (!head(p, sm, cs, p.codec_head, p.vocab, 0)) return false;
+    SampleCfg c;
+    c.V = p.vocab;
+    c.do_sample = p.sp.do_sample;
+    c.temperature = p.sp.temperature;
+    c.top_k = p.sp.top_k;
+    c.suppress_from = p.vocab - 1024;
+    c.eos = p.sp.eos;
+    c.mask_eos = p.sp.min_new_tokens > 0 ? 1 : 0;
+    c.penalty = 1.f;
+    c.seen = nullptr;
+    c.u24 = c.do_sample ? draw_u24(p.sp, 0, 0) : 0u;
+    const int g0 = sample(p, sm, cs, c);
+    if (cs.cta == 0 && cs.tid == 0) {
+      st->g0 = g0;
+      st->position = pos + 1;
+      st->step = 0;
+      st->done = 0;
+    }
+  }
+  return true;
+}
+
+extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < NSLOTS; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], NCW);
+    }
+    sm.abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int warp = tid >> 5;
+  if (warp == NCW) {
+    if ((tid & 31) == 0) producer_main(p, sm, blockIdx.x, gridDim.x);
+    return;
+  }
+  Cons cs;
+  cs.slot = 0;
+  cs.round = 0;
+  cs.bar_target = 0;
+  cs.cta = blockIdx.x;
+  cs.G = gridDim.x;
+  cs.tid = tid;
+  cs.warp = warp;
+  cs.lane = tid & 31;
+  bool ok;
+  if (p.mode == MODE_FRAME)
+    ok = run_frame(p, sm, cs);
+  else
+    ok = run_step(p, sm, cs, p.mode == MODE_CP_STEP);
+  if (!ok) *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// Host helpers
+// ------------------------------------------------------------------------------------------
+cudaError_t kernel_setup(int device, int* num_ctas, size_t* smem_bytes) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return e;
+  const size_t smem = sizeof(Smem);
+  e = cudaFuncSetAttribute(qtt_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int sms = 0, coop = 0, per_sm = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+  if (e != cudaSuccess) return e;
+  if (!coop) return cudaErrorNotSupported;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qtt_decode_kernel, NTHREADS, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  *num_ctas = sms;
+  *smem_bytes = smem;
+  return cudaSuccess;
+}
+
+cudaError_t launch(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(p.w.bar, 0, sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return e;
+  void* args[] = {const_cast<Params*>(&p)};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(qtt_decode_kernel), dim3(num_ctas), dim3(NTHREADS), args,
+                                     smem_bytes, stream);
+}
+
+}  // namespace qtt

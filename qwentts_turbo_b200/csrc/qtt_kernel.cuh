@@ -1,0 +1,157 @@
+// Shared definitions between the persistent decode kernel (qtt_kernel.cu) and the
+// host-side C-ABI (qtt_api.cu). Model shape constants are compile-time: the engine is
+// specialised for the Qwen3-TTS-12Hz-0.6B shape (config.cuh:33-40 in the reference) and
+// qtt_engine_create rejects any other qtt_dims.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace qtt {
+
+typedef __nv_bfloat16 bf16;
+
+constexpr int HID = 1024;
+constexpr int INTER = 3072;
+constexpr int NQH = 16;
+constexpr int NKVH = 8;
+constexpr int HD = 128;
+constexpr int QSZ = NQH * HD;              // 2048
+constexpr int KVSZ = NKVH * HD;            // 1024
+constexpr int QKV_ROWS = QSZ + 2 * KVSZ;   // 4096
+constexpr int NGROUPS = 16;                // codebooks per frame
+constexpr int NCPHEADS = NGROUPS - 1;      // 15
+constexpr int VMAX = 3072;                 // largest head (codec head)
+
+// Weight streaming: a "unit" is 1024 consecutive bf16 of one weight row (2 KB); a ring slot
+// holds 12 units (24 KB) so that rows of 1, 2 or 3 units (K = 1024, 2048, 3072) tile it and
+// every consumer warp keeps the same part of the activation vector for a whole stage.
+constexpr int UNIT = 1024;
+constexpr int UNIT_BYTES = UNIT * 2;
+constexpr int SLOT_UNITS = 12;
+constexpr int SLOT_BYTES = SLOT_UNITS * UNIT_BYTES;
+constexpr int NSLOTS = 7;
+constexpr int NCW = 12;                    // consumer warps
+constexpr int NCT = NCW * 32;              // consumer threads
+constexpr int NTHREADS = NCT + 32;         // + one producer warp
+constexpr int NTMAX = 2;                   // tokens per pass (2 = code-predictor prefill pair)
+constexpr int MAXPART = 256;               // partial-sum units per stage per CTA
+constexpr int ATT_TARGET = 64;             // attention positions per work item (target)
+constexpr int ATT_CHMAX = 256;             // attention positions per work item (max)
+constexpr int MAX_ATT_CHUNKS = 32;         // attention work items per KV head (max)
+constexpr int PRT_STRIDE = HD + 2;         // partial record: m, l, acc[128]
+
+// Same layout as TTSLayerWeights / CPLayerWeights of the reference
+// (fused_decode_tts.cu:22-34, fused_decode_code_predictor.cu:30-42).
+struct LayerW {
+  const bf16* in_norm;
+  const bf16* wq;
+  const bf16* wk;
+  const bf16* wv;
+  const bf16* q_norm;
+  const bf16* k_norm;
+  const bf16* wo;
+  const bf16* post_norm;
+  const bf16* wg;
+  const bf16* wu;
+  const bf16* wd;
+};
+
+// Per-utterance decode state kept on the device so that frames run back to back with no
+// host round trip.
+struct StreamState {
+  int position;   // next KV position of the backbone
+  int step;       // frames produced so far
+  int g0;         // group-0 token of the next frame
+  int done;       // 1 once group 0 == EOS was reached
+  int pad[4];
+  float h[HID];   // final-normed backbone hidden of the last step (fp32)
+  uint8_t seen[VMAX];  // repetition-penalty history of group-0 tokens
+};
+
+struct Sampling {
+  int do_sample;
+  float temperature;
+  int top_k;
+  int cp_do_sample;
+  float cp_temperature;
+  int cp_top_k;
+  int min_new_tokens;
+  float repetition_penalty;
+  int eos;
+  int philox_stream;
+  unsigned long long seed;
+};
+
+struct Work {
+  uint32_t* bar;       // grid barrier counter (zeroed before every launch)
+  int* err;            // first device error code (sticky until the host clears it)
+  uint32_t* att_cnt;   // [NKVH] last-arriver counters of the attention combine
+  float* hbuf;         // [2][NTMAX][HID] layer input / output
+  float* qkv;          // [NTMAX][QKV_ROWS]
+  float* attn;         // [NTMAX][QSZ]
+  float* prt;          // [NTMAX][NQH][MAX_ATT_CHUNKS][PRT_STRIDE]
+  float* hmid;         // [NTMAX][HID]
+  float* mlp;          // [NTMAX][INTER]
+  float* logits;       // [VMAX]
+};
+
+size_t work_bytes();
+void work_carve(void* base, Work* w);
+
+enum Mode : int { MODE_FRAME = 0, MODE_BB_STEP = 1, MODE_CP_STEP = 2 };
+enum Flags : int { FLAG_HEAD_SAMPLE = 1 };
+
+struct Params {
+  // model (device pointers)
+  const LayerW* bb_layers;
+  int n_bb;
+  const bf16* bb_norm;
+  const bf16* codec_emb;
+  const bf16* codec_head;
+  int vocab;
+  const LayerW* cp_layers;
+  int n_cp;
+  const bf16* cp_norm;
+  const bf16* const* cp_emb;   // device array [15]
+  const bf16* const* cp_head;  // device array [15]
+  int cp_vocab;
+  const bf16* cos_tab;
+  const bf16* sin_tab;
+  int rope_rows;
+  float attn_scale;
+  float eps;
+  // caches [layer][kv head][max_seq][128]
+  bf16* bb_k;
+  bf16* bb_v;
+  int bb_max_seq;
+  float* cp_k;
+  float* cp_v;
+  int cp_max_seq;
+  Work w;
+  // launch
+  int mode;
+  int flags;
+  int position;            // step modes
+  const bf16* in_emb;      // step modes: input embedding [HID] bf16
+  float* out_hidden;       // step modes: final-normed fp32 hidden [HID]
+  bf16* out_raw_hidden;    // optional: last layer's bf16 hidden [HID] (reference hidden_buffer)
+  // frame mode
+  StreamState* st;
+  int32_t* codes;          // [max_frames][16]
+  int max_frames;
+  const bf16* trailing;    // [n_trailing][HID]
+  int n_trailing;
+  const bf16* pad;         // [HID]
+  Sampling sp;
+  // optional copies of the raw bf16 head logits of the last frame (parity tests)
+  float* dbg_cp_logits;    // [15][cp_vocab]
+  float* dbg_g0_logits;    // [vocab]
+};
+
+// Host side: configure the kernel once per device and report the launch shape.
+cudaError_t kernel_setup(int device, int* num_ctas, size_t* smem_bytes);
+// Host side: zero the barrier counter and cooperatively launch one program.
+cudaError_t launch(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream);
+
+}  // namespace qtt
