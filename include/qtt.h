@@ -211,6 +211,9 @@ qtt_status qtt_cp_step(qtt_engine* e, const void* emb, int position, float* out_
 /* Test hook: when non-NULL, each frame copies its raw bf16 head logits (as fp32) into
  * cp_logits [15][cp_vocab] and g0_logits [vocab]. Pass NULLs to turn it off. */
 qtt_status qtt_set_debug_outputs(qtt_engine* e, float* cp_logits, float* g0_logits);
+/* Profiling hook: when n > 0, each launch writes %globaltimer (ns) into stamps[0] at start
+ * and stamps[k] after its k-th grid barrier (k < n). Pass n = 0 to turn it off. */
+qtt_status qtt_set_debug_timeline(qtt_engine* e, unsigned long long* stamps, int n);
 /* Synchronises `stream` and converts the engine's device error word into a status. */
 qtt_status qtt_check(qtt_engine* e, cudaStream_t stream);
 

@@ -51,8 +51,8 @@ HEAD_DIM = 128
 
 
 def bf16r(x: torch.Tensor) -> torch.Tensor:
-    """Round fp32 values to bf16 (round-to-nearest-even) and back to fp32."""
-    return x.to(torch.bfloat16).to(torch.float32)
+    """Round to bf16 (round-to-nearest-even) and back to the input's dtype (fp32 or fp64)."""
+    return x.to(torch.bfloat16).to(x.dtype)
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -153,8 +153,9 @@ def sample_token(logits: torch.Tensor, do_sample: bool, temperature: float, top_
                  top_p: float = 1.0, suppress_eos_id=None, u24: int | None = None) -> int:
     """generator.py:178-207 with the multinomial draw replaced by :func:`inverse_cdf_pick`.
     ``logits`` holds bf16 values (fp32 dtype). Intermediate tensors are bf16 as in the
-    reference: scaled = bf16(l / T), probs = bf16(softmax)."""
-    logits = logits.clone()
+    reference: scaled = bf16(l / T), probs = bf16(softmax), all with fp32 arithmetic (torch's
+    opmath for bf16 tensors) whatever the oracle's compute dtype."""
+    logits = logits.to(torch.float32).clone()
     if suppress_eos_id is not None:
         logits[suppress_eos_id] = float("-inf")
     if not do_sample:
@@ -183,7 +184,7 @@ def apply_repetition_penalty(logits: torch.Tensor, history, penalty: float) -> t
     """generator.py:161-167: s > 0 ? s / p : s * p on the history's tokens, bf16 result."""
     if penalty == 1.0 or not history:
         return logits
-    out = logits.clone()
+    out = logits.to(torch.float32).clone()
     idx = torch.tensor(sorted(set(int(t) for t in history)), dtype=torch.long)
     s = out[idx]
     out[idx] = bf16r(torch.where(s > 0, s / penalty, s * penalty))
@@ -194,15 +195,15 @@ def apply_repetition_penalty(logits: torch.Tensor, history, penalty: float) -> t
 # Model
 # ----------------------------------------------------------------------------------------
 class _Stack:
-    """fp32 copies of one decoder stack (backbone or code predictor)."""
+    """fp32 (or fp64) copies of one decoder stack (backbone or code predictor)."""
 
-    def __init__(self, weights: dict, prefix: str, n_layers: int):
+    def __init__(self, weights: dict, prefix: str, n_layers: int, dtype=torch.float32):
         from qwentts_turbo_b200.config import LAYER_TENSORS
         self.layers = []
         for li in range(n_layers):
-            self.layers.append({t: weights[f"{prefix}.layers.{li}.{t}"].float().contiguous()
+            self.layers.append({t: weights[f"{prefix}.layers.{li}.{t}"].to(dtype).contiguous()
                                 for t in LAYER_TENSORS})
-        self.norm = weights[f"{prefix}.norm"].float()
+        self.norm = weights[f"{prefix}.norm"].to(dtype)
 
 
 class Qwen3TTSOracle:
@@ -210,7 +211,7 @@ class Qwen3TTSOracle:
 
     def __init__(self, weights: dict, dims=None, backbone_layers: int | None = None,
                  cp_layers: int | None = None, max_seq: int = 4096, cp_max_seq: int = 32,
-                 exact_rope: bool = False):
+                 exact_rope: bool = False, dtype=torch.float32):
         from qwentts_turbo_b200.config import DEFAULT_DIMS
         from qwentts_turbo_b200.weights import rope_tables
         d = dims or DEFAULT_DIMS
@@ -219,12 +220,13 @@ class Qwen3TTSOracle:
         self.nc = d.cp_layers if cp_layers is None else cp_layers
         self.max_seq = max_seq
         self.cp_max_seq = cp_max_seq
-        self.bb = _Stack(weights, "talker", self.nb)
-        self.cp = _Stack(weights, "cp", self.nc)
-        self.codec_embedding = weights["talker.codec_embedding"].float()
-        self.codec_head = weights["talker.codec_head"].float()
-        self.cp_embed = [weights[f"cp.codec_embedding.{g}"].float() for g in range(d.n_groups - 1)]
-        self.cp_head = [weights[f"cp.lm_head.{g}"].float() for g in range(d.n_groups - 1)]
+        self.dt = dtype
+        self.bb = _Stack(weights, "talker", self.nb, dtype)
+        self.cp = _Stack(weights, "cp", self.nc, dtype)
+        self.codec_embedding = weights["talker.codec_embedding"].to(dtype)
+        self.codec_head = weights["talker.codec_head"].to(dtype)
+        self.cp_embed = [weights[f"cp.codec_embedding.{g}"].to(dtype) for g in range(d.n_groups - 1)]
+        self.cp_head = [weights[f"cp.lm_head.{g}"].to(dtype) for g in range(d.n_groups - 1)]
         rows = max(max_seq, cp_max_seq)
         if exact_rope:
             # fp32 tables without the bf16 cast (HF Qwen3RotaryEmbedding), for pinning the layer
@@ -233,10 +235,10 @@ class Qwen3TTSOracle:
             inv = 1.0 / (d.rope_theta ** (torch.arange(0, half, dtype=torch.float32) / half))
             emb = torch.outer(torch.arange(rows, dtype=torch.float32), inv)
             emb = torch.cat((emb, emb), dim=-1)
-            self.cos, self.sin = torch.cos(emb), torch.sin(emb)
+            self.cos, self.sin = torch.cos(emb).to(dtype), torch.sin(emb).to(dtype)
         else:
             cos, sin = rope_tables(rows, d.head_dim, d.rope_theta)
-            self.cos, self.sin = cos.float(), sin.float()
+            self.cos, self.sin = cos.to(dtype), sin.to(dtype)
         self.scale = 1.0 / math.sqrt(d.head_dim)
         self.reset_backbone()
         self.reset_cp()
@@ -244,21 +246,21 @@ class Qwen3TTSOracle:
     # ---- state -------------------------------------------------------------------------
     def reset_backbone(self):
         d = self.d
-        self.bk = torch.zeros(self.nb, d.n_kv_heads, self.max_seq, d.head_dim)
+        self.bk = torch.zeros(self.nb, d.n_kv_heads, self.max_seq, d.head_dim, dtype=self.dt)
         self.bv = torch.zeros_like(self.bk)
         self.position = 0
 
     def reset_cp(self):
         d = self.d
-        self.ck = torch.zeros(self.nc, d.n_kv_heads, self.cp_max_seq, d.head_dim)
+        self.ck = torch.zeros(self.nc, d.n_kv_heads, self.cp_max_seq, d.head_dim, dtype=self.dt)
         self.cv = torch.zeros_like(self.ck)
         self.cp_position = 0
 
     def set_kv_cache(self, k: torch.Tensor, v: torch.Tensor):
         """megakernel_backbone.py:285-294: copy [L, n_kv, len, hd] into the cache (bf16)."""
         n = k.shape[2]
-        self.bk[:, :, :n] = bf16r(k.float())
-        self.bv[:, :, :n] = bf16r(v.float())
+        self.bk[:, :, :n] = bf16r(k.to(self.dt))
+        self.bv[:, :, :n] = bf16r(v.to(self.dt))
 
     # ---- layer -------------------------------------------------------------------------
     def _layer(self, x, W, kc, vc, positions, kv_bf16: bool, out_bf16: bool):
@@ -300,7 +302,7 @@ class Qwen3TTSOracle:
         """Run tokens x [T, hidden] (bf16 values) at consecutive positions through the
         backbone; returns the final-RMSNorm fp32 hidden of every token [T, hidden]
         (fused_decode_tts.cu:728-831 for T = 1)."""
-        h = bf16r(x_bf16.float())
+        h = bf16r(x_bf16.to(self.dt))
         for li, W in enumerate(self.bb.layers):
             h = self._layer(h, W, self.bk[li], self.bv[li], positions, kv_bf16=True, out_bf16=True)
         return rms_norm(h, self.bb.norm, self.d.rms_eps)
@@ -325,7 +327,7 @@ class Qwen3TTSOracle:
     def cp_forward(self, x_bf16: torch.Tensor, positions) -> torch.Tensor:
         """Code-predictor layers on tokens [T, hidden] (bf16 inputs, fp32 hidden and KV,
         fused_decode_code_predictor.cu:565-668); returns final-normed fp32 [T, hidden]."""
-        h = bf16r(x_bf16.float())
+        h = bf16r(x_bf16.to(self.dt))
         for li, W in enumerate(self.cp.layers):
             h = self._layer(h, W, self.ck[li], self.cv[li], positions, kv_bf16=False, out_bf16=False)
         return rms_norm(h, self.cp.norm, self.d.rms_eps)
@@ -333,14 +335,14 @@ class Qwen3TTSOracle:
     @staticmethod
     def head_logits(W: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
         """bf16(W @ bf16(h)) (generator.py:158,331,351)."""
-        return bf16r(W @ bf16r(h.float()))
+        return bf16r(W @ bf16r(h.to(W.dtype)))
 
     def cp_chain(self, h_backbone: torch.Tensor, g0: int, do_sample=False, temperature=0.9,
                  top_k=50, seed=0, frame=0, stream=0, forced=None):
         """generator.py:309-354: groups 1..15 for one frame. Returns (tokens[15], logits list).
         ``forced`` (optional 15 ints) teacher-forces the tokens fed back (parity tests)."""
         self.reset_cp()
-        x0 = bf16r(h_backbone.float())
+        x0 = bf16r(h_backbone.to(self.dt))
         x1 = self.codec_embedding[g0]
         h = self.cp_forward(torch.stack([x0, x1]), [0, 1])[-1]
         tokens, all_logits = [], []
@@ -360,7 +362,7 @@ class Qwen3TTSOracle:
         c = self.codec_embedding[groups[0]].clone()
         for i in range(15):
             c = bf16r(c + self.cp_embed[i][groups[i + 1]])
-        return bf16r(c + bf16r(extra_row.float()))
+        return bf16r(c + bf16r(extra_row.to(self.dt)))
 
     def suppress_mask(self, eos: int):
         d = self.d

@@ -636,6 +636,13 @@ extern "C" qtt_status qtt_set_debug_outputs(qtt_engine* e, float* cp_logits, flo
   return QTT_OK;
 }
 
+extern "C" qtt_status qtt_set_debug_timeline(qtt_engine* e, unsigned long long* stamps, int n) {
+  if (!e || n < 0 || (n > 0 && !stamps)) return QTT_ERR_INVALID_ARG;
+  e->base.dbg_timeline = n > 0 ? stamps : nullptr;
+  e->base.dbg_timeline_len = n;
+  return QTT_OK;
+}
+
 extern "C" qtt_status qtt_check(qtt_engine* e, cudaStream_t stream) {
   if (!e) return QTT_ERR_INVALID_ARG;
   qtt_status r = set_device(e);

@@ -30,6 +30,7 @@ struct __align__(128) Smem {
   float xs[NTMAX * INTER];           // stage input vector; attention / sampler scratch
   float part[MAXPART * NTMAX];       // per-unit partial dot products of the current stage
   float red[4 * NCW];
+  double dred[NTMAX * NCW];
   unsigned long long ured[NCW + 1];
   int hist[256];
   uint64_t full[NSLOTS];
@@ -251,9 +252,33 @@ __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
       }
     }
     __threadfence();
+    if (p.dbg_timeline != nullptr && cs.cta == 0) {
+      const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+      if (k < static_cast<uint32_t>(p.dbg_timeline_len)) p.dbg_timeline[k] = globaltimer_ns();
+    }
   }
   named_sync(1, NCT);
   return !aborted(sm);
+}
+
+// fp64 sum of NT per-thread values over the consumer threads (fixed order, every thread gets
+// the same totals). Used for RMSNorm statistics.
+template <int NT>
+__device__ __forceinline__ void block_sum_d(Smem& sm, Cons& cs, double (&v)[NT]) {
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const double s = warp_sum_d(v[t]);
+    if (cs.lane == 0) sm.dred[t * NCW + cs.warp] = s;
+  }
+  named_sync(1, NCT);
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    double s = 0.0;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) s += sm.dred[t * NCW + w];
+    v[t] = s;
+  }
+  named_sync(1, NCT);
 }
 
 // Sum of NT per-thread values over the consumer threads; every thread gets the same totals.
@@ -278,17 +303,20 @@ __device__ __forceinline__ void block_sum(Smem& sm, Cons& cs, float (&v)[NT]) {
 // In-place RMSNorm of NT vectors of HID floats in shared memory: x * rsqrt(mean(x^2)+eps) * w.
 template <int NT>
 __device__ void rmsnorm_smem(Smem& sm, Cons& cs, float* x, const bf16* w, float eps) {
-  float ss[NT];
+  double ss[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    float a = 0.f;
-    for (int i = cs.tid; i < HID; i += NCT) a = fmaf(x[t * HID + i], x[t * HID + i], a);
+    double a = 0.0;
+    for (int i = cs.tid; i < HID; i += NCT) {
+      const double xv = x[t * HID + i];
+      a = fma(xv, xv, a);
+    }
     ss[t] = a;
   }
-  block_sum<NT>(sm, cs, ss);
+  block_sum_d<NT>(sm, cs, ss);
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    const float rstd = rsqrtf(ss[t] / static_cast<float>(HID) + eps);
+    const float rstd = rms_scale(ss[t], HID, eps);
     for (int i = cs.tid; i < HID; i += NCT) x[t * HID + i] = x[t * HID + i] * rstd * __bfloat162float(w[i]);
   }
   named_sync(1, NCT);
@@ -397,11 +425,11 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
 #pragma unroll
       for (int i = 0; i < 4; ++i) x[i] = __ldcg(src + cs.lane + 32 * i);
       if (vec < 3) {
-        float ss = 0.f;
+        double ss = 0.0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) ss = fmaf(x[i], x[i], ss);
-        ss = warp_sum(ss);
-        const float rstd = rsqrtf(ss / static_cast<float>(HD) + p.eps);
+        for (int i = 0; i < 4; ++i) ss = fma(static_cast<double>(x[i]), static_cast<double>(x[i]), ss);
+        ss = warp_sum_d(ss);
+        const float rstd = rms_scale(ss, HD, p.eps);
         const bf16* nw = vec < 2 ? L->q_norm : L->k_norm;
         float y[4], cv[4], sv[4];
 #pragma unroll
@@ -1049,6 +1077,8 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
     if ((tid & 31) == 0) producer_main(p, sm, blockIdx.x, gridDim.x);
     return;
   }
+  if (p.dbg_timeline != nullptr && blockIdx.x == 0 && tid == 0 && p.dbg_timeline_len > 0)
+    p.dbg_timeline[0] = globaltimer_ns();
   Cons cs;
   cs.slot = 0;
   cs.round = 0;

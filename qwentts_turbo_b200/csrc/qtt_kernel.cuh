@@ -147,6 +147,10 @@ struct Params {
   // optional copies of the raw bf16 head logits of the last frame (parity tests)
   float* dbg_cp_logits;    // [15][cp_vocab]
   float* dbg_g0_logits;    // [vocab]
+  // optional %globaltimer stamps (ns) taken by CTA 0 at launch start and after each grid
+  // barrier: dbg_timeline[0] = start, dbg_timeline[k] = barrier k (profiling)
+  unsigned long long* dbg_timeline;
+  int dbg_timeline_len;
 };
 
 // Host side: configure the kernel once per device and report the launch shape.

@@ -220,5 +220,13 @@ class Engine:
                                                   _ptr(g0_logits) if g0_logits is not None else None),
                    "qtt_set_debug_outputs")
 
+    def set_debug_timeline(self, stamps: torch.Tensor | None):
+        """stamps: int64 cuda tensor; each launch writes %globaltimer at start and after each
+        grid barrier into it (profiling). None turns it off."""
+        self._timeline = stamps
+        n = 0 if stamps is None else stamps.numel()
+        _lib.check(self.lib.qtt_set_debug_timeline(self.h, _ptr(stamps) if stamps is not None else None, n),
+                   "qtt_set_debug_timeline")
+
     def check(self, stream=None):
         _lib.check(self.lib.qtt_check(self.h, _stream_handle(stream)), "qtt_check")

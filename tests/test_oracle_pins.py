@@ -186,26 +186,25 @@ def test_repetition_penalty_matches_reference():
 @pytest.mark.skipif(not os.path.exists(GOLDEN), reason="reference-kernel golden vectors not generated yet")
 def test_oracle_matches_reference_kernel_golden():
     """Outputs of the reference's own CUDA kernels (run on a B200 by
-    tests/golden/make_ref_golden.py) vs the oracle on the same seeded inputs."""
+    tests/golden/make_ref_golden.py) vs the oracle on the same seeded inputs. The fp64 oracle
+    (exact math at the reference's rounding points) reproduces the reference kernel's C1
+    backbone step to < 1e-5 and its code-predictor steps to < 1e-5; the fp32 oracle differs by
+    a bf16 flip cascade (0.038 max-abs), which is why the GPU tests use the fp64 oracle."""
     from qwentts_turbo_b200.workloads import c1_inputs
     z = np.load(GOLDEN)
     nb, nc, ctx = int(z["bb_layers"]), int(z["cp_layers"]), int(z["ctx"])
     w = synthetic_weights(backbone_layers=nb, cp_layers=nc)
-    orc = O.Qwen3TTSOracle(w, backbone_layers=nb, cp_layers=nc, max_seq=512)
+    orc = O.Qwen3TTSOracle(w, backbone_layers=nb, cp_layers=nc, max_seq=512, dtype=torch.float64)
     k, v, emb = c1_inputs(nb, ctx, int(z["kv_seed"]))
-    orc.set_kv_cache(k.float(), v.float())
+    orc.set_kv_cache(k.double(), v.double())
     orc.position = ctx
-    h = orc.backbone_step(emb.float())
-    ref = torch.from_numpy(z["bb_hidden"])
-    assert (h - ref).abs().max().item() < 3e-2
-    lo = orc.head_logits(orc.codec_head, h)
-    lr = orc.head_logits(orc.codec_head, ref)
-    err = (lo - lr).abs().max().item()
-    assert err <= 2e-2 and err / lr.abs().max().item() <= 1e-2, err
+    h = orc.backbone_step(emb.double())
+    ref = torch.from_numpy(z["bb_hidden"]).double()
+    assert (h - ref).abs().max().item() < 1e-5
     # code-predictor steps (reference kernel: one token per launch from position 0)
     orc.reset_cp()
-    cp_in = torch.from_numpy(z["cp_emb"]).float()
-    cp_ref = torch.from_numpy(z["cp_hidden"])
+    cp_in = torch.from_numpy(z["cp_emb"]).double()
+    cp_ref = torch.from_numpy(z["cp_hidden"]).double()
     for i in range(cp_in.shape[0]):
         hi = orc.cp_forward(cp_in[i:i + 1], [i])[0]
-        assert (hi - cp_ref[i]).abs().max().item() < 1e-2, i
+        assert (hi - cp_ref[i]).abs().max().item() < 1e-5, i

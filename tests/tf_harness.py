@@ -1,0 +1,114 @@
+"""Teacher-forced frame comparison between the engine and the CPU oracle.
+
+Free-running greedy sequences of two correct implementations diverge at the first near-tie,
+so frame parity is measured the way the reference's own gate does it for early tokens
+(tests/test_audio.py:281-324 compares the first g0 tokens): each frame starts both sides
+from the SAME state -- the engine's backbone hidden, group-0 token, KV cache rows and
+repetition history -- and compares what each produces for that frame:
+
+* the 15 code-predictor logit vectors and tokens (the oracle runs the chain from the
+  engine's hidden and group-0 token, feeding back the engine's tokens),
+* the backbone step on the engine's combined embedding (same KV rows), the codec-head
+  logits and the next group-0 token (greedy, or sampled with the same Philox draw from
+  the engine's own logits, which isolates the device sampler).
+"""
+from __future__ import annotations
+
+import torch
+
+from oracle import qtt_oracle as O
+
+
+ATOL, RTOL = 2e-2, 1e-2   # BASELINE.json north_star logits tolerance (atol / rtol)
+
+
+def violation(a, b):
+    """max over finite elements of |a - b| - (ATOL + RTOL |b|); <= 0 means within tolerance."""
+    fin = torch.isfinite(b)
+    return float(((a - b).abs() - (ATOL + RTOL * b.abs()))[fin].max())
+
+
+def run_teacher_forced(eng, orc, embeds, trailing, pad, sp, n_frames, sampling=None):
+    """Returns a list of per-frame dicts. ``sampling``: None for greedy, else dict(temperature,
+    top_k, repetition_penalty, seed, stream, cp_temperature, cp_top_k, cp_do_sample,
+    min_new_tokens)."""
+    eng.prefill(0, embeds.cuda(), sp)
+    st = eng.state(0)
+    P = st["position"]
+    kc, vc = eng.kv(0)
+    orc.reset_backbone()
+    orc.set_kv_cache(kc[:, :, :P].cpu().to(orc.dt), vc[:, :, :P].cpu().to(orc.dt))
+    cp_dbg = torch.zeros(15, orc.d.cp_vocab, dtype=torch.float32, device="cuda")
+    g0_dbg = torch.zeros(orc.d.vocab, dtype=torch.float32, device="cuda")
+    eng.set_debug_outputs(cp_dbg, g0_dbg)
+    eos = orc.d.eos_token_id if sampling is None else sampling.get("eos", orc.d.eos_token_id)
+    sup = orc.suppress_mask(eos)
+    hist = []
+    out = []
+    try:
+        for _ in range(n_frames):
+            st = eng.state(0)
+            pos, g0, step = st["position"], st["g0"], st["frames"]
+            h_e = eng.hidden(0).cpu().to(orc.dt)
+            eng.frames(0, 1, trailing.cuda(), pad.cuda(), sp)
+            eng.check()
+            codes = eng.codes(0)[step].cpu().tolist()
+            g0_next = eng.state(0)["g0"]
+            cp_e = cp_dbg.cpu().double()
+            g0l_e = g0_dbg.cpu().double()
+            hist.append(g0)
+            rec = {"codes": codes, "g0_next": g0_next}
+            # --- code predictor from the engine's state, fed back with the engine's tokens
+            cp_do = sampling is not None and sampling.get("cp_do_sample", False)
+            _, cp_o = orc.cp_chain(h_e, g0, forced=codes[1:])
+            rec["cp_logits_err"] = max(float((cp_e[g] - cp_o[g].double()).abs().max()) for g in range(15))
+            rec["cp_logits_viol"] = max(violation(cp_e[g], cp_o[g].double()) for g in range(15))
+            cp_pred, cp_ties = [], []
+            for g in range(15):
+                if cp_do:   # sampled: same Philox draw on the ENGINE's logits (isolates the sampler)
+                    u = O.draw_u24(sampling["seed"], step, g + 1, sampling["stream"])
+                    cp_pred.append(O.sample_token(cp_e[g], True, sampling["cp_temperature"], sampling["cp_top_k"],
+                                                  1.0, None, u))
+                    cp_ties.append(None)
+                else:       # greedy: argmax of the oracle's own logits
+                    lo = cp_o[g].double()
+                    cp_pred.append(O.argmax_first(lo))
+                    srt = torch.sort(lo, descending=True)[0]
+                    cp_ties.append(float(srt[0] - srt[1]))
+            rec["cp_pred"] = cp_pred
+            rec["cp_gap"] = cp_ties
+            # --- backbone on the engine's combined input and KV rows
+            extra = trailing[step] if step < trailing.shape[0] else pad
+            x = orc.combine(codes, extra.to(orc.dt))
+            orc.position = pos
+            h_o = orc.backbone_step(x)
+            h_e2 = eng.hidden(0).cpu().to(orc.dt)
+            rec["h_rel"] = float((h_e2 - h_o).norm() / h_o.norm())
+            lo = orc.head_logits(orc.codec_head, h_o).double()
+            rec["g0_logits_err"] = float((g0l_e - lo).abs().max())
+            rec["g0_logits_viol"] = violation(g0l_e, lo)
+            # --- next group 0: greedy from the oracle's logits; sampled from the ENGINE's logits
+            min_new = sp.min_new_tokens
+            mask_eos = eos if step + 1 < min_new else None
+            if sampling is None:
+                l2 = lo.clone()
+                l2[sup] = float("-inf")
+                l2 = O.apply_repetition_penalty(l2, hist, sp.repetition_penalty)
+                rec["g0_pred"] = O.sample_token(l2, False, 0.9, 50, 1.0, mask_eos)
+                srt = torch.sort(l2[torch.isfinite(l2)], descending=True)[0]
+                rec["g0_gap"] = float(srt[0] - srt[1])
+            else:
+                l2 = g0l_e.clone()
+                l2[sup] = float("-inf")
+                l2 = O.apply_repetition_penalty(l2, hist, sampling["repetition_penalty"])
+                u = O.draw_u24(sampling["seed"], step + 1, 0, sampling["stream"])
+                rec["g0_pred"] = O.sample_token(l2, True, sampling["temperature"], sampling["top_k"], 1.0, mask_eos, u)
+                rec["g0_gap"] = None
+            # --- keep the oracle's cache identical to the engine's
+            kc, vc = eng.kv(0)
+            orc.bk[:, :, pos] = kc[:, :, pos].cpu().to(orc.dt)
+            orc.bv[:, :, pos] = vc[:, :, pos].cpu().to(orc.dt)
+            out.append(rec)
+    finally:
+        eng.set_debug_outputs(None, None)
+    return out
