@@ -101,7 +101,8 @@ int compat_step(bool cp, const void* input_embedding, const TTSLayerWeights* lay
                 int cache_len, int max_seq_len, float attn_scale, cudaStream_t stream) {
   if (!input_embedding || !layer_weights || !final_norm_weight || !cos_table || !sin_table || !k_cache ||
       !v_cache || !g_normalized || num_layers < 1 || max_seq_len < 1 || position < 0 ||
-      position >= max_seq_len || cache_len != position + 1 || !aligned16(input_embedding))
+      position >= max_seq_len || cache_len != position + 1 || !aligned16(input_embedding) ||
+      !aligned16(k_cache) || !aligned16(v_cache))
     return QTT_ERR_INVALID_ARG;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -28,6 +28,7 @@ enum StageKind : int { SK_QKV = 0, SK_O = 1, SK_GU = 2, SK_D = 3, SK_HEAD = 4 };
 struct __align__(128) Smem {
   uint8_t ring[NSLOTS][SLOT_BYTES];
   float xs[NTMAX * INTER];           // stage input vector; attention / sampler scratch
+  uint8_t att[ATT_STAGE_BYTES];      // attention: staged K and V rows of one sub-chunk
   float part[MAXPART * NTMAX];       // per-unit partial dot products of the current stage
   float red[4 * NCW];
   double dred[NTMAX * NCW];
@@ -164,8 +165,28 @@ __device__ void prod_stage(Smem& sm, Prod& pr, const Plan& pl, int* err) {
   }
 }
 
-__device__ void prod_layers(Smem& sm, Prod& pr, const LayerW* L, int n, int cta, int G, int* err) {
+__device__ __forceinline__ void att_split(int S, int G, int& nch, int& chunk);
+
+// L2 prefetch of the cached backbone K/V rows this CTA's attention item will read in layer
+// li (rows written by earlier launches only), issued when the producer reaches the layer.
+__device__ void prod_prefetch_attention(const Params& p, int li, int p0, int cta, int G) {
+  int nch, chunk;
+  att_split(p0 + 1, G, nch, chunk);
+  for (int item = cta; item < NKVH * nch; item += G) {
+    const int h = item / nch, c = item - h * nch;
+    const int s0 = c * chunk, a1 = min(s0 + chunk, p0);
+    if (a1 <= s0) continue;
+    const size_t off = ((static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq + s0) * HD;
+    const uint32_t bytes = static_cast<uint32_t>(a1 - s0) * HD * 2;
+    prefetch_l2_bulk(p.bb_k + off, bytes);
+    prefetch_l2_bulk(p.bb_v + off, bytes);
+  }
+}
+
+__device__ void prod_layers(const Params& p, Smem& sm, Prod& pr, const LayerW* L, int n, int cta, int G, int* err,
+                            int prefetch_pos) {
   for (int l = 0; l < n && pr.ok; ++l) {
+    if (prefetch_pos >= 0) prod_prefetch_attention(p, l, prefetch_pos, cta, G);
     prod_stage(sm, pr, make_plan(SK_QKV, L + l, nullptr, 0, cta, G), err);
     prod_stage(sm, pr, make_plan(SK_O, L + l, nullptr, 0, cta, G), err);
     prod_stage(sm, pr, make_plan(SK_GU, L + l, nullptr, 0, cta, G), err);
@@ -185,18 +206,21 @@ __device__ void producer_main(const Params& p, Smem& sm, int cta, int G) {
   int* err = p.w.err;
   if (p.mode == MODE_FRAME) {
     if (!frame_skipped(p)) {
+      int pos = ld_volatile_i32(&p.st->position);
+      if (pos < 0 || pos >= p.bb_max_seq) pos = -1;   // the consumers report the bad position
       for (int pass = 0; pass < NCPHEADS && pr.ok; ++pass) {
-        prod_layers(sm, pr, p.cp_layers, p.n_cp, cta, G, err);
+        prod_layers(p, sm, pr, p.cp_layers, p.n_cp, cta, G, err, -1);
         prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.cp_head[pass], p.cp_vocab, cta, G), err);
       }
-      prod_layers(sm, pr, p.bb_layers, p.n_bb, cta, G, err);
+      prod_layers(p, sm, pr, p.bb_layers, p.n_bb, cta, G, err, pos);
       prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err);
     }
   } else if (p.mode == MODE_BB_STEP) {
-    prod_layers(sm, pr, p.bb_layers, p.n_bb, cta, G, err);
+    prod_layers(p, sm, pr, p.bb_layers, p.n_bb, cta, G, err,
+                (p.position >= 0 && p.position < p.bb_max_seq) ? p.position : -1);
     if (p.flags & FLAG_HEAD_SAMPLE) prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err);
   } else {
-    prod_layers(sm, pr, p.cp_layers, p.n_cp, cta, G, err);
+    prod_layers(p, sm, pr, p.cp_layers, p.n_cp, cta, G, err, -1);
   }
   // Drain: wait (bounded) for the copies of the last ring's worth of fills so that no bulk
   // copy is still writing shared memory when this CTA exits early.
@@ -234,7 +258,8 @@ __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
   named_sync(1, NCT);
   cs.bar_target += static_cast<uint32_t>(cs.G);
   if (cs.tid == 0 && !aborted(sm)) {
-    __threadfence();
+    // bar.sync above orders this CTA's stores before thread 0; the release add publishes them
+    // at gpu scope and the acquire load below orders the other CTAs' stores before ours.
     red_release_gpu_add(p.w.bar, 1u);
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 0;; ++it) {
@@ -251,7 +276,6 @@ __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
         }
       }
     }
-    __threadfence();
     if (p.dbg_timeline != nullptr && cs.cta == 0) {
       const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
       if (k < static_cast<uint32_t>(p.dbg_timeline_len)) p.dbg_timeline[k] = globaltimer_ns();
@@ -350,21 +374,24 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
       if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
     } else if (cs.warp < n) {
       const uint4* src = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + cs.warp * UNIT_BYTES);
-      float acc[NT];
-#pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+      // four independent FMA chains (one per 16-byte chunk) keep the dependent chain short
+      float ch[NT][4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 v = src[cs.lane + 32 * i];
         const float w[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
                             bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
+        for (int t = 0; t < NT; ++t) {
+          float a = w[0] * xr[t][8 * i];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[t] = fmaf(w[j], xr[t][8 * i + j], acc[t]);
+          for (int j = 1; j < 8; ++j) a = fmaf(w[j], xr[t][8 * i + j], a);
+          ch[t][i] = a;
+        }
       }
+      float acc[NT];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = warp_sum(acc[t]);
+      for (int t = 0; t < NT; ++t) acc[t] = warp_sum((ch[t][0] + ch[t][1]) + (ch[t][2] + ch[t][3]));
       if (cs.lane == 0) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) sm.part[(u0 + cs.warp) * NT + t] = acc[t];
@@ -384,46 +411,95 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
 // ------------------------------------------------------------------------------------------
 // Attention: split over (KV head, chunk of positions) work items; the last item of a head to
 // finish combines the partial softmaxes (flash-decoding style), so no extra grid barrier.
+// Each item stages its q/k/v rows and its cached K/V rows into shared memory with one round
+// of cp.async, then works from shared memory; chunks longer than one staging buffer are
+// processed in sub-chunks with an online softmax.
 // ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void att_split(int S, int G, int& nch, int& chunk) {
+  nch = (S + ATT_TARGET - 1) / ATT_TARGET;
+  const int maxch = min(MAX_ATT_CHUNKS, max(1, G / NKVH));
+  nch = min(max(nch, 1), maxch);
+  chunk = (S + nch - 1) / nch;
+  nch = (S + chunk - 1) / chunk;
+}
+
+template <bool CP>
+__device__ __forceinline__ void stage_kv_rows(Cons& cs, uint8_t* dst_k, uint8_t* dst_v, const uint8_t* kb,
+                                              const uint8_t* vb, int a0, int a1) {
+  constexpr int ROWB = HD * (CP ? 4 : 2);
+  constexpr int PIECES = ROWB / 16;
+  const int n = (a1 - a0) * PIECES;
+  for (int e = cs.tid; e < 2 * n; e += NCT) {
+    const int which = e >= n, r = which ? e - n : e;
+    const size_t off = static_cast<size_t>(a0) * ROWB + static_cast<size_t>(r) * 16;
+    cp_async16((which ? dst_v : dst_k) + static_cast<size_t>(r) * 16, (which ? vb : kb) + off);
+  }
+}
+
 template <int NT, bool CP>
 __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0) {
   const int S = p0 + NT;
-  int nch = (S + ATT_TARGET - 1) / ATT_TARGET;
-  const int maxch = min(MAX_ATT_CHUNKS, max(1, cs.G / NKVH));
-  nch = min(max(nch, 1), maxch);
-  const int chunk = (S + nch - 1) / nch;
-  nch = (S + chunk - 1) / chunk;
+  int nch, chunk;
+  att_split(S, cs.G, nch, chunk);
   if (chunk > ATT_CHMAX) {
     fail(p, sm, DEV_ERR_BAD_POSITION);
     return false;
   }
+  constexpr int ESZ = CP ? 4 : 2;
+  constexpr int ROWB = HD * ESZ;
+  constexpr int SUB = ATT_STAGE_BYTES / (2 * ROWB);   // 48 bf16 rows or 24 fp32 rows
   const int max_seq = CP ? p.cp_max_seq : p.bb_max_seq;
   const size_t layer_off = static_cast<size_t>(li) * NKVH * max_seq * HD;
   const LayerW* L = lw;
+  constexpr int J = NT * 2;   // (token, q head) pairs
 
   // shared scratch inside xs
-  float* qr = sm.xs;                         // [NT][2][HD]
-  float* kn = qr + NT * 2 * HD;              // [NT][HD]
-  float* vn = kn + NT * HD;                  // [NT][HD]
-  float* sc = vn + NT * HD;                  // [NT][2][ATT_CHMAX]
-  float* accg = sc + NT * 2 * ATT_CHMAX;     // [3][NT*2][HD]
-  float* ml = accg + 3 * NT * 2 * HD;        // [NT*2][2]
+  float* qraw = sm.xs;                  // [NT][4][HD] raw q(2h), q(2h+1), k, v
+  float* qr = qraw + NT * 4 * HD;       // [NT][2][HD]
+  float* kn = qr + NT * 2 * HD;         // [NT][HD]
+  float* vn = kn + NT * HD;             // [NT][HD]
+  float* sc = vn + NT * HD;             // [J][SUB]
+  float* acc_s = sc + J * SUB;          // [J][HD] running P.V
+  float* accg = acc_s + J * HD;         // [3][J][HD]
+  float* ml = accg + 3 * J * HD;        // [J][4]: running max, running sum, rescale of this step
+  uint8_t* kst = sm.att;
+  uint8_t* vst = sm.att + SUB * ROWB;
 
   for (int item = cs.cta; item < NKVH * nch; item += cs.G) {
     const int h = item / nch, c = item - h * nch;
-    const int s0 = c * chunk, s1 = min(S, s0 + chunk), len = s1 - s0;
+    const int s0 = c * chunk, s1 = min(S, s0 + chunk);
+    const uint8_t* kb = reinterpret_cast<const uint8_t*>(CP ? static_cast<const void*>(p.cp_k) : p.bb_k) +
+                        (layer_off + static_cast<size_t>(h) * max_seq * HD) * ESZ;
+    const uint8_t* vb = reinterpret_cast<const uint8_t*>(CP ? static_cast<const void*>(p.cp_v) : p.bb_v) +
+                        (layer_off + static_cast<size_t>(h) * max_seq * HD) * ESZ;
 
-    // 1. q/k RMSNorm (per head, fused_decode_tts.cu:183-197) + RoPE; v copy. Warp j handles
-    //    vector j%4 (q head 2h, q head 2h+1, k, v) of token j/4; lane holds d = lane + 32 i,
-    //    so each rotation pair (d, d+64) lives in one lane.
+    // 1. one round trip: raw q/k/v rows of this head + the first sub-chunk of cached rows
+    for (int e = cs.tid; e < NT * 4 * (HD / 4); e += NCT) {
+      const int t = e / (4 * HD / 4), r = e - t * (4 * HD / 4), vec = r / (HD / 4), piece = r - vec * (HD / 4);
+      const int row0 = vec < 2 ? (2 * h + vec) * HD : (vec == 2 ? QSZ + h * HD : QSZ + KVSZ + h * HD);
+      cp_async16(qraw + (t * 4 + vec) * HD + piece * 4, p.w.qkv + t * QKV_ROWS + row0 + piece * 4);
+    }
+    {
+      const int a1 = min(min(s1, p0), s0 + SUB);
+      if (a1 > s0) stage_kv_rows<CP>(cs, kst, vst, kb, vb, s0, a1);
+    }
+    for (int j = cs.tid; j < J * HD; j += NCT) acc_s[j] = 0.f;
+    if (cs.tid < J) {
+      ml[cs.tid * 4 + 0] = -INFINITY;
+      ml[cs.tid * 4 + 1] = 0.f;
+    }
+    cp_async_wait_all();
+    named_sync(1, NCT);
+
+    // 2. q/k RMSNorm per head (fused_decode_tts.cu:183-197) + RoPE; warp j handles vector j%4
+    //    of token j/4 with d = lane + 32 i, so each rotation pair (d, d+64) sits in one lane.
     if (cs.warp < NT * 4) {
       const int t = cs.warp >> 2, vec = cs.warp & 3;
       const int pos = p0 + t;
-      const float* src = p.w.qkv + t * QKV_ROWS +
-                         (vec < 2 ? (2 * h + vec) * HD : (vec == 2 ? QSZ + h * HD : QSZ + KVSZ + h * HD));
+      const float* src = qraw + (t * 4 + vec) * HD;
       float x[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = __ldcg(src + cs.lane + 32 * i);
+      for (int i = 0; i < 4; ++i) x[i] = src[cs.lane + 32 * i];
       if (vec < 3) {
         double ss = 0.0;
 #pragma unroll
@@ -454,7 +530,7 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     }
     named_sync(1, NCT);
 
-    // 2. item 0 of each head stores the new K/V rows into the cache.
+    // 3. item 0 of each head stores the new K/V rows into the cache.
     if (c == 0) {
       for (int e = cs.tid; e < NT * HD; e += NCT) {
         const int t = e / HD, d = e - t * HD;
@@ -469,100 +545,108 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
       }
     }
 
-    // 3. scores: one warp per position, lane holds d = 4 lane .. 4 lane + 3.
-    for (int s = s0 + cs.warp; s < s1; s += NCW) {
-      float k4[4];
-      if (s < p0) {
-        const size_t off = layer_off + (static_cast<size_t>(h) * max_seq + s) * HD + 4 * cs.lane;
-        if (CP) {
-          const float4 kk = __ldcg(reinterpret_cast<const float4*>(p.cp_k + off));
-          k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
-        } else {
-          const uint2 kk = __ldcg(reinterpret_cast<const uint2*>(p.bb_k + off));
-          k4[0] = bf16_lo(kk.x); k4[1] = bf16_hi(kk.x); k4[2] = bf16_lo(kk.y); k4[3] = bf16_hi(kk.y);
-        }
-      } else {
-        const float4 kk = *reinterpret_cast<const float4*>(kn + (s - p0) * HD + 4 * cs.lane);
-        k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+    // 4. sub-chunks of at most SUB positions (one for every chunk up to SUB long)
+    for (int sa = s0; sa < s1; sa += SUB) {
+      const int sb = min(s1, sa + SUB), len = sb - sa;
+      if (sa != s0) {
+        const int a1 = min(sb, p0);
+        if (a1 > sa) stage_kv_rows<CP>(cs, kst, vst, kb, vb, sa, a1);
+        cp_async_wait_all();
+        named_sync(1, NCT);
       }
+      // scores: one warp per position, lane holds d = 4 lane .. 4 lane + 3
+      for (int s = sa + cs.warp; s < sb; s += NCW) {
+        float k4[4];
+        if (s < p0) {
+          const uint8_t* row = kst + static_cast<size_t>(s - sa) * ROWB;
+          if (CP) {
+            const float4 kk = *reinterpret_cast<const float4*>(row + 16 * cs.lane);
+            k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+          } else {
+            const uint2 kk = *reinterpret_cast<const uint2*>(row + 8 * cs.lane);
+            k4[0] = bf16_lo(kk.x); k4[1] = bf16_hi(kk.x); k4[2] = bf16_lo(kk.y); k4[3] = bf16_hi(kk.y);
+          }
+        } else {
+          const float4 kk = *reinterpret_cast<const float4*>(kn + (s - p0) * HD + 4 * cs.lane);
+          k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+        }
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float4 q = *reinterpret_cast<const float4*>(qr + (t * 2 + hh) * HD + 4 * cs.lane);
+        for (int j = 0; j < J; ++j) {
+          const float4 q = *reinterpret_cast<const float4*>(qr + j * HD + 4 * cs.lane);
           float d = q.x * k4[0];
           d = fmaf(q.y, k4[1], d);
           d = fmaf(q.z, k4[2], d);
           d = fmaf(q.w, k4[3], d);
           d = warp_sum(d) * p.attn_scale;
-          if (cs.lane == 0) sc[(t * 2 + hh) * ATT_CHMAX + (s - s0)] = (s <= p0 + t) ? d : -INFINITY;
+          if (cs.lane == 0) sc[j * SUB + (s - sa)] = (s <= p0 + (j >> 1)) ? d : -INFINITY;
         }
       }
-    }
-    named_sync(1, NCT);
-
-    // 4. chunk-local softmax statistics: warp j handles (token, head) j.
-    if (cs.warp < NT * 2) {
-      float* row = sc + cs.warp * ATT_CHMAX;
-      float m = -INFINITY;
-      for (int i = cs.lane; i < len; i += 32) m = fmaxf(m, row[i]);
-      m = warp_max(m);
-      float l = 0.f;
-      for (int i = cs.lane; i < len; i += 32) {
-        const float e = (m == -INFINITY) ? 0.f : expf(row[i] - m);
-        row[i] = e;
-        l += e;
+      named_sync(1, NCT);
+      // online softmax statistics: warp j handles (token, q head) j
+      if (cs.warp < J) {
+        float* row = sc + cs.warp * SUB;
+        float m = -INFINITY;
+        for (int i = cs.lane; i < len; i += 32) m = fmaxf(m, row[i]);
+        m = warp_max(m);
+        const float m_old = ml[cs.warp * 4 + 0];
+        const float m_new = fmaxf(m_old, m);
+        float l = 0.f;
+        for (int i = cs.lane; i < len; i += 32) {
+          const float e = (m_new == -INFINITY) ? 0.f : expf(row[i] - m_new);
+          row[i] = e;
+          l += e;
+        }
+        l = warp_sum(l);
+        if (cs.lane == 0) {
+          const float rescale = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+          ml[cs.warp * 4 + 0] = m_new;
+          ml[cs.warp * 4 + 1] = ml[cs.warp * 4 + 1] * rescale + l;
+          ml[cs.warp * 4 + 2] = rescale;
+        }
       }
-      l = warp_sum(l);
-      if (cs.lane == 0) {
-        ml[cs.warp * 2 + 0] = m;
-        ml[cs.warp * 2 + 1] = l;
-      }
-    }
-    named_sync(1, NCT);
-
-    // 5. P.V: thread -> (d, position residue g mod 3).
-    {
-      const int d = cs.tid & (HD - 1), g = cs.tid >> 7;
-      float acc[NT * 2];
+      named_sync(1, NCT);
+      // P.V: thread -> (d, position residue g mod 3)
+      {
+        const int d = cs.tid & (HD - 1), g = cs.tid >> 7;
+        float acc[J];
 #pragma unroll
-      for (int j = 0; j < NT * 2; ++j) acc[j] = 0.f;
-      for (int s = s0 + g; s < s1; s += 3) {
-        float v;
-        if (s < p0) {
-          const size_t off = layer_off + (static_cast<size_t>(h) * max_seq + s) * HD + d;
-          v = CP ? __ldcg(p.cp_v + off) : __bfloat162float(__ldcg(p.bb_v + off));
-        } else {
-          v = vn[(s - p0) * HD + d];
+        for (int j = 0; j < J; ++j) acc[j] = 0.f;
+        for (int s = sa + g; s < sb; s += 3) {
+          float v;
+          if (s < p0) {
+            const uint8_t* row = vst + static_cast<size_t>(s - sa) * ROWB;
+            v = CP ? reinterpret_cast<const float*>(row)[d]
+                   : __bfloat162float(reinterpret_cast<const bf16*>(row)[d]);
+          } else {
+            v = vn[(s - p0) * HD + d];
+          }
+#pragma unroll
+          for (int j = 0; j < J; ++j) acc[j] = fmaf(sc[j * SUB + (s - sa)], v, acc[j]);
         }
 #pragma unroll
-        for (int j = 0; j < NT * 2; ++j) acc[j] = fmaf(sc[j * ATT_CHMAX + (s - s0)], v, acc[j]);
+        for (int j = 0; j < J; ++j) accg[(g * J + j) * HD + d] = acc[j];
       }
-#pragma unroll
-      for (int j = 0; j < NT * 2; ++j) accg[(g * NT * 2 + j) * HD + d] = acc[j];
+      named_sync(1, NCT);
+      for (int e = cs.tid; e < J * HD; e += NCT) {
+        const int j = e / HD, d = e - j * HD;
+        const float a = (accg[(0 * J + j) * HD + d] + accg[(1 * J + j) * HD + d]) + accg[(2 * J + j) * HD + d];
+        acc_s[e] = acc_s[e] * ml[j * 4 + 2] + a;
+      }
+      named_sync(1, NCT);
     }
-    named_sync(1, NCT);
 
-    // 6. publish (or finish directly when the head has a single item).
+    // 5. publish (or finish directly when the head has a single item).
     if (nch == 1) {
-      for (int e = cs.tid; e < NT * 2 * HD; e += NCT) {
+      for (int e = cs.tid; e < J * HD; e += NCT) {
         const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
-        const float a = (accg[(0 * NT * 2 + j) * HD + d] + accg[(1 * NT * 2 + j) * HD + d]) +
-                        accg[(2 * NT * 2 + j) * HD + d];
-        p.w.attn[t * QSZ + (2 * h + hh) * HD + d] = a / ml[j * 2 + 1];
+        p.w.attn[t * QSZ + (2 * h + hh) * HD + d] = acc_s[e] / ml[j * 4 + 1];
       }
       named_sync(1, NCT);
       continue;
     }
-    for (int e = cs.tid; e < NT * 2 * PRT_STRIDE; e += NCT) {
+    for (int e = cs.tid; e < J * PRT_STRIDE; e += NCT) {
       const int j = e / PRT_STRIDE, k = e - j * PRT_STRIDE, t = j >> 1, hh = j & 1;
-      float val;
-      if (k < 2) {
-        val = ml[j * 2 + k];
-      } else {
-        const int d = k - 2;
-        val = (accg[(0 * NT * 2 + j) * HD + d] + accg[(1 * NT * 2 + j) * HD + d]) + accg[(2 * NT * 2 + j) * HD + d];
-      }
+      const float val = k < 2 ? ml[j * 4 + k] : acc_s[j * HD + (k - 2)];
       p.w.prt[((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + c) * PRT_STRIDE + k] = val;
     }
     named_sync(1, NCT);
@@ -575,7 +659,7 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     named_sync(1, NCT);
     if (sm.bcast[0]) {
       // combine the nch partials of KV head h in chunk order
-      for (int e = cs.tid; e < NT * 2 * HD; e += NCT) {
+      for (int e = cs.tid; e < J * HD; e += NCT) {
         const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
         const float* rec = p.w.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE;
         float M = -INFINITY;
