@@ -206,6 +206,7 @@ def run_ours(args, rank, world, local_rank):
 
     from qwentts_turbo_b200 import _lib
     from qwentts_turbo_b200.config import frame_weight_bytes, kv_read_bytes_per_frame
+    from qwentts_turbo_b200.dist import gather_codes, max_over_ranks
     from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
     from qwentts_turbo_b200.weights import synthetic_weights
     from qwentts_turbo_b200.workloads import c3_inputs
@@ -228,12 +229,6 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     # ---- device-resident run: inputs already in HBM --------------------------------------
     eng.prefill(0, embeds_d, sp)
@@ -291,12 +286,8 @@ def run_ours(args, rank, world, local_rank):
     assert torch.equal(codes_h, codes[W:].cpu()), "e2e path produced different codes"
 
     # ---- gather codes to rank 0 (after timing; NCCL over NVLink) ---------------------------
-    if world > 1:
-        gathered = [torch.empty_like(codes) for _ in range(world)]
-        dist.all_gather(gathered, codes)
-        n_codes = sum(g.shape[0] for g in gathered)
-    else:
-        n_codes = codes.shape[0]
+    gathered = gather_codes(codes)
+    n_codes = sum(g.shape[0] for g in gathered) if gathered is not None else 0
 
     if rank != 0:
         eng.close()

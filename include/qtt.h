@@ -214,6 +214,11 @@ qtt_status qtt_set_debug_outputs(qtt_engine* e, float* cp_logits, float* g0_logi
 /* Profiling hook: when n > 0, each launch writes %globaltimer (ns) into stamps[0] at start
  * and stamps[k] after its k-th grid barrier (k < n). Pass n = 0 to turn it off. */
 qtt_status qtt_set_debug_timeline(qtt_engine* e, unsigned long long* stamps, int n);
+/* Profiling hook: CTA 0 stamps marks[3 k + {0,1,2}] = start of the k-th stage's GEMV, its
+ * end, and the barrier arrival; every CTA stamps arrivals[(k - arrival_stage0) * num_ctas +
+ * cta] for stages k in [arrival_stage0, arrival_stage0 + arrival_stages). Zeros turn it off. */
+qtt_status qtt_set_debug_profile(qtt_engine* e, unsigned long long* marks, int n_marks,
+                                 unsigned long long* arrivals, int arrival_stage0, int arrival_stages);
 /* Synchronises `stream` and converts the engine's device error word into a status. */
 qtt_status qtt_check(qtt_engine* e, cudaStream_t stream);
 

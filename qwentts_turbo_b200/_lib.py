@@ -97,6 +97,7 @@ SIGNATURES = {
     "qtt_set_debug_outputs": (_I, [_P, _P, _P]),
     "qtt_set_decode_state": (_I, [_P, _I, _P, _I, _I, _P]),
     "qtt_set_debug_timeline": (_I, [_P, _P, _I]),
+    "qtt_set_debug_profile": (_I, [_P, _P, _I, _P, _I, _I]),
     "qtt_get_hidden": (_I, [_P, _I, _P, _P]),
     "qtt_check": (_I, [_P, _P]),
 }

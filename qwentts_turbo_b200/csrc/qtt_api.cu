@@ -110,7 +110,7 @@ int compat_step(bool cp, const void* input_embedding, const TTSLayerWeights* lay
   DevShape shape;
   e = device_shape(dev, &shape);
   if (e != cudaSuccess) return from_cuda(e);
-  if (max_seq_len > (shape.ctas / qtt::NKVH) * qtt::ATT_CHMAX) return QTT_ERR_UNSUPPORTED;
+  if (max_seq_len > (shape.ctas / qtt::NKVH) * qtt::ATT_CHMAX || shape.ctas < 128) return QTT_ERR_UNSUPPORTED;
   qtt::Work w;
   e = compat_work(dev, stream, &w);
   if (e != cudaSuccess) return from_cuda(e);
@@ -351,7 +351,7 @@ extern "C" qtt_status qtt_engine_create(const qtt_weights* w, const qtt_dims* d,
     delete e;
     return from_cuda(ce);
   }
-  if (max_seq > (e->shape.ctas / qtt::NKVH) * qtt::ATT_CHMAX || e->shape.ctas < 64) {
+  if (max_seq > (e->shape.ctas / qtt::NKVH) * qtt::ATT_CHMAX || e->shape.ctas < 128) {
     delete e;
     return QTT_ERR_UNSUPPORTED;
   }
@@ -641,6 +641,17 @@ extern "C" qtt_status qtt_set_debug_timeline(qtt_engine* e, unsigned long long* 
   if (!e || n < 0 || (n > 0 && !stamps)) return QTT_ERR_INVALID_ARG;
   e->base.dbg_timeline = n > 0 ? stamps : nullptr;
   e->base.dbg_timeline_len = n;
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_set_debug_profile(qtt_engine* e, unsigned long long* marks, int n_marks,
+                                            unsigned long long* arrivals, int arrival_stage0, int arrival_stages) {
+  if (!e || n_marks < 0 || arrival_stages < 0) return QTT_ERR_INVALID_ARG;
+  e->base.dbg_marks = n_marks > 0 ? marks : nullptr;
+  e->base.dbg_marks_len = n_marks;
+  e->base.dbg_arrivals = arrival_stages > 0 ? arrivals : nullptr;
+  e->base.dbg_arr_stage0 = arrival_stage0;
+  e->base.dbg_arr_n = arrival_stages;
   return QTT_OK;
 }
 

@@ -253,9 +253,24 @@ __device__ __forceinline__ void fail(const Params& p, Smem& sm, int code) {
   *reinterpret_cast<volatile int*>(&sm.abort) = 1;
 }
 
+// Profiling stamp of CTA 0 for the current stage (no-op unless dbg_marks is set).
+__device__ __forceinline__ void stage_mark(const Params& p, const Cons& cs, int id) {
+  if (p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0) {
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+    if (static_cast<int>(k * 3 + id) < p.dbg_marks_len) p.dbg_marks[k * 3 + id] = globaltimer_ns();
+  }
+}
+
 // Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded).
 __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
   named_sync(1, NCT);
+  if (cs.tid == 0) {
+    stage_mark(p, cs, 2);
+    if (p.dbg_arrivals != nullptr) {
+      const int k = static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G)) - p.dbg_arr_stage0;
+      if (k >= 0 && k < p.dbg_arr_n) p.dbg_arrivals[k * cs.G + cs.cta] = globaltimer_ns();
+    }
+  }
   cs.bar_target += static_cast<uint32_t>(cs.G);
   if (cs.tid == 0 && !aborted(sm)) {
     // bar.sync above orders this CTA's stores before thread 0; the release add publishes them
@@ -324,24 +339,48 @@ __device__ __forceinline__ void block_sum(Smem& sm, Cons& cs, float (&v)[NT]) {
   named_sync(1, NCT);
 }
 
-// In-place RMSNorm of NT vectors of HID floats in shared memory: x * rsqrt(mean(x^2)+eps) * w.
-template <int NT>
-__device__ void rmsnorm_smem(Smem& sm, Cons& cs, float* x, const bf16* w, float eps) {
+// RMSNorm prologue of a stage: NT vectors of HID floats (from global memory written by other
+// CTAs, or from shared memory) are normalised into dst = x * rsqrt(mean(x^2) + eps) * w.
+// The activation and the norm weights are loaded in the same round trip; thread t < 256 owns
+// elements 4t .. 4t+3 of every token.
+template <int NT, bool FROM_SMEM>
+__device__ void load_rmsnorm(Smem& sm, Cons& cs, const float* src, const bf16* w, float eps, float* dst) {
+  const bool act = cs.tid < HID / 4;
+  float4 x[NT];
+  uint2 wv = make_uint2(0u, 0u);
   double ss[NT];
+  if (act) {
+    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float4* s4 = reinterpret_cast<const float4*>(src + t * HID) + cs.tid;
+      x[t] = FROM_SMEM ? *s4 : __ldcg(s4);
+    }
+  }
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     double a = 0.0;
-    for (int i = cs.tid; i < HID; i += NCT) {
-      const double xv = x[t * HID + i];
-      a = fma(xv, xv, a);
+    if (act) {
+      a = fma(static_cast<double>(x[t].x), static_cast<double>(x[t].x), a);
+      a = fma(static_cast<double>(x[t].y), static_cast<double>(x[t].y), a);
+      a = fma(static_cast<double>(x[t].z), static_cast<double>(x[t].z), a);
+      a = fma(static_cast<double>(x[t].w), static_cast<double>(x[t].w), a);
     }
     ss[t] = a;
   }
   block_sum_d<NT>(sm, cs, ss);
+  if (act) {
+    const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
 #pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    const float rstd = rms_scale(ss[t], HID, eps);
-    for (int i = cs.tid; i < HID; i += NCT) x[t * HID + i] = x[t * HID + i] * rstd * __bfloat162float(w[i]);
+    for (int t = 0; t < NT; ++t) {
+      const float rstd = rms_scale(ss[t], HID, eps);
+      float4 o;
+      o.x = x[t].x * rstd * w0;
+      o.y = x[t].y * rstd * w1;
+      o.z = x[t].z * rstd * w2;
+      o.w = x[t].w * rstd * w3;
+      reinterpret_cast<float4*>(dst + t * HID)[cs.tid] = o;
+    }
   }
   named_sync(1, NCT);
 }
@@ -355,6 +394,12 @@ __device__ __forceinline__ void load_vec(Cons& cs, float* dst, const float* src,
 // GEMV over this CTA's units of one stage: part[u * NT + t] = dot(unit u, x part of u).
 template <int NT>
 __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const float* xsrc, int xstride) {
+  stage_mark(p, cs, 0);
+  if (pl.units > MAXUNITS) {
+    fail(p, sm, DEV_ERR_BAD_POSITION);
+    return false;
+  }
+  float* lp = reinterpret_cast<float*>(sm.att);   // [units * NT][LP_STRIDE] lane partials
   const int part = cs.warp % pl.P;
   float xr[NT][32];
 #pragma unroll
@@ -368,9 +413,17 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
       xr[t][8 * i + 4] = b.x; xr[t][8 * i + 5] = b.y; xr[t][8 * i + 6] = b.z; xr[t][8 * i + 7] = b.w;
     }
   }
+  const bool prof = p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0;
+  unsigned long long waited = 0;
+  const uint32_t kst = cs.bar_target / static_cast<uint32_t>(cs.G);
+  const bool fine = prof && static_cast<int>(4 * 1024 + 4 * kst + 3) < p.dbg_marks_len;
+  if (fine) p.dbg_marks[4 * 1024 + 4 * kst + 0] = globaltimer_ns();
   for (int u0 = 0; u0 < pl.units; u0 += SLOT_UNITS) {
     const int n = min(SLOT_UNITS, pl.units - u0);
-    if (!mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort)) {
+    unsigned long long tw = prof ? globaltimer_ns() : 0ull;
+    const bool got = mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort);
+    if (prof) waited += globaltimer_ns() - tw;
+    if (!got) {
       if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
     } else if (cs.warp < n) {
       const uint4* src = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + cs.warp * UNIT_BYTES);
@@ -389,13 +442,10 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
           ch[t][i] = a;
         }
       }
-      float acc[NT];
+      // lane partials go to shared memory; the cross-lane sums are done once per stage below
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = warp_sum((ch[t][0] + ch[t][1]) + (ch[t][2] + ch[t][3]));
-      if (cs.lane == 0) {
-#pragma unroll
-        for (int t = 0; t < NT; ++t) sm.part[(u0 + cs.warp) * NT + t] = acc[t];
-      }
+      for (int t = 0; t < NT; ++t)
+        lp[((u0 + cs.warp) * NT + t) * LP_STRIDE + cs.lane] = (ch[t][0] + ch[t][1]) + (ch[t][2] + ch[t][3]);
     }
     __syncwarp();
     if (cs.lane == 0) mbar_arrive(&sm.empty[cs.slot]);
@@ -404,7 +454,27 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
       cs.round++;
     }
   }
+  if (prof) {
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+    if (static_cast<int>(k) < p.dbg_marks_len / 3 - 1024) p.dbg_marks[3 * 1024 + k] = waited;
+  }
+  if (fine) p.dbg_marks[4 * 1024 + 4 * kst + 1] = globaltimer_ns();
   named_sync(1, NCT);
+  if (fine) p.dbg_marks[4 * 1024 + 4 * kst + 2] = globaltimer_ns();
+  // one thread per (unit, token): fixed-order pairwise sum of the 32 lane partials
+  for (int e = cs.tid; e < pl.units * NT; e += NCT) {
+    const float* row = lp + e * LP_STRIDE;
+    float a[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) a[k] = row[k] + row[k + 16];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] += a[k + 8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) a[k] += a[k + 4];
+    sm.part[e] = (a[0] + a[2]) + (a[1] + a[3]);
+  }
+  named_sync(1, NCT);
+  stage_mark(p, cs, 1);
   return !aborted(sm);
 }
 
@@ -488,6 +558,19 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
       ml[cs.tid * 4 + 0] = -INFINITY;
       ml[cs.tid * 4 + 1] = 0.f;
     }
+    // norm weights and RoPE rows travel with the staged rows (same round trip)
+    float nwv[4], cv[4], sv[4];
+    if (cs.warp < NT * 4 && (cs.warp & 3) < 3) {
+      const int pos = p0 + (cs.warp >> 2);
+      const bf16* nw = (cs.warp & 3) < 2 ? L->q_norm : L->k_norm;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int d = cs.lane + 32 * i;
+        nwv[i] = __bfloat162float(nw[d]);
+        cv[i] = __bfloat162float(p.cos_tab[static_cast<size_t>(pos) * HD + d]);
+        sv[i] = __bfloat162float(p.sin_tab[static_cast<size_t>(pos) * HD + d]);
+      }
+    }
     cp_async_wait_all();
     named_sync(1, NCT);
 
@@ -495,7 +578,6 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     //    of token j/4 with d = lane + 32 i, so each rotation pair (d, d+64) sits in one lane.
     if (cs.warp < NT * 4) {
       const int t = cs.warp >> 2, vec = cs.warp & 3;
-      const int pos = p0 + t;
       const float* src = qraw + (t * 4 + vec) * HD;
       float x[4];
 #pragma unroll
@@ -506,15 +588,9 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
         for (int i = 0; i < 4; ++i) ss = fma(static_cast<double>(x[i]), static_cast<double>(x[i]), ss);
         ss = warp_sum_d(ss);
         const float rstd = rms_scale(ss, HD, p.eps);
-        const bf16* nw = vec < 2 ? L->q_norm : L->k_norm;
-        float y[4], cv[4], sv[4];
+        float y[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int d = cs.lane + 32 * i;
-          y[i] = x[i] * rstd * __bfloat162float(nw[d]);
-          cv[i] = __bfloat162float(p.cos_tab[static_cast<size_t>(pos) * HD + d]);
-          sv[i] = __bfloat162float(p.sin_tab[static_cast<size_t>(pos) * HD + d]);
-        }
+        for (int i = 0; i < 4; ++i) y[i] = x[i] * rstd * nwv[i];
         float o[4];
         o[0] = y[0] * cv[0] - y[2] * sv[0];
         o[1] = y[1] * cv[1] - y[3] * sv[1];
@@ -646,7 +722,7 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     }
     for (int e = cs.tid; e < J * PRT_STRIDE; e += NCT) {
       const int j = e / PRT_STRIDE, k = e - j * PRT_STRIDE, t = j >> 1, hh = j & 1;
-      const float val = k < 2 ? ml[j * 4 + k] : acc_s[j * HD + (k - 2)];
+      const float val = k < 2 ? ml[j * 4 + k] : (k < 4 ? 0.f : acc_s[j * HD + (k - 4)]);
       p.w.prt[((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + c) * PRT_STRIDE + k] = val;
     }
     named_sync(1, NCT);
@@ -658,19 +734,42 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     }
     named_sync(1, NCT);
     if (sm.bcast[0]) {
-      // combine the nch partials of KV head h in chunk order
+      // combine the nch partials of KV head h in chunk order, staged with one round trip
+      const bool staged = J * nch * PRT_STRIDE * 4 <= ATT_STAGE_BYTES;
+      float* recs = reinterpret_cast<float*>(sm.att);   // [J][nch][PRT_STRIDE]
+      if (staged) {
+        const int pieces = nch * PRT_STRIDE / 4;
+        for (int e = cs.tid; e < J * pieces; e += NCT) {
+          const int j = e / pieces, r = e - j * pieces, t = j >> 1, hh = j & 1;
+          cp_async16(recs + (j * nch) * PRT_STRIDE + r * 4,
+                     p.w.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE + r * 4);
+        }
+        cp_async_wait_all();
+        named_sync(1, NCT);
+      }
       for (int e = cs.tid; e < J * HD; e += NCT) {
         const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
-        const float* rec = p.w.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE;
-        float M = -INFINITY;
-        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(rec + cc * PRT_STRIDE));
-        float Ls = 0.f, O = 0.f;
-        for (int cc = 0; cc < nch; ++cc) {
-          const float mc = __ldcg(rec + cc * PRT_STRIDE);
-          if (mc == -INFINITY) continue;
-          const float wgt = expf(mc - M);
-          Ls = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 1), Ls);
-          O = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 2 + d), O);
+        float M = -INFINITY, Ls = 0.f, O = 0.f;
+        if (staged) {
+          const float* rec = recs + (j * nch) * PRT_STRIDE;
+          for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, rec[cc * PRT_STRIDE]);
+          for (int cc = 0; cc < nch; ++cc) {
+            const float mc = rec[cc * PRT_STRIDE];
+            if (mc == -INFINITY) continue;
+            const float wgt = expf(mc - M);
+            Ls = fmaf(wgt, rec[cc * PRT_STRIDE + 1], Ls);
+            O = fmaf(wgt, rec[cc * PRT_STRIDE + 4 + d], O);
+          }
+        } else {
+          const float* rec = p.w.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE;
+          for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(rec + cc * PRT_STRIDE));
+          for (int cc = 0; cc < nch; ++cc) {
+            const float mc = __ldcg(rec + cc * PRT_STRIDE);
+            if (mc == -INFINITY) continue;
+            const float wgt = expf(mc - M);
+            Ls = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 1), Ls);
+            O = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 4 + d), O);
+          }
         }
         p.w.attn[t * QSZ + (2 * h + hh) * HD + d] = O / Ls;
       }
@@ -688,9 +787,12 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
 // ------------------------------------------------------------------------------------------
 template <int NT, bool CP>
 __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const float* hin,
-                      float* hout) {
+                      float* hout, bool input_in_smem) {
   // ---- input RMSNorm + QKV
-  rmsnorm_smem<NT>(sm, cs, sm.xs, lw->in_norm, p.eps);
+  if (input_in_smem)
+    load_rmsnorm<NT, true>(sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
+  else
+    load_rmsnorm<NT, false>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
@@ -706,25 +808,24 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   if (!attention<NT, CP>(p, sm, cs, lw, li, p0)) return false;
   if (!grid_sync(p, sm, cs)) return false;
 
-  // ---- o_proj + residual
-  load_vec(cs, sm.xs, p.w.attn, NT * QSZ);
-  named_sync(1, NCT);
+  // ---- o_proj + residual (the residual rows are fetched with the attention output)
   {
     const Plan pl = make_plan(SK_O, lw, nullptr, 0, cs.cta, cs.G);
-    if (!gemv<NT>(p, pl, sm, cs, sm.xs, QSZ)) return false;
     const int nr = pl.r1 - pl.r0;
-    for (int e = cs.tid; e < NT * nr; e += NCT) {
-      const int t = e / nr, r = e - t * nr;
-      const float v = (sm.part[(2 * r) * NT + t] + sm.part[(2 * r + 1) * NT + t]) + __ldcg(hin + t * HID + pl.r0 + r);
-      __stcg(p.w.hmid + t * HID + pl.r0 + r, v);
+    float res = 0.f;
+    if (cs.tid < NT * nr) res = __ldcg(hin + (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
+    load_vec(cs, sm.xs, p.w.attn, NT * QSZ);
+    named_sync(1, NCT);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, QSZ)) return false;
+    if (cs.tid < NT * nr) {
+      const int t = cs.tid / nr, r = cs.tid % nr;
+      __stcg(p.w.hmid + t * HID + pl.r0 + r, (sm.part[(2 * r) * NT + t] + sm.part[(2 * r + 1) * NT + t]) + res);
     }
   }
   if (!grid_sync(p, sm, cs)) return false;
 
   // ---- post-attention RMSNorm + gate/up + SiLU
-  load_vec(cs, sm.xs, p.w.hmid, NT * HID);
-  named_sync(1, NCT);
-  rmsnorm_smem<NT>(sm, cs, sm.xs, lw->post_norm, p.eps);
+  load_rmsnorm<NT, false>(sm, cs, p.w.hmid, lw->post_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_GU, lw, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
@@ -738,24 +839,22 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   if (!grid_sync(p, sm, cs)) return false;
 
   // ---- down_proj + residual
-  load_vec(cs, sm.xs, p.w.mlp, NT * INTER);
-  named_sync(1, NCT);
   {
     const Plan pl = make_plan(SK_D, lw, nullptr, 0, cs.cta, cs.G);
-    if (!gemv<NT>(p, pl, sm, cs, sm.xs, INTER)) return false;
     const int nr = pl.r1 - pl.r0;
-    for (int e = cs.tid; e < NT * nr; e += NCT) {
-      const int t = e / nr, r = e - t * nr;
-      float v = ((sm.part[(3 * r) * NT + t] + sm.part[(3 * r + 1) * NT + t]) + sm.part[(3 * r + 2) * NT + t]) +
-                __ldcg(p.w.hmid + t * HID + pl.r0 + r);
+    float res = 0.f;
+    if (cs.tid < NT * nr) res = __ldcg(p.w.hmid + (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
+    load_vec(cs, sm.xs, p.w.mlp, NT * INTER);
+    named_sync(1, NCT);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, INTER)) return false;
+    if (cs.tid < NT * nr) {
+      const int t = cs.tid / nr, r = cs.tid % nr;
+      float v = ((sm.part[(3 * r) * NT + t] + sm.part[(3 * r + 1) * NT + t]) + sm.part[(3 * r + 2) * NT + t]) + res;
       if (!CP) v = round_bf16(v);
       __stcg(hout + t * HID + pl.r0 + r, v);
     }
   }
-  if (!grid_sync(p, sm, cs)) return false;
-  load_vec(cs, sm.xs, hout, NT * HID);
-  named_sync(1, NCT);
-  return true;
+  return grid_sync(p, sm, cs);
 }
 
 // Runs a stack of layers; on return sm.xs holds the final-normed hidden (fp32) of NT tokens.
@@ -771,9 +870,10 @@ __device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0) {
   for (int l = 0; l < n; ++l) {
     const float* hin = (l & 1) ? hb1 : hb0;
     float* hout = (l & 1) ? hb0 : hb1;
-    if (!layer<NT, CP>(p, sm, cs, L + l, l, p0, hin, hout)) return false;
+    if (!layer<NT, CP>(p, sm, cs, L + l, l, p0, hin, hout, l == 0)) return false;
   }
-  rmsnorm_smem<NT>(sm, cs, sm.xs, CP ? p.cp_norm : p.bb_norm, p.eps);
+  const float* last = (n & 1) ? hb1 : hb0;
+  load_rmsnorm<NT, false>(sm, cs, last, CP ? p.cp_norm : p.bb_norm, p.eps, sm.xs);
   return true;
 }
 
@@ -1143,6 +1243,8 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
   return true;
 }
 
+// 13 warps over 4 SM sub-partitions: one sub-partition holds 4 warps of its 16K registers,
+// so a thread gets at most 128.
 extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);

@@ -40,7 +40,9 @@ constexpr int ATT_TARGET = 48;             // attention positions per work item 
 constexpr int ATT_STAGE_BYTES = 24576;     // shared staging of one K+V sub-chunk
 constexpr int ATT_CHMAX = 256;             // attention positions per work item (max)
 constexpr int MAX_ATT_CHUNKS = 32;         // attention work items per KV head (max)
-constexpr int PRT_STRIDE = HD + 2;         // partial record: m, l, acc[128]
+constexpr int PRT_STRIDE = HD + 4;         // partial record: m, l, 2 pad, acc[128] (16-byte rows)
+constexpr int MAXUNITS = 48;               // weight units per stage per CTA (needs >= 128 CTAs)
+constexpr int LP_STRIDE = 33;              // padded row of 32 lane partials
 
 // Same layout as TTSLayerWeights / CPLayerWeights of the reference
 // (fused_decode_tts.cu:22-34, fused_decode_code_predictor.cu:30-42).
@@ -152,6 +154,13 @@ struct Params {
   // barrier: dbg_timeline[0] = start, dbg_timeline[k] = barrier k (profiling)
   unsigned long long* dbg_timeline;
   int dbg_timeline_len;
+  // optional stage breakdown (profiling): CTA 0 stamps [stage][3] = GEMV start, GEMV end,
+  // barrier arrival; every CTA stamps its arrival time for stages [arr_stage0, +arr_n)
+  unsigned long long* dbg_marks;
+  int dbg_marks_len;
+  unsigned long long* dbg_arrivals;
+  int dbg_arr_stage0;
+  int dbg_arr_n;
 };
 
 // Host side: configure the kernel once per device and report the launch shape.
