@@ -111,6 +111,22 @@ typedef enum qtt_status {
   QTT_ERR_DEVICE = 8
 } qtt_status;
 
+/* No counterpart in the reference. The backbone decode step of
+ * launch_tts_decode_with_embedding for callers that must not allocate device memory while
+ * decoding (a service that reserves its whole memory budget at start-up, or a host whose caching
+ * allocator owns the device memory): the scratch lives in a fixed 636 KB device array inside the
+ * library instead of a per-stream cudaMalloc. Same arguments as the drop-in launcher minus the
+ * unused g_* scratch pointers and cache_len (= position + 1). The first call on a device takes
+ * the array's device address (cudaGetSymbolAddress) with that device current; make it before any
+ * stream capture. Calls share the array: calls that overlap on the GPU race, so keep them on one
+ * stream. max_seq_len above 8192 (or above what the device's CTA count supports) returns
+ * QTT_ERR_UNSUPPORTED. Returns the status of the argument checks and the launch. */
+qtt_status qtt_backbone_step_noalloc(const void* input_embedding, const TTSLayerWeights* layer_weights,
+                                     const void* final_norm_weight, const void* cos_table,
+                                     const void* sin_table, void* k_cache, void* v_cache, void* hidden_buffer,
+                                     void* g_normalized, int num_layers, int position, int max_seq_len,
+                                     float attn_scale, cudaStream_t stream);
+
 typedef struct qtt_engine qtt_engine;
 
 /* Model shape; must equal the compiled-in Qwen3-TTS-12Hz-0.6B shape
