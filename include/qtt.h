@@ -235,6 +235,10 @@ qtt_status qtt_set_debug_timeline(qtt_engine* e, unsigned long long* stamps, int
  * cta] for stages k in [arrival_stage0, arrival_stage0 + arrival_stages). Zeros turn it off. */
 qtt_status qtt_set_debug_profile(qtt_engine* e, unsigned long long* marks, int n_marks,
                                  unsigned long long* arrivals, int arrival_stage0, int arrival_stages);
+/* Weight-ring refill policy of the persistent kernel: 0 (default) refills a freed slot only
+ * after the consumers' next grid barrier, keeping refill traffic out of the barrier; 1 refills
+ * as soon as a slot is free. */
+qtt_status qtt_set_refill_policy(qtt_engine* e, int eager);
 /* Synchronises `stream` and converts the engine's device error word into a status. */
 qtt_status qtt_check(qtt_engine* e, cudaStream_t stream);
 

@@ -100,6 +100,7 @@ SIGNATURES = {
     "qtt_set_debug_profile": (_I, [_P, _P, _I, _P, _I, _I]),
     "qtt_get_hidden": (_I, [_P, _I, _P, _P]),
     "qtt_check": (_I, [_P, _P]),
+    "qtt_set_refill_policy": (_I, [_P, _I]),
     "qtt_backbone_step_noalloc": (_I, [_P, ctypes.POINTER(TTSLayerWeights), _P, _P, _P, _P, _P, _P, _P,
                                        _I, _I, _I, _F, _P]),
 }

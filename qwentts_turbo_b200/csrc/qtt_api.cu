@@ -1,4 +1,5 @@
 // Host side of libqtt: the drop-in launchers and the engine API declared in include/qtt.h.
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -411,6 +412,11 @@ extern "C" qtt_status qtt_engine_create(const qtt_weights* w, const qtt_dims* d,
   p.rope_rows = w->rope_rows;
   p.attn_scale = d->attn_scale;
   p.eps = d->rms_eps;
+  p.att_target = qtt::ATT_TARGET;
+  if (const char* v = std::getenv("QTT_ATT_TARGET")) {   // tuning knob: attention positions per item
+    const int t = std::atoi(v);
+    if (t >= 8 && t <= qtt::ATT_CHMAX) p.att_target = t;
+  }
   p.bb_max_seq = max_seq;
   p.cp_k = e->cp_k;
   p.cp_v = e->cp_v;
@@ -542,7 +548,7 @@ extern "C" qtt_status qtt_prefill(qtt_engine* e, int s, const void* embeds, int 
   for (int i = 0; i < len; ++i) {
     p.position = i;
     p.in_emb = static_cast<const bf16*>(embeds) + static_cast<size_t>(i) * qtt::HID;
-    p.flags = (i == len - 1) ? qtt::FLAG_HEAD_SAMPLE : 0;
+    p.flags = (e->base.flags & qtt::FLAG_EAGER_REFILL) | ((i == len - 1) ? qtt::FLAG_HEAD_SAMPLE : 0);
     cudaError_t ce = qtt::launch(p, e->shape.ctas, e->shape.smem, stream);
     if (ce != cudaSuccess) return from_cuda(ce);
   }
@@ -652,6 +658,12 @@ extern "C" qtt_status qtt_set_debug_profile(qtt_engine* e, unsigned long long* m
   e->base.dbg_arrivals = arrival_stages > 0 ? arrivals : nullptr;
   e->base.dbg_arr_stage0 = arrival_stage0;
   e->base.dbg_arr_n = arrival_stages;
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_set_refill_policy(qtt_engine* e, int eager) {
+  if (!e) return QTT_ERR_INVALID_ARG;
+  e->base.flags = eager ? (e->base.flags | qtt::FLAG_EAGER_REFILL) : (e->base.flags & ~qtt::FLAG_EAGER_REFILL);
   return QTT_OK;
 }
 

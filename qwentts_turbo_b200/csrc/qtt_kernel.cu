@@ -37,6 +37,8 @@ struct __align__(128) Smem {
   uint64_t full[NSLOTS];
   uint64_t empty[NSLOTS];
   int abort;
+  int epoch;                         // grid barriers completed by this CTA (producer pacing)
+  int free_epoch[NSLOTS];            // epoch during which the consumers freed each slot
   int bcast[4];
 };
 
@@ -58,6 +60,7 @@ void work_carve(void* base, Work* w) {
   w->bar = reinterpret_cast<uint32_t*>(c);
   w->err = reinterpret_cast<int*>(c + 64);
   w->att_cnt = reinterpret_cast<uint32_t*>(c + 128);
+  w->amax = reinterpret_cast<unsigned long long*>(c + 192);
   c += 256;
   w->hbuf = reinterpret_cast<float*>(c); c += sizeof(float) * 2 * NTMAX * HID;
   w->qkv = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * QKV_ROWS;
@@ -140,10 +143,34 @@ struct Prod {
   bool ok;
 };
 
-__device__ void prod_stage(Smem& sm, Prod& pr, const Plan& pl, int* err) {
+// Waits (bounded) until the consumers complete their next grid barrier after `seen`.
+__device__ bool wait_epoch_after(Smem& sm, int seen) {
+  volatile int* ep = &sm.epoch;
+  volatile int* ab = &sm.abort;
+  if (*ep != seen) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (*ep != seen) return true;
+    if ((it & 63u) == 63u) {
+      if (*ab) return false;
+      if (globaltimer_ns() - t0 > QTT_WAIT_NS) return false;
+    }
+  }
+}
+
+__device__ void prod_stage(Smem& sm, Prod& pr, const Plan& pl, int* err, bool eager) {
   for (int u = 0; u < pl.units && pr.ok; u += SLOT_UNITS) {
     const int n = min(SLOT_UNITS, pl.units - u);
     if (!mbar_wait(&sm.empty[pr.slot], (pr.round & 1u) ^ 1u, &sm.abort)) {
+      if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+      pr.ok = false;
+      return;
+    }
+    // A slot freed by the consumers is refilled only after the grid barrier that ends the stage
+    // in which it was freed, so that a stage's refill traffic does not compete with that stage's
+    // barrier; the ring holds two stages of weights, so the refill still lands in time.
+    if (!eager && pr.round > 0 &&
+        !wait_epoch_after(sm, *reinterpret_cast<volatile int*>(&sm.free_epoch[pr.slot]))) {
       if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
       pr.ok = false;
       return;
@@ -165,13 +192,13 @@ __device__ void prod_stage(Smem& sm, Prod& pr, const Plan& pl, int* err) {
   }
 }
 
-__device__ __forceinline__ void att_split(int S, int G, int& nch, int& chunk);
+__device__ __forceinline__ void att_split(int S, int G, int target, int& nch, int& chunk);
 
 // L2 prefetch of the cached backbone K/V rows this CTA's attention item will read in layer
 // li (rows written by earlier launches only), issued when the producer reaches the layer.
 __device__ void prod_prefetch_attention(const Params& p, int li, int p0, int cta, int G) {
   int nch, chunk;
-  att_split(p0 + 1, G, nch, chunk);
+  att_split(p0 + 1, G, p.att_target, nch, chunk);
   for (int item = cta; item < NKVH * nch; item += G) {
     const int h = item / nch, c = item - h * nch;
     const int s0 = c * chunk, a1 = min(s0 + chunk, p0);
@@ -183,14 +210,59 @@ __device__ void prod_prefetch_attention(const Params& p, int li, int p0, int cta
   }
 }
 
+// Rows [r0, r1) of this CTA's share of its KV head's o_proj columns (code-predictor layers):
+// head h = cta / (G/8) owns columns [2h*HD, 2h*HD + 2*HD) of W_o [HID][QSZ].
+__device__ __forceinline__ bool oh_rows(int cta, int G, int& h, int& r0, int& r1) {
+  const int gph = G / NKVH;
+  if (cta >= NKVH * gph) return false;
+  h = cta / gph;
+  const int i = cta - h * gph;
+  r0 = split_lo(HID, gph, i);
+  r1 = split_lo(HID, gph, i + 1);
+  return r1 > r0;
+}
+
+constexpr int OH_ROW_BYTES = 2 * HD * 2;            // 256 bf16 = 512 B
+constexpr int OH_ROWS_PER_SLOT = SLOT_BYTES / OH_ROW_BYTES;   // 48
+
+// Streams the CTA's o_proj row pieces (512 B each, stride QSZ) into the ring.
+__device__ void prod_oh(const LayerW* lw, Smem& sm, Prod& pr, int cta, int G, int* err, bool eager) {
+  int h, r0, r1;
+  if (!oh_rows(cta, G, h, r0, r1)) return;
+  const int n = r1 - r0;
+  for (int u = 0; u < n && pr.ok; u += OH_ROWS_PER_SLOT) {
+    const int m = min(OH_ROWS_PER_SLOT, n - u);
+    if (!mbar_wait(&sm.empty[pr.slot], (pr.round & 1u) ^ 1u, &sm.abort) ||
+        (!eager && pr.round > 0 &&
+         !wait_epoch_after(sm, *reinterpret_cast<volatile int*>(&sm.free_epoch[pr.slot])))) {
+      if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+      pr.ok = false;
+      return;
+    }
+    mbar_arrive_expect_tx(&sm.full[pr.slot], static_cast<uint32_t>(m * OH_ROW_BYTES));
+    for (int k = 0; k < m; ++k)
+      bulk_g2s(sm.ring[pr.slot] + k * OH_ROW_BYTES, lw->wo + static_cast<size_t>(r0 + u + k) * QSZ + 2 * h * HD,
+               OH_ROW_BYTES, &sm.full[pr.slot]);
+    pr.issued++;
+    if (++pr.slot == NSLOTS) {
+      pr.slot = 0;
+      pr.round++;
+    }
+  }
+}
+
 __device__ void prod_layers(const Params& p, Smem& sm, Prod& pr, const LayerW* L, int n, int cta, int G, int* err,
-                            int prefetch_pos) {
+                            int prefetch_pos, bool cp) {
+  const bool eager = (p.flags & FLAG_EAGER_REFILL) != 0;
   for (int l = 0; l < n && pr.ok; ++l) {
     if (prefetch_pos >= 0) prod_prefetch_attention(p, l, prefetch_pos, cta, G);
-    prod_stage(sm, pr, make_plan(SK_QKV, L + l, nullptr, 0, cta, G), err);
-    prod_stage(sm, pr, make_plan(SK_O, L + l, nullptr, 0, cta, G), err);
-    prod_stage(sm, pr, make_plan(SK_GU, L + l, nullptr, 0, cta, G), err);
-    prod_stage(sm, pr, make_plan(SK_D, L + l, nullptr, 0, cta, G), err);
+    prod_stage(sm, pr, make_plan(SK_QKV, L + l, nullptr, 0, cta, G), err, eager);
+    if (cp)
+      prod_oh(L + l, sm, pr, cta, G, err, eager);
+    else
+      prod_stage(sm, pr, make_plan(SK_O, L + l, nullptr, 0, cta, G), err, eager);
+    prod_stage(sm, pr, make_plan(SK_GU, L + l, nullptr, 0, cta, G), err, eager);
+    prod_stage(sm, pr, make_plan(SK_D, L + l, nullptr, 0, cta, G), err, eager);
   }
 }
 
@@ -209,18 +281,29 @@ __device__ void producer_main(const Params& p, Smem& sm, int cta, int G) {
       int pos = ld_volatile_i32(&p.st->position);
       if (pos < 0 || pos >= p.bb_max_seq) pos = -1;   // the consumers report the bad position
       for (int pass = 0; pass < NCPHEADS && pr.ok; ++pass) {
-        prod_layers(p, sm, pr, p.cp_layers, p.n_cp, cta, G, err, -1);
-        prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.cp_head[pass], p.cp_vocab, cta, G), err);
+        if (pass + 1 < NCPHEADS) {
+          // the next pass reads one row of code-predictor embedding table `pass` (chosen by this
+          // pass's token): bring this CTA's slice of the table into L2 while this pass runs
+          const int r0 = split_lo(p.cp_vocab, G, cta), r1 = split_lo(p.cp_vocab, G, cta + 1);
+          if (r1 > r0)
+            prefetch_l2_bulk(p.cp_emb[pass] + static_cast<size_t>(r0) * HID, static_cast<uint32_t>(r1 - r0) * HID * 2);
+        }
+        prod_layers(p, sm, pr, p.cp_layers, p.n_cp, cta, G, err, -1, true);
+        prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.cp_head[pass], p.cp_vocab, cta, G), err,
+                   (p.flags & FLAG_EAGER_REFILL) != 0);
       }
-      prod_layers(p, sm, pr, p.bb_layers, p.n_bb, cta, G, err, pos);
-      prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err);
+      prod_layers(p, sm, pr, p.bb_layers, p.n_bb, cta, G, err, pos, false);
+      prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err,
+                 (p.flags & FLAG_EAGER_REFILL) != 0);
     }
   } else if (p.mode == MODE_BB_STEP) {
     prod_layers(p, sm, pr, p.bb_layers, p.n_bb, cta, G, err,
-                (p.position >= 0 && p.position < p.bb_max_seq) ? p.position : -1);
-    if (p.flags & FLAG_HEAD_SAMPLE) prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err);
+                (p.position >= 0 && p.position < p.bb_max_seq) ? p.position : -1, false);
+    if (p.flags & FLAG_HEAD_SAMPLE)
+      prod_stage(sm, pr, make_plan(SK_HEAD, nullptr, p.codec_head, p.vocab, cta, G), err,
+                 (p.flags & FLAG_EAGER_REFILL) != 0);
   } else {
-    prod_layers(p, sm, pr, p.cp_layers, p.n_cp, cta, G, err, -1);
+    prod_layers(p, sm, pr, p.cp_layers, p.n_cp, cta, G, err, -1, true);
   }
   // Drain: wait (bounded) for the copies of the last ring's worth of fills so that no bulk
   // copy is still writing shared memory when this CTA exits early.
@@ -291,6 +374,7 @@ __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
         }
       }
     }
+    *reinterpret_cast<volatile int*>(&sm.epoch) = static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
     if (p.dbg_timeline != nullptr && cs.cta == 0) {
       const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
       if (k < static_cast<uint32_t>(p.dbg_timeline_len)) p.dbg_timeline[k] = globaltimer_ns();
@@ -448,7 +532,11 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
         lp[((u0 + cs.warp) * NT + t) * LP_STRIDE + cs.lane] = (ch[t][0] + ch[t][1]) + (ch[t][2] + ch[t][3]);
     }
     __syncwarp();
-    if (cs.lane == 0) mbar_arrive(&sm.empty[cs.slot]);
+    if (cs.lane == 0) {
+      *reinterpret_cast<volatile int*>(&sm.free_epoch[cs.slot]) =
+          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
+      mbar_arrive(&sm.empty[cs.slot]);
+    }
     if (++cs.slot == NSLOTS) {
       cs.slot = 0;
       cs.round++;
@@ -485,8 +573,9 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
 // of cp.async, then works from shared memory; chunks longer than one staging buffer are
 // processed in sub-chunks with an online softmax.
 // ------------------------------------------------------------------------------------------
-__device__ __forceinline__ void att_split(int S, int G, int& nch, int& chunk) {
-  nch = (S + ATT_TARGET - 1) / ATT_TARGET;
+__device__ __forceinline__ void att_split(int S, int G, int target, int& nch, int& chunk) {
+  target = target > 0 ? target : ATT_TARGET;
+  nch = (S + target - 1) / target;
   const int maxch = min(MAX_ATT_CHUNKS, max(1, G / NKVH));
   nch = min(max(nch, 1), maxch);
   chunk = (S + nch - 1) / nch;
@@ -506,12 +595,19 @@ __device__ __forceinline__ void stage_kv_rows(Cons& cs, uint8_t* dst_k, uint8_t*
   }
 }
 
-template <int NT, bool CP>
+// GROUP (code predictor): the CTAs are split into 8 groups of G/8, one per KV head; every CTA
+// of a group computes that head's whole attention (the context is at most 17 positions) and
+// leaves the result in sm.xs[t][2][HD] for the head's o_proj columns; the first CTA of the
+// group writes the new K/V rows.
+template <int NT, bool CP, bool GROUP>
 __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0) {
   const int S = p0 + NT;
   int nch, chunk;
-  att_split(S, cs.G, nch, chunk);
-  if (chunk > ATT_CHMAX) {
+  att_split(S, cs.G, p.att_target, nch, chunk);
+  if (GROUP) {
+    nch = 1;
+    chunk = S;
+  } else if (chunk > ATT_CHMAX) {
     fail(p, sm, DEV_ERR_BAD_POSITION);
     return false;
   }
@@ -535,8 +631,12 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
   uint8_t* kst = sm.att;
   uint8_t* vst = sm.att + SUB * ROWB;
 
-  for (int item = cs.cta; item < NKVH * nch; item += cs.G) {
-    const int h = item / nch, c = item - h * nch;
+  const int gph = cs.G / NKVH;
+  const int n_items = GROUP ? (cs.cta < NKVH * gph ? 1 : 0) : NKVH * nch;
+  for (int item = GROUP ? 0 : cs.cta; item < n_items; item += GROUP ? 1 : cs.G) {
+    const int h = GROUP ? cs.cta / gph : item / nch;
+    const int c = GROUP ? 0 : item - h * nch;
+    const bool writer = GROUP ? (cs.cta % gph == 0) : (c == 0);
     const int s0 = c * chunk, s1 = min(S, s0 + chunk);
     const uint8_t* kb = reinterpret_cast<const uint8_t*>(CP ? static_cast<const void*>(p.cp_k) : p.bb_k) +
                         (layer_off + static_cast<size_t>(h) * max_seq * HD) * ESZ;
@@ -607,7 +707,7 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     named_sync(1, NCT);
 
     // 3. item 0 of each head stores the new K/V rows into the cache.
-    if (c == 0) {
+    if (writer) {
       for (int e = cs.tid; e < NT * HD; e += NCT) {
         const int t = e / HD, d = e - t * HD;
         const size_t off = layer_off + (static_cast<size_t>(h) * max_seq + p0 + t) * HD + d;
@@ -712,6 +812,14 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     }
 
     // 5. publish (or finish directly when the head has a single item).
+    if (GROUP) {   // head output stays in shared memory: xs[t][hh * HD + d]
+      for (int e = cs.tid; e < J * HD; e += NCT) {
+        const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
+        sm.xs[t * 2 * HD + hh * HD + d] = acc_s[e] / ml[j * 4 + 1];
+      }
+      named_sync(1, NCT);
+      continue;
+    }
     if (nch == 1) {
       for (int e = cs.tid; e < J * HD; e += NCT) {
         const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
@@ -805,7 +913,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   if (!grid_sync(p, sm, cs)) return false;
 
   // ---- q/k norm + RoPE + KV write + attention
-  if (!attention<NT, CP>(p, sm, cs, lw, li, p0)) return false;
+  if (!attention<NT, CP, false>(p, sm, cs, lw, li, p0)) return false;
   if (!grid_sync(p, sm, cs)) return false;
 
   // ---- o_proj + residual (the residual rows are fetched with the attention output)
@@ -857,6 +965,202 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   return grid_sync(p, sm, cs);
 }
 
+// o_proj of one KV head for the code predictor: this CTA's rows of W_o restricted to the head's
+// 2*HD columns (512-byte row pieces in the ring), x = the head's attention output [NT][2*HD] in
+// shared memory. Result part[r * NT + t].
+template <int NT>
+__device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const float* x) {
+  if (nrows * NT * LP_STRIDE * 4 > ATT_STAGE_BYTES) {
+    fail(p, sm, DEV_ERR_BAD_POSITION);
+    return false;
+  }
+  float* lp = reinterpret_cast<float*>(sm.att);
+  float xr[NT][8];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const float4 a = *reinterpret_cast<const float4*>(x + t * 2 * HD + 8 * cs.lane);
+    const float4 b = *reinterpret_cast<const float4*>(x + t * 2 * HD + 8 * cs.lane + 4);
+    xr[t][0] = a.x; xr[t][1] = a.y; xr[t][2] = a.z; xr[t][3] = a.w;
+    xr[t][4] = b.x; xr[t][5] = b.y; xr[t][6] = b.z; xr[t][7] = b.w;
+  }
+  for (int u0 = 0; u0 < nrows; u0 += OH_ROWS_PER_SLOT) {
+    const int m = min(OH_ROWS_PER_SLOT, nrows - u0);
+    if (!mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort)) {
+      if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
+    } else {
+      for (int r = cs.warp; r < m; r += NCW) {
+        const uint4 v = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + r * OH_ROW_BYTES)[cs.lane];
+        const float w[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
+                            bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          float a = w[0] * xr[t][0];
+#pragma unroll
+          for (int j = 1; j < 8; ++j) a = fmaf(w[j], xr[t][j], a);
+          lp[((u0 + r) * NT + t) * LP_STRIDE + cs.lane] = a;
+        }
+      }
+    }
+    __syncwarp();
+    if (cs.lane == 0) {
+      *reinterpret_cast<volatile int*>(&sm.free_epoch[cs.slot]) =
+          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
+      mbar_arrive(&sm.empty[cs.slot]);
+    }
+    if (++cs.slot == NSLOTS) {
+      cs.slot = 0;
+      cs.round++;
+    }
+  }
+  named_sync(1, NCT);
+  for (int e = cs.tid; e < nrows * NT; e += NCT) {
+    const float* row = lp + e * LP_STRIDE;
+    float a[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) a[k] = row[k] + row[k + 16];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] += a[k + 8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) a[k] += a[k + 4];
+    sm.part[e] = (a[0] + a[2]) + (a[1] + a[3]);
+  }
+  named_sync(1, NCT);
+  return !aborted(sm);
+}
+
+// Code-predictor post-attention prologue: o = (sum over the 8 heads' o_proj partials, in head
+// order) + residual, RMSNorm into dst; this CTA's down_proj rows of o are also stored to hmid
+// for the down_proj residual.
+template <int NT>
+__device__ void load_rmsnorm_oh(Smem& sm, Cons& cs, const float* opart, const float* hin, const bf16* w, float eps,
+                                float* dst, float* hmid, int d0, int d1) {
+  const bool act = cs.tid < HID / 4;
+  float4 x[NT];
+  uint2 wv = make_uint2(0u, 0u);
+  double ss[NT];
+  if (act) {
+    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      float4 parts[NKVH];
+#pragma unroll
+      for (int h = 0; h < NKVH; ++h)
+        parts[h] = __ldcg(reinterpret_cast<const float4*>(opart + (h * NTMAX + t) * HID) + cs.tid);
+      const float4 r = __ldcg(reinterpret_cast<const float4*>(hin + t * HID) + cs.tid);
+      float4 a = parts[0];
+#pragma unroll
+      for (int h = 1; h < NKVH; ++h) {
+        a.x += parts[h].x; a.y += parts[h].y; a.z += parts[h].z; a.w += parts[h].w;
+      }
+      a.x += r.x; a.y += r.y; a.z += r.z; a.w += r.w;
+      x[t] = a;
+      const float v4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int idx = 4 * cs.tid + k;
+        if (idx >= d0 && idx < d1) __stcg(hmid + t * HID + idx, v4[k]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    double a = 0.0;
+    if (act) {
+      a = fma(static_cast<double>(x[t].x), static_cast<double>(x[t].x), a);
+      a = fma(static_cast<double>(x[t].y), static_cast<double>(x[t].y), a);
+      a = fma(static_cast<double>(x[t].z), static_cast<double>(x[t].z), a);
+      a = fma(static_cast<double>(x[t].w), static_cast<double>(x[t].w), a);
+    }
+    ss[t] = a;
+  }
+  block_sum_d<NT>(sm, cs, ss);
+  if (act) {
+    const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float rstd = rms_scale(ss[t], HID, eps);
+      float4 o;
+      o.x = x[t].x * rstd * w0;
+      o.y = x[t].y * rstd * w1;
+      o.z = x[t].z * rstd * w2;
+      o.w = x[t].w * rstd * w3;
+      reinterpret_cast<float4*>(dst + t * HID)[cs.tid] = o;
+    }
+  }
+  named_sync(1, NCT);
+}
+
+// One code-predictor layer in four grid-wide stages: QKV | attention + o_proj per KV-head group
+// | RMSNorm + gate/up | down (the attention context is at most 17 positions, so each head's
+// attention is computed by every CTA of its group instead of being gathered).
+template <int NT>
+__device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const float* hin,
+                         float* hout, bool input_in_smem) {
+  if (input_in_smem)
+    load_rmsnorm<NT, true>(sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
+  else
+    load_rmsnorm<NT, false>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
+  {
+    const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+    const int nr = pl.r1 - pl.r0;
+    for (int e = cs.tid; e < NT * nr; e += NCT) {
+      const int t = e / nr, r = e - t * nr;
+      __stcg(p.w.qkv + t * QKV_ROWS + pl.r0 + r, sm.part[r * NT + t]);
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return false;
+
+  // ---- attention of this group's KV head + its o_proj columns
+  if (!attention<NT, true, true>(p, sm, cs, lw, li, p0)) return false;
+  {
+    int h, r0, r1;
+    if (oh_rows(cs.cta, cs.G, h, r0, r1)) {
+      const int nr = r1 - r0;
+      if (!gemv_oh<NT>(p, sm, cs, nr, sm.xs)) return false;
+      for (int e = cs.tid; e < NT * nr; e += NCT) {
+        const int t = e / nr, r = e - t * nr;
+        __stcg(p.w.prt + (h * NTMAX + t) * HID + r0 + r, sm.part[r * NT + t]);
+      }
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return false;
+
+  // ---- o = sum of head partials + residual; RMSNorm + gate/up + SiLU
+  {
+    const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
+    load_rmsnorm_oh<NT>(sm, cs, p.w.prt, hin, lw->post_norm, p.eps, sm.xs, p.w.hmid, d0, d1);
+  }
+  {
+    const Plan pl = make_plan(SK_GU, lw, nullptr, 0, cs.cta, cs.G);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+    const int nj = pl.r1 - pl.r0;
+    for (int e = cs.tid; e < NT * nj; e += NCT) {
+      const int t = e / nj, j = e - t * nj;
+      const float g = sm.part[j * NT + t], u = sm.part[(nj + j) * NT + t];
+      __stcg(p.w.mlp + t * INTER + pl.r0 + j, (g / (1.0f + expf(-g))) * u);
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return false;
+
+  // ---- down_proj + residual (hmid rows were stored by this CTA in the previous stage)
+  {
+    const Plan pl = make_plan(SK_D, lw, nullptr, 0, cs.cta, cs.G);
+    const int nr = pl.r1 - pl.r0;
+    float res = 0.f;
+    if (cs.tid < NT * nr) res = __ldcg(p.w.hmid + (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
+    load_vec(cs, sm.xs, p.w.mlp, NT * INTER);
+    named_sync(1, NCT);
+    if (!gemv<NT>(p, pl, sm, cs, sm.xs, INTER)) return false;
+    if (cs.tid < NT * nr) {
+      const int t = cs.tid / nr, r = cs.tid % nr;
+      const float v = ((sm.part[(3 * r) * NT + t] + sm.part[(3 * r + 1) * NT + t]) + sm.part[(3 * r + 2) * NT + t]) + res;
+      __stcg(hout + t * HID + pl.r0 + r, v);
+    }
+  }
+  return grid_sync(p, sm, cs);
+}
+
 // Runs a stack of layers; on return sm.xs holds the final-normed hidden (fp32) of NT tokens.
 template <int NT, bool CP>
 __device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0) {
@@ -870,24 +1174,32 @@ __device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0) {
   for (int l = 0; l < n; ++l) {
     const float* hin = (l & 1) ? hb1 : hb0;
     float* hout = (l & 1) ? hb0 : hb1;
-    if (!layer<NT, CP>(p, sm, cs, L + l, l, p0, hin, hout, l == 0)) return false;
+    const bool ok = CP ? layer_cp<NT>(p, sm, cs, L + l, l, p0, hin, hout, l == 0)
+                       : layer<NT, CP>(p, sm, cs, L + l, l, p0, hin, hout, l == 0);
+    if (!ok) return false;
   }
   const float* last = (n & 1) ? hb1 : hb0;
   load_rmsnorm<NT, false>(sm, cs, last, CP ? p.cp_norm : p.bb_norm, p.eps, sm.xs);
   return true;
 }
 
-// Head GEMV on token t of sm.xs (bf16-cast hidden, generator.py:158,351) -> bf16 logits in
-// global, followed by a grid barrier.
-__device__ bool head(const Params& p, Smem& sm, Cons& cs, const bf16* W, int rows, int t) {
-  float* x = sm.xs + t * HID;
-  for (int i = cs.tid; i < HID; i += NCT) x[i] = round_bf16(x[i]);
-  named_sync(1, NCT);
-  const Plan pl = make_plan(SK_HEAD, nullptr, W, rows, cs.cta, cs.G);
-  if (!gemv<1>(p, pl, sm, cs, x, HID)) return false;
-  for (int r = cs.tid; r < pl.r1 - pl.r0; r += NCT) __stcg(p.w.logits + pl.r0 + r, round_bf16(sm.part[r]));
-  return grid_sync(p, sm, cs);
+struct SampleCfg;
+__device__ __forceinline__ float head_mask(const SampleCfg& c, int i, float x);
+
+// Orderable 64-bit key: larger value first, then smaller index (torch.argmax semantics).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(idx));
 }
+
+// Head GEMV on token t of sm.xs (bf16-cast hidden, generator.py:158,351) -> bf16 logits in
+// global memory, then a grid barrier. Greedy heads (c.do_sample == 0) also apply the masks and
+// fold their rows' argmax into a packed atomicMax before the barrier, so every CTA learns the
+// token with one 8-byte load; returns the token, -1 when the caller must run the sampler, or -2
+// on abort. `call` alternates the two argmax slots.
+__device__ int head(const Params& p, Smem& sm, Cons& cs, const bf16* W, int rows, int t, const SampleCfg& c,
+                    int call);
 
 // ------------------------------------------------------------------------------------------
 // Sampler (generator.py:158-172,178-207), computed redundantly by every CTA so that the
@@ -972,12 +1284,7 @@ __device__ int sample(const Params& p, Smem& sm, Cons& cs, const SampleCfg& c) {
   for (int j = 0; j < SPT; ++j) {
     const int i = base + j;
     float x = -INFINITY;
-    if (i < c.V) {
-      x = __ldcg(p.w.logits + i);
-      if (i >= c.suppress_from && i != c.eos) x = -INFINITY;
-      if (c.seen != nullptr && __ldcg(c.seen + i)) x = round_bf16(x > 0.f ? __fdiv_rn(x, c.penalty) : x * c.penalty);
-      if (c.mask_eos && i == c.eos) x = -INFINITY;
-    }
+    if (i < c.V) x = head_mask(c, i, __ldcg(p.w.logits + i));
     v[j] = x;
   }
   if (!c.do_sample) {
@@ -1085,6 +1392,52 @@ __device__ int sample(const Params& p, Smem& sm, Cons& cs, const SampleCfg& c) {
   return pick < c.V ? pick : c.V - 1;
 }
 
+__device__ __forceinline__ float head_mask(const SampleCfg& c, int i, float x) {
+  if (i >= c.suppress_from && i != c.eos) x = -INFINITY;
+  if (c.seen != nullptr && __ldcg(c.seen + i)) x = round_bf16(x > 0.f ? __fdiv_rn(x, c.penalty) : x * c.penalty);
+  if (c.mask_eos && i == c.eos) x = -INFINITY;
+  return x;
+}
+
+__device__ int head(const Params& p, Smem& sm, Cons& cs, const bf16* W, int rows, int t, const SampleCfg& c,
+                    int call) {
+  float* x = sm.xs + t * HID;
+  for (int i = cs.tid; i < HID; i += NCT) x[i] = round_bf16(x[i]);
+  named_sync(1, NCT);
+  const Plan pl = make_plan(SK_HEAD, nullptr, W, rows, cs.cta, cs.G);
+  if (!gemv<1>(p, pl, sm, cs, x, HID)) return -2;
+  const bool greedy = c.do_sample == 0;
+  unsigned long long best = 0ull;
+  for (int r = cs.tid; r < pl.r1 - pl.r0; r += NCT) {
+    const float lg = round_bf16(sm.part[r]);
+    __stcg(p.w.logits + pl.r0 + r, lg);
+    if (greedy) {
+      const unsigned long long k = argmax_key(head_mask(c, pl.r0 + r, lg), pl.r0 + r);
+      best = k > best ? k : best;
+    }
+  }
+  if (greedy) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (cs.lane == 0) sm.ured[cs.warp] = best;
+    named_sync(1, NCT);
+    if (cs.tid == 0) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < NCW; ++w) b = sm.ured[w] > b ? sm.ured[w] : b;
+      if (b != 0ull) atomicMax(p.w.amax + (call & 1), b);
+    }
+  }
+  if (!grid_sync(p, sm, cs)) return -2;
+  if (!greedy) return -1;
+  const unsigned long long k = __ldcg(p.w.amax + (call & 1));
+  named_sync(1, NCT);   // every thread has read the slot before it can be reused
+  if (cs.cta == 0 && cs.tid == 0) p.w.amax[(call + 1) & 1] = 0ull;   // next call's slot
+  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+}
+
 __device__ __forceinline__ uint32_t draw_u24(const Sampling& sp, int frame, int group) {
   const uint4 r = philox4x32_10(make_uint4(static_cast<uint32_t>(frame), static_cast<uint32_t>(group),
                                            static_cast<uint32_t>(sp.philox_stream), 0u),
@@ -1138,9 +1491,6 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
       named_sync(1, NCT);
       if (!run_stack<1, true>(p, sm, cs, g + 1)) return false;
     }
-    if (!head(p, sm, cs, p.cp_head[g], p.cp_vocab, g == 0 ? 1 : 0)) return false;
-    if (p.dbg_cp_logits && cs.cta == 0)
-      for (int i = cs.tid; i < p.cp_vocab; i += NCT) p.dbg_cp_logits[g * p.cp_vocab + i] = __ldcg(p.w.logits + i);
     SampleCfg c;
     c.V = p.cp_vocab;
     c.do_sample = p.sp.cp_do_sample;
@@ -1152,7 +1502,11 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
     c.penalty = 1.f;
     c.seen = nullptr;
     c.u24 = c.do_sample ? draw_u24(p.sp, step, g + 1) : 0u;
-    toks[g + 1] = sample(p, sm, cs, c);
+    const int tk = head(p, sm, cs, p.cp_head[g], p.cp_vocab, g == 0 ? 1 : 0, c, g);
+    if (tk == -2) return false;
+    if (p.dbg_cp_logits && cs.cta == 0)
+      for (int i = cs.tid; i < p.cp_vocab; i += NCT) p.dbg_cp_logits[g * p.cp_vocab + i] = __ldcg(p.w.logits + i);
+    toks[g + 1] = tk >= 0 ? tk : sample(p, sm, cs, c);
   }
   // ---- combine (generator.py:143-149,356-362): sequential bf16 adds
   {
@@ -1170,9 +1524,6 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   if (!run_stack<1, false>(p, sm, cs, pos)) return false;
   if (cs.cta == 0)
     for (int i = cs.tid; i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
-  if (!head(p, sm, cs, p.codec_head, p.vocab, 0)) return false;
-  if (p.dbg_g0_logits && cs.cta == 0)
-    for (int i = cs.tid; i < p.vocab; i += NCT) p.dbg_g0_logits[i] = __ldcg(p.w.logits + i);
   SampleCfg c;
   c.V = p.vocab;
   c.do_sample = p.sp.do_sample;
@@ -1184,7 +1535,11 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   c.penalty = p.sp.repetition_penalty;
   c.seen = (p.sp.repetition_penalty != 1.f) ? st->seen : nullptr;
   c.u24 = c.do_sample ? draw_u24(p.sp, step + 1, 0) : 0u;
-  const int g0n = sample(p, sm, cs, c);
+  const int tk = head(p, sm, cs, p.codec_head, p.vocab, 0, c, NCPHEADS);
+  if (tk == -2) return false;
+  if (p.dbg_g0_logits && cs.cta == 0)
+    for (int i = cs.tid; i < p.vocab; i += NCT) p.dbg_g0_logits[i] = __ldcg(p.w.logits + i);
+  const int g0n = tk >= 0 ? tk : sample(p, sm, cs, c);
   if (cs.cta == 0 && cs.tid == 0) {
     int32_t* out = p.codes + static_cast<size_t>(step) * NGROUPS;
     for (int g = 0; g < NGROUPS; ++g) out[g] = toks[g];
@@ -1220,7 +1575,6 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
     StreamState* st = p.st;
     if (cs.cta == 0)
       for (int i = cs.tid; i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
-    if (!head(p, sm, cs, p.codec_head, p.vocab, 0)) return false;
     SampleCfg c;
     c.V = p.vocab;
     c.do_sample = p.sp.do_sample;
@@ -1232,7 +1586,9 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
     c.penalty = 1.f;
     c.seen = nullptr;
     c.u24 = c.do_sample ? draw_u24(p.sp, 0, 0) : 0u;
-    const int g0 = sample(p, sm, cs, c);
+    const int tk = head(p, sm, cs, p.codec_head, p.vocab, 0, c, 0);
+    if (tk == -2) return false;
+    const int g0 = tk >= 0 ? tk : sample(p, sm, cs, c);
     if (cs.cta == 0 && cs.tid == 0) {
       st->g0 = g0;
       st->position = pos + 1;
@@ -1255,6 +1611,7 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
       mbar_init(&sm.empty[s], NCW);
     }
     sm.abort = 0;
+    sm.epoch = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -1265,6 +1622,10 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
   }
   if (p.dbg_timeline != nullptr && blockIdx.x == 0 && tid == 0 && p.dbg_timeline_len > 0)
     p.dbg_timeline[0] = globaltimer_ns();
+  if (blockIdx.x == 0 && tid == 0) {   // argmax slots; the first head is several barriers away
+    p.w.amax[0] = 0ull;
+    p.w.amax[1] = 0ull;
+  }
   Cons cs;
   cs.slot = 0;
   cs.round = 0;

@@ -90,6 +90,7 @@ struct Work {
   uint32_t* bar;       // grid barrier counter (zeroed before every launch)
   int* err;            // first device error code (sticky until the host clears it)
   uint32_t* att_cnt;   // [NKVH] last-arriver counters of the attention combine
+  unsigned long long* amax;  // [2] packed (value, first index) greedy argmax of a head
   float* hbuf;         // [2][NTMAX][HID] layer input / output
   float* qkv;          // [NTMAX][QKV_ROWS]
   float* attn;         // [NTMAX][QSZ]
@@ -103,7 +104,7 @@ size_t work_bytes();
 void work_carve(void* base, Work* w);
 
 enum Mode : int { MODE_FRAME = 0, MODE_BB_STEP = 1, MODE_CP_STEP = 2 };
-enum Flags : int { FLAG_HEAD_SAMPLE = 1 };
+enum Flags : int { FLAG_HEAD_SAMPLE = 1, FLAG_EAGER_REFILL = 2 };
 
 struct Params {
   // model (device pointers)
@@ -124,6 +125,7 @@ struct Params {
   int rope_rows;
   float attn_scale;
   float eps;
+  int att_target;          // attention positions per work item (target)
   // caches [layer][kv head][max_seq][128]
   bf16* bb_k;
   bf16* bb_v;
