@@ -114,7 +114,7 @@ typedef enum qtt_status {
 /* No counterpart in the reference. The backbone decode step of
  * launch_tts_decode_with_embedding for callers that must not allocate device memory while
  * decoding (a service that reserves its whole memory budget at start-up, or a host whose caching
- * allocator owns the device memory): the scratch lives in a fixed 636 KB device array inside the
+ * allocator owns the device memory): the scratch lives in a fixed 684 KB device array inside the
  * library instead of a per-stream cudaMalloc. Same arguments as the drop-in launcher minus the
  * unused g_* scratch pointers and cache_len (= position + 1). The first call on a device takes
  * the array's device address (cudaGetSymbolAddress) with that device current; make it before any

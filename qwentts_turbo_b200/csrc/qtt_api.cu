@@ -6,6 +6,8 @@
 #include <utility>
 #include <vector>
 
+#include <cuda.h>
+
 #include "../../include/qtt.h"
 #include "qtt_kernel.cuh"
 #include "qtt_device.cuh"
@@ -13,6 +15,40 @@
 using qtt::bf16;
 
 namespace {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// Tensor map of one W_down [HID][INTER] (bf16, row-major) for the fused MLP stage: boxes of
+// WD_BOX_ROWS rows x WD_BOX_COLS columns, no swizzle, zero fill beyond the last column.
+bool encode_wd_map(const void* wd, CUtensorMap* out) {
+  static_assert(sizeof(CUtensorMap) == qtt::TMAP_BYTES, "CUtensorMap size");
+  const EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(qtt::INTER), static_cast<cuuint64_t>(qtt::HID)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(qtt::INTER) * sizeof(bf16)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(qtt::WD_BOX_COLS), static_cast<cuuint32_t>(qtt::WD_BOX_ROWS)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(wd), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 thread_local int g_last_status = QTT_OK;
 
@@ -235,6 +271,7 @@ struct qtt_engine {
   qtt::LayerW* d_cp = nullptr;
   const bf16** d_cp_emb = nullptr;
   const bf16** d_cp_head = nullptr;
+  void* d_maps = nullptr;   // W_down tensor maps: [backbone layers] then [cp layers]
   void* d_work = nullptr;
   float* cp_k = nullptr;
   float* cp_v = nullptr;
@@ -284,6 +321,7 @@ void engine_free(qtt_engine* e) {
   cudaFree(e->d_cp);
   cudaFree(e->d_cp_emb);
   cudaFree(e->d_cp_head);
+  cudaFree(e->d_maps);
   cudaFree(e->d_work);
   cudaFree(e->cp_k);
   cudaFree(e->cp_v);
@@ -373,6 +411,23 @@ extern "C" qtt_status qtt_engine_create(const qtt_weights* w, const qtt_dims* d,
   QTT_TRY(cudaMemcpy(e->d_cp_emb, w->cp_codec_embedding, sizeof(void*) * qtt::NCPHEADS, cudaMemcpyHostToDevice));
   QTT_TRY(cudaMalloc(reinterpret_cast<void**>(&e->d_cp_head), sizeof(void*) * qtt::NCPHEADS));
   QTT_TRY(cudaMemcpy(e->d_cp_head, w->cp_lm_head, sizeof(void*) * qtt::NCPHEADS, cudaMemcpyHostToDevice));
+  // Fused gate/up + down stage: one W_down tensor map per layer (QTT_FUSED_MLP=0 selects the
+  // two-stage MLP, for comparison).
+  bool fused_mlp = true;
+  if (const char* v = std::getenv("QTT_FUSED_MLP")) fused_mlp = std::atoi(v) != 0;
+  if (fused_mlp) {
+    const int nl = d->backbone_layers + d->cp_layers;
+    std::vector<CUtensorMap> maps(nl);
+    for (int i = 0; i < nl && fused_mlp; ++i) {
+      const void* wd = i < d->backbone_layers ? w->backbone_layers[i].down_proj_weight
+                                              : w->cp_layers[i - d->backbone_layers].down_proj_weight;
+      fused_mlp = encode_wd_map(wd, &maps[i]);
+    }
+    if (fused_mlp) {
+      QTT_TRY(cudaMalloc(&e->d_maps, qtt::TMAP_BYTES * nl));
+      QTT_TRY(cudaMemcpy(e->d_maps, maps.data(), qtt::TMAP_BYTES * nl, cudaMemcpyHostToDevice));
+    }
+  }
   QTT_TRY(cudaMalloc(&e->d_work, qtt::work_bytes()));
   QTT_TRY(cudaMemset(e->d_work, 0, qtt::work_bytes()));
   const size_t cp_kv = sizeof(float) * d->cp_layers * qtt::NKVH * kCpMaxSeq * qtt::HD;
@@ -416,6 +471,10 @@ extern "C" qtt_status qtt_engine_create(const qtt_weights* w, const qtt_dims* d,
   if (const char* v = std::getenv("QTT_ATT_TARGET")) {   // tuning knob: attention positions per item
     const int t = std::atoi(v);
     if (t >= 8 && t <= qtt::ATT_CHMAX) p.att_target = t;
+  }
+  if (e->d_maps) {
+    p.bb_wd_map = e->d_maps;
+    p.cp_wd_map = static_cast<const uint8_t*>(e->d_maps) + qtt::TMAP_BYTES * d->backbone_layers;
   }
   p.bb_max_seq = max_seq;
   p.cp_k = e->cp_k;

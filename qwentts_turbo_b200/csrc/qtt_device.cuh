@@ -24,6 +24,7 @@ enum DevErr : int {
   DEV_ERR_BAD_TOKEN = 4,      // sampled / supplied token out of range
   DEV_ERR_BAD_POSITION = 5,   // position beyond the KV cache
   DEV_ERR_ABORTED = 6,        // another CTA reported an error first
+  DEV_ERR_SMEM_ALIGN = 7,     // shared memory base not aligned for 2-D TMA boxes
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -90,6 +91,22 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
           smem_u32(smem_dst)),
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 2-D tiled TMA load of one box of a tensor map held in global memory (no multicast). The
+// innermost coordinate x must be a multiple of 16 bytes / element size.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders earlier generic-proxy writes of a tensor map in global memory (the host's copy)
+// before this thread's tensor-map reads.
+__device__ __forceinline__ void tensormap_acquire(const void* tmap) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(tmap) : "memory");
 }
 
 // Ampere-style 16-byte async copy global -> shared, cached in L2 only (data written by other

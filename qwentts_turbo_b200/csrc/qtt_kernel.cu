@@ -23,7 +23,7 @@
 
 namespace qtt {
 
-enum StageKind : int { SK_QKV = 0, SK_O = 1, SK_GU = 2, SK_D = 3, SK_HEAD = 4 };
+enum StageKind : int { SK_QKV = 0, SK_O = 1, SK_GU = 2, SK_D = 3, SK_HEAD = 4, SK_GUF = 5 };
 
 struct __align__(128) Smem {
   uint8_t ring[NSLOTS][SLOT_BYTES];
@@ -52,6 +52,7 @@ size_t work_bytes() {
   n += sizeof(float) * NTMAX * HID;                     // hmid
   n += sizeof(float) * NTMAX * INTER;                   // mlp
   n += sizeof(float) * VMAX;                            // logits
+  n += sizeof(long long) * NHACC * NTMAX * HID;         // hacc
   return n;
 }
 
@@ -68,7 +69,8 @@ void work_carve(void* base, Work* w) {
   w->prt = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * NQH * MAX_ATT_CHUNKS * PRT_STRIDE;
   w->hmid = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * HID;
   w->mlp = reinterpret_cast<float*>(c); c += sizeof(float) * NTMAX * INTER;
-  w->logits = reinterpret_cast<float*>(c);
+  w->logits = reinterpret_cast<float*>(c); c += sizeof(float) * VMAX;
+  w->hacc = reinterpret_cast<long long*>(c);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -122,6 +124,13 @@ __device__ Plan make_plan(int kind, const LayerW* lw, const bf16* head, int head
       plan_add(pl, lw->wg + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
       plan_add(pl, lw->wu + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
     }
+  } else if (kind == SK_GUF) {   // fused MLP stage: intermediate columns in blocks of 8
+    pl.r0 = 8 * split_lo(INTER / 8, G, cta);
+    pl.r1 = 8 * split_lo(INTER / 8, G, cta + 1);
+    if (pl.r1 > pl.r0) {
+      plan_add(pl, lw->wg + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
+      plan_add(pl, lw->wu + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
+    }
   } else if (kind == SK_D) {
     pl.P = INTER / UNIT;
     pl.r0 = split_lo(HID, G, cta);
@@ -158,23 +167,33 @@ __device__ bool wait_epoch_after(Smem& sm, int seen) {
   }
 }
 
+// Waits (bounded) until the producer may refill its current slot. A slot freed by the
+// consumers is refilled only after the grid barrier that ends the stage in which it was freed,
+// so that a stage's refill traffic does not compete with that stage's barrier; the ring holds
+// two stages of weights, so the refill still lands in time.
+__device__ __forceinline__ bool prod_acquire(Smem& sm, Prod& pr, int* err, bool eager) {
+  if (!mbar_wait(&sm.empty[pr.slot], (pr.round & 1u) ^ 1u, &sm.abort) ||
+      (!eager && pr.round > 0 &&
+       !wait_epoch_after(sm, *reinterpret_cast<volatile int*>(&sm.free_epoch[pr.slot])))) {
+    if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+    pr.ok = false;
+    return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void prod_advance(Prod& pr) {
+  pr.issued++;
+  if (++pr.slot == NSLOTS) {
+    pr.slot = 0;
+    pr.round++;
+  }
+}
+
 __device__ void prod_stage(Smem& sm, Prod& pr, const Plan& pl, int* err, bool eager) {
   for (int u = 0; u < pl.units && pr.ok; u += SLOT_UNITS) {
     const int n = min(SLOT_UNITS, pl.units - u);
-    if (!mbar_wait(&sm.empty[pr.slot], (pr.round & 1u) ^ 1u, &sm.abort)) {
-      if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
-      pr.ok = false;
-      return;
-    }
-    // A slot freed by the consumers is refilled only after the grid barrier that ends the stage
-    // in which it was freed, so that a stage's refill traffic does not compete with that stage's
-    // barrier; the ring holds two stages of weights, so the refill still lands in time.
-    if (!eager && pr.round > 0 &&
-        !wait_epoch_after(sm, *reinterpret_cast<volatile int*>(&sm.free_epoch[pr.slot]))) {
-      if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
-      pr.ok = false;
-      return;
-    }
+    if (!prod_acquire(sm, pr, err, eager)) return;
     mbar_arrive_expect_tx(&sm.full[pr.slot], static_cast<uint32_t>(n * UNIT_BYTES));
     int base = 0;
     for (int s = 0; s < pl.nseg; ++s) {
@@ -184,11 +203,20 @@ __device__ void prod_stage(Smem& sm, Prod& pr, const Plan& pl, int* err, bool ea
                  static_cast<uint32_t>((b - a) * UNIT_BYTES), &sm.full[pr.slot]);
       base += pl.nun[s];
     }
-    pr.issued++;
-    if (++pr.slot == NSLOTS) {
-      pr.slot = 0;
-      pr.round++;
-    }
+    prod_advance(pr);
+  }
+}
+
+// W_down columns of this CTA's intermediate block for the fused MLP stage: four 2-D boxes
+// (256 rows x 24 columns, 12 KB) from the layer's tensor map, two per slot.
+__device__ void prod_wd(const void* tmap, Smem& sm, Prod& pr, int cta, int G, int* err, bool eager) {
+  const int j0 = 8 * split_lo(INTER / 8, G, cta);
+  for (int b = 0; b < WD_BOXES && pr.ok; b += WD_BOXES_PER_SLOT) {
+    if (!prod_acquire(sm, pr, err, eager)) return;
+    mbar_arrive_expect_tx(&sm.full[pr.slot], static_cast<uint32_t>(WD_BOXES_PER_SLOT * WD_BOX_BYTES));
+    for (int k = 0; k < WD_BOXES_PER_SLOT; ++k)
+      tma_load_2d(sm.ring[pr.slot] + k * WD_BOX_BYTES, tmap, j0, (b + k) * WD_BOX_ROWS, &sm.full[pr.slot]);
+    prod_advance(pr);
   }
 }
 
@@ -232,28 +260,19 @@ __device__ void prod_oh(const LayerW* lw, Smem& sm, Prod& pr, int cta, int G, in
   const int n = r1 - r0;
   for (int u = 0; u < n && pr.ok; u += OH_ROWS_PER_SLOT) {
     const int m = min(OH_ROWS_PER_SLOT, n - u);
-    if (!mbar_wait(&sm.empty[pr.slot], (pr.round & 1u) ^ 1u, &sm.abort) ||
-        (!eager && pr.round > 0 &&
-         !wait_epoch_after(sm, *reinterpret_cast<volatile int*>(&sm.free_epoch[pr.slot])))) {
-      if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
-      pr.ok = false;
-      return;
-    }
+    if (!prod_acquire(sm, pr, err, eager)) return;
     mbar_arrive_expect_tx(&sm.full[pr.slot], static_cast<uint32_t>(m * OH_ROW_BYTES));
     for (int k = 0; k < m; ++k)
       bulk_g2s(sm.ring[pr.slot] + k * OH_ROW_BYTES, lw->wo + static_cast<size_t>(r0 + u + k) * QSZ + 2 * h * HD,
                OH_ROW_BYTES, &sm.full[pr.slot]);
-    pr.issued++;
-    if (++pr.slot == NSLOTS) {
-      pr.slot = 0;
-      pr.round++;
-    }
+    prod_advance(pr);
   }
 }
 
 __device__ void prod_layers(const Params& p, Smem& sm, Prod& pr, const LayerW* L, int n, int cta, int G, int* err,
                             int prefetch_pos, bool cp) {
   const bool eager = (p.flags & FLAG_EAGER_REFILL) != 0;
+  const uint8_t* maps = static_cast<const uint8_t*>(cp ? p.cp_wd_map : p.bb_wd_map);
   for (int l = 0; l < n && pr.ok; ++l) {
     if (prefetch_pos >= 0) prod_prefetch_attention(p, l, prefetch_pos, cta, G);
     prod_stage(sm, pr, make_plan(SK_QKV, L + l, nullptr, 0, cta, G), err, eager);
@@ -261,8 +280,13 @@ __device__ void prod_layers(const Params& p, Smem& sm, Prod& pr, const LayerW* L
       prod_oh(L + l, sm, pr, cta, G, err, eager);
     else
       prod_stage(sm, pr, make_plan(SK_O, L + l, nullptr, 0, cta, G), err, eager);
-    prod_stage(sm, pr, make_plan(SK_GU, L + l, nullptr, 0, cta, G), err, eager);
-    prod_stage(sm, pr, make_plan(SK_D, L + l, nullptr, 0, cta, G), err, eager);
+    if (maps) {
+      prod_stage(sm, pr, make_plan(SK_GUF, L + l, nullptr, 0, cta, G), err, eager);
+      prod_wd(maps + l * TMAP_BYTES, sm, pr, cta, G, err, eager);
+    } else {
+      prod_stage(sm, pr, make_plan(SK_GU, L + l, nullptr, 0, cta, G), err, eager);
+      prod_stage(sm, pr, make_plan(SK_D, L + l, nullptr, 0, cta, G), err, eager);
+    }
   }
 }
 
@@ -276,6 +300,10 @@ __device__ bool frame_skipped(const Params& p) {
 __device__ void producer_main(const Params& p, Smem& sm, int cta, int G) {
   Prod pr{0u, 0u, 0u, true};
   int* err = p.w.err;
+  if (p.bb_wd_map != nullptr)
+    for (int l = 0; l < p.n_bb; ++l) tensormap_acquire(static_cast<const uint8_t*>(p.bb_wd_map) + l * TMAP_BYTES);
+  if (p.cp_wd_map != nullptr)
+    for (int l = 0; l < p.n_cp; ++l) tensormap_acquire(static_cast<const uint8_t*>(p.cp_wd_map) + l * TMAP_BYTES);
   if (p.mode == MODE_FRAME) {
     if (!frame_skipped(p)) {
       int pos = ld_volatile_i32(&p.st->position);
@@ -327,7 +355,47 @@ __device__ void producer_main(const Params& p, Smem& sm, int cta, int G) {
 struct Cons {
   uint32_t slot, round, bar_target;
   int cta, G, tid, warp, lane;
+  int dk;   // fused MLP stages completed in this launch (selects the fixed-point output buffer)
 };
+
+// A layer's input or output hidden state in global memory: fp32 (first layer of a stack,
+// separate MLP stages) or the fixed-point sum of the fused MLP stage.
+struct HIn {
+  const float* f;
+  const long long* q;
+};
+
+__device__ __forceinline__ long long float_to_fix(float v) {
+  return __double2ll_rn(static_cast<double>(v) * 4294967296.0);
+}
+__device__ __forceinline__ float fix_to_float(long long q) {
+  return __double2float_rn(static_cast<double>(q) * (1.0 / 4294967296.0));
+}
+// BB: backbone hidden states are bf16 between layers (fused_decode_tts.cu:541).
+template <bool BB>
+__device__ __forceinline__ float h_ld(const HIn& h, int i) {
+  if (h.q) {
+    const float v = fix_to_float(__ldcg(h.q + i));
+    return BB ? round_bf16(v) : v;
+  }
+  return __ldcg(h.f + i);
+}
+template <bool BB>
+__device__ __forceinline__ float4 h_ld4(const HIn& h, int i) {   // i: multiple of 4
+  if (h.q) {
+    const longlong2 a = __ldcg(reinterpret_cast<const longlong2*>(h.q + i));
+    const longlong2 b = __ldcg(reinterpret_cast<const longlong2*>(h.q + i + 2));
+    float4 v = make_float4(fix_to_float(a.x), fix_to_float(a.y), fix_to_float(b.x), fix_to_float(b.y));
+    if (BB) {
+      v.x = round_bf16(v.x);
+      v.y = round_bf16(v.y);
+      v.z = round_bf16(v.z);
+      v.w = round_bf16(v.w);
+    }
+    return v;
+  }
+  return __ldcg(reinterpret_cast<const float4*>(h.f + i));
+}
 
 __device__ __forceinline__ bool aborted(Smem& sm) { return *reinterpret_cast<volatile int*>(&sm.abort) != 0; }
 
@@ -427,12 +495,14 @@ __device__ __forceinline__ void block_sum(Smem& sm, Cons& cs, float (&v)[NT]) {
 // CTAs, or from shared memory) are normalised into dst = x * rsqrt(mean(x^2) + eps) * w.
 // The activation and the norm weights are loaded in the same round trip; thread t < 256 owns
 // elements 4t .. 4t+3 of every token.
+template <int NT>
+__device__ void rmsnorm_finish(Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps, float* dst);
+
 template <int NT, bool FROM_SMEM>
 __device__ void load_rmsnorm(Smem& sm, Cons& cs, const float* src, const bf16* w, float eps, float* dst) {
   const bool act = cs.tid < HID / 4;
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
-  double ss[NT];
   if (act) {
     wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
 #pragma unroll
@@ -441,6 +511,26 @@ __device__ void load_rmsnorm(Smem& sm, Cons& cs, const float* src, const bf16* w
       x[t] = FROM_SMEM ? *s4 : __ldcg(s4);
     }
   }
+  rmsnorm_finish<NT>(sm, cs, x, wv, eps, dst);
+}
+
+// Same, from a layer input in global memory (fp32 or fixed point).
+template <int NT, bool BB>
+__device__ void load_rmsnorm_h(Smem& sm, Cons& cs, const HIn& h, const bf16* w, float eps, float* dst) {
+  float4 x[NT];
+  uint2 wv = make_uint2(0u, 0u);
+  if (cs.tid < HID / 4) {
+    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) x[t] = h_ld4<BB>(h, t * HID + 4 * cs.tid);
+  }
+  rmsnorm_finish<NT>(sm, cs, x, wv, eps, dst);
+}
+
+template <int NT>
+__device__ void rmsnorm_finish(Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps, float* dst) {
+  const bool act = cs.tid < HID / 4;
+  double ss[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     double a = 0.0;
@@ -894,13 +984,16 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
 // values (written by the previous stage or by CTA 0 before the first barrier).
 // ------------------------------------------------------------------------------------------
 template <int NT, bool CP>
-__device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const float* hin,
-                      float* hout, bool input_in_smem) {
+__device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, float* hout_f, HIn& hout);
+
+template <int NT, bool CP>
+__device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const HIn& hin,
+                      float* hout_f, HIn& hout, bool input_in_smem) {
   // ---- input RMSNorm + QKV
   if (input_in_smem)
     load_rmsnorm<NT, true>(sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
   else
-    load_rmsnorm<NT, false>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm_h<NT, !CP>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
@@ -921,7 +1014,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
     const Plan pl = make_plan(SK_O, lw, nullptr, 0, cs.cta, cs.G);
     const int nr = pl.r1 - pl.r0;
     float res = 0.f;
-    if (cs.tid < NT * nr) res = __ldcg(hin + (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
+    if (cs.tid < NT * nr) res = h_ld<!CP>(hin, (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
     load_vec(cs, sm.xs, p.w.attn, NT * QSZ);
     named_sync(1, NCT);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, QSZ)) return false;
@@ -932,8 +1025,111 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   }
   if (!grid_sync(p, sm, cs)) return false;
 
-  // ---- post-attention RMSNorm + gate/up + SiLU
+  // ---- post-attention RMSNorm, MLP
   load_rmsnorm<NT, false>(sm, cs, p.w.hmid, lw->post_norm, p.eps, sm.xs);
+  return mlp_tail<NT, CP>(p, sm, cs, lw, hout_f, hout);
+}
+
+// Fused gate/up + down stage (layers with a W_down tensor map). On entry sm.xs holds the
+// post-attention RMSNorm output of the NT tokens and p.w.hmid (rows [d0, d1) of this CTA, as
+// split_lo(HID, G, cta)) the residual. This CTA computes the SiLU(gate) * up values of its
+// intermediate columns, their down-projection into all HID rows from the W_down boxes in the
+// ring, and adds the partials (plus the residual of its own rows) into the fixed-point layer
+// output hacc[dk % 3] with 64-bit integer atomics: integer addition is associative, so the
+// sum does not depend on the order in which CTAs arrive. It also clears its rows of
+// hacc[(dk + 1) % 3], the buffer of the next fused stage (last read two stages before).
+template <int NT>
+__device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, long long*& out) {
+  const Plan pl = make_plan(SK_GUF, lw, nullptr, 0, cs.cta, cs.G);
+  if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+  const int nj = pl.r1 - pl.r0;
+  float* mv = sm.xs + NTMAX * HID;   // [NT][WD_BOX_COLS], zero beyond this CTA's columns
+  if (cs.tid < NT * WD_BOX_COLS) {
+    const int t = cs.tid / WD_BOX_COLS, j = cs.tid - t * WD_BOX_COLS;
+    float m = 0.f;
+    if (j < nj) {
+      const float g = sm.part[j * NT + t], u = sm.part[(nj + j) * NT + t];
+      m = (g / (1.0f + expf(-g))) * u;
+    }
+    mv[t * WD_BOX_COLS + j] = m;
+  }
+  named_sync(1, NCT);
+
+  uint32_t sl[WD_SLOTS];
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < WD_SLOTS; ++i) {
+    sl[i] = cs.slot;
+    if (ok && !mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort)) {
+      if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
+      ok = false;
+    }
+    if (++cs.slot == NSLOTS) {
+      cs.slot = 0;
+      cs.round++;
+    }
+  }
+  const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
+  long long* acc = p.w.hacc + static_cast<size_t>(cs.dk % NHACC) * NTMAX * HID;
+  if (ok) {
+    for (int r = cs.tid; r < HID; r += NCT) {
+      const int box = r / WD_BOX_ROWS;
+      const uint8_t* row = sm.ring[box < WD_BOXES_PER_SLOT ? sl[0] : sl[1]] +
+                           (box % WD_BOXES_PER_SLOT) * WD_BOX_BYTES + (r % WD_BOX_ROWS) * (WD_BOX_COLS * 2);
+      float w[WD_BOX_COLS];
+#pragma unroll
+      for (int k = 0; k < WD_BOX_COLS / 8; ++k) {
+        const uint4 v = reinterpret_cast<const uint4*>(row)[k];
+        w[8 * k + 0] = bf16_lo(v.x); w[8 * k + 1] = bf16_hi(v.x);
+        w[8 * k + 2] = bf16_lo(v.y); w[8 * k + 3] = bf16_hi(v.y);
+        w[8 * k + 4] = bf16_lo(v.z); w[8 * k + 5] = bf16_hi(v.z);
+        w[8 * k + 6] = bf16_lo(v.w); w[8 * k + 7] = bf16_hi(v.w);
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const float* m = mv + t * WD_BOX_COLS;
+        float a0 = w[0] * m[0], a1 = w[1] * m[1];
+#pragma unroll
+        for (int j = 2; j < WD_BOX_COLS; j += 2) {
+          a0 = fmaf(w[j], m[j], a0);
+          a1 = fmaf(w[j + 1], m[j + 1], a1);
+        }
+        long long q = float_to_fix(a0 + a1);
+        if (r >= d0 && r < d1) q += float_to_fix(__ldcg(p.w.hmid + t * HID + r));
+        atomicAdd(reinterpret_cast<unsigned long long*>(acc + t * HID + r), static_cast<unsigned long long>(q));
+      }
+    }
+  }
+  __syncwarp();
+  if (cs.lane == 0) {
+#pragma unroll
+    for (int i = 0; i < WD_SLOTS; ++i) {
+      *reinterpret_cast<volatile int*>(&sm.free_epoch[sl[i]]) =
+          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
+      mbar_arrive(&sm.empty[sl[i]]);
+    }
+  }
+  long long* nxt = p.w.hacc + static_cast<size_t>((cs.dk + 1) % NHACC) * NTMAX * HID;
+  for (int e = cs.tid; e < NTMAX * (d1 - d0); e += NCT) {
+    const int t = e / (d1 - d0), r = d0 + e % (d1 - d0);
+    __stcg(nxt + t * HID + r, 0ll);
+  }
+  cs.dk++;
+  out = acc;
+  return !aborted(sm);
+}
+
+// MLP half of a layer after its post-attention RMSNorm (in sm.xs): the fused stage when the
+// stack has W_down tensor maps, else gate/up and down as two stages.
+template <int NT, bool CP>
+__device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, float* hout_f, HIn& hout) {
+  if ((CP ? p.cp_wd_map : p.bb_wd_map) != nullptr) {
+    long long* acc = nullptr;
+    if (!mlp_fused<NT>(p, sm, cs, lw, acc)) return false;
+    hout.f = nullptr;
+    hout.q = acc;
+    return grid_sync(p, sm, cs);
+  }
   {
     const Plan pl = make_plan(SK_GU, lw, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
@@ -959,9 +1155,11 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
       const int t = cs.tid / nr, r = cs.tid % nr;
       float v = ((sm.part[(3 * r) * NT + t] + sm.part[(3 * r + 1) * NT + t]) + sm.part[(3 * r + 2) * NT + t]) + res;
       if (!CP) v = round_bf16(v);
-      __stcg(hout + t * HID + pl.r0 + r, v);
+      __stcg(hout_f + t * HID + pl.r0 + r, v);
     }
   }
+  hout.f = hout_f;
+  hout.q = nullptr;
   return grid_sync(p, sm, cs);
 }
 
@@ -1032,7 +1230,7 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
 // order) + residual, RMSNorm into dst; this CTA's down_proj rows of o are also stored to hmid
 // for the down_proj residual.
 template <int NT>
-__device__ void load_rmsnorm_oh(Smem& sm, Cons& cs, const float* opart, const float* hin, const bf16* w, float eps,
+__device__ void load_rmsnorm_oh(Smem& sm, Cons& cs, const float* opart, const HIn& hin, const bf16* w, float eps,
                                 float* dst, float* hmid, int d0, int d1) {
   const bool act = cs.tid < HID / 4;
   float4 x[NT];
@@ -1046,7 +1244,7 @@ __device__ void load_rmsnorm_oh(Smem& sm, Cons& cs, const float* opart, const fl
 #pragma unroll
       for (int h = 0; h < NKVH; ++h)
         parts[h] = __ldcg(reinterpret_cast<const float4*>(opart + (h * NTMAX + t) * HID) + cs.tid);
-      const float4 r = __ldcg(reinterpret_cast<const float4*>(hin + t * HID) + cs.tid);
+      const float4 r = h_ld4<false>(hin, t * HID + 4 * cs.tid);
       float4 a = parts[0];
 #pragma unroll
       for (int h = 1; h < NKVH; ++h) {
@@ -1094,12 +1292,12 @@ __device__ void load_rmsnorm_oh(Smem& sm, Cons& cs, const float* opart, const fl
 // | RMSNorm + gate/up | down (the attention context is at most 17 positions, so each head's
 // attention is computed by every CTA of its group instead of being gathered).
 template <int NT>
-__device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const float* hin,
-                         float* hout, bool input_in_smem) {
+__device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const HIn& hin,
+                         float* hout_f, HIn& hout, bool input_in_smem) {
   if (input_in_smem)
     load_rmsnorm<NT, true>(sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
   else
-    load_rmsnorm<NT, false>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm_h<NT, false>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
@@ -1126,44 +1324,17 @@ __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
   }
   if (!grid_sync(p, sm, cs)) return false;
 
-  // ---- o = sum of head partials + residual; RMSNorm + gate/up + SiLU
+  // ---- o = sum of head partials + residual; RMSNorm, MLP
   {
     const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
     load_rmsnorm_oh<NT>(sm, cs, p.w.prt, hin, lw->post_norm, p.eps, sm.xs, p.w.hmid, d0, d1);
   }
-  {
-    const Plan pl = make_plan(SK_GU, lw, nullptr, 0, cs.cta, cs.G);
-    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
-    const int nj = pl.r1 - pl.r0;
-    for (int e = cs.tid; e < NT * nj; e += NCT) {
-      const int t = e / nj, j = e - t * nj;
-      const float g = sm.part[j * NT + t], u = sm.part[(nj + j) * NT + t];
-      __stcg(p.w.mlp + t * INTER + pl.r0 + j, (g / (1.0f + expf(-g))) * u);
-    }
-  }
-  if (!grid_sync(p, sm, cs)) return false;
-
-  // ---- down_proj + residual (hmid rows were stored by this CTA in the previous stage)
-  {
-    const Plan pl = make_plan(SK_D, lw, nullptr, 0, cs.cta, cs.G);
-    const int nr = pl.r1 - pl.r0;
-    float res = 0.f;
-    if (cs.tid < NT * nr) res = __ldcg(p.w.hmid + (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
-    load_vec(cs, sm.xs, p.w.mlp, NT * INTER);
-    named_sync(1, NCT);
-    if (!gemv<NT>(p, pl, sm, cs, sm.xs, INTER)) return false;
-    if (cs.tid < NT * nr) {
-      const int t = cs.tid / nr, r = cs.tid % nr;
-      const float v = ((sm.part[(3 * r) * NT + t] + sm.part[(3 * r + 1) * NT + t]) + sm.part[(3 * r + 2) * NT + t]) + res;
-      __stcg(hout + t * HID + pl.r0 + r, v);
-    }
-  }
-  return grid_sync(p, sm, cs);
+  return mlp_tail<NT, true>(p, sm, cs, lw, hout_f, hout);
 }
 
 // Runs a stack of layers; on return sm.xs holds the final-normed hidden (fp32) of NT tokens.
 template <int NT, bool CP>
-__device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0) {
+__device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0, HIn* last = nullptr) {
   const LayerW* L = CP ? p.cp_layers : p.bb_layers;
   const int n = CP ? p.n_cp : p.n_bb;
   // layer input already in sm.xs; CTA 0 publishes it for the o_proj residual.
@@ -1171,15 +1342,17 @@ __device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0) {
   float* hb1 = p.w.hbuf + NTMAX * HID;
   if (cs.cta == 0)
     for (int i = cs.tid; i < NT * HID; i += NCT) __stcg(hb0 + i, sm.xs[i]);
+  HIn h{hb0, nullptr};
   for (int l = 0; l < n; ++l) {
-    const float* hin = (l & 1) ? hb1 : hb0;
-    float* hout = (l & 1) ? hb0 : hb1;
-    const bool ok = CP ? layer_cp<NT>(p, sm, cs, L + l, l, p0, hin, hout, l == 0)
-                       : layer<NT, CP>(p, sm, cs, L + l, l, p0, hin, hout, l == 0);
+    float* hout_f = (l & 1) ? hb0 : hb1;
+    HIn hout{nullptr, nullptr};
+    const bool ok = CP ? layer_cp<NT>(p, sm, cs, L + l, l, p0, h, hout_f, hout, l == 0)
+                       : layer<NT, CP>(p, sm, cs, L + l, l, p0, h, hout_f, hout, l == 0);
     if (!ok) return false;
+    h = hout;
   }
-  const float* last = (n & 1) ? hb1 : hb0;
-  load_rmsnorm<NT, false>(sm, cs, last, CP ? p.cp_norm : p.bb_norm, p.eps, sm.xs);
+  load_rmsnorm_h<NT, !CP>(sm, cs, h, CP ? p.cp_norm : p.bb_norm, p.eps, sm.xs);
+  if (last) *last = h;
   return true;
 }
 
@@ -1559,15 +1732,13 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
   }
   xs_from_bf16(cs, sm.xs, p.in_emb);
   named_sync(1, NCT);
-  const bool ok = cp ? run_stack<1, true>(p, sm, cs, pos) : run_stack<1, false>(p, sm, cs, pos);
+  HIn last{nullptr, nullptr};
+  const bool ok = cp ? run_stack<1, true>(p, sm, cs, pos, &last) : run_stack<1, false>(p, sm, cs, pos, &last);
   if (!ok) return false;
   if (cs.cta == 0) {
     for (int i = cs.tid; i < HID; i += NCT) {
       if (p.out_hidden) p.out_hidden[i] = sm.xs[i];
-      if (p.out_raw_hidden) {
-        const float* last = p.w.hbuf + ((cp ? p.n_cp : p.n_bb) & 1 ? NTMAX * HID : 0);
-        p.out_raw_hidden[i] = __float2bfloat16_rn(__ldcg(last + i));
-      }
+      if (p.out_raw_hidden) p.out_raw_hidden[i] = __float2bfloat16_rn(cp ? h_ld<false>(last, i) : h_ld<true>(last, i));
     }
   }
   if (!cp && (p.flags & FLAG_HEAD_SAMPLE)) {
@@ -1605,6 +1776,11 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int tid = threadIdx.x;
+  if ((p.bb_wd_map != nullptr || p.cp_wd_map != nullptr) && (smem_u32(smem_raw) & 127u) != 0u) {
+    // 2-D TMA boxes land at 128-byte aligned ring offsets; every CTA leaves before any wait
+    if (tid == 0) set_error(p.w.err, DEV_ERR_SMEM_ALIGN);
+    return;
+  }
   if (tid == 0) {
     for (int s = 0; s < NSLOTS; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -1635,6 +1811,15 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
   cs.tid = tid;
   cs.warp = warp;
   cs.lane = tid & 31;
+  cs.dk = 0;
+  if (p.bb_wd_map != nullptr || p.cp_wd_map != nullptr) {
+    // the first fused MLP stage (several barriers away) accumulates into hacc[0]
+    const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
+    for (int e = tid; e < NTMAX * (d1 - d0); e += NCT) {
+      const int t = e / (d1 - d0), r = d0 + e % (d1 - d0);
+      __stcg(p.w.hacc + t * HID + r, 0ll);
+    }
+  }
   bool ok;
   if (p.mode == MODE_FRAME)
     ok = run_frame(p, sm, cs);

@@ -43,6 +43,19 @@ constexpr int MAX_ATT_CHUNKS = 32;         // attention work items per KV head (
 constexpr int PRT_STRIDE = HD + 4;         // partial record: m, l, 2 pad, acc[128] (16-byte rows)
 constexpr int MAXUNITS = 48;               // weight units per stage per CTA (needs >= 128 CTAs)
 constexpr int LP_STRIDE = 33;              // padded row of 32 lane partials
+// Fused gate/up + down stage: each CTA owns a block of intermediate columns (multiples of 8,
+// at most 24 with >= 128 CTAs) and streams the matching columns of W_down as four 2-D TMA
+// boxes of 256 rows x 24 columns; the down-projection partials of all CTAs are summed with
+// 64-bit integer atomics in fixed point (scale 2^32), which makes the sum independent of the
+// order of arrival.
+constexpr int WD_BOX_COLS = 24;
+constexpr int WD_BOX_ROWS = 256;
+constexpr int WD_BOX_BYTES = WD_BOX_COLS * WD_BOX_ROWS * 2;   // 12 KB
+constexpr int WD_BOXES = HID / WD_BOX_ROWS;                   // 4
+constexpr int WD_BOXES_PER_SLOT = SLOT_BYTES / WD_BOX_BYTES;  // 2
+constexpr int WD_SLOTS = WD_BOXES / WD_BOXES_PER_SLOT;        // 2
+constexpr int NHACC = 3;                                      // rotating fixed-point layer outputs
+constexpr size_t TMAP_BYTES = 128;                            // one CUtensorMap
 
 // Same layout as TTSLayerWeights / CPLayerWeights of the reference
 // (fused_decode_tts.cu:22-34, fused_decode_code_predictor.cu:30-42).
@@ -98,6 +111,7 @@ struct Work {
   float* hmid;         // [NTMAX][HID]
   float* mlp;          // [NTMAX][INTER]
   float* logits;       // [VMAX]
+  long long* hacc;     // [NHACC][NTMAX][HID] fused-MLP layer outputs, fixed point 2^-32
 };
 
 size_t work_bytes();
@@ -126,6 +140,10 @@ struct Params {
   float attn_scale;
   float eps;
   int att_target;          // attention positions per work item (target)
+  // optional W_down tensor maps (device arrays of CUtensorMap, one per layer): when set, the
+  // stack runs the fused gate/up + down stage; when null, separate gate/up and down stages
+  const void* bb_wd_map;
+  const void* cp_wd_map;
   // caches [layer][kv head][max_seq][128]
   bf16* bb_k;
   bf16* bb_v;

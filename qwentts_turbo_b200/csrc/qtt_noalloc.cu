@@ -32,11 +32,13 @@
 namespace {
 
 // Same layout as qtt::work_carve (barrier / error / combine counters, per-token activations
-// for up to NTMAX tokens and MAX_ATT_CHUNKS attention partial records per query head).
+// for up to NTMAX tokens, MAX_ATT_CHUNKS attention partial records per query head, and the
+// fixed-point layer outputs of the fused MLP stage).
 constexpr size_t kNoAllocScratchBytes =
     256 + sizeof(float) * (2 * qtt::NTMAX * qtt::HID + qtt::NTMAX * qtt::QKV_ROWS + qtt::NTMAX * qtt::QSZ +
                            qtt::NTMAX * qtt::NQH * qtt::MAX_ATT_CHUNKS * qtt::PRT_STRIDE + qtt::NTMAX * qtt::HID +
-                           qtt::NTMAX * qtt::INTER + qtt::VMAX);
+                           qtt::NTMAX * qtt::INTER + qtt::VMAX) +
+    sizeof(long long) * qtt::NHACC * qtt::NTMAX * qtt::HID;
 
 // Largest cache length one step supports: at most (CTAs / 8) attention work items per KV head,
 // each over at most ATT_CHMAX positions, and never more than the scratch's MAX_ATT_CHUNKS
