@@ -103,6 +103,25 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, in
       : "memory");
 }
 
+// Bulk element-wise add of a shared-memory block into global memory (TMA reduction, u64
+// lanes; integer addition, so concurrent reductions from many CTAs commute exactly).
+__device__ __forceinline__ void bulk_reduce_add_u64(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.u64 [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_and_wait_all() {
+  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Generic-proxy shared-memory writes -> visible to a following bulk (async-proxy) read.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Completed async-proxy global writes -> ordered before this thread's later generic operations.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // Orders earlier generic-proxy writes of a tensor map in global memory (the host's copy)
 // before this thread's tensor-map reads.
 __device__ __forceinline__ void tensormap_acquire(const void* tmap) {

@@ -85,8 +85,9 @@ struct Plan {
   int nun[3];
 };
 
+// First row of part c when n rows are split over G parts (n * G < 2^32 for every use here).
 __device__ __forceinline__ int split_lo(int n, int G, int c) {
-  return static_cast<int>((static_cast<long long>(n) * c) / G);
+  return static_cast<int>((static_cast<uint32_t>(n) * static_cast<uint32_t>(c)) / static_cast<uint32_t>(G));
 }
 
 __device__ __forceinline__ void plan_add(Plan& pl, const bf16* base, int rows) {
@@ -269,11 +270,28 @@ __device__ void prod_oh(const LayerW* lw, Smem& sm, Prod& pr, int cta, int G, in
   }
 }
 
+// L1 prefetch of what the consumers of this SM read with plain loads in a layer's prologues:
+// the layer's pointer table and its RMSNorm weights (issued a stage or two ahead).
+__device__ void prod_prefetch_norms(const LayerW* lw) {
+  prefetch_l1(lw);
+  prefetch_l1(reinterpret_cast<const uint8_t*>(lw) + sizeof(LayerW) - 1);
+  const bf16* v[2] = {lw->in_norm, lw->post_norm};
+  for (int i = 0; i < 2; ++i)
+    for (int o = 0; o < HID * 2; o += 128) prefetch_l1(reinterpret_cast<const uint8_t*>(v[i]) + o);
+  for (int o = 0; o < HD * 2; o += 128) {
+    prefetch_l1(reinterpret_cast<const uint8_t*>(lw->q_norm) + o);
+    prefetch_l1(reinterpret_cast<const uint8_t*>(lw->k_norm) + o);
+  }
+}
+
 __device__ void prod_layers(const Params& p, Smem& sm, Prod& pr, const LayerW* L, int n, int cta, int G, int* err,
                             int prefetch_pos, bool cp) {
   const bool eager = (p.flags & FLAG_EAGER_REFILL) != 0;
   const uint8_t* maps = static_cast<const uint8_t*>(cp ? p.cp_wd_map : p.bb_wd_map);
   for (int l = 0; l < n && pr.ok; ++l) {
+    prod_prefetch_norms(L + l);
+    if (l + 1 == n)
+      for (int o = 0; o < HID * 2; o += 128) prefetch_l1(reinterpret_cast<const uint8_t*>(cp ? p.cp_norm : p.bb_norm) + o);
     if (prefetch_pos >= 0) prod_prefetch_attention(p, l, prefetch_pos, cta, G);
     prod_stage(sm, pr, make_plan(SK_QKV, L + l, nullptr, 0, cta, G), err, eager);
     if (cp)
@@ -412,6 +430,14 @@ __device__ __forceinline__ void stage_mark(const Params& p, const Cons& cs, int 
   }
 }
 
+// Profiling stamps of CTA 0 inside a stage's RMSNorm prologue (input loaded, norm reduced).
+__device__ __forceinline__ void prologue_mark(const Params& p, const Cons& cs, int id) {
+  if (p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0) {
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+    if (static_cast<int>(8 * 1024 + 4 * k + id) < p.dbg_marks_len) p.dbg_marks[8 * 1024 + 4 * k + id] = globaltimer_ns();
+  }
+}
+
 // Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded).
 __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
   named_sync(1, NCT);
@@ -496,10 +522,12 @@ __device__ __forceinline__ void block_sum(Smem& sm, Cons& cs, float (&v)[NT]) {
 // The activation and the norm weights are loaded in the same round trip; thread t < 256 owns
 // elements 4t .. 4t+3 of every token.
 template <int NT>
-__device__ void rmsnorm_finish(Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps, float* dst);
+__device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps,
+                               float* dst);
 
 template <int NT, bool FROM_SMEM>
-__device__ void load_rmsnorm(Smem& sm, Cons& cs, const float* src, const bf16* w, float eps, float* dst) {
+__device__ void load_rmsnorm(const Params& p, Smem& sm, Cons& cs, const float* src, const bf16* w, float eps,
+                             float* dst) {
   const bool act = cs.tid < HID / 4;
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
@@ -511,12 +539,13 @@ __device__ void load_rmsnorm(Smem& sm, Cons& cs, const float* src, const bf16* w
       x[t] = FROM_SMEM ? *s4 : __ldcg(s4);
     }
   }
-  rmsnorm_finish<NT>(sm, cs, x, wv, eps, dst);
+  rmsnorm_finish<NT>(p, sm, cs, x, wv, eps, dst);
 }
 
 // Same, from a layer input in global memory (fp32 or fixed point).
 template <int NT, bool BB>
-__device__ void load_rmsnorm_h(Smem& sm, Cons& cs, const HIn& h, const bf16* w, float eps, float* dst) {
+__device__ void load_rmsnorm_h(const Params& p, Smem& sm, Cons& cs, const HIn& h, const bf16* w, float eps,
+                               float* dst) {
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
   if (cs.tid < HID / 4) {
@@ -524,11 +553,12 @@ __device__ void load_rmsnorm_h(Smem& sm, Cons& cs, const HIn& h, const bf16* w, 
 #pragma unroll
     for (int t = 0; t < NT; ++t) x[t] = h_ld4<BB>(h, t * HID + 4 * cs.tid);
   }
-  rmsnorm_finish<NT>(sm, cs, x, wv, eps, dst);
+  rmsnorm_finish<NT>(p, sm, cs, x, wv, eps, dst);
 }
 
 template <int NT>
-__device__ void rmsnorm_finish(Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps, float* dst) {
+__device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps,
+                               float* dst) {
   const bool act = cs.tid < HID / 4;
   double ss[NT];
 #pragma unroll
@@ -542,7 +572,12 @@ __device__ void rmsnorm_finish(Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 
     }
     ss[t] = a;
   }
+  if (p.dbg_marks != nullptr) {
+    asm volatile("" ::"d"(ss[0]));
+    prologue_mark(p, cs, 0);
+  }
   block_sum_d<NT>(sm, cs, ss);
+  prologue_mark(p, cs, 1);
   if (act) {
     const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
 #pragma unroll
@@ -556,7 +591,9 @@ __device__ void rmsnorm_finish(Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 
       reinterpret_cast<float4*>(dst + t * HID)[cs.tid] = o;
     }
   }
+  prologue_mark(p, cs, 2);
   named_sync(1, NCT);
+  prologue_mark(p, cs, 3);
 }
 
 // Copy NT vectors of n floats from global (L2, written by other CTAs) into shared memory.
@@ -991,9 +1028,9 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
                       float* hout_f, HIn& hout, bool input_in_smem) {
   // ---- input RMSNorm + QKV
   if (input_in_smem)
-    load_rmsnorm<NT, true>(sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm<NT, true>(p, sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
   else
-    load_rmsnorm_h<NT, !CP>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm_h<NT, !CP>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
@@ -1026,7 +1063,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   if (!grid_sync(p, sm, cs)) return false;
 
   // ---- post-attention RMSNorm, MLP
-  load_rmsnorm<NT, false>(sm, cs, p.w.hmid, lw->post_norm, p.eps, sm.xs);
+  load_rmsnorm<NT, false>(p, sm, cs, p.w.hmid, lw->post_norm, p.eps, sm.xs);
   return mlp_tail<NT, CP>(p, sm, cs, lw, hout_f, hout);
 }
 
@@ -1069,8 +1106,13 @@ __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
       cs.round++;
     }
   }
+  if (p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0) {   // profiling: W_down boxes ready
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+    if (static_cast<int>(4 * 1024 + 4 * k + 3) < p.dbg_marks_len) p.dbg_marks[4 * 1024 + 4 * k + 3] = globaltimer_ns();
+  }
   const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
   long long* acc = p.w.hacc + static_cast<size_t>(cs.dk % NHACC) * NTMAX * HID;
+  long long* part = reinterpret_cast<long long*>(sm.att);   // [NT][HID] this CTA's fixed-point partials
   if (ok) {
     for (int r = cs.tid; r < HID; r += NCT) {
       const int box = r / WD_BOX_ROWS;
@@ -1096,7 +1138,7 @@ __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
         }
         long long q = float_to_fix(a0 + a1);
         if (r >= d0 && r < d1) q += float_to_fix(__ldcg(p.w.hmid + t * HID + r));
-        atomicAdd(reinterpret_cast<unsigned long long*>(acc + t * HID + r), static_cast<unsigned long long>(q));
+        part[t * HID + r] = q;
       }
     }
   }
@@ -1108,6 +1150,15 @@ __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
           static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
       mbar_arrive(&sm.empty[sl[i]]);
     }
+  }
+  // one TMA bulk reduction adds the CTA's whole partial vector into the layer output
+  fence_proxy_async_smem();
+  named_sync(1, NCT);
+  if (cs.tid == 0 && ok) {
+    fence_proxy_async_global();   // the zeroing of acc (generic stores, earlier stages) first
+    bulk_reduce_add_u64(acc, part, static_cast<uint32_t>(NT * HID * sizeof(long long)));
+    bulk_commit_and_wait_all();
+    fence_proxy_async_global();
   }
   long long* nxt = p.w.hacc + static_cast<size_t>((cs.dk + 1) % NHACC) * NTMAX * HID;
   for (int e = cs.tid; e < NTMAX * (d1 - d0); e += NCT) {
@@ -1230,8 +1281,8 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
 // order) + residual, RMSNorm into dst; this CTA's down_proj rows of o are also stored to hmid
 // for the down_proj residual.
 template <int NT>
-__device__ void load_rmsnorm_oh(Smem& sm, Cons& cs, const float* opart, const HIn& hin, const bf16* w, float eps,
-                                float* dst, float* hmid, int d0, int d1) {
+__device__ void load_rmsnorm_oh(const Params& p, Smem& sm, Cons& cs, const float* opart, const HIn& hin,
+                                const bf16* w, float eps, float* dst, float* hmid, int d0, int d1) {
   const bool act = cs.tid < HID / 4;
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
@@ -1271,7 +1322,12 @@ __device__ void load_rmsnorm_oh(Smem& sm, Cons& cs, const float* opart, const HI
     }
     ss[t] = a;
   }
+  if (p.dbg_marks != nullptr) {
+    asm volatile("" ::"d"(ss[0]));
+    prologue_mark(p, cs, 0);
+  }
   block_sum_d<NT>(sm, cs, ss);
+  prologue_mark(p, cs, 1);
   if (act) {
     const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
 #pragma unroll
@@ -1295,9 +1351,9 @@ template <int NT>
 __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const HIn& hin,
                          float* hout_f, HIn& hout, bool input_in_smem) {
   if (input_in_smem)
-    load_rmsnorm<NT, true>(sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm<NT, true>(p, sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
   else
-    load_rmsnorm_h<NT, false>(sm, cs, hin, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm_h<NT, false>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
@@ -1327,7 +1383,7 @@ __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
   // ---- o = sum of head partials + residual; RMSNorm, MLP
   {
     const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
-    load_rmsnorm_oh<NT>(sm, cs, p.w.prt, hin, lw->post_norm, p.eps, sm.xs, p.w.hmid, d0, d1);
+    load_rmsnorm_oh<NT>(p, sm, cs, p.w.prt, hin, lw->post_norm, p.eps, sm.xs, p.w.hmid, d0, d1);
   }
   return mlp_tail<NT, true>(p, sm, cs, lw, hout_f, hout);
 }
@@ -1351,7 +1407,7 @@ __device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0, HIn* last
     if (!ok) return false;
     h = hout;
   }
-  load_rmsnorm_h<NT, !CP>(sm, cs, h, CP ? p.cp_norm : p.bb_norm, p.eps, sm.xs);
+  load_rmsnorm_h<NT, !CP>(p, sm, cs, h, CP ? p.cp_norm : p.bb_norm, p.eps, sm.xs);
   if (last) *last = h;
   return true;
 }

@@ -46,8 +46,8 @@ constexpr int LP_STRIDE = 33;              // padded row of 32 lane partials
 // Fused gate/up + down stage: each CTA owns a block of intermediate columns (multiples of 8,
 // at most 24 with >= 128 CTAs) and streams the matching columns of W_down as four 2-D TMA
 // boxes of 256 rows x 24 columns; the down-projection partials of all CTAs are summed with
-// 64-bit integer atomics in fixed point (scale 2^32), which makes the sum independent of the
-// order of arrival.
+// TMA bulk reductions (cp.reduce.async.bulk .add.u64) of fixed-point values (scale 2^32),
+// which makes the sum independent of the order of arrival.
 constexpr int WD_BOX_COLS = 24;
 constexpr int WD_BOX_ROWS = 256;
 constexpr int WD_BOX_BYTES = WD_BOX_COLS * WD_BOX_ROWS * 2;   // 12 KB
