@@ -97,6 +97,8 @@ __device__ __forceinline__ void plan_add(Plan& pl, const bf16* base, int rows) {
   pl.nseg++;
 }
 
+// With lw == nullptr (consumer side) only the shape is computed: the segment pointers are null
+// and no layer table is read.
 __device__ Plan make_plan(int kind, const LayerW* lw, const bf16* head, int head_rows, int cta, int G) {
   Plan pl;
   pl.nseg = 0;
@@ -105,38 +107,38 @@ __device__ Plan make_plan(int kind, const LayerW* lw, const bf16* head, int head
   if (kind == SK_QKV) {
     pl.r0 = split_lo(QKV_ROWS, G, cta);
     pl.r1 = split_lo(QKV_ROWS, G, cta + 1);
-    const bf16* mats[3] = {lw->wq, lw->wk, lw->wv};
+    const bf16* mats[3] = {lw ? lw->wq : nullptr, lw ? lw->wk : nullptr, lw ? lw->wv : nullptr};
     const int lo[3] = {0, QSZ, QSZ + KVSZ};
     const int hi[3] = {QSZ, QSZ + KVSZ, QKV_ROWS};
 #pragma unroll
     for (int m = 0; m < 3; ++m) {
       const int a = max(pl.r0, lo[m]), b = min(pl.r1, hi[m]);
-      if (a < b) plan_add(pl, mats[m] + static_cast<size_t>(a - lo[m]) * HID, b - a);
+      if (a < b) plan_add(pl, mats[m] ? mats[m] + static_cast<size_t>(a - lo[m]) * HID : nullptr, b - a);
     }
   } else if (kind == SK_O) {
     pl.P = QSZ / UNIT;
     pl.r0 = split_lo(HID, G, cta);
     pl.r1 = split_lo(HID, G, cta + 1);
-    if (pl.r1 > pl.r0) plan_add(pl, lw->wo + static_cast<size_t>(pl.r0) * QSZ, pl.r1 - pl.r0);
+    if (pl.r1 > pl.r0) plan_add(pl, lw ? lw->wo + static_cast<size_t>(pl.r0) * QSZ : nullptr, pl.r1 - pl.r0);
   } else if (kind == SK_GU) {
     pl.r0 = split_lo(INTER, G, cta);
     pl.r1 = split_lo(INTER, G, cta + 1);
     if (pl.r1 > pl.r0) {
-      plan_add(pl, lw->wg + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
-      plan_add(pl, lw->wu + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
+      plan_add(pl, lw ? lw->wg + static_cast<size_t>(pl.r0) * HID : nullptr, pl.r1 - pl.r0);
+      plan_add(pl, lw ? lw->wu + static_cast<size_t>(pl.r0) * HID : nullptr, pl.r1 - pl.r0);
     }
   } else if (kind == SK_GUF) {   // fused MLP stage: intermediate columns in blocks of 8
     pl.r0 = 8 * split_lo(INTER / 8, G, cta);
     pl.r1 = 8 * split_lo(INTER / 8, G, cta + 1);
     if (pl.r1 > pl.r0) {
-      plan_add(pl, lw->wg + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
-      plan_add(pl, lw->wu + static_cast<size_t>(pl.r0) * HID, pl.r1 - pl.r0);
+      plan_add(pl, lw ? lw->wg + static_cast<size_t>(pl.r0) * HID : nullptr, pl.r1 - pl.r0);
+      plan_add(pl, lw ? lw->wu + static_cast<size_t>(pl.r0) * HID : nullptr, pl.r1 - pl.r0);
     }
   } else if (kind == SK_D) {
     pl.P = INTER / UNIT;
     pl.r0 = split_lo(HID, G, cta);
     pl.r1 = split_lo(HID, G, cta + 1);
-    if (pl.r1 > pl.r0) plan_add(pl, lw->wd + static_cast<size_t>(pl.r0) * INTER, pl.r1 - pl.r0);
+    if (pl.r1 > pl.r0) plan_add(pl, lw ? lw->wd + static_cast<size_t>(pl.r0) * INTER : nullptr, pl.r1 - pl.r0);
   } else {  // SK_HEAD
     pl.r0 = split_lo(head_rows, G, cta);
     pl.r1 = split_lo(head_rows, G, cta + 1);
@@ -1032,7 +1034,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   else
     load_rmsnorm_h<NT, !CP>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
-    const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nr = pl.r1 - pl.r0;
     for (int e = cs.tid; e < NT * nr; e += NCT) {
@@ -1048,7 +1050,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
 
   // ---- o_proj + residual (the residual rows are fetched with the attention output)
   {
-    const Plan pl = make_plan(SK_O, lw, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_O, nullptr, nullptr, 0, cs.cta, cs.G);
     const int nr = pl.r1 - pl.r0;
     float res = 0.f;
     if (cs.tid < NT * nr) res = h_ld<!CP>(hin, (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
@@ -1077,7 +1079,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
 // hacc[(dk + 1) % 3], the buffer of the next fused stage (last read two stages before).
 template <int NT>
 __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, long long*& out) {
-  const Plan pl = make_plan(SK_GUF, lw, nullptr, 0, cs.cta, cs.G);
+  const Plan pl = make_plan(SK_GUF, nullptr, nullptr, 0, cs.cta, cs.G);
   if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
   const int nj = pl.r1 - pl.r0;
   float* mv = sm.xs + NTMAX * HID;   // [NT][WD_BOX_COLS], zero beyond this CTA's columns
@@ -1182,7 +1184,7 @@ __device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
     return grid_sync(p, sm, cs);
   }
   {
-    const Plan pl = make_plan(SK_GU, lw, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_GU, nullptr, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nj = pl.r1 - pl.r0;
     for (int e = cs.tid; e < NT * nj; e += NCT) {
@@ -1195,7 +1197,7 @@ __device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
 
   // ---- down_proj + residual
   {
-    const Plan pl = make_plan(SK_D, lw, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_D, nullptr, nullptr, 0, cs.cta, cs.G);
     const int nr = pl.r1 - pl.r0;
     float res = 0.f;
     if (cs.tid < NT * nr) res = __ldcg(p.w.hmid + (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
@@ -1355,7 +1357,7 @@ __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
   else
     load_rmsnorm_h<NT, false>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
-    const Plan pl = make_plan(SK_QKV, lw, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta, cs.G);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nr = pl.r1 - pl.r0;
     for (int e = cs.tid; e < NT * nr; e += NCT) {

@@ -36,7 +36,7 @@ constexpr int NCT = NCW * 32;              // consumer threads
 constexpr int NTHREADS = NCT + 32;         // + one producer warp
 constexpr int NTMAX = 2;                   // tokens per pass (2 = code-predictor prefill pair)
 constexpr int MAXPART = 256;               // partial-sum units per stage per CTA
-constexpr int ATT_TARGET = 48;             // attention positions per work item (target)
+constexpr int ATT_TARGET = 24;             // attention positions per work item (target)
 constexpr int ATT_STAGE_BYTES = 24576;     // shared staging of one K+V sub-chunk
 constexpr int ATT_CHMAX = 256;             // attention positions per work item (max)
 constexpr int MAX_ATT_CHUNKS = 32;         // attention work items per KV head (max)
