@@ -182,7 +182,7 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 // 1 / sqrt(mean_sq + eps) rounded once to fp32 (IEEE double sqrt and division), so the
 // scale applied to a whole vector carries no systematic fp32 error.
 __device__ __forceinline__ float rms_scale(double sum_sq, int n, float eps) {
-  return static_cast<float>(1.0 / sqrt(sum_sq / static_cast<double>(n) + static_cast<double>(eps)));
+  return static_cast<float>(rsqrt(sum_sq / static_cast<double>(n) + static_cast<double>(eps)));
 }
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

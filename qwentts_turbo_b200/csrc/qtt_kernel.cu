@@ -523,11 +523,14 @@ __device__ __forceinline__ void block_sum(Smem& sm, Cons& cs, float (&v)[NT]) {
 // CTAs, or from shared memory) are normalised into dst = x * rsqrt(mean(x^2) + eps) * w.
 // The activation and the norm weights are loaded in the same round trip; thread t < 256 owns
 // elements 4t .. 4t+3 of every token.
-template <int NT>
+// DEFER: dst = x * w only, and each warp's sum of squares goes to sm.dred; the GEMV that
+// reads dst applies 1 / rms to its dot products (gemv<NT, true>), which takes the norm's
+// block reduction off the path to the GEMV.
+template <int NT, bool DEFER>
 __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps,
                                float* dst);
 
-template <int NT, bool FROM_SMEM>
+template <int NT, bool FROM_SMEM, bool DEFER = false>
 __device__ void load_rmsnorm(const Params& p, Smem& sm, Cons& cs, const float* src, const bf16* w, float eps,
                              float* dst) {
   const bool act = cs.tid < HID / 4;
@@ -541,11 +544,11 @@ __device__ void load_rmsnorm(const Params& p, Smem& sm, Cons& cs, const float* s
       x[t] = FROM_SMEM ? *s4 : __ldcg(s4);
     }
   }
-  rmsnorm_finish<NT>(p, sm, cs, x, wv, eps, dst);
+  rmsnorm_finish<NT, DEFER>(p, sm, cs, x, wv, eps, dst);
 }
 
 // Same, from a layer input in global memory (fp32 or fixed point).
-template <int NT, bool BB>
+template <int NT, bool BB, bool DEFER = false>
 __device__ void load_rmsnorm_h(const Params& p, Smem& sm, Cons& cs, const HIn& h, const bf16* w, float eps,
                                float* dst) {
   float4 x[NT];
@@ -555,13 +558,34 @@ __device__ void load_rmsnorm_h(const Params& p, Smem& sm, Cons& cs, const HIn& h
 #pragma unroll
     for (int t = 0; t < NT; ++t) x[t] = h_ld4<BB>(h, t * HID + 4 * cs.tid);
   }
-  rmsnorm_finish<NT>(p, sm, cs, x, wv, eps, dst);
+  rmsnorm_finish<NT, DEFER>(p, sm, cs, x, wv, eps, dst);
 }
 
-template <int NT>
+template <int NT, bool DEFER>
 __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps,
                                float* dst) {
   const bool act = cs.tid < HID / 4;
+  if (DEFER) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      double a = 0.0;
+      if (act) {
+        a = fma(static_cast<double>(x[t].x), static_cast<double>(x[t].x), a);
+        a = fma(static_cast<double>(x[t].y), static_cast<double>(x[t].y), a);
+        a = fma(static_cast<double>(x[t].z), static_cast<double>(x[t].z), a);
+        a = fma(static_cast<double>(x[t].w), static_cast<double>(x[t].w), a);
+        const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
+        reinterpret_cast<float4*>(dst + t * HID)[cs.tid] =
+            make_float4(x[t].x * w0, x[t].y * w1, x[t].z * w2, x[t].w * w3);
+      }
+      a = warp_sum_d(a);
+      if (cs.lane == 0) sm.dred[t * NCW + cs.warp] = a;
+    }
+    prologue_mark(p, cs, 0);
+    named_sync(1, NCT);
+    prologue_mark(p, cs, 3);
+    return;
+  }
   double ss[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
@@ -605,7 +629,9 @@ __device__ __forceinline__ void load_vec(Cons& cs, float* dst, const float* src,
 }
 
 // GEMV over this CTA's units of one stage: part[u * NT + t] = dot(unit u, x part of u).
-template <int NT>
+// NORM: the input was prepared by a deferred RMSNorm (x * w, sums of squares per warp in
+// sm.dred); the dot products are multiplied by 1 / rms of their token.
+template <int NT, bool NORM = false>
 __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const float* xsrc, int xstride) {
   stage_mark(p, cs, 0);
   if (pl.units > MAXUNITS) {
@@ -624,6 +650,18 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
       const float4 b = *reinterpret_cast<const float4*>(xp + 256 * i + 4);
       xr[t][8 * i + 0] = a.x; xr[t][8 * i + 1] = a.y; xr[t][8 * i + 2] = a.z; xr[t][8 * i + 3] = a.w;
       xr[t][8 * i + 4] = b.x; xr[t][8 * i + 5] = b.y; xr[t][8 * i + 6] = b.z; xr[t][8 * i + 7] = b.w;
+    }
+  }
+  // 1 / rms of each token (deferred norm); computed here so that its latency overlaps the loop
+  float rs[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    rs[t] = 1.f;
+    if (NORM) {
+      double a = 0.0;
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) a += sm.dred[t * NCW + w];
+      rs[t] = rms_scale(a, HID, p.eps);
     }
   }
   const bool prof = p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0;
@@ -688,7 +726,8 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
     for (int k = 0; k < 8; ++k) a[k] += a[k + 8];
 #pragma unroll
     for (int k = 0; k < 4; ++k) a[k] += a[k + 4];
-    sm.part[e] = (a[0] + a[2]) + (a[1] + a[3]);
+    const float v = (a[0] + a[2]) + (a[1] + a[3]);
+    sm.part[e] = NORM ? v * ((NT == 1 || (e & 1) == 0) ? rs[0] : rs[NT - 1]) : v;
   }
   named_sync(1, NCT);
   stage_mark(p, cs, 1);
@@ -1030,12 +1069,12 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
                       float* hout_f, HIn& hout, bool input_in_smem) {
   // ---- input RMSNorm + QKV
   if (input_in_smem)
-    load_rmsnorm<NT, true>(p, sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm<NT, true, true>(p, sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
   else
-    load_rmsnorm_h<NT, !CP>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm_h<NT, !CP, true>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta, cs.G);
-    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+    if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nr = pl.r1 - pl.r0;
     for (int e = cs.tid; e < NT * nr; e += NCT) {
       const int t = e / nr, r = e - t * nr;
@@ -1065,7 +1104,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   if (!grid_sync(p, sm, cs)) return false;
 
   // ---- post-attention RMSNorm, MLP
-  load_rmsnorm<NT, false>(p, sm, cs, p.w.hmid, lw->post_norm, p.eps, sm.xs);
+  load_rmsnorm<NT, false, true>(p, sm, cs, p.w.hmid, lw->post_norm, p.eps, sm.xs);
   return mlp_tail<NT, CP>(p, sm, cs, lw, hout_f, hout);
 }
 
@@ -1080,7 +1119,7 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
 template <int NT>
 __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, long long*& out) {
   const Plan pl = make_plan(SK_GUF, nullptr, nullptr, 0, cs.cta, cs.G);
-  if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+  if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
   const int nj = pl.r1 - pl.r0;
   float* mv = sm.xs + NTMAX * HID;   // [NT][WD_BOX_COLS], zero beyond this CTA's columns
   if (cs.tid < NT * WD_BOX_COLS) {
@@ -1172,7 +1211,8 @@ __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
   return !aborted(sm);
 }
 
-// MLP half of a layer after its post-attention RMSNorm (in sm.xs): the fused stage when the
+// MLP half of a layer after its deferred post-attention RMSNorm (x * w in sm.xs, sums of squares
+// in sm.dred): the fused stage when the
 // stack has W_down tensor maps, else gate/up and down as two stages.
 template <int NT, bool CP>
 __device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, float* hout_f, HIn& hout) {
@@ -1185,7 +1225,7 @@ __device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
   }
   {
     const Plan pl = make_plan(SK_GU, nullptr, nullptr, 0, cs.cta, cs.G);
-    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+    if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nj = pl.r1 - pl.r0;
     for (int e = cs.tid; e < NT * nj; e += NCT) {
       const int t = e / nj, j = e - t * nj;
@@ -1282,14 +1322,12 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
 // Code-predictor post-attention prologue: o = (sum over the 8 heads' o_proj partials, in head
 // order) + residual, RMSNorm into dst; this CTA's down_proj rows of o are also stored to hmid
 // for the down_proj residual.
-template <int NT>
+template <int NT, bool DEFER>
 __device__ void load_rmsnorm_oh(const Params& p, Smem& sm, Cons& cs, const float* opart, const HIn& hin,
                                 const bf16* w, float eps, float* dst, float* hmid, int d0, int d1) {
-  const bool act = cs.tid < HID / 4;
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
-  double ss[NT];
-  if (act) {
+  if (cs.tid < HID / 4) {
     wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
@@ -1313,37 +1351,7 @@ __device__ void load_rmsnorm_oh(const Params& p, Smem& sm, Cons& cs, const float
       }
     }
   }
-#pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    double a = 0.0;
-    if (act) {
-      a = fma(static_cast<double>(x[t].x), static_cast<double>(x[t].x), a);
-      a = fma(static_cast<double>(x[t].y), static_cast<double>(x[t].y), a);
-      a = fma(static_cast<double>(x[t].z), static_cast<double>(x[t].z), a);
-      a = fma(static_cast<double>(x[t].w), static_cast<double>(x[t].w), a);
-    }
-    ss[t] = a;
-  }
-  if (p.dbg_marks != nullptr) {
-    asm volatile("" ::"d"(ss[0]));
-    prologue_mark(p, cs, 0);
-  }
-  block_sum_d<NT>(sm, cs, ss);
-  prologue_mark(p, cs, 1);
-  if (act) {
-    const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const float rstd = rms_scale(ss[t], HID, eps);
-      float4 o;
-      o.x = x[t].x * rstd * w0;
-      o.y = x[t].y * rstd * w1;
-      o.z = x[t].z * rstd * w2;
-      o.w = x[t].w * rstd * w3;
-      reinterpret_cast<float4*>(dst + t * HID)[cs.tid] = o;
-    }
-  }
-  named_sync(1, NCT);
+  rmsnorm_finish<NT, DEFER>(p, sm, cs, x, wv, eps, dst);
 }
 
 // One code-predictor layer in four grid-wide stages: QKV | attention + o_proj per KV-head group
@@ -1353,12 +1361,12 @@ template <int NT>
 __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0, const HIn& hin,
                          float* hout_f, HIn& hout, bool input_in_smem) {
   if (input_in_smem)
-    load_rmsnorm<NT, true>(p, sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm<NT, true, true>(p, sm, cs, sm.xs, lw->in_norm, p.eps, sm.xs);
   else
-    load_rmsnorm_h<NT, false>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
+    load_rmsnorm_h<NT, false, true>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
     const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta, cs.G);
-    if (!gemv<NT>(p, pl, sm, cs, sm.xs, HID)) return false;
+    if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nr = pl.r1 - pl.r0;
     for (int e = cs.tid; e < NT * nr; e += NCT) {
       const int t = e / nr, r = e - t * nr;
@@ -1385,7 +1393,7 @@ __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
   // ---- o = sum of head partials + residual; RMSNorm, MLP
   {
     const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
-    load_rmsnorm_oh<NT>(p, sm, cs, p.w.prt, hin, lw->post_norm, p.eps, sm.xs, p.w.hmid, d0, d1);
+    load_rmsnorm_oh<NT, true>(p, sm, cs, p.w.prt, hin, lw->post_norm, p.eps, sm.xs, p.w.hmid, d0, d1);
   }
   return mlp_tail<NT, true>(p, sm, cs, lw, hout_f, hout);
 }
