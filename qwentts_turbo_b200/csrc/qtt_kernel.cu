@@ -40,6 +40,10 @@ struct __align__(128) Smem {
   int epoch;                         // grid barriers completed by this CTA (producer pacing)
   int free_epoch[NSLOTS];            // epoch during which the consumers freed each slot
   int bcast[4];
+  // batched kernel only
+  uint64_t bbar[32];                 // pipeline mbarriers
+  uint32_t tmem_base;                // tensor-memory address of the accumulator
+  int bstate[4 * BMAX];              // per utterance: position, step, g0, active
 };
 
 size_t work_bytes() {
@@ -565,7 +569,7 @@ template <int NT, bool DEFER>
 __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps,
                                float* dst) {
   const bool act = cs.tid < HID / 4;
-  if (DEFER) {
+  if constexpr (DEFER) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       double a = 0.0;
@@ -584,42 +588,42 @@ __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4
     prologue_mark(p, cs, 0);
     named_sync(1, NCT);
     prologue_mark(p, cs, 3);
-    return;
-  }
-  double ss[NT];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    double a = 0.0;
-    if (act) {
-      a = fma(static_cast<double>(x[t].x), static_cast<double>(x[t].x), a);
-      a = fma(static_cast<double>(x[t].y), static_cast<double>(x[t].y), a);
-      a = fma(static_cast<double>(x[t].z), static_cast<double>(x[t].z), a);
-      a = fma(static_cast<double>(x[t].w), static_cast<double>(x[t].w), a);
-    }
-    ss[t] = a;
-  }
-  if (p.dbg_marks != nullptr) {
-    asm volatile("" ::"d"(ss[0]));
-    prologue_mark(p, cs, 0);
-  }
-  block_sum_d<NT>(sm, cs, ss);
-  prologue_mark(p, cs, 1);
-  if (act) {
-    const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
+  } else {
+    double ss[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      const float rstd = rms_scale(ss[t], HID, eps);
-      float4 o;
-      o.x = x[t].x * rstd * w0;
-      o.y = x[t].y * rstd * w1;
-      o.z = x[t].z * rstd * w2;
-      o.w = x[t].w * rstd * w3;
-      reinterpret_cast<float4*>(dst + t * HID)[cs.tid] = o;
+      double a = 0.0;
+      if (act) {
+        a = fma(static_cast<double>(x[t].x), static_cast<double>(x[t].x), a);
+        a = fma(static_cast<double>(x[t].y), static_cast<double>(x[t].y), a);
+        a = fma(static_cast<double>(x[t].z), static_cast<double>(x[t].z), a);
+        a = fma(static_cast<double>(x[t].w), static_cast<double>(x[t].w), a);
+      }
+      ss[t] = a;
     }
+    if (p.dbg_marks != nullptr) {
+      asm volatile("" ::"d"(ss[0]));
+      prologue_mark(p, cs, 0);
+    }
+    block_sum_d<NT>(sm, cs, ss);
+    prologue_mark(p, cs, 1);
+    if (act) {
+      const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const float rstd = rms_scale(ss[t], HID, eps);
+        float4 o;
+        o.x = x[t].x * rstd * w0;
+        o.y = x[t].y * rstd * w1;
+        o.z = x[t].z * rstd * w2;
+        o.w = x[t].w * rstd * w3;
+        reinterpret_cast<float4*>(dst + t * HID)[cs.tid] = o;
+      }
+    }
+    prologue_mark(p, cs, 2);
+    named_sync(1, NCT);
+    prologue_mark(p, cs, 3);
   }
-  prologue_mark(p, cs, 2);
-  named_sync(1, NCT);
-  prologue_mark(p, cs, 3);
 }
 
 // Copy NT vectors of n floats from global (L2, written by other CTAs) into shared memory.
@@ -763,6 +767,305 @@ __device__ __forceinline__ void stage_kv_rows(Cons& cs, uint8_t* dst_k, uint8_t*
   }
 }
 
+// One attention work item's inputs and outputs: NT consecutive tokens of one utterance at
+// positions p0 .. p0 + NT - 1, one KV head, context positions [s0, s1).
+struct AttIO {
+  const float* qkv;   // raw q/k/v rows of the item's first token (row stride QKV_ROWS)
+  uint8_t* kb;        // the utterance's cached K rows of this (layer, KV head): row s at kb + s * HD * esize
+  uint8_t* vb;        // same for V; rows p0 .. p0 + NT - 1 are written by the item's writer
+  float* out;         // fp32 output rows of the item's first token (row stride QSZ), or nullptr:
+  bf16* hilo;         //   then bf16 hi/lo GEMM operand planes (batched decode), token row tok0 + t
+  int tok0;
+  float* prt;         // partial records of the item's first token [NT][NQH][MAX_ATT_CHUNKS][PRT_STRIDE]
+  uint32_t* cnt;      // last-arriver counter of (utterance, KV head)
+};
+
+// v = hi + lo with hi = bf16(v), lo = bf16(v - hi): two bf16 GEMM operands that carry ~16
+// mantissa bits, so the tensor-core product stays close to an fp32 GEMV. Plane 0 (rows
+// 0..TBMAX-1) holds the hi parts, plane 1 the lo parts; row = token.
+__device__ __forceinline__ void hilo_store(bf16* buf, int t, int col, float v) {
+  const bf16 hi = __float2bfloat16_rn(v);
+  const bf16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+  buf[static_cast<size_t>(t) * ABUF_LD + col] = hi;
+  buf[static_cast<size_t>(TBMAX + t) * ABUF_LD + col] = lo;
+}
+
+__device__ __forceinline__ void att_store(const AttIO& io, int t, int col, float v) {
+  if (io.out != nullptr)
+    io.out[t * QSZ + col] = v;
+  else
+    hilo_store(io.hilo, io.tok0 + t, col, v);
+}
+
+// One work item: stage q/k/v and the cached rows, q/k RMSNorm + RoPE, write the new K/V rows
+// (writer), scores / softmax / P.V over [s0, s1) in sub-chunks with an online softmax, then
+// either the final output (single item per head) or a partial record, the last item of the head
+// combining all partials (flash-decoding style). GROUP: output stays in sm.xs.
+template <int NT, bool CP, bool GROUP>
+__device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, const AttIO& io, int p0, int h, int c,
+                         int nch, int s0, int s1, bool writer) {
+  constexpr int ESZ = CP ? 4 : 2;
+  constexpr int ROWB = HD * ESZ;
+  constexpr int SUB = ATT_STAGE_BYTES / (2 * ROWB);   // 48 bf16 rows or 24 fp32 rows
+  constexpr int J = NT * 2;   // (token, q head) pairs
+  // shared scratch inside xs
+  float* qraw = sm.xs;                  // [NT][4][HD] raw q(2h), q(2h+1), k, v
+  float* qr = qraw + NT * 4 * HD;       // [NT][2][HD]
+  float* kn = qr + NT * 2 * HD;         // [NT][HD]
+  float* vn = kn + NT * HD;             // [NT][HD]
+  float* sc = vn + NT * HD;             // [J][SUB]
+  float* acc_s = sc + J * SUB;          // [J][HD] running P.V
+  float* accg = acc_s + J * HD;         // [3][J][HD]
+  float* ml = accg + 3 * J * HD;        // [J][4]: running max, running sum, rescale of this step
+  uint8_t* kst = sm.att;
+  uint8_t* vst = sm.att + SUB * ROWB;
+
+  // 1. one round trip: raw q/k/v rows of this head + the first sub-chunk of cached rows
+  for (int e = cs.tid; e < NT * 4 * (HD / 4); e += NCT) {
+    const int t = e / (4 * HD / 4), r = e - t * (4 * HD / 4), vec = r / (HD / 4), piece = r - vec * (HD / 4);
+    const int row0 = vec < 2 ? (2 * h + vec) * HD : (vec == 2 ? QSZ + h * HD : QSZ + KVSZ + h * HD);
+    cp_async16(qraw + (t * 4 + vec) * HD + piece * 4, io.qkv + t * QKV_ROWS + row0 + piece * 4);
+  }
+  {
+    const int a1 = min(min(s1, p0), s0 + SUB);
+    if (a1 > s0) stage_kv_rows<CP>(cs, kst, vst, io.kb, io.vb, s0, a1);
+  }
+  for (int j = cs.tid; j < J * HD; j += NCT) acc_s[j] = 0.f;
+  if (cs.tid < J) {
+    ml[cs.tid * 4 + 0] = -INFINITY;
+    ml[cs.tid * 4 + 1] = 0.f;
+  }
+  // norm weights and RoPE rows travel with the staged rows (same round trip)
+  float nwv[4], cv[4], sv[4];
+  if (cs.warp < NT * 4 && (cs.warp & 3) < 3) {
+    const int pos = p0 + (cs.warp >> 2);
+    const bf16* nw = (cs.warp & 3) < 2 ? L->q_norm : L->k_norm;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int d = cs.lane + 32 * i;
+      nwv[i] = __bfloat162float(nw[d]);
+      cv[i] = __bfloat162float(p.cos_tab[static_cast<size_t>(pos) * HD + d]);
+      sv[i] = __bfloat162float(p.sin_tab[static_cast<size_t>(pos) * HD + d]);
+    }
+  }
+  cp_async_wait_all();
+  named_sync(1, NCT);
+
+  // 2. q/k RMSNorm per head (fused_decode_tts.cu:183-197) + RoPE; warp j handles vector j%4
+  //    of token j/4 with d = lane + 32 i, so each rotation pair (d, d+64) sits in one lane.
+  if (cs.warp < NT * 4) {
+    const int t = cs.warp >> 2, vec = cs.warp & 3;
+    const float* src = qraw + (t * 4 + vec) * HD;
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = src[cs.lane + 32 * i];
+    if (vec < 3) {
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ss = fma(static_cast<double>(x[i]), static_cast<double>(x[i]), ss);
+      ss = warp_sum_d(ss);
+      const float rstd = rms_scale(ss, HD, p.eps);
+      float y[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = x[i] * rstd * nwv[i];
+      float o[4];
+      o[0] = y[0] * cv[0] - y[2] * sv[0];
+      o[1] = y[1] * cv[1] - y[3] * sv[1];
+      o[2] = y[2] * cv[2] + y[0] * sv[2];
+      o[3] = y[3] * cv[3] + y[1] * sv[3];
+      float* dst = vec < 2 ? qr + (t * 2 + vec) * HD : kn + t * HD;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[cs.lane + 32 * i] = (vec == 2 && !CP) ? round_bf16(o[i]) : o[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) vn[t * HD + cs.lane + 32 * i] = CP ? x[i] : round_bf16(x[i]);
+    }
+  }
+  named_sync(1, NCT);
+
+  // 3. item 0 of each head stores the new K/V rows into the cache.
+  if (writer) {
+    for (int e = cs.tid; e < NT * HD; e += NCT) {
+      const int t = e / HD, d = e - t * HD;
+      const size_t off = static_cast<size_t>(p0 + t) * HD + d;
+      if (CP) {
+        reinterpret_cast<float*>(io.kb)[off] = kn[e];
+        reinterpret_cast<float*>(io.vb)[off] = vn[e];
+      } else {
+        reinterpret_cast<bf16*>(io.kb)[off] = __float2bfloat16_rn(kn[e]);
+        reinterpret_cast<bf16*>(io.vb)[off] = __float2bfloat16_rn(vn[e]);
+      }
+    }
+  }
+
+  // 4. sub-chunks of at most SUB positions (one for every chunk up to SUB long)
+  for (int sa = s0; sa < s1; sa += SUB) {
+    const int sb = min(s1, sa + SUB), len = sb - sa;
+    if (sa != s0) {
+      const int a1 = min(sb, p0);
+      if (a1 > sa) stage_kv_rows<CP>(cs, kst, vst, io.kb, io.vb, sa, a1);
+      cp_async_wait_all();
+      named_sync(1, NCT);
+    }
+    // scores: one warp per position, lane holds d = 4 lane .. 4 lane + 3
+    for (int s = sa + cs.warp; s < sb; s += NCW) {
+      float k4[4];
+      if (s < p0) {
+        const uint8_t* row = kst + static_cast<size_t>(s - sa) * ROWB;
+        if (CP) {
+          const float4 kk = *reinterpret_cast<const float4*>(row + 16 * cs.lane);
+          k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+        } else {
+          const uint2 kk = *reinterpret_cast<const uint2*>(row + 8 * cs.lane);
+          k4[0] = bf16_lo(kk.x); k4[1] = bf16_hi(kk.x); k4[2] = bf16_lo(kk.y); k4[3] = bf16_hi(kk.y);
+        }
+      } else {
+        const float4 kk = *reinterpret_cast<const float4*>(kn + (s - p0) * HD + 4 * cs.lane);
+        k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+      }
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const float4 q = *reinterpret_cast<const float4*>(qr + j * HD + 4 * cs.lane);
+        float d = q.x * k4[0];
+        d = fmaf(q.y, k4[1], d);
+        d = fmaf(q.z, k4[2], d);
+        d = fmaf(q.w, k4[3], d);
+        d = warp_sum(d) * p.attn_scale;
+        if (cs.lane == 0) sc[j * SUB + (s - sa)] = (s <= p0 + (j >> 1)) ? d : -INFINITY;
+      }
+    }
+    named_sync(1, NCT);
+    // online softmax statistics: warp j handles (token, q head) j
+    if (cs.warp < J) {
+      float* row = sc + cs.warp * SUB;
+      float m = -INFINITY;
+      for (int i = cs.lane; i < len; i += 32) m = fmaxf(m, row[i]);
+      m = warp_max(m);
+      const float m_old = ml[cs.warp * 4 + 0];
+      const float m_new = fmaxf(m_old, m);
+      float l = 0.f;
+      for (int i = cs.lane; i < len; i += 32) {
+        const float e = (m_new == -INFINITY) ? 0.f : expf(row[i] - m_new);
+        row[i] = e;
+        l += e;
+      }
+      l = warp_sum(l);
+      if (cs.lane == 0) {
+        const float rescale = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+        ml[cs.warp * 4 + 0] = m_new;
+        ml[cs.warp * 4 + 1] = ml[cs.warp * 4 + 1] * rescale + l;
+        ml[cs.warp * 4 + 2] = rescale;
+      }
+    }
+    named_sync(1, NCT);
+    // P.V: thread -> (d, position residue g mod 3)
+    {
+      const int d = cs.tid & (HD - 1), g = cs.tid >> 7;
+      float acc[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) acc[j] = 0.f;
+      for (int s = sa + g; s < sb; s += 3) {
+        float v;
+        if (s < p0) {
+          const uint8_t* row = vst + static_cast<size_t>(s - sa) * ROWB;
+          v = CP ? reinterpret_cast<const float*>(row)[d]
+                 : __bfloat162float(reinterpret_cast<const bf16*>(row)[d]);
+        } else {
+          v = vn[(s - p0) * HD + d];
+        }
+#pragma unroll
+        for (int j = 0; j < J; ++j) acc[j] = fmaf(sc[j * SUB + (s - sa)], v, acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < J; ++j) accg[(g * J + j) * HD + d] = acc[j];
+    }
+    named_sync(1, NCT);
+    for (int e = cs.tid; e < J * HD; e += NCT) {
+      const int j = e / HD, d = e - j * HD;
+      const float a = (accg[(0 * J + j) * HD + d] + accg[(1 * J + j) * HD + d]) + accg[(2 * J + j) * HD + d];
+      acc_s[e] = acc_s[e] * ml[j * 4 + 2] + a;
+    }
+    named_sync(1, NCT);
+  }
+
+
+  // 5. publish (or finish directly when the head has a single item).
+  if (GROUP) {   // head output stays in shared memory: xs[t][hh * HD + d]
+    for (int e = cs.tid; e < J * HD; e += NCT) {
+      const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
+      sm.xs[t * 2 * HD + hh * HD + d] = acc_s[e] / ml[j * 4 + 1];
+    }
+    named_sync(1, NCT);
+    return true;
+  }
+  if (nch == 1) {
+    for (int e = cs.tid; e < J * HD; e += NCT) {
+      const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
+      att_store(io, t, (2 * h + hh) * HD + d, acc_s[e] / ml[j * 4 + 1]);
+    }
+    named_sync(1, NCT);
+    return true;
+  }
+  for (int e = cs.tid; e < J * PRT_STRIDE; e += NCT) {
+    const int j = e / PRT_STRIDE, k = e - j * PRT_STRIDE, t = j >> 1, hh = j & 1;
+    const float val = k < 2 ? ml[j * 4 + k] : (k < 4 ? 0.f : acc_s[j * HD + (k - 4)]);
+    io.prt[((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + c) * PRT_STRIDE + k] = val;
+  }
+  named_sync(1, NCT);
+  if (cs.tid == 0) {
+    __threadfence();
+    const uint32_t old = atomicAdd(io.cnt, 1u);
+    sm.bcast[0] = (old == static_cast<uint32_t>(nch - 1)) ? 1 : 0;
+    __threadfence();
+  }
+  named_sync(1, NCT);
+  if (sm.bcast[0]) {
+    // combine the nch partials of KV head h in chunk order, staged with one round trip
+    const bool staged = J * nch * PRT_STRIDE * 4 <= ATT_STAGE_BYTES;
+    float* recs = reinterpret_cast<float*>(sm.att);   // [J][nch][PRT_STRIDE]
+    if (staged) {
+      const int pieces = nch * PRT_STRIDE / 4;
+      for (int e = cs.tid; e < J * pieces; e += NCT) {
+        const int j = e / pieces, r = e - j * pieces, t = j >> 1, hh = j & 1;
+        cp_async16(recs + (j * nch) * PRT_STRIDE + r * 4,
+                   io.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE + r * 4);
+      }
+      cp_async_wait_all();
+      named_sync(1, NCT);
+    }
+    for (int e = cs.tid; e < J * HD; e += NCT) {
+      const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
+      float M = -INFINITY, Ls = 0.f, O = 0.f;
+      if (staged) {
+        const float* rec = recs + (j * nch) * PRT_STRIDE;
+        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, rec[cc * PRT_STRIDE]);
+        for (int cc = 0; cc < nch; ++cc) {
+          const float mc = rec[cc * PRT_STRIDE];
+          if (mc == -INFINITY) continue;
+          const float wgt = expf(mc - M);
+          Ls = fmaf(wgt, rec[cc * PRT_STRIDE + 1], Ls);
+          O = fmaf(wgt, rec[cc * PRT_STRIDE + 4 + d], O);
+        }
+      } else {
+        const float* rec = io.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE;
+        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(rec + cc * PRT_STRIDE));
+        for (int cc = 0; cc < nch; ++cc) {
+          const float mc = __ldcg(rec + cc * PRT_STRIDE);
+          if (mc == -INFINITY) continue;
+          const float wgt = expf(mc - M);
+          Ls = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 1), Ls);
+          O = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 4 + d), O);
+        }
+      }
+      att_store(io, t, (2 * h + hh) * HD + d, O / Ls);
+    }
+    if (cs.tid == 0) atomicExch(io.cnt, 0u);
+  }
+  named_sync(1, NCT);
+return true;
+}
+
+
 // GROUP (code predictor): the CTAs are split into 8 groups of G/8, one per KV head; every CTA
 // of a group computes that head's whole attention (the context is at most 17 positions) and
 // leaves the result in sm.xs[t][2][HD] for the head's o_proj columns; the first CTA of the
@@ -780,25 +1083,8 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     return false;
   }
   constexpr int ESZ = CP ? 4 : 2;
-  constexpr int ROWB = HD * ESZ;
-  constexpr int SUB = ATT_STAGE_BYTES / (2 * ROWB);   // 48 bf16 rows or 24 fp32 rows
   const int max_seq = CP ? p.cp_max_seq : p.bb_max_seq;
   const size_t layer_off = static_cast<size_t>(li) * NKVH * max_seq * HD;
-  const LayerW* L = lw;
-  constexpr int J = NT * 2;   // (token, q head) pairs
-
-  // shared scratch inside xs
-  float* qraw = sm.xs;                  // [NT][4][HD] raw q(2h), q(2h+1), k, v
-  float* qr = qraw + NT * 4 * HD;       // [NT][2][HD]
-  float* kn = qr + NT * 2 * HD;         // [NT][HD]
-  float* vn = kn + NT * HD;             // [NT][HD]
-  float* sc = vn + NT * HD;             // [J][SUB]
-  float* acc_s = sc + J * SUB;          // [J][HD] running P.V
-  float* accg = acc_s + J * HD;         // [3][J][HD]
-  float* ml = accg + 3 * J * HD;        // [J][4]: running max, running sum, rescale of this step
-  uint8_t* kst = sm.att;
-  uint8_t* vst = sm.att + SUB * ROWB;
-
   const int gph = cs.G / NKVH;
   const int n_items = GROUP ? (cs.cta < NKVH * gph ? 1 : 0) : NKVH * nch;
   for (int item = GROUP ? 0 : cs.cta; item < n_items; item += GROUP ? 1 : cs.G) {
@@ -806,252 +1092,18 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     const int c = GROUP ? 0 : item - h * nch;
     const bool writer = GROUP ? (cs.cta % gph == 0) : (c == 0);
     const int s0 = c * chunk, s1 = min(S, s0 + chunk);
-    const uint8_t* kb = reinterpret_cast<const uint8_t*>(CP ? static_cast<const void*>(p.cp_k) : p.bb_k) +
-                        (layer_off + static_cast<size_t>(h) * max_seq * HD) * ESZ;
-    const uint8_t* vb = reinterpret_cast<const uint8_t*>(CP ? static_cast<const void*>(p.cp_v) : p.bb_v) +
-                        (layer_off + static_cast<size_t>(h) * max_seq * HD) * ESZ;
-
-    // 1. one round trip: raw q/k/v rows of this head + the first sub-chunk of cached rows
-    for (int e = cs.tid; e < NT * 4 * (HD / 4); e += NCT) {
-      const int t = e / (4 * HD / 4), r = e - t * (4 * HD / 4), vec = r / (HD / 4), piece = r - vec * (HD / 4);
-      const int row0 = vec < 2 ? (2 * h + vec) * HD : (vec == 2 ? QSZ + h * HD : QSZ + KVSZ + h * HD);
-      cp_async16(qraw + (t * 4 + vec) * HD + piece * 4, p.w.qkv + t * QKV_ROWS + row0 + piece * 4);
-    }
-    {
-      const int a1 = min(min(s1, p0), s0 + SUB);
-      if (a1 > s0) stage_kv_rows<CP>(cs, kst, vst, kb, vb, s0, a1);
-    }
-    for (int j = cs.tid; j < J * HD; j += NCT) acc_s[j] = 0.f;
-    if (cs.tid < J) {
-      ml[cs.tid * 4 + 0] = -INFINITY;
-      ml[cs.tid * 4 + 1] = 0.f;
-    }
-    // norm weights and RoPE rows travel with the staged rows (same round trip)
-    float nwv[4], cv[4], sv[4];
-    if (cs.warp < NT * 4 && (cs.warp & 3) < 3) {
-      const int pos = p0 + (cs.warp >> 2);
-      const bf16* nw = (cs.warp & 3) < 2 ? L->q_norm : L->k_norm;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int d = cs.lane + 32 * i;
-        nwv[i] = __bfloat162float(nw[d]);
-        cv[i] = __bfloat162float(p.cos_tab[static_cast<size_t>(pos) * HD + d]);
-        sv[i] = __bfloat162float(p.sin_tab[static_cast<size_t>(pos) * HD + d]);
-      }
-    }
-    cp_async_wait_all();
-    named_sync(1, NCT);
-
-    // 2. q/k RMSNorm per head (fused_decode_tts.cu:183-197) + RoPE; warp j handles vector j%4
-    //    of token j/4 with d = lane + 32 i, so each rotation pair (d, d+64) sits in one lane.
-    if (cs.warp < NT * 4) {
-      const int t = cs.warp >> 2, vec = cs.warp & 3;
-      const float* src = qraw + (t * 4 + vec) * HD;
-      float x[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = src[cs.lane + 32 * i];
-      if (vec < 3) {
-        double ss = 0.0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ss = fma(static_cast<double>(x[i]), static_cast<double>(x[i]), ss);
-        ss = warp_sum_d(ss);
-        const float rstd = rms_scale(ss, HD, p.eps);
-        float y[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) y[i] = x[i] * rstd * nwv[i];
-        float o[4];
-        o[0] = y[0] * cv[0] - y[2] * sv[0];
-        o[1] = y[1] * cv[1] - y[3] * sv[1];
-        o[2] = y[2] * cv[2] + y[0] * sv[2];
-        o[3] = y[3] * cv[3] + y[1] * sv[3];
-        float* dst = vec < 2 ? qr + (t * 2 + vec) * HD : kn + t * HD;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[cs.lane + 32 * i] = (vec == 2 && !CP) ? round_bf16(o[i]) : o[i];
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) vn[t * HD + cs.lane + 32 * i] = CP ? x[i] : round_bf16(x[i]);
-      }
-    }
-    named_sync(1, NCT);
-
-    // 3. item 0 of each head stores the new K/V rows into the cache.
-    if (writer) {
-      for (int e = cs.tid; e < NT * HD; e += NCT) {
-        const int t = e / HD, d = e - t * HD;
-        const size_t off = layer_off + (static_cast<size_t>(h) * max_seq + p0 + t) * HD + d;
-        if (CP) {
-          p.cp_k[off] = kn[e];
-          p.cp_v[off] = vn[e];
-        } else {
-          p.bb_k[off] = __float2bfloat16_rn(kn[e]);
-          p.bb_v[off] = __float2bfloat16_rn(vn[e]);
-        }
-      }
-    }
-
-    // 4. sub-chunks of at most SUB positions (one for every chunk up to SUB long)
-    for (int sa = s0; sa < s1; sa += SUB) {
-      const int sb = min(s1, sa + SUB), len = sb - sa;
-      if (sa != s0) {
-        const int a1 = min(sb, p0);
-        if (a1 > sa) stage_kv_rows<CP>(cs, kst, vst, kb, vb, sa, a1);
-        cp_async_wait_all();
-        named_sync(1, NCT);
-      }
-      // scores: one warp per position, lane holds d = 4 lane .. 4 lane + 3
-      for (int s = sa + cs.warp; s < sb; s += NCW) {
-        float k4[4];
-        if (s < p0) {
-          const uint8_t* row = kst + static_cast<size_t>(s - sa) * ROWB;
-          if (CP) {
-            const float4 kk = *reinterpret_cast<const float4*>(row + 16 * cs.lane);
-            k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
-          } else {
-            const uint2 kk = *reinterpret_cast<const uint2*>(row + 8 * cs.lane);
-            k4[0] = bf16_lo(kk.x); k4[1] = bf16_hi(kk.x); k4[2] = bf16_lo(kk.y); k4[3] = bf16_hi(kk.y);
-          }
-        } else {
-          const float4 kk = *reinterpret_cast<const float4*>(kn + (s - p0) * HD + 4 * cs.lane);
-          k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
-        }
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-          const float4 q = *reinterpret_cast<const float4*>(qr + j * HD + 4 * cs.lane);
-          float d = q.x * k4[0];
-          d = fmaf(q.y, k4[1], d);
-          d = fmaf(q.z, k4[2], d);
-          d = fmaf(q.w, k4[3], d);
-          d = warp_sum(d) * p.attn_scale;
-          if (cs.lane == 0) sc[j * SUB + (s - sa)] = (s <= p0 + (j >> 1)) ? d : -INFINITY;
-        }
-      }
-      named_sync(1, NCT);
-      // online softmax statistics: warp j handles (token, q head) j
-      if (cs.warp < J) {
-        float* row = sc + cs.warp * SUB;
-        float m = -INFINITY;
-        for (int i = cs.lane; i < len; i += 32) m = fmaxf(m, row[i]);
-        m = warp_max(m);
-        const float m_old = ml[cs.warp * 4 + 0];
-        const float m_new = fmaxf(m_old, m);
-        float l = 0.f;
-        for (int i = cs.lane; i < len; i += 32) {
-          const float e = (m_new == -INFINITY) ? 0.f : expf(row[i] - m_new);
-          row[i] = e;
-          l += e;
-        }
-        l = warp_sum(l);
-        if (cs.lane == 0) {
-          const float rescale = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-          ml[cs.warp * 4 + 0] = m_new;
-          ml[cs.warp * 4 + 1] = ml[cs.warp * 4 + 1] * rescale + l;
-          ml[cs.warp * 4 + 2] = rescale;
-        }
-      }
-      named_sync(1, NCT);
-      // P.V: thread -> (d, position residue g mod 3)
-      {
-        const int d = cs.tid & (HD - 1), g = cs.tid >> 7;
-        float acc[J];
-#pragma unroll
-        for (int j = 0; j < J; ++j) acc[j] = 0.f;
-        for (int s = sa + g; s < sb; s += 3) {
-          float v;
-          if (s < p0) {
-            const uint8_t* row = vst + static_cast<size_t>(s - sa) * ROWB;
-            v = CP ? reinterpret_cast<const float*>(row)[d]
-                   : __bfloat162float(reinterpret_cast<const bf16*>(row)[d]);
-          } else {
-            v = vn[(s - p0) * HD + d];
-          }
-#pragma unroll
-          for (int j = 0; j < J; ++j) acc[j] = fmaf(sc[j * SUB + (s - sa)], v, acc[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < J; ++j) accg[(g * J + j) * HD + d] = acc[j];
-      }
-      named_sync(1, NCT);
-      for (int e = cs.tid; e < J * HD; e += NCT) {
-        const int j = e / HD, d = e - j * HD;
-        const float a = (accg[(0 * J + j) * HD + d] + accg[(1 * J + j) * HD + d]) + accg[(2 * J + j) * HD + d];
-        acc_s[e] = acc_s[e] * ml[j * 4 + 2] + a;
-      }
-      named_sync(1, NCT);
-    }
-
-    // 5. publish (or finish directly when the head has a single item).
-    if (GROUP) {   // head output stays in shared memory: xs[t][hh * HD + d]
-      for (int e = cs.tid; e < J * HD; e += NCT) {
-        const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
-        sm.xs[t * 2 * HD + hh * HD + d] = acc_s[e] / ml[j * 4 + 1];
-      }
-      named_sync(1, NCT);
-      continue;
-    }
-    if (nch == 1) {
-      for (int e = cs.tid; e < J * HD; e += NCT) {
-        const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
-        p.w.attn[t * QSZ + (2 * h + hh) * HD + d] = acc_s[e] / ml[j * 4 + 1];
-      }
-      named_sync(1, NCT);
-      continue;
-    }
-    for (int e = cs.tid; e < J * PRT_STRIDE; e += NCT) {
-      const int j = e / PRT_STRIDE, k = e - j * PRT_STRIDE, t = j >> 1, hh = j & 1;
-      const float val = k < 2 ? ml[j * 4 + k] : (k < 4 ? 0.f : acc_s[j * HD + (k - 4)]);
-      p.w.prt[((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + c) * PRT_STRIDE + k] = val;
-    }
-    named_sync(1, NCT);
-    if (cs.tid == 0) {
-      __threadfence();
-      const uint32_t old = atomicAdd(p.w.att_cnt + h, 1u);
-      sm.bcast[0] = (old == static_cast<uint32_t>(nch - 1)) ? 1 : 0;
-      __threadfence();
-    }
-    named_sync(1, NCT);
-    if (sm.bcast[0]) {
-      // combine the nch partials of KV head h in chunk order, staged with one round trip
-      const bool staged = J * nch * PRT_STRIDE * 4 <= ATT_STAGE_BYTES;
-      float* recs = reinterpret_cast<float*>(sm.att);   // [J][nch][PRT_STRIDE]
-      if (staged) {
-        const int pieces = nch * PRT_STRIDE / 4;
-        for (int e = cs.tid; e < J * pieces; e += NCT) {
-          const int j = e / pieces, r = e - j * pieces, t = j >> 1, hh = j & 1;
-          cp_async16(recs + (j * nch) * PRT_STRIDE + r * 4,
-                     p.w.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE + r * 4);
-        }
-        cp_async_wait_all();
-        named_sync(1, NCT);
-      }
-      for (int e = cs.tid; e < J * HD; e += NCT) {
-        const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
-        float M = -INFINITY, Ls = 0.f, O = 0.f;
-        if (staged) {
-          const float* rec = recs + (j * nch) * PRT_STRIDE;
-          for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, rec[cc * PRT_STRIDE]);
-          for (int cc = 0; cc < nch; ++cc) {
-            const float mc = rec[cc * PRT_STRIDE];
-            if (mc == -INFINITY) continue;
-            const float wgt = expf(mc - M);
-            Ls = fmaf(wgt, rec[cc * PRT_STRIDE + 1], Ls);
-            O = fmaf(wgt, rec[cc * PRT_STRIDE + 4 + d], O);
-          }
-        } else {
-          const float* rec = p.w.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE;
-          for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(rec + cc * PRT_STRIDE));
-          for (int cc = 0; cc < nch; ++cc) {
-            const float mc = __ldcg(rec + cc * PRT_STRIDE);
-            if (mc == -INFINITY) continue;
-            const float wgt = expf(mc - M);
-            Ls = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 1), Ls);
-            O = fmaf(wgt, __ldcg(rec + cc * PRT_STRIDE + 4 + d), O);
-          }
-        }
-        p.w.attn[t * QSZ + (2 * h + hh) * HD + d] = O / Ls;
-      }
-      if (cs.tid == 0) atomicExch(p.w.att_cnt + h, 0u);
-    }
-    named_sync(1, NCT);
+    AttIO io;
+    io.qkv = p.w.qkv;
+    io.kb = reinterpret_cast<uint8_t*>(CP ? static_cast<void*>(p.cp_k) : static_cast<void*>(p.bb_k)) +
+            (layer_off + static_cast<size_t>(h) * max_seq * HD) * ESZ;
+    io.vb = reinterpret_cast<uint8_t*>(CP ? static_cast<void*>(p.cp_v) : static_cast<void*>(p.bb_v)) +
+            (layer_off + static_cast<size_t>(h) * max_seq * HD) * ESZ;
+    io.out = p.w.attn;
+    io.hilo = nullptr;
+    io.tok0 = 0;
+    io.prt = p.w.prt;
+    io.cnt = p.w.att_cnt + h;
+    if (!att_item<NT, CP, GROUP>(p, sm, cs, lw, io, p0, h, c, nch, s0, s1, writer)) return false;
   }
   return !aborted(sm);
 }
@@ -1516,14 +1568,14 @@ __device__ uint32_t radix_threshold(Smem& sm, Cons& cs, const uint32_t (&key)[SP
   return prefix;
 }
 
-__device__ int sample(const Params& p, Smem& sm, Cons& cs, const SampleCfg& c) {
+__device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& c) {
   float v[SPT];
   const int base = cs.tid * SPT;
 #pragma unroll
   for (int j = 0; j < SPT; ++j) {
     const int i = base + j;
     float x = -INFINITY;
-    if (i < c.V) x = head_mask(c, i, __ldcg(p.w.logits + i));
+    if (i < c.V) x = head_mask(c, i, __ldcg(logits + i));
     v[j] = x;
   }
   if (!c.do_sample) {
@@ -1745,7 +1797,7 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
     if (tk == -2) return false;
     if (p.dbg_cp_logits && cs.cta == 0)
       for (int i = cs.tid; i < p.cp_vocab; i += NCT) p.dbg_cp_logits[g * p.cp_vocab + i] = __ldcg(p.w.logits + i);
-    toks[g + 1] = tk >= 0 ? tk : sample(p, sm, cs, c);
+    toks[g + 1] = tk >= 0 ? tk : sample(p.w.logits, sm, cs, c);
   }
   // ---- combine (generator.py:143-149,356-362): sequential bf16 adds
   {
@@ -1778,7 +1830,7 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   if (tk == -2) return false;
   if (p.dbg_g0_logits && cs.cta == 0)
     for (int i = cs.tid; i < p.vocab; i += NCT) p.dbg_g0_logits[i] = __ldcg(p.w.logits + i);
-  const int g0n = tk >= 0 ? tk : sample(p, sm, cs, c);
+  const int g0n = tk >= 0 ? tk : sample(p.w.logits, sm, cs, c);
   if (cs.cta == 0 && cs.tid == 0) {
     int32_t* out = p.codes + static_cast<size_t>(step) * NGROUPS;
     for (int g = 0; g < NGROUPS; ++g) out[g] = toks[g];
@@ -1825,7 +1877,7 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
     c.u24 = c.do_sample ? draw_u24(p.sp, 0, 0) : 0u;
     const int tk = head(p, sm, cs, p.codec_head, p.vocab, 0, c, 0);
     if (tk == -2) return false;
-    const int g0 = tk >= 0 ? tk : sample(p, sm, cs, c);
+    const int g0 = tk >= 0 ? tk : sample(p.w.logits, sm, cs, c);
     if (cs.cta == 0 && cs.tid == 0) {
       st->g0 = g0;
       st->position = pos + 1;

@@ -34,6 +34,7 @@ constexpr int NSLOTS = 7;
 constexpr int NCW = 12;                    // consumer warps
 constexpr int NCT = NCW * 32;              // consumer threads
 constexpr int NTHREADS = NCT + 32;         // + one producer warp
+constexpr int NTHREADS_B = NTHREADS + 32;  // batched kernel: + one MMA warp
 constexpr int NTMAX = 2;                   // tokens per pass (2 = code-predictor prefill pair)
 constexpr int MAXPART = 256;               // partial-sum units per stage per CTA
 constexpr int ATT_TARGET = 24;             // attention positions per work item (target)
@@ -56,6 +57,7 @@ constexpr int WD_BOXES_PER_SLOT = SLOT_BYTES / WD_BOX_BYTES;  // 2
 constexpr int WD_SLOTS = WD_BOXES / WD_BOXES_PER_SLOT;        // 2
 constexpr int NHACC = 3;                                      // rotating fixed-point layer outputs
 constexpr size_t TMAP_BYTES = 128;                            // one CUtensorMap
+constexpr int ABUF_LD = INTER;   // row length (elements) of the batched bf16 hi/lo GEMM operand planes
 
 // Same layout as TTSLayerWeights / CPLayerWeights of the reference
 // (fused_decode_tts.cu:22-34, fused_decode_code_predictor.cu:30-42).
@@ -117,7 +119,47 @@ struct Work {
 size_t work_bytes();
 void work_carve(void* base, Work* w);
 
-enum Mode : int { MODE_FRAME = 0, MODE_BB_STEP = 1, MODE_CP_STEP = 2 };
+// ---- batched decode (qtt_batch_kernel): B utterances advance together, tcgen05 GEMMs
+constexpr int BMAX = 64;                  // utterances per batched launch
+constexpr int TBMAX = 2 * BMAX;           // tokens per stage (code-predictor first pass: 2 per utterance)
+constexpr int NLMAPS = 7;                 // tensor maps per layer: q, k, v, o, gate, up, down
+// Per-utterance device pointers of a batched launch.
+struct BStream {
+  bf16* k;                 // backbone KV [layers][8][max_seq][128] bf16
+  bf16* v;
+  float* cpk;              // code-predictor KV [5][8][16][128] fp32
+  float* cpv;
+  StreamState* st;
+  int32_t* codes;          // [max_frames][16]
+  const bf16* trailing;    // [n_trailing][HID]
+  int n_trailing;
+  int len;                 // prefill: context length
+  const bf16* pad;         // [HID]
+  const bf16* emb;         // prefill: context embeddings [len][HID]
+};
+// Batched scratch (one per engine).
+struct BWork {
+  bf16* abuf[2];           // [2 planes][TBMAX][ABUF_LD] bf16 GEMM operand: plane 0 = hi, plane 1 = lo
+  float* x;                // [TBMAX][HID] stack input (residual of the first layer)
+  float* hb[2];            // [TBMAX][HID] layer outputs
+  float* qkv;              // [TBMAX][QKV_ROWS]
+  float* hmid;             // [TBMAX][HID]
+  float* logits;           // [BMAX][VMAX] sampled heads
+  float* prt;              // [TBMAX][NQH][MAX_ATT_CHUNKS][PRT_STRIDE]
+  uint32_t* att_cnt;       // [TBMAX][NKVH]
+  unsigned long long* ssq; // [3][TBMAX] sums of squares for the next RMSNorm, fixed point 2^-32
+  unsigned long long* amax;// [2][TBMAX] packed argmax of greedy heads
+  int32_t* tok;            // [BMAX][NGROUPS] tokens of the frame
+};
+size_t bwork_bytes();
+void bwork_carve(void* base, BWork* w);
+
+enum Mode : int {
+  MODE_FRAME = 0, MODE_BB_STEP = 1, MODE_CP_STEP = 2,
+  MODE_B_FRAME = 3,        // batched: one frame of every utterance
+  MODE_B_PREFILL = 4,      // batched: backbone step b_step of every utterance with b_step < len
+  MODE_B_HEAD = 5,         // batched: first group-0 token of every utterance after its prefill
+};
 enum Flags : int { FLAG_HEAD_SAMPLE = 1, FLAG_EAGER_REFILL = 2 };
 
 struct Params {
@@ -144,6 +186,13 @@ struct Params {
   // stack runs the fused gate/up + down stage; when null, separate gate/up and down stages
   const void* bb_wd_map;
   const void* cp_wd_map;
+  // batched decode: tensor maps [(n_bb + n_cp) * 7 layer matrices][codec head, 15 cp heads]
+  // [abuf 0 box 64, abuf 0 box 128, abuf 1 box 64, abuf 1 box 128]
+  const uint8_t* bmaps;
+  int nb;                  // utterances of the batched launch
+  const BStream* bs;       // [nb]
+  BWork bw;
+  int b_step;              // MODE_B_PREFILL: context index of this step
   // caches [layer][kv head][max_seq][128]
   bf16* bb_k;
   bf16* bb_v;
@@ -187,5 +236,8 @@ struct Params {
 cudaError_t kernel_setup(int device, int* num_ctas, size_t* smem_bytes);
 // Host side: zero the barrier counter and cooperatively launch one program.
 cudaError_t launch(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream);
+// Batched kernel: the same for qtt_batch_kernel (also clears the sums-of-squares and argmax words).
+cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes);
+cudaError_t launch_b(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream);
 
 }  // namespace qtt
