@@ -222,6 +222,25 @@ qtt_status qtt_set_decode_state(qtt_engine* e, int s, const float* h, int g0, in
 qtt_status qtt_get_hidden(qtt_engine* e, int s, float* out, cudaStream_t stream);
 /* Device pointer of the stream's code buffer int32 [max_frames][16]. */
 qtt_status qtt_codes_ptr(qtt_engine* e, int s, int32_t** codes);
+
+/* Batched decode (no counterpart in the reference, which decodes one utterance at a time:
+ * generator.py:77-176 is the per-utterance loop these replace for B utterances). Streams
+ * 0..B-1 of the engine (B <= 64 and <= max_streams) advance together: every launch streams the
+ * weights once for the whole batch and runs the projections on tcgen05 tensor cores.
+ * qtt_batch_prefill: resets the streams, decodes each utterance's context (embeds[s]: device
+ * bf16 [lens[s]][1024]) and samples its first group-0 token (as qtt_prefill per stream).
+ * qtt_batch_frames: n_frames frames of every stream that has not reached EOS (as qtt_frames per
+ * stream; trailing[s] device bf16 [n_trailing[s]][1024] or NULL when n_trailing[s] == 0,
+ * pad[s] device bf16 [1024]). Sampling draws of stream s use Philox stream sp->philox_stream + s.
+ * The pointer and length arrays are host arrays of B entries. */
+qtt_status qtt_batch_prefill(qtt_engine* e, int B, const void* const* embeds, const int* lens,
+                             const qtt_sampling* sp, cudaStream_t stream);
+qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const void* const* trailing, const int* n_trailing,
+                            const void* const* pad, const qtt_sampling* sp, cudaStream_t stream);
+/* Diagnostics of the batched path (parity tests): device pointers of its GEMM operand planes
+ * (bf16 [2][128][3072] each: plane 0 = hi, plane 1 = lo, row = token), of the last sampled
+ * head's bf16-valued logits (fp32 [64][3072]) and of the frame's tokens (int32 [64][16]). */
+qtt_status qtt_batch_debug_buffers(qtt_engine* e, void** abuf0, void** abuf1, float** logits, int32_t** tok);
 /* One code-predictor decode step on the engine's own fp32 CP cache (position < 16). */
 qtt_status qtt_cp_step(qtt_engine* e, const void* emb, int position, float* out_hidden, cudaStream_t stream);
 /* Test hook: when non-NULL, each frame copies its raw bf16 head logits (as fp32) into

@@ -35,6 +35,20 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
+// Tensor map of a bf16 row-major matrix [rows][cols] for the batched GEMMs: boxes of 64 columns
+// (128 bytes) x box_rows rows with the 128-byte swizzle that tcgen05 K-major operands use.
+bool encode_sw128(const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows, CUtensorMap* out) {
+  const EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * sizeof(bf16)};
+  const cuuint32_t box[2] = {64u, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Tensor map of one W_down [HID][INTER] (bf16, row-major) for the fused MLP stage: boxes of
 // WD_BOX_ROWS rows x WD_BOX_COLS columns, no swizzle, zero fill beyond the last column.
 bool encode_wd_map(const void* wd, CUtensorMap* out) {
@@ -263,6 +277,17 @@ struct StreamBufs {
 };
 
 struct qtt_engine {
+  // batched decode resources (allocated on the first batched call)
+  std::vector<TTSLayerWeights> h_bb, h_cp;   // host copies of the layer tables
+  const void* h_codec_head = nullptr;
+  const void* h_cp_head[qtt::NCPHEADS] = {};
+  DevShape bshape;
+  bool b_ready = false;
+  void* d_bwork = nullptr;
+  void* d_bmaps = nullptr;
+  qtt::BStream* d_bs = nullptr;
+  float* d_cpkv = nullptr;
+  std::vector<qtt::BStream> h_bs;
   int device = 0;
   DevShape shape;
   qtt_dims dims{};
@@ -322,6 +347,10 @@ void engine_free(qtt_engine* e) {
   cudaFree(e->d_cp_emb);
   cudaFree(e->d_cp_head);
   cudaFree(e->d_maps);
+  cudaFree(e->d_bwork);
+  cudaFree(e->d_bmaps);
+  cudaFree(e->d_bs);
+  cudaFree(e->d_cpkv);
   cudaFree(e->d_work);
   cudaFree(e->cp_k);
   cudaFree(e->cp_v);
@@ -448,6 +477,11 @@ extern "C" qtt_status qtt_engine_create(const qtt_weights* w, const qtt_dims* d,
     QTT_TRY(cudaMemset(s.codes, 0, sizeof(int32_t) * qtt::NGROUPS * max_frames));
   }
 #undef QTT_TRY
+  e->h_bb.assign(w->backbone_layers, w->backbone_layers + d->backbone_layers);
+  e->h_cp.assign(reinterpret_cast<const TTSLayerWeights*>(w->cp_layers),
+                 reinterpret_cast<const TTSLayerWeights*>(w->cp_layers) + d->cp_layers);
+  e->h_codec_head = w->codec_head;
+  for (int g = 0; g < qtt::NCPHEADS; ++g) e->h_cp_head[g] = w->cp_lm_head[g];
   qtt::Params& p = e->base;
   std::memset(&p, 0, sizeof(p));
   p.bb_layers = e->d_bb;
@@ -636,6 +670,170 @@ extern "C" qtt_status qtt_frames(qtt_engine* e, int s, int n_frames, const void*
     cudaError_t ce = qtt::launch(p, e->shape.ctas, e->shape.smem, stream);
     if (ce != cudaSuccess) return from_cuda(ce);
   }
+  return QTT_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Batched decode
+// ------------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kCpKvFloats = static_cast<size_t>(qtt::NKVH) * kCpMaxSeq * qtt::HD;   // per layer
+
+// Kernel attributes, scratch, per-utterance code-predictor KV and the tensor maps of every
+// weight matrix, once per engine.
+qtt_status ensure_batch(qtt_engine* e) {
+  if (e->b_ready) return QTT_OK;
+  cudaError_t ce = qtt::kernel_setup_b(e->device, &e->bshape.ctas, &e->bshape.smem);
+  if (ce != cudaSuccess) return from_cuda(ce);
+  const int nbb = e->dims.backbone_layers, ncp = e->dims.cp_layers;
+  const int h0 = (nbb + ncp) * qtt::NLMAPS;
+  const int nmaps = h0 + 1 + qtt::NCPHEADS + 4;
+  std::vector<CUtensorMap> maps(nmaps);
+  bool ok = true;
+  auto layer_maps = [&](const TTSLayerWeights& L, CUtensorMap* m) {
+    ok = ok && encode_sw128(L.q_proj_weight, qtt::QSZ, qtt::HID, 16, m + 0);
+    ok = ok && encode_sw128(L.k_proj_weight, qtt::KVSZ, qtt::HID, 16, m + 1);
+    ok = ok && encode_sw128(L.v_proj_weight, qtt::KVSZ, qtt::HID, 16, m + 2);
+    ok = ok && encode_sw128(L.o_proj_weight, qtt::HID, qtt::QSZ, 16, m + 3);
+    ok = ok && encode_sw128(L.gate_proj_weight, qtt::INTER, qtt::HID, 16, m + 4);
+    ok = ok && encode_sw128(L.up_proj_weight, qtt::INTER, qtt::HID, 16, m + 5);
+    ok = ok && encode_sw128(L.down_proj_weight, qtt::HID, qtt::INTER, 16, m + 6);
+  };
+  for (int l = 0; l < nbb; ++l) layer_maps(e->h_bb[l], maps.data() + l * qtt::NLMAPS);
+  for (int l = 0; l < ncp; ++l) layer_maps(e->h_cp[l], maps.data() + (nbb + l) * qtt::NLMAPS);
+  ok = ok && encode_sw128(e->h_codec_head, e->dims.vocab, qtt::HID, 16, &maps[h0]);
+  for (int g = 0; g < qtt::NCPHEADS; ++g)
+    ok = ok && encode_sw128(e->h_cp_head[g], e->dims.cp_vocab, qtt::HID, 16, &maps[h0 + 1 + g]);
+  if (!ok) return QTT_ERR_UNSUPPORTED;
+  ce = cudaMalloc(&e->d_bwork, qtt::bwork_bytes());
+  if (ce == cudaSuccess) ce = cudaMemset(e->d_bwork, 0, qtt::bwork_bytes());
+  if (ce != cudaSuccess) return from_cuda(ce);
+  qtt::BWork bw;
+  qtt::bwork_carve(e->d_bwork, &bw);
+  for (int b = 0; b < 2; ++b)
+    if (!encode_sw128(bw.abuf[b], 2 * qtt::TBMAX, qtt::ABUF_LD, 64, &maps[h0 + 1 + qtt::NCPHEADS + 2 * b]) ||
+        !encode_sw128(bw.abuf[b], 2 * qtt::TBMAX, qtt::ABUF_LD, 128, &maps[h0 + 1 + qtt::NCPHEADS + 2 * b + 1]))
+      return QTT_ERR_UNSUPPORTED;
+  ce = cudaMalloc(&e->d_bmaps, qtt::TMAP_BYTES * nmaps);
+  if (ce == cudaSuccess) ce = cudaMemcpy(e->d_bmaps, maps.data(), qtt::TMAP_BYTES * nmaps, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_bs), sizeof(qtt::BStream) * e->max_streams);
+  const size_t cpkv = 2 * kCpKvFloats * ncp * e->max_streams;
+  if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_cpkv), sizeof(float) * cpkv);
+  if (ce == cudaSuccess) ce = cudaMemset(e->d_cpkv, 0, sizeof(float) * cpkv);
+  if (ce != cudaSuccess) return from_cuda(ce);
+  e->h_bs.assign(e->max_streams, qtt::BStream{});
+  for (int s = 0; s < e->max_streams; ++s) {
+    qtt::BStream& b = e->h_bs[s];
+    b.k = e->streams[s].k;
+    b.v = e->streams[s].v;
+    b.cpk = e->d_cpkv + 2 * kCpKvFloats * ncp * s;
+    b.cpv = b.cpk + kCpKvFloats * ncp;
+    b.st = e->streams[s].st;
+    b.codes = e->streams[s].codes;
+  }
+  e->b_ready = true;
+  return QTT_OK;
+}
+
+qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
+  qtt::Params p = e->base;
+  p.bmaps = static_cast<const uint8_t*>(e->d_bmaps);
+  p.nb = B;
+  p.bs = e->d_bs;
+  qtt::bwork_carve(e->d_bwork, &p.bw);
+  p.sp = to_dev(sp);
+  p.bb_wd_map = nullptr;
+  p.cp_wd_map = nullptr;
+  return p;
+}
+
+qtt_status batch_check(qtt_engine* e, int B, const qtt_sampling* sp) {
+  if (!e || B < 1 || B > e->max_streams || B > qtt::BMAX) return QTT_ERR_INVALID_ARG;
+  qtt_status r = check_sampling(sp, e);
+  if (r != QTT_OK) return r;
+  r = set_device(e);
+  if (r != QTT_OK) return r;
+  return ensure_batch(e);
+}
+
+}  // namespace
+
+extern "C" qtt_status qtt_batch_prefill(qtt_engine* e, int B, const void* const* embeds, const int* lens,
+                                        const qtt_sampling* sp, cudaStream_t stream) {
+  qtt_status r = batch_check(e, B, sp);
+  if (r != QTT_OK) return r;
+  if (!embeds || !lens) return QTT_ERR_INVALID_ARG;
+  int maxlen = 0;
+  for (int s = 0; s < B; ++s) {
+    if (!embeds[s] || !aligned16(embeds[s]) || lens[s] < 1 || lens[s] >= e->max_seq || lens[s] > e->base.rope_rows)
+      return QTT_ERR_INVALID_ARG;
+    maxlen = lens[s] > maxlen ? lens[s] : maxlen;
+  }
+  for (int s = 0; s < B; ++s) {
+    r = qtt_reset(e, s, stream);
+    if (r != QTT_OK) return r;
+    qtt::BStream& b = e->h_bs[s];
+    b.trailing = nullptr;
+    b.n_trailing = 0;
+    b.pad = nullptr;
+    b.len = lens[s];
+    b.emb = static_cast<const bf16*>(embeds[s]);
+  }
+  // pageable source: the copy is staged before the call returns
+  cudaError_t ce = cudaMemcpyAsync(e->d_bs, e->h_bs.data(), sizeof(qtt::BStream) * B, cudaMemcpyHostToDevice, stream);
+  if (ce != cudaSuccess) return from_cuda(ce);
+  qtt::Params p = batch_params(e, B, sp);
+  p.mode = qtt::MODE_B_PREFILL;
+  for (int i = 0; i < maxlen; ++i) {
+    p.b_step = i;
+    ce = qtt::launch_b(p, e->bshape.ctas, e->bshape.smem, stream);
+    if (ce != cudaSuccess) return from_cuda(ce);
+  }
+  p.mode = qtt::MODE_B_HEAD;
+  return from_cuda(qtt::launch_b(p, e->bshape.ctas, e->bshape.smem, stream));
+}
+
+extern "C" qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const void* const* trailing,
+                                       const int* n_trailing, const void* const* pad, const qtt_sampling* sp,
+                                       cudaStream_t stream) {
+  qtt_status r = batch_check(e, B, sp);
+  if (r != QTT_OK) return r;
+  if (n_frames < 0 || !pad || !n_trailing) return QTT_ERR_INVALID_ARG;
+  for (int s = 0; s < B; ++s)
+    if (!pad[s] || n_trailing[s] < 0 || (n_trailing[s] > 0 && (!trailing || !trailing[s]))) return QTT_ERR_INVALID_ARG;
+  for (int s = 0; s < B; ++s) {
+    qtt::BStream& b = e->h_bs[s];
+    b.trailing = n_trailing[s] > 0 ? static_cast<const bf16*>(trailing[s]) : nullptr;
+    b.n_trailing = n_trailing[s];
+    b.pad = static_cast<const bf16*>(pad[s]);
+    b.emb = nullptr;
+    b.len = 0;
+  }
+  cudaError_t ce = cudaMemcpyAsync(e->d_bs, e->h_bs.data(), sizeof(qtt::BStream) * B, cudaMemcpyHostToDevice, stream);
+  if (ce != cudaSuccess) return from_cuda(ce);
+  qtt::Params p = batch_params(e, B, sp);
+  p.mode = qtt::MODE_B_FRAME;
+  for (int i = 0; i < n_frames; ++i) {
+    ce = qtt::launch_b(p, e->bshape.ctas, e->bshape.smem, stream);
+    if (ce != cudaSuccess) return from_cuda(ce);
+  }
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_batch_debug_buffers(qtt_engine* e, void** abuf0, void** abuf1, float** logits,
+                                              int32_t** tok) {
+  if (!e) return QTT_ERR_INVALID_ARG;
+  qtt_status r = set_device(e);
+  if (r != QTT_OK) return r;
+  r = ensure_batch(e);
+  if (r != QTT_OK) return r;
+  qtt::BWork bw;
+  qtt::bwork_carve(e->d_bwork, &bw);
+  if (abuf0) *abuf0 = bw.abuf[0];
+  if (abuf1) *abuf1 = bw.abuf[1];
+  if (logits) *logits = bw.logits;
+  if (tok) *tok = bw.tok;
   return QTT_OK;
 }
 

@@ -1946,9 +1946,75 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
   if (!ok) *reinterpret_cast<volatile int*>(&sm.abort) = 1;
 }
 
+#include "qtt_batch.cuh"
+
 // ------------------------------------------------------------------------------------------
 // Host helpers
 // ------------------------------------------------------------------------------------------
+size_t bwork_bytes() {
+  size_t n = 256;
+  n += sizeof(unsigned long long) * 5 * TBMAX;                       // ssq, amax
+  n += sizeof(uint32_t) * TBMAX * NKVH;                              // att_cnt
+  n += sizeof(int32_t) * BMAX * NGROUPS;                             // tok
+  n += 2 * sizeof(bf16) * 2 * TBMAX * ABUF_LD;                      // abuf
+  n += sizeof(float) * TBMAX * HID * 3;                              // x, hb[2]
+  n += sizeof(float) * TBMAX * QKV_ROWS;                             // qkv
+  n += sizeof(float) * TBMAX * HID;                                  // hmid
+  n += sizeof(float) * BMAX * VMAX;                                  // logits
+  n += sizeof(float) * TBMAX * NQH * MAX_ATT_CHUNKS * PRT_STRIDE;   // prt
+  return n;
+}
+
+void bwork_carve(void* base, BWork* w) {
+  char* c = static_cast<char*>(base);
+  // ssq and amax first and contiguous: one memset per launch clears both
+  w->ssq = reinterpret_cast<unsigned long long*>(c); c += sizeof(unsigned long long) * 3 * TBMAX;
+  w->amax = reinterpret_cast<unsigned long long*>(c); c += sizeof(unsigned long long) * 2 * TBMAX;
+  w->att_cnt = reinterpret_cast<uint32_t*>(c); c += sizeof(uint32_t) * TBMAX * NKVH;
+  w->tok = reinterpret_cast<int32_t*>(c); c += sizeof(int32_t) * BMAX * NGROUPS;
+  c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c) + 255) & ~static_cast<uintptr_t>(255));
+  for (int i = 0; i < 2; ++i) {
+    w->abuf[i] = reinterpret_cast<bf16*>(c);
+    c += sizeof(bf16) * 2 * TBMAX * ABUF_LD;
+  }
+  w->x = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * HID;
+  for (int i = 0; i < 2; ++i) {
+    w->hb[i] = reinterpret_cast<float*>(c);
+    c += sizeof(float) * TBMAX * HID;
+  }
+  w->qkv = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * QKV_ROWS;
+  w->hmid = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * HID;
+  w->logits = reinterpret_cast<float*>(c); c += sizeof(float) * BMAX * VMAX;
+  w->prt = reinterpret_cast<float*>(c);
+}
+
+cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return e;
+  const size_t smem = sizeof(Smem);
+  e = cudaFuncSetAttribute(qtt_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int sms = 0, per_sm = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qtt_batch_kernel, NTHREADS_B, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  *num_ctas = sms;
+  *smem_bytes = smem;
+  return cudaSuccess;
+}
+
+cudaError_t launch_b(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(p.w.bar, 0, sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(p.bw.ssq, 0, sizeof(unsigned long long) * 5 * TBMAX, stream);   // ssq + amax
+  if (e != cudaSuccess) return e;
+  void* args[] = {const_cast<Params*>(&p)};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(qtt_batch_kernel), dim3(num_ctas), dim3(NTHREADS_B),
+                                     args, smem_bytes, stream);
+}
+
 cudaError_t kernel_setup(int device, int* num_ctas, size_t* smem_bytes) {
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return e;

@@ -202,6 +202,45 @@ class Engine:
         _lib.check(self.lib.qtt_frames(self.h, s, n, tp, nt, _ptr(pad), ctypes.byref(sampling),
                                        _stream_handle(stream)), "qtt_frames")
 
+    # ---- batched decode (streams 0..B-1 advance together, tcgen05 GEMMs) ----------------------
+    def batch_prefill(self, embeds: list, sampling: _lib.QttSampling, stream=None):
+        """Prefill utterances 0..B-1 (``embeds[s]``: bf16 [len_s, 1024] on the engine's GPU) and
+        sample each one's first group-0 token."""
+        embeds = [e.contiguous() for e in embeds]
+        for e in embeds:
+            assert e.is_cuda and e.dtype == torch.bfloat16 and e.dim() == 2
+        B = len(embeds)
+        self._keep_b = embeds
+        ptrs = (ctypes.c_void_p * B)(*[_ptr(e) for e in embeds])
+        lens = (ctypes.c_int * B)(*[e.shape[0] for e in embeds])
+        _lib.check(self.lib.qtt_batch_prefill(self.h, B, ptrs, lens, ctypes.byref(sampling), _stream_handle(stream)),
+                   "qtt_batch_prefill")
+
+    def batch_frames(self, n: int, trailing: list, pads: list, sampling: _lib.QttSampling, stream=None):
+        """n frames of utterances 0..B-1 (``trailing[s]``: bf16 [T_s, 1024] or None, ``pads[s]``:
+        bf16 [1024])."""
+        B = len(pads)
+        trailing = [None if t is None else t.contiguous() for t in trailing]
+        pads = [x.contiguous() for x in pads]
+        self._keep_f = (trailing, pads)
+        tp = (ctypes.c_void_p * B)(*[None if t is None or t.shape[0] == 0 else _ptr(t) for t in trailing])
+        nt = (ctypes.c_int * B)(*[0 if t is None else t.shape[0] for t in trailing])
+        pp = (ctypes.c_void_p * B)(*[_ptr(x) for x in pads])
+        _lib.check(self.lib.qtt_batch_frames(self.h, B, n, tp, nt, pp, ctypes.byref(sampling), _stream_handle(stream)),
+                   "qtt_batch_frames")
+
+    def batch_buffers(self) -> dict:
+        """Diagnostic views of the batched path's buffers (GEMM operand planes, sampled logits,
+        frame tokens)."""
+        a0, a1, lg, tk = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(self.lib.qtt_batch_debug_buffers(self.h, ctypes.byref(a0), ctypes.byref(a1), ctypes.byref(lg),
+                                                    ctypes.byref(tk)), "qtt_batch_debug_buffers")
+        dev = f"cuda:{self.model.device}"
+        planes = lambda a: torch.as_tensor(_DevArray(a.value, (2, 128, 3072), "<u2"), device=dev).view(torch.bfloat16)
+        return {"abuf0": planes(a0), "abuf1": planes(a1),
+                "logits": torch.as_tensor(_DevArray(lg.value, (64, 3072), "<f4"), device=dev),
+                "tok": torch.as_tensor(_DevArray(tk.value, (64, 16), "<i4"), device=dev)}
+
     def set_decode_state(self, s: int, h: torch.Tensor, g0: int, position: int, stream=None):
         """KV handoff: decode from ``position`` with hidden ``h`` (fp32 [1024]) and token g0."""
         h = h.to(torch.float32).contiguous()
