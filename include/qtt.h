@@ -237,10 +237,15 @@ qtt_status qtt_batch_prefill(qtt_engine* e, int B, const void* const* embeds, co
                              const qtt_sampling* sp, cudaStream_t stream);
 qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const void* const* trailing, const int* n_trailing,
                             const void* const* pad, const qtt_sampling* sp, cudaStream_t stream);
-/* Diagnostics of the batched path (parity tests): device pointers of its GEMM operand planes
- * (bf16 [2][128][3072] each: plane 0 = hi, plane 1 = lo, row = token), of the last sampled
- * head's bf16-valued logits (fp32 [64][3072]) and of the frame's tokens (int32 [64][16]). */
-qtt_status qtt_batch_debug_buffers(qtt_engine* e, void** abuf0, void** abuf1, float** logits, int32_t** tok);
+/* Diagnostics of the batched path (parity tests): the first n of its scratch device pointers,
+ * in this order: GEMM operand planes 0 and 1 (bf16 [2][128][3072] each: plane 0 = hi, plane 1 =
+ * lo, row = token), sampled-head logits (fp32 [64][3072]), frame tokens (int32 [64][16]), stack
+ * input, layer outputs 0 and 1, post-attention residual (fp32 [128][1024] each), q/k/v
+ * (fp32 [128][4096]). */
+qtt_status qtt_batch_debug_buffers(qtt_engine* e, void** ptrs, int n);
+/* Parity tests: when set, batched frames also write every head's bf16-valued logits, fp32
+ * [B][15][cp_vocab] for the code-predictor heads and [B][vocab] for the codec head (NULL: off). */
+qtt_status qtt_batch_set_debug_outputs(qtt_engine* e, float* cp_logits, float* g0_logits);
 /* One code-predictor decode step on the engine's own fp32 CP cache (position < 16). */
 qtt_status qtt_cp_step(qtt_engine* e, const void* emb, int position, float* out_hidden, cudaStream_t stream);
 /* Test hook: when non-NULL, each frame copies its raw bf16 head logits (as fp32) into

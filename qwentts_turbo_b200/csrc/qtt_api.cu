@@ -288,6 +288,8 @@ struct qtt_engine {
   qtt::BStream* d_bs = nullptr;
   float* d_cpkv = nullptr;
   std::vector<qtt::BStream> h_bs;
+  float* b_dbg_cp = nullptr;   // batched debug logits [B][15][cp_vocab], [B][vocab]
+  float* b_dbg_g0 = nullptr;
   int device = 0;
   DevShape shape;
   qtt_dims dims{};
@@ -745,6 +747,11 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   p.sp = to_dev(sp);
   p.bb_wd_map = nullptr;
   p.cp_wd_map = nullptr;
+  p.dbg_cp_logits = e->b_dbg_cp;
+  p.dbg_g0_logits = e->b_dbg_g0;
+  p.dbg_timeline = nullptr;
+  p.dbg_marks = nullptr;
+  p.dbg_arrivals = nullptr;
   return p;
 }
 
@@ -821,19 +828,23 @@ extern "C" qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const
   return QTT_OK;
 }
 
-extern "C" qtt_status qtt_batch_debug_buffers(qtt_engine* e, void** abuf0, void** abuf1, float** logits,
-                                              int32_t** tok) {
+extern "C" qtt_status qtt_batch_set_debug_outputs(qtt_engine* e, float* cp_logits, float* g0_logits) {
   if (!e) return QTT_ERR_INVALID_ARG;
+  e->b_dbg_cp = cp_logits;
+  e->b_dbg_g0 = g0_logits;
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_batch_debug_buffers(qtt_engine* e, void** ptrs, int n) {
+  if (!e || !ptrs || n < 1) return QTT_ERR_INVALID_ARG;
   qtt_status r = set_device(e);
   if (r != QTT_OK) return r;
   r = ensure_batch(e);
   if (r != QTT_OK) return r;
   qtt::BWork bw;
   qtt::bwork_carve(e->d_bwork, &bw);
-  if (abuf0) *abuf0 = bw.abuf[0];
-  if (abuf1) *abuf1 = bw.abuf[1];
-  if (logits) *logits = bw.logits;
-  if (tok) *tok = bw.tok;
+  void* all[9] = {bw.abuf[0], bw.abuf[1], bw.logits, bw.tok, bw.x, bw.hb[0], bw.hb[1], bw.hmid, bw.qkv};
+  for (int i = 0; i < n && i < 9; ++i) ptrs[i] = all[i];
   return QTT_OK;
 }
 

@@ -576,6 +576,10 @@ __device__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hi
         for (int i = 0; i < 16; ++i) {
           const int row = WBOX * b0 + c0 + i;
           const float lg = round_bf16(v[i]);
+          if (hidx > 0 && p.dbg_cp_logits != nullptr)   // parity tests: [B][15][cp_vocab]
+            p.dbg_cp_logits[(static_cast<size_t>(t) * NCPHEADS + hidx - 1) * p.cp_vocab + row] = lg;
+          if (hidx == 0 && p.dbg_g0_logits != nullptr && p.mode == MODE_B_FRAME)   // [B][vocab]
+            p.dbg_g0_logits[static_cast<size_t>(t) * p.vocab + row] = lg;
           if (c.do_sample) {
             __stcg(p.bw.logits + static_cast<size_t>(t) * VMAX + row, lg);
           } else {

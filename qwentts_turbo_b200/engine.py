@@ -229,17 +229,27 @@ class Engine:
         _lib.check(self.lib.qtt_batch_frames(self.h, B, n, tp, nt, pp, ctypes.byref(sampling), _stream_handle(stream)),
                    "qtt_batch_frames")
 
+    def batch_set_debug_outputs(self, cp_logits: torch.Tensor | None, g0_logits: torch.Tensor | None):
+        """Parity tests: batched frames also write each head's logits into cp_logits fp32
+        [B, 15, cp_vocab] and g0_logits fp32 [B, vocab]."""
+        self._bdbg = (cp_logits, g0_logits)
+        _lib.check(self.lib.qtt_batch_set_debug_outputs(
+            self.h, None if cp_logits is None else _ptr(cp_logits), None if g0_logits is None else _ptr(g0_logits)),
+            "qtt_batch_set_debug_outputs")
+
     def batch_buffers(self) -> dict:
-        """Diagnostic views of the batched path's buffers (GEMM operand planes, sampled logits,
-        frame tokens)."""
-        a0, a1, lg, tk = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
-        _lib.check(self.lib.qtt_batch_debug_buffers(self.h, ctypes.byref(a0), ctypes.byref(a1), ctypes.byref(lg),
-                                                    ctypes.byref(tk)), "qtt_batch_debug_buffers")
+        """Diagnostic views of the batched path's scratch (GEMM operand planes, sampled logits,
+        frame tokens, activations of the last stage that wrote them)."""
+        ptrs = (ctypes.c_void_p * 9)()
+        _lib.check(self.lib.qtt_batch_debug_buffers(self.h, ptrs, 9), "qtt_batch_debug_buffers")
         dev = f"cuda:{self.model.device}"
-        planes = lambda a: torch.as_tensor(_DevArray(a.value, (2, 128, 3072), "<u2"), device=dev).view(torch.bfloat16)
-        return {"abuf0": planes(a0), "abuf1": planes(a1),
-                "logits": torch.as_tensor(_DevArray(lg.value, (64, 3072), "<f4"), device=dev),
-                "tok": torch.as_tensor(_DevArray(tk.value, (64, 16), "<i4"), device=dev)}
+        view = lambda i, shape, ts: torch.as_tensor(_DevArray(ptrs[i], shape, ts), device=dev)
+        return {"abuf0": view(0, (2, 128, 3072), "<u2").view(torch.bfloat16),
+                "abuf1": view(1, (2, 128, 3072), "<u2").view(torch.bfloat16),
+                "logits": view(2, (64, 3072), "<f4"), "tok": view(3, (64, 16), "<i4"),
+                "x": view(4, (128, 1024), "<f4"), "hb0": view(5, (128, 1024), "<f4"),
+                "hb1": view(6, (128, 1024), "<f4"), "hmid": view(7, (128, 1024), "<f4"),
+                "qkv": view(8, (128, 4096), "<f4")}
 
     def set_decode_state(self, s: int, h: torch.Tensor, g0: int, position: int, stream=None):
         """KV handoff: decode from ``position`` with hidden ``h`` (fp32 [1024]) and token g0."""

@@ -1,0 +1,152 @@
+"""Batched decode (qtt_batch_prefill / qtt_batch_frames): several utterances advance together,
+every projection a tcgen05 GEMM over bf16 hi/lo activation planes. Checked against the fp64
+oracle the same way as the batch-1 engine (tests/tf_harness.py): each frame of each utterance
+starts the oracle from the engine's state for that utterance, and the tokens (ties excepted),
+the code-predictor and codec-head logits (atol 2e-2 / rtol 1e-2) and the backbone hidden must
+agree. Also: batched prefill vs the oracle's causal prefill, batched vs batch-1 engine codes,
+and the argument checks."""
+import pytest
+import torch
+
+from oracle import qtt_oracle as O
+from qwentts_turbo_b200 import _lib
+from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
+from qwentts_turbo_b200.workloads import c3_inputs
+from tests.tf_harness import run_teacher_forced_batch
+
+pytestmark = pytest.mark.gpu
+
+F64 = torch.float64
+TIE_TOL = 4e-2     # two bf16 ulps at |logit| in [2, 4)
+HID_REL = 1.5e-2   # final-normed hidden ||a - b|| / ||b|| (allows one bf16 flip cascade)
+
+
+def _greedy_sp(**kw):
+    base = dict(do_sample=False, min_new_tokens=10_000)
+    base.update(kw)
+    return sampling_struct(**base)
+
+
+def _frame_stats(recs, greedy=True):
+    full, bad = 0, []
+    for f, r in enumerate(recs):
+        ok = True
+        for g in range(15):
+            if r["codes"][g + 1] != r["cp_pred"][g]:
+                ok = False
+                if not greedy or r["cp_gap"][g] > TIE_TOL:
+                    bad.append((f, g + 1, r["codes"][g + 1], r["cp_pred"][g], r["cp_gap"][g]))
+        if r["g0_next"] != r["g0_pred"]:
+            ok = False
+            if not greedy or r["g0_gap"] > TIE_TOL:
+                bad.append((f, 0, r["g0_next"], r["g0_pred"], r["g0_gap"]))
+        full += ok
+    return full, bad
+
+
+def _inputs(ctxs, n_trailing, seed):
+    out = [c3_inputs(ctx=c, n_trailing=n_trailing, seed=seed + i) for i, c in enumerate(ctxs)]
+    return [o[0] for o in out], [o[1] for o in out], [o[2] for o in out]
+
+
+@pytest.fixture(scope="module")
+def dev_small(small_weights):
+    return DeviceModel(small_weights, rope_rows=1024, backbone_layers=2, cp_layers=2)
+
+
+@pytest.fixture(scope="module")
+def orc_small(small_weights):
+    return O.Qwen3TTSOracle(small_weights, backbone_layers=2, cp_layers=2, max_seq=512, dtype=F64)
+
+
+def test_batch_prefill_matches_oracle(dev_small, orc_small):
+    """Uneven contexts in one batch: each utterance's decode state equals the oracle's causal
+    prefill of its own context."""
+    embeds, _, _ = _inputs([9, 23, 40], 0, 31)
+    eng = Engine(dev_small, max_streams=3, max_seq=512, max_frames=16)
+    try:
+        eng.batch_prefill([e.cuda() for e in embeds], _greedy_sp())
+        eng.check()
+        for s, e in enumerate(embeds):
+            ref = orc_small.prefill(e.to(F64))
+            got = eng.hidden(s).cpu().to(F64)
+            assert eng.state(s)["position"] == e.shape[0]
+            rel = float((got - ref).norm() / ref.norm())
+            assert rel <= HID_REL, f"utterance {s}: rel {rel:.3g}"
+    finally:
+        eng.close()
+
+
+def test_batch_small_teacher_forced(dev_small, orc_small):
+    """2+2-layer model with random norm weights, 3 utterances of different contexts, greedy with
+    repetition penalty, 8 frames (trailing rows, then the pad row)."""
+    embeds, trailing, pads = _inputs([17, 30, 41], 5, 21)
+    eng = Engine(dev_small, max_streams=3, max_seq=512, max_frames=16)
+    try:
+        recs = run_teacher_forced_batch(eng, orc_small, embeds, trailing, pads, _greedy_sp(repetition_penalty=1.3), 8)
+    finally:
+        eng.close()
+    for s, r in enumerate(recs):
+        full, bad = _frame_stats(r)
+        assert not bad, (s, bad)
+        assert full >= len(r) - 1, (s, full)
+        assert max(x["cp_logits_viol"] for x in r) <= 0
+        assert max(x["g0_logits_viol"] for x in r) <= 0
+        assert max(x["h_rel"] for x in r) <= HID_REL
+
+
+def test_batch_sampling_teacher_forced(dev_small, orc_small):
+    """Temperature / top-k / repetition penalty with per-utterance Philox streams, code predictor
+    sampled too: each utterance's picks equal the oracle sampler's on the engine's logits."""
+    embeds, trailing, pads = _inputs([20, 33], 4, 41)
+    cfg = dict(temperature=0.9, top_k=50, repetition_penalty=1.2, seed=77, stream=5, cp_do_sample=True,
+               cp_temperature=0.9, cp_top_k=50)
+    sp = sampling_struct(do_sample=True, temperature=0.9, top_k=50, repetition_penalty=1.2, min_new_tokens=10_000,
+                         cp_do_sample=True, cp_temperature=0.9, cp_top_k=50, seed=77, philox_stream=5)
+    eng = Engine(dev_small, max_streams=2, max_seq=512, max_frames=16)
+    try:
+        recs = run_teacher_forced_batch(eng, orc_small, embeds, trailing, pads, sp, 5, sampling=cfg)
+    finally:
+        eng.close()
+    for s, r in enumerate(recs):
+        _, bad = _frame_stats(r, greedy=False)
+        assert len(bad) <= 1, (s, bad)
+        assert max(x["cp_logits_viol"] for x in r) <= 0
+
+
+def test_batch_matches_batch1_engine(dev_small):
+    """Free-running greedy codes of the batched path equal the batch-1 engine's on the same
+    utterances until the first near-tie (checked over the first 2 frames)."""
+    embeds, trailing, pads = _inputs([12, 25], 3, 51)
+    sp = _greedy_sp()
+    e1 = Engine(dev_small, max_streams=1, max_seq=512, max_frames=16)
+    ref = []
+    try:
+        for s in range(2):
+            e1.prefill(0, embeds[s].cuda(), sp)
+            e1.frames(0, 2, trailing[s].cuda(), pads[s].cuda(), sp)
+            e1.check()
+            ref.append(e1.codes(0)[:2].cpu())
+    finally:
+        e1.close()
+    eb = Engine(dev_small, max_streams=2, max_seq=512, max_frames=16)
+    try:
+        eb.batch_prefill([e.cuda() for e in embeds], sp)
+        eb.batch_frames(2, [t.cuda() for t in trailing], [x.cuda() for x in pads], sp)
+        eb.check()
+        same = sum(int((eb.codes(s)[:2].cpu() == ref[s]).sum()) for s in range(2))
+    finally:
+        eb.close()
+    assert same >= 60, f"{same}/64 codes equal"
+
+
+def test_batch_argument_errors(dev_small):
+    eng = Engine(dev_small, max_streams=2, max_seq=64, max_frames=4)
+    try:
+        e = torch.zeros(8, 1024, dtype=torch.bfloat16, device="cuda")
+        with pytest.raises(_lib.QTTError):
+            eng.batch_prefill([e, e, e], _greedy_sp())          # more utterances than streams
+        with pytest.raises(_lib.QTTError):
+            eng.batch_prefill([torch.zeros(64, 1024, dtype=torch.bfloat16, device="cuda")], _greedy_sp())  # >= max_seq
+    finally:
+        eng.close()
