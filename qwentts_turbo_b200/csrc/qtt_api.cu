@@ -688,6 +688,7 @@ qtt_status ensure_batch(qtt_engine* e) {
   if (e->b_ready) return QTT_OK;
   cudaError_t ce = qtt::kernel_setup_b(e->device, &e->bshape.ctas, &e->bshape.smem);
   if (ce != cudaSuccess) return from_cuda(ce);
+  if (e->bshape.ctas > qtt::BKCTAS) return QTT_ERR_UNSUPPORTED;
   const int nbb = e->dims.backbone_layers, ncp = e->dims.cp_layers;
   const int h0 = (nbb + ncp) * qtt::NLMAPS;
   const int nmaps = h0 + 1 + qtt::NCPHEADS + 4;
@@ -749,9 +750,7 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   p.cp_wd_map = nullptr;
   p.dbg_cp_logits = e->b_dbg_cp;
   p.dbg_g0_logits = e->b_dbg_g0;
-  p.dbg_timeline = nullptr;
-  p.dbg_marks = nullptr;
-  p.dbg_arrivals = nullptr;
+  p.dbg_arrivals = nullptr;     // (the stage timeline and profile marks, if set, are kept)
   return p;
 }
 

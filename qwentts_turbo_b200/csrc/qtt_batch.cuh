@@ -8,18 +8,22 @@
 // per program for the whole batch. Every projection is a GEMM
 //     D[tokens x rows] = A[tokens x K] * W[rows x K]^T
 //   * W: this CTA's rows of the matrix in blocks of 16. The producer warp streams them as 2-D
-//     TMA boxes of 16 rows x 64 columns with the 128-byte swizzle into an 8-slot ring and runs
-//     ahead across grid barriers (weights do not depend on activations).
+//     TMA boxes of 16 rows x 64 columns with the 128-byte swizzle (two per K step of 128) into a
+//     4-slot ring and runs ahead across grid barriers (weights do not depend on activations).
 //   * A: the activations of all tokens as two bf16 planes, hi = bf16(v) and lo = bf16(v - hi),
 //     written to global memory by the stage that produced them (row = token, plane 1 TBMAX rows
-//     below plane 0). After the stage's grid barrier the MMA warp loads them with 2-D TMA boxes
-//     (64 columns x 64 or 128 token rows per plane) into a 3-slot ring.
-//   * D: fp32 in tensor memory, 128 token lanes x N = 16..64 columns. For every K step of 64
-//     the MMA thread issues 4 x 2 tcgen05.mma (K = 16; hi plane, then lo plane accumulating),
-//     so D = W (hi + lo): ~16 mantissa bits of the activations, close to an fp32 GEMV.
-// The epilogue warps read D with tcgen05.ld (warp w owns token lanes 32w..32w+31, one thread
-// per token), apply the deferred RMSNorm scale and the stage's elementwise work, and write the
-// next GEMM's A planes. Sums of squares for the next RMSNorm are accumulated per token with
+//     below plane 0). After the stage's grid barrier the activation-loader warp streams them with
+//     2-D TMA boxes (64 columns x 64 tokens per plane; one slot per 64-token tile and K step of
+//     128 = two 128-byte swizzle atoms) into a 3-slot ring, independently of the MMA issue.
+//   * D: fp32 in tensor memory, N = 16..64 columns. An activation slot holds a 64-token tile's
+//     hi plane in rows 0..63 and its lo plane in rows 64..127, so one M = 128 tcgen05.mma per
+//     K sub-step of 16 gives D lane t = W hi[t] and lane 64 + t = W lo[t]; the epilogue adds
+//     them: D = W (hi + lo), ~16 mantissa bits of the activations, close to an fp32 GEMV. The
+//     four K sub-steps of a K step go to four independent accumulators (added by the epilogue
+//     in a fixed order), so four MMAs can be in flight.
+// The epilogue warps read D with tcgen05.ld (warp 4j + q owns tile j's token lanes 32q..32q+31,
+// one thread per token), apply the deferred RMSNorm scale and the stage's elementwise work, and
+// write the next GEMM's A planes. Sums of squares for the next RMSNorm are accumulated per token with
 // 64-bit fixed-point atomics (order independent).
 //
 // Stages of a code-predictor pass: INPUT (embedding rows -> x, A planes, sums of squares) |
@@ -27,16 +31,23 @@
 // frame adds COMBINE (the 16-embedding sum + text row) before the backbone layers and the
 // codec head (+ sampler) at the end.
 
-constexpr int KSTEP = 64;                 // K elements per pipeline step (one 128-byte row)
+constexpr int KSUB = 64;                  // K elements of one 128-byte swizzle atom row
+constexpr int NSUB = 2;                   // atoms per pipeline step
+constexpr int KSTEP = KSUB * NSUB;        // K elements per pipeline step
 constexpr int WBOX = 16;                  // weight rows per TMA box
-constexpr int WS_BYTES = 64 * 128;        // weight slot: up to 64 rows of 128 bytes
-constexpr int NWS = 8;
-constexpr int APLANE_BYTES = 128 * 128;   // one plane of an activation slot: 128 token rows
-constexpr int AS_BYTES = 2 * APLANE_BYTES;
+constexpr int WS_BYTES = NSUB * 64 * 128; // weight slot: per atom up to 64 rows of 128 bytes
+constexpr int NWS = 4;
+constexpr int APLANE_BYTES = 64 * 128;    // one plane of an activation atom: 64 token rows
+constexpr int ASUB_BYTES = 2 * APLANE_BYTES;  // hi plane, then lo plane
+constexpr int AS_BYTES = NSUB * ASUB_BYTES;
 constexpr int NAS = 3;
-constexpr uint32_t TMEM_COLS = 64;        // D: 128 lanes x up to 64 fp32 columns
+constexpr int NCHAIN = 4;                 // independent accumulators per tile (see b_mma)
+constexpr int DCOLS = 64;                 // tensor-memory columns of one accumulator (N <= 64)
+constexpr uint32_t TMEM_COLS = 2 * NCHAIN * DCOLS;   // 2 tiles x 4 chains x 64 columns = all 512
 constexpr int BATT_SPAN = 96;             // backbone attention: positions per work item (target)
+// An M = 128 MMA reads the whole slot: rows 0..63 (hi plane) and 64..127 (lo plane).
 static_assert(NWS * WS_BYTES + NAS * AS_BYTES <= NSLOTS * SLOT_BYTES, "batched rings fit the ring region");
+constexpr int YLO_STRIDE = DCOLS + 1;     // epilogue staging of the lo lanes: [2 tiles][64 tokens][65]
 // mbarriers in sm.bbar (all with one expected arrival)
 enum : int {
   BB_WFULL = 0,                  // weight slot filled (producer expect_tx + TMA bytes)
@@ -69,8 +80,17 @@ __device__ __forceinline__ int bmap_abuf(const Params& p, int buf, bool box128) 
   return (p.n_bb + p.n_cp) * NLMAPS + 1 + NCPHEADS + 2 * buf + (box128 ? 1 : 0);
 }
 
-// Blocks [b0, b0 + nb) of this CTA (16 rows; gate/up: 16 intermediate columns) and the MMA N.
-__device__ __forceinline__ void bg_blocks(const Params& p, const BGemm& g, int cta, int G, int& b0, int& nb) {
+// Work of a CTA in a GEMM stage. Rows are grouped into row blocks of `nb` blocks of 16 rows
+// (gate/up: 16 intermediate columns, i.e. 16 gate + 16 up rows per block), N <= 64 columns of D;
+// for o_proj and down the K steps are split too: CTA c < R * nk takes row block
+// c / nk and K steps [ks0, ks1) of slice c % nk, and the last CTA of a row block to finish sums
+// the slices' partial results (fixed order) and runs the epilogue.
+struct BSplit {
+  int b0, nb;        // first 16-row block, blocks (0: idle in this stage)
+  int rb, kspl, nk;  // row block, K slice, K slices per row block
+  int ks0, ks1;      // K steps of this CTA
+};
+__device__ __forceinline__ BSplit bg_split(const Params& p, const BGemm& g, int cta, int G) {
   int total;
   switch (g.kind) {
     case BK_QKV: total = QKV_ROWS / WBOX; break;
@@ -78,8 +98,27 @@ __device__ __forceinline__ void bg_blocks(const Params& p, const BGemm& g, int c
     case BK_HEAD: total = (g.hidx == 0 ? p.vocab : p.cp_vocab) / WBOX; break;
     default: total = HID / WBOX; break;
   }
-  b0 = split_lo(total, G, cta);
-  nb = split_lo(total, G, cta + 1) - b0;
+  // o_proj and down (1024 rows, K = 2048 / 3072): 16 row blocks of 64 rows, K split over the
+  // other CTAs; the rest: ceil(blocks / CTAs) blocks per CTA, no split
+  const bool ksplit = g.kind == BK_O || g.kind == BK_D;
+  const int bpc = ksplit ? 4 : (total + G - 1) / G;
+  const int R = total / bpc;
+  const int nks = (g.kind == BK_O ? QSZ : g.kind == BK_D ? INTER : HID) / (KSUB * NSUB);
+  int nk = ksplit ? G / R : 1;
+  nk = nk < 1 ? 1 : (nk > nks ? nks : nk);
+  BSplit s;
+  s.nk = nk;
+  if (cta < R * nk) {
+    s.rb = cta / nk;
+    s.kspl = cta - s.rb * nk;
+    s.b0 = s.rb * bpc;
+    s.nb = bpc;
+    s.ks0 = split_lo(nks, nk, s.kspl);
+    s.ks1 = split_lo(nks, nk, s.kspl + 1);
+  } else {
+    s.rb = s.kspl = s.b0 = s.nb = s.ks0 = s.ks1 = 0;
+  }
+  return s;
 }
 __device__ __forceinline__ int bg_N(int kind, int nb) { return (kind == BK_GU ? 2 : 1) * WBOX * nb; }
 
@@ -143,23 +182,25 @@ __device__ void b_producer(const Params& p, Smem& sm, int cta, int G) {
   uint32_t m = 0;
   int* err = p.w.err;
   b_walk(p, [&](const BGemm& g) -> bool {
-    int b0, nb;
-    bg_blocks(p, g, cta, G, b0, nb);
+    const BSplit sp = bg_split(p, g, cta, G);
+    const int b0 = sp.b0, nb = sp.nb;
     if (nb == 0) return true;
-    const int N = bg_N(g.kind, nb), nks = bg_K(g.kind) / KSTEP, nbox = N / WBOX;
-    for (int ks = 0; ks < nks; ++ks, ++m) {
+    const int N = bg_N(g.kind, nb), nbox = N / WBOX;
+    for (int ks = sp.ks0; ks < sp.ks1; ++ks, ++m) {
       const uint32_t slot = m % NWS, round = m / NWS;
-      if (!mbar_wait(&sm.bbar[BB_WEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
+      if (!mbar_spin(&sm.bbar[BB_WEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
         if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
         return false;
       }
-      mbar_arrive_expect_tx(&sm.bbar[BB_WFULL + slot], static_cast<uint32_t>(N * 128));
+      mbar_arrive_expect_tx(&sm.bbar[BB_WFULL + slot], static_cast<uint32_t>(NSUB * N * 128));
       for (int i = 0; i < nbox; ++i) {
         const uint8_t* map;
         int y;
         bg_wbox(p, g, b0, nb, i, map, y);
-        if (ks == 0) tensormap_acquire(map);   // the host's copy of the map, before its first use
-        tma_load_2d(wring + slot * WS_BYTES + i * (WBOX * 128), map, ks * KSTEP, y, &sm.bbar[BB_WFULL + slot]);
+        if (ks == sp.ks0) tensormap_acquire(map);   // the host's copy of the map, before its first use
+        for (int a = 0; a < NSUB; ++a)
+          tma_load_2d(wring + slot * WS_BYTES + a * (N * 128) + i * (WBOX * 128), map, ks * KSTEP + a * KSUB, y,
+                      &sm.bbar[BB_WFULL + slot]);
       }
     }
     return true;
@@ -167,23 +208,60 @@ __device__ void b_producer(const Params& p, Smem& sm, int cta, int G) {
   // drain: no box may still be landing in shared memory when the CTA exits
   int zero = 0;
   for (uint32_t i = (m > NWS ? m - NWS : 0u); i < m; ++i)
-    mbar_wait(&sm.bbar[BB_WFULL + i % NWS], (i / NWS) & 1u, &zero);
+    mbar_spin(&sm.bbar[BB_WFULL + i % NWS], (i / NWS) & 1u, &zero);
 }
 
 // ------------------------------------------------------------------------------------------
-// MMA warp (one thread): activation boxes + tcgen05.mma of every GEMM stage.
+// Activation-loader warp (one thread): after each GEMM stage's grid barrier, the A planes of
+// every (K step, 64-token tile) into the 6-slot ring.
+// ------------------------------------------------------------------------------------------
+__device__ void b_aloader(const Params& p, Smem& sm, int cta, int G) {
+  uint8_t* aring = reinterpret_cast<uint8_t*>(sm.ring) + NWS * WS_BYTES;
+  uint32_t na = 0, n = 0;
+  int* err = p.w.err;
+  for (int b = 0; b < 2; ++b) tensormap_acquire(bmap(p, bmap_abuf(p, b, false)));
+  b_walk(p, [&](const BGemm& g) -> bool {
+    const BSplit sp = bg_split(p, g, cta, G);
+    if (sp.nb == 0) return true;
+    const int ntiles = (g.T + 63) >> 6;
+    const uint8_t* amap = bmap(p, bmap_abuf(p, bg_abuf(g.kind), false));
+    // the consumers arrive on GO after the stage's grid barrier: the A planes are complete
+    if (!mbar_spin(&sm.bbar[BB_GO], n & 1u, &sm.abort)) {
+      if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_FULL_TIMEOUT);
+      return false;
+    }
+    ++n;
+    fence_proxy_async_global();
+    for (int ks = sp.ks0; ks < sp.ks1; ++ks)
+      for (int j = 0; j < ntiles; ++j, ++na) {
+        const uint32_t slot = na % NAS, round = na / NAS;
+        if (!mbar_spin(&sm.bbar[BB_AEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
+          if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+          return false;
+        }
+        mbar_arrive_expect_tx(&sm.bbar[BB_AFULL + slot], static_cast<uint32_t>(AS_BYTES));
+        for (int a = 0; a < NSUB; ++a) {
+          uint8_t* dst = aring + slot * AS_BYTES + a * ASUB_BYTES;
+          tma_load_2d(dst, amap, ks * KSTEP + a * KSUB, 64 * j, &sm.bbar[BB_AFULL + slot]);
+          tma_load_2d(dst + APLANE_BYTES, amap, ks * KSTEP + a * KSUB, TBMAX + 64 * j, &sm.bbar[BB_AFULL + slot]);
+        }
+      }
+    return true;
+  });
+  int zero = 0;
+  for (uint32_t i = (na > NAS ? na - NAS : 0u); i < na; ++i)
+    mbar_spin(&sm.bbar[BB_AFULL + i % NAS], (i / NAS) & 1u, &zero);
+}
+
+// ------------------------------------------------------------------------------------------
+// MMA warp (one thread): tcgen05.mma of every GEMM stage.
 // ------------------------------------------------------------------------------------------
 __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
-  uint8_t* aring = reinterpret_cast<uint8_t*>(sm.ring) + NWS * WS_BYTES;
-  const uint32_t wbase = smem_u32(sm.ring), abase = smem_u32(aring);
+  const uint32_t wbase = smem_u32(sm.ring), abase = wbase + NWS * WS_BYTES;
   const uint32_t tmem = sm.tmem_base;
-  uint32_t m = 0, na = 0, ua = 0, n = 0;
+  uint32_t m = 0, ua = 0, n = 0;
   bool any = false;
   int* err = p.w.err;
-  for (int b = 0; b < 2; ++b) {
-    tensormap_acquire(bmap(p, bmap_abuf(p, b, false)));
-    tensormap_acquire(bmap(p, bmap_abuf(p, b, true)));
-  }
   auto fail_mma = [&](int code) {
     if (!*reinterpret_cast<volatile int*>(&sm.abort)) {
       set_error(err, code);
@@ -191,80 +269,92 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
     }
   };
   b_walk(p, [&](const BGemm& g) -> bool {
-    int b0, nb;
-    bg_blocks(p, g, cta, G, b0, nb);
-    if (nb == 0) return true;
-    const int N = bg_N(g.kind, nb), nks = bg_K(g.kind) / KSTEP;
-    const bool big = g.T > 64;
+    const BSplit sp = bg_split(p, g, cta, G);
+    if (sp.nb == 0) return true;
+    const int N = bg_N(g.kind, sp.nb), nks = sp.ks1 - sp.ks0, ntiles = (g.T + 63) >> 6;
     const uint32_t idesc = umma_idesc_bf16(128, N);
-    const uint8_t* amap = bmap(p, bmap_abuf(p, bg_abuf(g.kind), big));
-    const uint32_t abytes = 2u * (big ? 128u : 64u) * 128u;
-    // the consumers arrive on GO after the stage's grid barrier: the A planes are complete
-    if (!mbar_wait(&sm.bbar[BB_GO], n & 1u, &sm.abort)) {
-      fail_mma(DEV_ERR_FULL_TIMEOUT);
-      return false;
-    }
-    fence_proxy_async_global();
+    // profiling (CTA 0, dbg_marks set), dbg_marks[8192 + 8 n]: accumulator free, first
+    // activation slot ready, last MMA issued; the consumers add GO, D ready, epilogue done,
+    // barrier passed
+    const bool prof = p.dbg_marks != nullptr && cta == 0 && static_cast<int>(8192 + 8 * n + 7) < p.dbg_marks_len;
+    unsigned long long tw = 0, ta = 0, t_first = 0;
+    long long cyc_fence = 0, cyc_mma = 0, cyc_commit = 0;
     // the previous stage's epilogue has read D
-    if (!mbar_wait(&sm.bbar[BB_ACCEMPTY], (n & 1u) ^ 1u, &sm.abort)) {
+    if (!mbar_spin(&sm.bbar[BB_ACCEMPTY], (n & 1u) ^ 1u, &sm.abort)) {
       fail_mma(DEV_ERR_FULL_TIMEOUT);
       return false;
     }
     tc_fence_after();
-    auto load_a = [&](int ks) -> bool {
-      const uint32_t slot = na % NAS, round = na / NAS;
-      if (!mbar_wait(&sm.bbar[BB_AEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) return false;
-      mbar_arrive_expect_tx(&sm.bbar[BB_AFULL + slot], abytes);
-      uint8_t* dst = aring + slot * AS_BYTES;
-      tma_load_2d(dst, amap, ks * KSTEP, 0, &sm.bbar[BB_AFULL + slot]);
-      tma_load_2d(dst + APLANE_BYTES, amap, ks * KSTEP, TBMAX, &sm.bbar[BB_AFULL + slot]);
-      ++na;
-      return true;
-    };
-    int ka = 0;
-    for (; ka < nks && ka < NAS; ++ka)
-      if (!load_a(ka)) {
-        fail_mma(DEV_ERR_EMPTY_TIMEOUT);
-        return false;
-      }
-    for (int ks = 0; ks < nks; ++ks) {
-      const uint32_t ws = m % NWS, wr = m / NWS, as = ua % NAS, ar = ua / NAS;
-      if (!mbar_wait(&sm.bbar[BB_WFULL + ws], wr & 1u, &sm.abort) ||
-          !mbar_wait(&sm.bbar[BB_AFULL + as], ar & 1u, &sm.abort)) {
+    const unsigned long long t_start = prof ? globaltimer_ns() : 0ull;
+    for (int ks = 0; ks < nks; ++ks) {   // ks: index within this CTA's K slice
+      const uint32_t ws = m % NWS, wr = m / NWS;
+      unsigned long long t0 = prof ? globaltimer_ns() : 0ull;
+      if (!mbar_spin(&sm.bbar[BB_WFULL + ws], wr & 1u, &sm.abort)) {
         fail_mma(DEV_ERR_FULL_TIMEOUT);
         return false;
       }
-      tc_fence_after();
-      const uint32_t wa = wbase + ws * WS_BYTES, aa = abase + as * AS_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < KSTEP / 16; ++kk) {
-        const uint64_t bd = umma_desc_sw128(wa + kk * 32);
-        tc_mma_bf16(tmem, umma_desc_sw128(aa + kk * 32), bd, idesc, (ks | kk) != 0 ? 1u : 0u);
-        tc_mma_bf16(tmem, umma_desc_sw128(aa + APLANE_BYTES + kk * 32), bd, idesc, 1u);
-      }
-      any = true;
-      tc_commit(&sm.bbar[BB_WEMPTY + ws]);
-      tc_commit(&sm.bbar[BB_AEMPTY + as]);
-      ++m;
-      ++ua;
-      if (ka < nks) {
-        if (!load_a(ka)) {
-          fail_mma(DEV_ERR_EMPTY_TIMEOUT);
+      if (prof && ks > 0) tw += globaltimer_ns() - t0;
+      const uint32_t wa = wbase + ws * WS_BYTES;
+      for (int j = 0; j < ntiles; ++j, ++ua) {
+        const uint32_t as = ua % NAS, ar = ua / NAS;
+        t0 = prof ? globaltimer_ns() : 0ull;
+        if (!mbar_spin(&sm.bbar[BB_AFULL + as], ar & 1u, &sm.abort)) {
+          fail_mma(DEV_ERR_FULL_TIMEOUT);
           return false;
         }
-        ++ka;
+        if (prof) {
+          if (ks > 0) ta += globaltimer_ns() - t0;
+          if (t_first == 0ull) t_first = globaltimer_ns();
+        }
+        long long c0 = prof ? clock64() : 0;
+        tc_fence_after();
+        long long c1 = prof ? clock64() : 0;
+        const uint32_t aa = abase + as * AS_BYTES;
+        // one M = 128 MMA covers both planes: A rows 0..63 = hi, 64..127 = lo of the tile's tokens
+        const uint32_t dt = tmem + j * NCHAIN * DCOLS;
+#pragma unroll
+        for (int a = 0; a < NSUB; ++a) {
+          const uint32_t acc = (ks != 0 || a != 0) ? 1u : 0u;   // the first use of each chain overwrites
+#pragma unroll
+          for (int kk = 0; kk < KSUB / 16; ++kk)
+            tc_mma_bf16(dt + kk * DCOLS, umma_desc_sw128(aa + a * ASUB_BYTES + kk * 32),
+                        umma_desc_sw128(wa + a * (N * 128) + kk * 32), idesc, acc);
+        }
+        long long c2 = prof ? clock64() : 0;
+        any = true;
+        tc_commit(&sm.bbar[BB_AEMPTY + as]);
+        long long c3 = prof ? clock64() : 0;
+        if (prof) {
+          cyc_fence += c1 - c0;
+          cyc_mma += c2 - c1;
+          cyc_commit += c3 - c2;
+        }
       }
+      long long c4 = prof ? clock64() : 0;
+      tc_commit(&sm.bbar[BB_WEMPTY + ws]);
+      if (prof) cyc_commit += clock64() - c4;
+      ++m;
     }
     tc_commit(&sm.bbar[BB_ACCFULL]);
+    if (prof) {
+      p.dbg_marks[8192 + 8 * n + 0] = t_start;
+      p.dbg_marks[8192 + 8 * n + 1] = t_first;
+      p.dbg_marks[8192 + 8 * n + 2] = globaltimer_ns();
+      p.dbg_marks[8192 + 8 * n + 7] = (tw << 32) | (ta & 0xFFFFFFFFull);
+      if (static_cast<int>(12288 + 4 * n + 3) < p.dbg_marks_len) {
+        p.dbg_marks[12288 + 4 * n + 0] = cyc_fence;
+        p.dbg_marks[12288 + 4 * n + 1] = cyc_mma;
+        p.dbg_marks[12288 + 4 * n + 2] = cyc_commit;
+        p.dbg_marks[12288 + 4 * n + 3] = nks;
+      }
+    }
     ++n;
     return true;
   });
-  // drain: activation boxes still in flight, then every issued MMA
-  int zero = 0;
-  for (uint32_t i = ua; i < na; ++i) mbar_wait(&sm.bbar[BB_AFULL + i % NAS], (i / NAS) & 1u, &zero);
-  if (any) {
+  if (any) {   // every issued MMA done before the accumulator is freed
+    int zero = 0;
     tc_commit(&sm.bbar[BB_DRAIN]);
-    mbar_wait(&sm.bbar[BB_DRAIN], 0u, &zero);
+    mbar_spin(&sm.bbar[BB_DRAIN], 0u, &zero);
   }
 }
 
@@ -287,31 +377,176 @@ __device__ __forceinline__ float b_rstd(const unsigned long long* ssq, int t, fl
   return rms_scale(s, HID, eps);
 }
 
-// Consumer side of one GEMM stage: release the MMA warp, wait for D, run the epilogue on the
-// token lanes (epi(t, taddr, b0, nb, N), all lanes of warps 0..3 taking part in the tensor-memory
-// loads), free D, grid barrier.
+// Columns [c, c + 16) of D for this thread's token: the four chains added in a fixed order.
+__device__ __forceinline__ void b_ld16(uint32_t taddr, int c, float (&v)[16]) {
+  float a[16], b[16], d[16];
+  tmem_ld16(taddr + c, v);
+  tmem_ld16(taddr + DCOLS + c, a);
+  tmem_ld16(taddr + 2 * DCOLS + c, b);
+  tmem_ld16(taddr + 3 * DCOLS + c, d);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = (v[i] + a[i]) + (b[i] + d[i]);
+}
+
+// Columns [c, c + 16) of D for token t: hi lanes (chains added) + the lo lanes staged in smem.
+// hilo_store of 16 consecutive columns (col0 a multiple of 16): 32-byte stores per plane.
+__device__ __forceinline__ void hilo_store16(bf16* buf, int t, int col0, const float (&v)[16]) {
+  uint32_t hi[8], lo[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bf16 h0 = __float2bfloat16_rn(v[2 * i]), h1 = __float2bfloat16_rn(v[2 * i + 1]);
+    const bf16 l0 = __float2bfloat16_rn(v[2 * i] - __bfloat162float(h0));
+    const bf16 l1 = __float2bfloat16_rn(v[2 * i + 1] - __bfloat162float(h1));
+    hi[i] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+    lo[i] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+  }
+  uint4* ph = reinterpret_cast<uint4*>(buf + static_cast<size_t>(t) * ABUF_LD + col0);
+  uint4* pl = reinterpret_cast<uint4*>(buf + static_cast<size_t>(TBMAX + t) * ABUF_LD + col0);
+  ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  ph[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+  pl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  pl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+}
+// 16 consecutive fp32 from global (L2) / bf16 weights as fp32.
+__device__ __forceinline__ void ld16_f32(const float* src, float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(src + i));
+    v[i] = a.x; v[i + 1] = a.y; v[i + 2] = a.z; v[i + 3] = a.w;
+  }
+}
+__device__ __forceinline__ void ld16_bf16(const bf16* src, float (&v)[16]) {
+  const uint4 a = reinterpret_cast<const uint4*>(src)[0], b = reinterpret_cast<const uint4*>(src)[1];
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = bf16_lo(w[i]);
+    v[2 * i + 1] = bf16_hi(w[i]);
+  }
+}
+__device__ __forceinline__ void st16_f32(float* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) __stcg(reinterpret_cast<float4*>(dst + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+}
+
+// Columns [c, c + 16) of D for the thread's token. TMEM mode: the hi lanes (chains added) + the
+// lo lanes staged in shared memory. Summed mode (K split): the row of the slices' sum.
+struct BAcc {
+  uint32_t taddr;      // this thread's hi lane, tile base column
+  const float* lo;     // staged lo lane row of this token
+  const float* y;      // summed row of this token, or nullptr
+  __device__ __forceinline__ void ld16(int c, float (&v)[16]) const {
+    if (y != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = y[c + i];
+      return;
+    }
+    b_ld16(taddr, c, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += lo[c + i];
+  }
+};
+
+// Consumer side of one GEMM stage: release the activation loader, wait for D, stage the lo
+// lanes (warps 2, 3 of each 64-token tile) in shared memory, then on the hi lanes (warps 0, 1 of
+// tile 0 and 4, 5 of tile 1, all lanes taking part in the tensor-memory loads):
+//   * one K slice: the epilogue epi(t, acc, b0, nb, N) directly;
+//   * K split: the slice's partial D rows to global memory; the last CTA of the row block
+//     (counter) sums the slices in slice order and runs the epilogue.
+// Then free D and the grid barrier.
 template <class EPI>
 __device__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, EPI&& epi) {
-  int b0, nb;
-  bg_blocks(p, g, cs.cta, cs.G, b0, nb);
-  if (nb > 0) {
-    const int N = bg_N(g.kind, nb);
-    if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_GO]);
-    if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
-      if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
+  const BSplit sp = bg_split(p, g, cs.cta, cs.G);
+  const bool prof = p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0 &&
+                    static_cast<int>(8192 + 8 * gemm_n + 7) < p.dbg_marks_len;
+  if (sp.nb == 0) return grid_sync(p, sm, cs);
+  const int N = bg_N(g.kind, sp.nb);
+  if (prof) p.dbg_marks[8192 + 8 * gemm_n + 3] = globaltimer_ns();
+  if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_GO]);
+  bool freed = false;
+  if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
+    if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
+  } else {
+    if (prof) p.dbg_marks[8192 + 8 * gemm_n + 4] = globaltimer_ns();
+    tc_fence_after();
+    const int q = cs.warp & 3, j = cs.warp >> 2;   // lane quarter, 64-token tile
+    float* ylo = sm.xs;                            // [2][64][YLO_STRIDE]
+    const uint32_t tq = sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * NCHAIN * DCOLS;
+    if (j < 2 && q >= 2 && 64 * j + 32 * (q - 2) < g.T) {
+      float* row = ylo + (j * 64 + 32 * (q - 2) + cs.lane) * YLO_STRIDE;
+      for (int c = 0; c < N; c += 16) {
+        float v[16];
+        b_ld16(tq, c, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) row[c + i] = v[i];
+      }
+    }
+    named_sync(1, NCT);
+    const bool mine = j < 2 && q < 2 && 64 * j + 32 * q < g.T;
+    const int t = 64 * j + 32 * q + cs.lane;
+    const BAcc dacc{tq, ylo + (j * 64 + 32 * q + cs.lane) * YLO_STRIDE, nullptr};
+    if (sp.nk == 1) {
+      if (mine) epi(t, dacc, sp.b0, sp.nb, N);
+      tc_fence_before();
     } else {
-      tc_fence_after();
-      if (cs.warp < 4 && 32 * cs.warp < g.T) {
-        const int t = 32 * cs.warp + cs.lane;
-        epi(t, sm.tmem_base + (static_cast<uint32_t>(32 * cs.warp) << 16), b0, nb, N);
+      if (mine) {
+        float* dst = p.bw.kpart + (static_cast<size_t>(cs.cta) * TBMAX + t) * DCOLS;
+        for (int c = 0; c < N; c += 16) {
+          float v[16];
+          dacc.ld16(c, v);
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            __stcg(reinterpret_cast<float4*>(dst + c + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+        }
       }
       tc_fence_before();
+      named_sync(1, NCT);
+      if (cs.tid == 0) {
+        mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
+        __threadfence();
+        const uint32_t old = atomicAdd(p.bw.kcnt + sp.rb, 1u);
+        const bool last = old == static_cast<uint32_t>(sp.nk - 1);
+        if (last) atomicExch(p.bw.kcnt + sp.rb, 0u);
+        sm.bcast[0] = last ? 1 : 0;
+        __threadfence();
+      }
+      freed = true;
+      named_sync(1, NCT);
+      if (sm.bcast[0]) {
+        float* y = sm.xs;   // [T][YLO_STRIDE]: the slices' sum (the lo staging is no longer read)
+        const float* base = p.bw.kpart + static_cast<size_t>(sp.rb * sp.nk) * TBMAX * DCOLS;
+        const int n4 = N / 4;
+        for (int e = cs.tid; e < g.T * n4; e += NCT) {
+          const int tt = e / n4, c = 4 * (e - tt * n4);
+          const float* src = base + static_cast<size_t>(tt) * DCOLS + c;
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int k0 = 0; k0 < sp.nk; k0 += 4) {   // four slices' loads in flight, added in order
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (k0 + k < sp.nk)
+                v[k] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(k0 + k) * TBMAX * DCOLS));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (k0 + k < sp.nk) {
+                a.x += v[k].x; a.y += v[k].y; a.z += v[k].z; a.w += v[k].w;
+              }
+          }
+          float* d = y + tt * YLO_STRIDE + c;
+          d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
+        }
+        named_sync(1, NCT);
+        if (mine) epi(t, BAcc{0u, nullptr, y + t * YLO_STRIDE}, sp.b0, sp.nb, N);
+      }
     }
-    gemm_n++;
-    named_sync(1, NCT);
-    if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);
   }
-  return grid_sync(p, sm, cs);
+  named_sync(1, NCT);
+  if (prof) p.dbg_marks[8192 + 8 * gemm_n + 5] = globaltimer_ns();
+  if (cs.tid == 0 && !freed) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);
+  const bool ok = grid_sync(p, sm, cs);
+  if (prof) p.dbg_marks[8192 + 8 * gemm_n + 6] = globaltimer_ns();
+  gemm_n++;
+  return ok;
 }
 
 // Sums-of-squares buffer written by the next producing stage (INPUT, O, down); that stage also
@@ -453,17 +688,15 @@ __device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int l
   // ---- QKV (deferred input norm)
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, [&](int t, uint32_t taddr, int b0, int nb, int N) {
+    if (!b_gemm(p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
           const float rs = t < T ? b_rstd(ssq, t, eps) : 0.f;
           for (int c0 = 0; c0 < N; c0 += 16) {
             float v[16];
-            tmem_ld16(taddr + c0, v);
+            acc.ld16(c0, v);
             if (t < T) {
-              float* dst = p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + WBOX * b0 + c0;
 #pragma unroll
-              for (int i = 0; i < 16; i += 4)
-                __stcg(reinterpret_cast<float4*>(dst + i),
-                       make_float4(v[i] * rs, v[i + 1] * rs, v[i + 2] * rs, v[i + 3] * rs));
+              for (int i = 0; i < 16; ++i) v[i] *= rs;
+              st16_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + WBOX * b0 + c0, v);
             }
           }
         }))
@@ -474,39 +707,47 @@ __device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int l
   // ---- o_proj + residual -> hmid, A planes of gate/up (post-attention norm), sums of squares
   {
     unsigned long long* ssq = b_ssq_next(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_O, li, 0, T}, gn, [&](int t, uint32_t taddr, int b0, int nb, int N) {
-          float v[16];
-          tmem_ld16(taddr, v);
-          if (t < T) {
-            const int r0 = WBOX * b0;
-            double ss = 0.0;
+    if (!b_gemm(p, sm, cs, BGemm{BK_O, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
+          double ss = 0.0;
+          for (int c0 = 0; c0 < N; c0 += 16) {
+            float v[16];
+            acc.ld16(c0, v);
+            if (t < T) {
+              const int r0 = WBOX * b0 + c0;
+              float res[16], wn[16], a[16];
+              ld16_f32(hin + t * HID + r0, res);
+              ld16_bf16(L->post_norm + r0, wn);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float hm = v[i] + __ldcg(hin + t * HID + r0 + i);
-              __stcg(p.bw.hmid + t * HID + r0 + i, hm);
-              hilo_store(p.bw.abuf[0], t, r0 + i, hm * __bfloat162float(L->post_norm[r0 + i]));
-              ss = fma(static_cast<double>(hm), static_cast<double>(hm), ss);
+              for (int i = 0; i < 16; ++i) {
+                v[i] += res[i];
+                a[i] = v[i] * wn[i];
+                ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+              }
+              st16_f32(p.bw.hmid + t * HID + r0, v);
+              hilo_store16(p.bw.abuf[0], t, r0, a);
             }
-            b_ssq_add(ssq, t, ss);
           }
+          if (t < T) b_ssq_add(ssq, t, ss);
         }))
       return false;
   }
   // ---- gate/up + SiLU (deferred post-attention norm) -> A planes of down
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_GU, li, 0, T}, gn, [&](int t, uint32_t taddr, int b0, int nb, int N) {
+    if (!b_gemm(p, sm, cs, BGemm{BK_GU, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
           const float rs = t < T ? b_rstd(ssq, t, eps) : 0.f;
           for (int c0 = 0; c0 < WBOX * nb; c0 += 16) {
             float gv[16], uv[16];
-            tmem_ld16(taddr + c0, gv);
-            tmem_ld16(taddr + WBOX * nb + c0, uv);
+            acc.ld16(c0, gv);
+            acc.ld16(WBOX * nb + c0, uv);
             if (t < T) {
+              float m[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
                 const float gg = gv[i] * rs, uu = uv[i] * rs;
-                hilo_store(p.bw.abuf[1], t, WBOX * b0 + c0 + i, (gg / (1.0f + expf(-gg))) * uu);
+                m[i] = (gg / (1.0f + expf(-gg))) * uu;
               }
+              hilo_store16(p.bw.abuf[1], t, WBOX * b0 + c0, m);
             }
           }
         }))
@@ -515,22 +756,32 @@ __device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int l
   // ---- down + residual -> layer output, A planes of the next layer (its input norm), sums
   {
     unsigned long long* ssq = b_ssq_next(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_D, li, 0, T}, gn, [&](int t, uint32_t taddr, int b0, int nb, int N) {
-          float v[16];
-          tmem_ld16(taddr, v);
-          if (t < T) {
-            const int r0 = WBOX * b0;
-            double ss = 0.0;
+    if (!b_gemm(p, sm, cs, BGemm{BK_D, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
+          double ss = 0.0;
+          for (int c0 = 0; c0 < N; c0 += 16) {
+            float v[16];
+            acc.ld16(c0, v);
+            if (t < T) {
+              const int r0 = WBOX * b0 + c0;
+              float res[16], a[16];
+              ld16_f32(p.bw.hmid + t * HID + r0, res);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float hv = v[i] + __ldcg(p.bw.hmid + t * HID + r0 + i);
-              if (!cp) hv = round_bf16(hv);
-              __stcg(hout + t * HID + r0 + i, hv);
-              if (next_norm) hilo_store(p.bw.abuf[0], t, r0 + i, hv * __bfloat162float(next_norm[r0 + i]));
-              ss = fma(static_cast<double>(hv), static_cast<double>(hv), ss);
+              for (int i = 0; i < 16; ++i) {
+                v[i] += res[i];
+                if (!cp) v[i] = round_bf16(v[i]);
+                ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+              }
+              st16_f32(hout + t * HID + r0, v);
+              if (next_norm) {
+                float wn[16];
+                ld16_bf16(next_norm + r0, wn);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) a[i] = v[i] * wn[i];
+                hilo_store16(p.bw.abuf[0], t, r0, a);
+              }
             }
-            b_ssq_add(ssq, t, ss);
           }
+          if (t < T) b_ssq_add(ssq, t, ss);
         }))
       return false;
   }
@@ -560,7 +811,7 @@ __device__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hi
   unsigned long long* amax = p.bw.amax + slot * TBMAX;
   if (cs.cta == 0)
     for (int t = cs.tid; t < TBMAX; t += NCT) __stcg(p.bw.amax + (slot ^ 1) * TBMAX + t, 0ull);
-  return b_gemm(p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, [&](int t, uint32_t taddr, int b0, int nb, int N) {
+  return b_gemm(p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
     SampleCfg c = cfg;
     if (t < p.nb && hidx == 0) {
       c.seen = (c.penalty != 1.f) ? p.bs[t].st->seen : nullptr;
@@ -570,7 +821,7 @@ __device__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hi
     unsigned long long best = 0ull;
     for (int c0 = 0; c0 < N; c0 += 16) {
       float v[16];
-      tmem_ld16(taddr + c0, v);
+      acc.ld16(c0, v);
       if (t < p.nb) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -850,6 +1101,9 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     __syncwarp();
   } else if (warp == NCW + 1) {
     if ((tid & 31) == 0) b_mma(p, sm, blockIdx.x, gridDim.x);
+    __syncwarp();
+  } else if (warp == NCW + 2) {
+    if ((tid & 31) == 0) b_aloader(p, sm, blockIdx.x, gridDim.x);
     __syncwarp();
   } else {
     Cons cs;

@@ -1956,6 +1956,8 @@ size_t bwork_bytes() {
   n += sizeof(unsigned long long) * 5 * TBMAX;                       // ssq, amax
   n += sizeof(uint32_t) * TBMAX * NKVH;                              // att_cnt
   n += sizeof(int32_t) * BMAX * NGROUPS;                             // tok
+  n += sizeof(uint32_t) * BKCTAS;                                    // kcnt
+  n += sizeof(float) * BKCTAS * TBMAX * 64 + 256;                    // kpart
   n += 2 * sizeof(bf16) * 2 * TBMAX * ABUF_LD;                      // abuf
   n += sizeof(float) * TBMAX * HID * 3;                              // x, hb[2]
   n += sizeof(float) * TBMAX * QKV_ROWS;                             // qkv
@@ -1972,6 +1974,7 @@ void bwork_carve(void* base, BWork* w) {
   w->amax = reinterpret_cast<unsigned long long*>(c); c += sizeof(unsigned long long) * 2 * TBMAX;
   w->att_cnt = reinterpret_cast<uint32_t*>(c); c += sizeof(uint32_t) * TBMAX * NKVH;
   w->tok = reinterpret_cast<int32_t*>(c); c += sizeof(int32_t) * BMAX * NGROUPS;
+  w->kcnt = reinterpret_cast<uint32_t*>(c); c += sizeof(uint32_t) * BKCTAS;
   c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c) + 255) & ~static_cast<uintptr_t>(255));
   for (int i = 0; i < 2; ++i) {
     w->abuf[i] = reinterpret_cast<bf16*>(c);
@@ -1985,6 +1988,7 @@ void bwork_carve(void* base, BWork* w) {
   w->qkv = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * QKV_ROWS;
   w->hmid = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * HID;
   w->logits = reinterpret_cast<float*>(c); c += sizeof(float) * BMAX * VMAX;
+  w->kpart = reinterpret_cast<float*>(c); c += sizeof(float) * BKCTAS * TBMAX * 64;
   w->prt = reinterpret_cast<float*>(c);
 }
 

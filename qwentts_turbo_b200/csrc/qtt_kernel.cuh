@@ -34,7 +34,7 @@ constexpr int NSLOTS = 7;
 constexpr int NCW = 12;                    // consumer warps
 constexpr int NCT = NCW * 32;              // consumer threads
 constexpr int NTHREADS = NCT + 32;         // + one producer warp
-constexpr int NTHREADS_B = NTHREADS + 32;  // batched kernel: + one MMA warp
+constexpr int NTHREADS_B = NTHREADS + 64;  // batched kernel: + an MMA warp and an activation-loader warp
 constexpr int NTMAX = 2;                   // tokens per pass (2 = code-predictor prefill pair)
 constexpr int MAXPART = 256;               // partial-sum units per stage per CTA
 constexpr int ATT_TARGET = 24;             // attention positions per work item (target)
@@ -150,7 +150,10 @@ struct BWork {
   unsigned long long* ssq; // [3][TBMAX] sums of squares for the next RMSNorm, fixed point 2^-32
   unsigned long long* amax;// [2][TBMAX] packed argmax of greedy heads
   int32_t* tok;            // [BMAX][NGROUPS] tokens of the frame
+  float* kpart;            // [BKCTAS][TBMAX][64] K-split GEMM partials, one block per CTA
+  uint32_t* kcnt;          // [BKCTAS] last-arriver counters of K-split row blocks
 };
+constexpr int BKCTAS = 160;               // most CTAs a batched launch may have
 size_t bwork_bytes();
 void bwork_carve(void* base, BWork* w);
 
