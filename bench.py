@@ -1,18 +1,23 @@
 #!/usr/bin/env python
 """Benchmark of the Qwen3-TTS per-frame decode on B200.
 
-Workload ("C3"): batch-1 frame loop of Qwen3-TTS-12Hz-0.6B with
-random-init bf16 weights (seed 0 backbone / seed 1 code predictor), a 200-token N(0,1) prefill
-context, 64 trailing-text rows, greedy decoding with EOS disabled. One step = one frame =
-code-predictor chain (15 weight sweeps) + 16-embedding combine + 28-layer backbone step +
-codec head + group-0 sampling, i.e. one launch of the persistent sm_100a kernel.
+Default workload ("C4"; per GPU of configs[4], "C5"): 64 independent
+utterances per GPU decoded together by the batched engine (qtt_batch_frames: one launch per
+frame of all 64, projections on tcgen05 tensor cores). Random-init bf16 weights (seed 0
+backbone / seed 1 code predictor), prefill contexts ~ U[100, 400] tokens of N(0,1) embeddings,
+64 trailing-text rows, temperature 0.9 / top-k 50 / repetition penalty 1.2 with a Philox stream
+per utterance, code predictor greedy (the reference's default), EOS masked so that every
+utterance decodes the same number of frames. One step = one frame of every utterance.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+The batch-1 frame loop ("C3": 200-token context, greedy) is measured too and reported under
+"bs1" (``--workload c3`` makes it the headline instead).
 
-N > 1 runs under torchrun, one rank per GPU, each rank decoding its own utterance (replicas,
-weak scaling, no collective on the decode path; codes are gathered to rank 0 afterwards).
-Rank 0 prints one JSON line. ``--impl reference`` times the reference algorithm on the host
-CPU cores (the oracle port of the reference's PyTorch path) on the same workload.
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload c4|c3]
+
+N > 1 runs under torchrun, one rank per GPU, each rank decoding its own utterances (weak
+scaling, no collective on the decode path; codes are gathered to rank 0 afterwards). Rank 0
+prints one JSON line. ``--impl reference`` times the reference algorithm on the host CPU cores
+(the oracle port of the reference's PyTorch path, one utterance at a time).
 """
 from __future__ import annotations
 
@@ -39,28 +44,49 @@ N_TRAILING = 64
 FALLBACK_HBM_GBS = 6650.0
 
 
+CTX_LO, CTX_HI = 100, 400     # C4 prefill contexts
+CTX_MID = (CTX_LO + CTX_HI) // 2
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("c4", "c3"), default="c4")
+    ap.add_argument("--batch", type=int, default=64, help="utterances per GPU (c4)")
+    ap.add_argument("--bs1-steps", type=int, default=100, help="frames of the batch-1 side measurement (c4)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
 
 def workload_config(args):
+    if args.workload == "c3":
+        return {
+            "workload": "C3: bs1 frame loop (15-step code predictor + combine + 28-layer backbone step + codec "
+                        "head + sampling), 200-token context, 64 trailing rows, greedy, EOS disabled",
+            "model": "Qwen3-TTS-12Hz-0.6B (random-init bf16)",
+            "global_batch": args.gpus,
+            "batch_per_gpu": 1,
+            "ctx": CTX,
+            "seq_len": CTX + args.warmup + args.steps,
+            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU",
+            "l2": "inputs larger than L2: 3.31 GB of weights streamed per frame (L2 126 MB)",
+        }
     return {
-        "workload": "C3: bs1 frame loop (15-step code predictor + combine + 28-layer backbone step + codec head "
-                    "+ sampling), 200-token context, 64 trailing rows, greedy, EOS disabled",
+        "workload": f"C4/C5: {args.batch} utterances per GPU decoded together (one launch per frame of all: "
+                    "15-step code predictor + combine + 28-layer backbone + codec head + sampling), prefill "
+                    f"ctx ~ U[{CTX_LO},{CTX_HI}], 64 trailing rows, T 0.9 / top-k 50 / repetition 1.2 with a "
+                    "Philox stream per utterance, code predictor greedy, EOS masked",
         "model": "Qwen3-TTS-12Hz-0.6B (random-init bf16)",
-        "global_batch": args.gpus,
-        "batch_per_gpu": 1,
-        "ctx": CTX,
-        "seq_len": CTX + args.warmup + args.steps,
-        "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU",
-        "l2": "inputs larger than L2: 3.31 GB of weights streamed per frame (L2 126 MB)",
+        "global_batch": args.gpus * args.batch,
+        "batch_per_gpu": args.batch,
+        "ctx": f"U[{CTX_LO},{CTX_HI}]",
+        "seq_len": CTX_HI + args.warmup + args.steps,
+        "parallelism": f"data parallel x{args.gpus} (independent utterances)" if args.gpus > 1 else "single GPU",
+        "l2": "inputs larger than L2: 3.31 GB of weights + KV streamed per frame (L2 126 MB)",
     }
 
 
@@ -127,9 +153,9 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic_per_frame():
+def ncu_traffic_per_frame(name="qtt_decode_kernel_frame_c3.txt"):
     """DRAM bytes per frame launch from the committed ncu summary (or None)."""
-    p = os.path.join(ROOT, "profiles", "qtt_decode_kernel_frame_c3.txt")
+    p = os.path.join(ROOT, "profiles", name)
     try:
         with open(p) as f:
             for line in f:
@@ -140,16 +166,18 @@ def ncu_traffic_per_frame():
     return None
 
 
-def cpu_frames_per_s(seconds: float, warmup: int = 1, max_frames: int | None = None, seed: int = 4):
-    """Oracle (CPU port of the reference path) frames/s on the C3 workload, all host threads."""
+def cpu_frames_per_s(seconds: float, warmup: int = 1, max_frames: int | None = None, seed: int = 4,
+                     sampled: bool = False, ctx: int = CTX):
+    """Oracle (CPU port of the reference path) frames/s, all host threads: the C3 loop, or with
+    ``sampled`` the C4 per-utterance loop (T 0.9 / top-k 50 / repetition 1.2, Philox draws)."""
     from oracle.qtt_oracle import Qwen3TTSOracle
     from qwentts_turbo_b200.weights import synthetic_weights
     from qwentts_turbo_b200.workloads import c3_inputs
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     w = synthetic_weights()
-    embeds, trailing, pad = c3_inputs(CTX, N_TRAILING, seed)
-    orc = Qwen3TTSOracle(w, max_seq=CTX + 2048)
+    embeds, trailing, pad = c3_inputs(ctx, N_TRAILING, seed)
+    orc = Qwen3TTSOracle(w, max_seq=ctx + 2048)
     del w
     # the oracle's generate() loop, frame by frame, with a time budget
     from oracle import qtt_oracle as O
@@ -159,6 +187,7 @@ def cpu_frames_per_s(seconds: float, warmup: int = 1, max_frames: int | None = N
     logits = orc.head_logits(orc.codec_head, h)
     logits[sup] = float("-inf")
     g0 = O.sample_token(logits, False, 0.9, 50, 1.0, eos)
+    hist = [g0]
     t_start = None
     timed = 0
     step = 0
@@ -171,7 +200,12 @@ def cpu_frames_per_s(seconds: float, warmup: int = 1, max_frames: int | None = N
         h = orc.backbone_step(orc.combine(groups, extra))
         logits = orc.head_logits(orc.codec_head, h)
         logits[sup] = float("-inf")
-        g0 = O.sample_token(logits, False, 0.9, 50, 1.0, None)
+        if sampled:
+            logits = O.apply_repetition_penalty(logits, hist, 1.2)
+            g0 = O.sample_token(logits, True, 0.9, 50, 1.0, eos, O.draw_u24(1234, step + 1, 0, 0))
+        else:
+            g0 = O.sample_token(logits, False, 0.9, 50, 1.0, None)
+        hist.append(g0)
         step += 1
         if t_start is not None:
             timed += 1
@@ -183,25 +217,36 @@ def cpu_frames_per_s(seconds: float, warmup: int = 1, max_frames: int | None = N
 
 
 # ------------------------------------------------------------------------------------------
+def cpu_sample_text(c4, timed, el, cores):
+    if c4:
+        return (f"{timed} frames of one utterance of the C4 loop (sampled, repetition 1.2) after a {CTX_MID}-token "
+                f"prefill, the mean C4 context ({el:.1f} s, fp32 torch oracle on {cores} host threads; the CPU path "
+                "decodes one utterance at a time, so its frames/s does not depend on the batch)")
+    return (f"{timed} frames of the C3 loop after a {CTX}-token prefill ({el:.1f} s, fp32 torch oracle on "
+            f"{cores} host threads)")
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
     budget = 60.0
-    fps, cores, timed, el = cpu_frames_per_s(budget, warmup=min(args.warmup, 2), max_frames=args.steps)
+    c4 = args.workload == "c4"
+    fps, cores, timed, el = cpu_frames_per_s(budget, warmup=min(args.warmup, 2), max_frames=args.steps,
+                                             sampled=c4, ctx=CTX_MID if c4 else CTX)
     line = {
         "impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus, "steps": timed,
         "warmup": min(args.warmup, 2), "ms_per_step": 1000.0 * el / timed, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args),
         "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{timed} frames of the C3 loop after a 200-token prefill ({el:.1f} s, "
-                                   f"fp32 torch on {cores} host threads)"},
+                         "sample": cpu_sample_text(c4, timed, el, cores)},
         "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, rank, world, local_rank):
+def run_c3(args, rank, world, local_rank, K, W):
+    """Batch-1 frame loop; returns rank 0's JSON fields (None on other ranks)."""
     import torch.distributed as dist
 
     from qwentts_turbo_b200 import _lib
@@ -213,7 +258,6 @@ def run_ours(args, rank, world, local_rank):
 
     dev = local_rank
     torch.cuda.set_device(dev)
-    K, W = args.steps, args.warmup
     max_seq = CTX + W + K + 8
     weights = synthetic_weights()
     dm = DeviceModel(weights, rope_rows=max_seq)
@@ -291,7 +335,7 @@ def run_ours(args, rank, world, local_rank):
 
     if rank != 0:
         eng.close()
-        return
+        return None
 
     # ---- roofline -------------------------------------------------------------------------
     wbytes = frame_weight_bytes()
@@ -322,11 +366,160 @@ def run_ours(args, rank, world, local_rank):
         "codes_gathered": n_codes,
     }
     eng.close()
+    return line
+
+
+def run_c4(args, rank, world, local_rank, K, W):
+    """Batched frame loop of args.batch utterances per GPU; returns rank 0's JSON fields."""
+    import torch.distributed as dist
+
+    from qwentts_turbo_b200 import _lib
+    from qwentts_turbo_b200.config import frame_weight_bytes, kv_read_bytes_per_frame
+    from qwentts_turbo_b200.dist import gather_codes, max_over_ranks
+    from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
+    from qwentts_turbo_b200.weights import synthetic_weights
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    B = args.batch
+    max_seq = CTX_HI + W + K + 8
+    weights = synthetic_weights()
+    dm = DeviceModel(weights, rope_rows=max_seq)
+    del weights
+    eng = Engine(dm, max_streams=B, max_seq=max_seq, max_frames=W + K + 1)
+    g = torch.Generator().manual_seed(4 + rank)
+    ctx = torch.randint(CTX_LO, CTX_HI + 1, (B,), generator=g).tolist()
+    embeds = [torch.randn(L, 1024, generator=g).to(torch.bfloat16) for L in ctx]
+    trailing = [torch.randn(N_TRAILING, 1024, generator=g).to(torch.bfloat16) for _ in range(B)]
+    pads = [torch.randn(1024, generator=g).to(torch.bfloat16) for _ in range(B)]
+    embeds_d = [e.cuda() for e in embeds]
+    trailing_d = [t.cuda() for t in trailing]
+    pads_d = [x.cuda() for x in pads]
+    sp = sampling_struct(do_sample=True, temperature=0.9, top_k=50, repetition_penalty=1.2,
+                         min_new_tokens=1 << 30, seed=1234 + rank)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident run: inputs already in HBM --------------------------------------
+    eng.batch_prefill(embeds_d, sp)
+    eng.batch_frames(W, trailing_d, pads_d, sp)
+    eng.check()
+    clocks = ClockSampler(dev)
+    time.sleep(0.3)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(stream)
+    eng.batch_frames(K, trailing_d, pads_d, sp)
+    e1.record(stream)
+    barrier()
+    t1 = time.time()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks.stop()
+    eng.check()
+    for s in range(B):
+        st = eng.state(s)
+        assert st["frames"] == W + K and st["done"] == 0, (s, st)
+    codes = torch.stack([eng.codes(s)[: W + K].clone() for s in range(B)])   # [B, W+K, 16]
+
+    # ---- end to end through the C-ABI with host buffers: per frame the B text rows H2D from
+    # pinned memory, one qtt_batch_frames call, the B code rows D2H ------------------------
+    lib = _lib.load()
+    rows_h = torch.empty(K, B, 1024, dtype=torch.bfloat16).pin_memory()
+    for f in range(K):
+        for s in range(B):
+            step = W + f
+            rows_h[f, s] = trailing[s][step] if step < N_TRAILING else pads[s]
+    rows_d = torch.empty(B, 1024, dtype=torch.bfloat16, device="cuda")
+    codes_devs = [eng.codes(s) for s in range(B)]
+    codes_h = torch.empty(K, B, 16, dtype=torch.int32).pin_memory()
+    sh = stream.cuda_stream
+    spb = ctypes.byref(sp)
+    no_trail = (ctypes.c_void_p * B)()
+    zeros = (ctypes.c_int * B)(*([0] * B))
+    row_ptrs = (ctypes.c_void_p * B)(*[rows_d[s].data_ptr() for s in range(B)])
+
+    eng.batch_prefill(embeds_d, sp)
+    eng.batch_frames(W, trailing_d, pads_d, sp)
+    eng.check()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for f in range(K):
+        rows_d.copy_(rows_h[f], non_blocking=True)
+        rc = lib.qtt_batch_frames(eng.h, B, 1, no_trail, zeros, row_ptrs, spb, sh)
+        if rc != 0:
+            raise _lib.QTTError(rc, "qtt_batch_frames")
+        for s in range(B):
+            codes_h[f, s].copy_(codes_devs[s][W + f], non_blocking=True)
+    e3.record(stream)
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    eng.check()
+    assert torch.equal(codes_h, codes[:, W:].permute(1, 0, 2).cpu()), "e2e path produced different codes"
+
+    gathered = gather_codes(codes.reshape(-1, 16))
+    n_codes = sum(x.shape[0] for x in gathered) if gathered is not None else 0
+    if rank != 0:
+        eng.close()
+        return None
+
+    # ---- roofline: weights once per frame for the batch + every utterance's KV ----------
+    wbytes = frame_weight_bytes()
+    kv = sum(kv_read_bytes_per_frame(ctx[s] + W + f) for s in range(B) for f in range(K)) / K
+    bytes_per_frame = wbytes + kv
+    frame_s = ms / 1000.0 / K
+    achieved = bytes_per_frame / frame_s / 1e9
+    peak, peak_src = measured_hbm_peak()
+    # tensor work: every weight element meets every token's hi and lo operand (2 x 2 FLOP)
+    tflops = 4.0 * (wbytes / 2) * B / frame_s / 1e12
+    bstream_bytes = 80   # sizeof(qtt::BStream), copied H2D by every qtt_batch_frames call
+    line = {
+        "metric": METRIC, "value": world * B * K / (ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random-init weights, seeded N(0,1) inputs)",
+        "config": workload_config(args),
+        "frames_per_s_per_gpu": B * K / (ms / 1000.0),
+        "batch_frame_ms": ms / K,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "traffic": ncu_traffic_per_frame("qtt_batch_kernel_frame_c4.txt"),
+                     "algorithmic_bytes_per_launch": bytes_per_frame,
+                     "tensor_tflops": tflops,
+                     "kernel": "qtt_batch_kernel (1 launch per frame of all utterances)"},
+        "e2e": {"value": world * B * K / (ms_e2e / 1000.0), "unit": UNIT,
+                "h2d_bytes_per_step": B * 2048 + B * bstream_bytes, "d2h_bytes_per_step": B * 64,
+                "path": "qtt_batch_frames C-ABI per frame: pinned H2D of the B text rows, D2H of the B code rows"},
+        "gpu_launches": K,
+        "clocks": clocks.summary(t0, t1),
+        "codes_gathered": n_codes,
+    }
+    eng.close()
+    return line
+
+
+def run_ours(args, rank, world, local_rank):
+    if args.workload == "c3":
+        line = run_c3(args, rank, world, local_rank, args.steps, args.warmup)
+    else:
+        line = run_c4(args, rank, world, local_rank, args.steps, args.warmup)
+        if args.bs1_steps > 0:
+            bs1 = run_c3(args, rank, world, local_rank, args.bs1_steps, min(args.warmup, 3))
+            if line is not None:
+                line["bs1"] = {"workload": "C3 (batch-1 frame loop, 200-token context, greedy)",
+                               "frames_per_s": bs1["value"] / world, "frame_latency_us": bs1["frame_latency_us"],
+                               "rtf": bs1["rtf"], "e2e_frames_per_s": bs1["e2e"]["value"] / world,
+                               "hbm_frac": bs1["roofline"]["frac"], "steps": args.bs1_steps}
+    if line is None:
+        return
     if world == 1 and not args.no_cpu_baseline:
-        fps, cores, timed, el = cpu_frames_per_s(args.cpu_seconds)
+        c4 = args.workload == "c4"
+        fps, cores, timed, el = cpu_frames_per_s(args.cpu_seconds, sampled=c4, ctx=CTX_MID if c4 else CTX)
         line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": f"{timed} frames of the C3 loop after a 200-token prefill ({el:.1f} s, "
-                                          f"fp32 torch oracle on {cores} host threads)"}
+                                "sample": cpu_sample_text(c4, timed, el, cores)}
     print(json.dumps(line), flush=True)
 
 

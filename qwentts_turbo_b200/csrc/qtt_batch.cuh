@@ -18,9 +18,7 @@
 //   * D: fp32 in tensor memory, N = 16..64 columns. An activation slot holds a 64-token tile's
 //     hi plane in rows 0..63 and its lo plane in rows 64..127, so one M = 128 tcgen05.mma per
 //     K sub-step of 16 gives D lane t = W hi[t] and lane 64 + t = W lo[t]; the epilogue adds
-//     them: D = W (hi + lo), ~16 mantissa bits of the activations, close to an fp32 GEMV. The
-//     four K sub-steps of a K step go to four independent accumulators (added by the epilogue
-//     in a fixed order), so four MMAs can be in flight.
+//     them: D = W (hi + lo), ~16 mantissa bits of the activations, close to an fp32 GEMV.
 // The epilogue warps read D with tcgen05.ld (warp 4j + q owns tile j's token lanes 32q..32q+31,
 // one thread per token), apply the deferred RMSNorm scale and the stage's elementwise work, and
 // write the next GEMM's A planes. Sums of squares for the next RMSNorm are accumulated per token with
@@ -41,9 +39,9 @@ constexpr int APLANE_BYTES = 64 * 128;    // one plane of an activation atom: 64
 constexpr int ASUB_BYTES = 2 * APLANE_BYTES;  // hi plane, then lo plane
 constexpr int AS_BYTES = NSUB * ASUB_BYTES;
 constexpr int NAS = 3;
-constexpr int NCHAIN = 4;                 // independent accumulators per tile (see b_mma)
+constexpr int NCHAIN = 1;                 // accumulators per tile
 constexpr int DCOLS = 64;                 // tensor-memory columns of one accumulator (N <= 64)
-constexpr uint32_t TMEM_COLS = 2 * NCHAIN * DCOLS;   // 2 tiles x 4 chains x 64 columns = all 512
+constexpr uint32_t TMEM_COLS = 2 * NCHAIN * DCOLS;   // 2 tiles x 64 columns
 constexpr int BATT_SPAN = 96;             // backbone attention: positions per work item (target)
 // An M = 128 MMA reads the whole slot: rows 0..63 (hi plane) and 64..127 (lo plane).
 static_assert(NWS * WS_BYTES + NAS * AS_BYTES <= NSLOTS * SLOT_BYTES, "batched rings fit the ring region");
@@ -313,13 +311,11 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
         // one M = 128 MMA covers both planes: A rows 0..63 = hi, 64..127 = lo of the tile's tokens
         const uint32_t dt = tmem + j * NCHAIN * DCOLS;
 #pragma unroll
-        for (int a = 0; a < NSUB; ++a) {
-          const uint32_t acc = (ks != 0 || a != 0) ? 1u : 0u;   // the first use of each chain overwrites
+        for (int a = 0; a < NSUB; ++a)
 #pragma unroll
-          for (int kk = 0; kk < KSUB / 16; ++kk)
-            tc_mma_bf16(dt + kk * DCOLS, umma_desc_sw128(aa + a * ASUB_BYTES + kk * 32),
-                        umma_desc_sw128(wa + a * (N * 128) + kk * 32), idesc, acc);
-        }
+          for (int kk = 0; kk < KSUB / 16; ++kk)   // the first MMA of the slice overwrites D
+            tc_mma_bf16(dt, umma_desc_sw128(aa + a * ASUB_BYTES + kk * 32),
+                        umma_desc_sw128(wa + a * (N * 128) + kk * 32), idesc, (ks | a | kk) != 0 ? 1u : 0u);
         long long c2 = prof ? clock64() : 0;
         any = true;
         tc_commit(&sm.bbar[BB_AEMPTY + as]);
@@ -377,16 +373,8 @@ __device__ __forceinline__ float b_rstd(const unsigned long long* ssq, int t, fl
   return rms_scale(s, HID, eps);
 }
 
-// Columns [c, c + 16) of D for this thread's token: the four chains added in a fixed order.
-__device__ __forceinline__ void b_ld16(uint32_t taddr, int c, float (&v)[16]) {
-  float a[16], b[16], d[16];
-  tmem_ld16(taddr + c, v);
-  tmem_ld16(taddr + DCOLS + c, a);
-  tmem_ld16(taddr + 2 * DCOLS + c, b);
-  tmem_ld16(taddr + 3 * DCOLS + c, d);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = (v[i] + a[i]) + (b[i] + d[i]);
-}
+// Columns [c, c + 16) of D for this thread's token lane.
+__device__ __forceinline__ void b_ld16(uint32_t taddr, int c, float (&v)[16]) { tmem_ld16(taddr + c, v); }
 
 // Columns [c, c + 16) of D for token t: hi lanes (chains added) + the lo lanes staged in smem.
 // hilo_store of 16 consecutive columns (col0 a multiple of 16): 32-byte stores per plane.
