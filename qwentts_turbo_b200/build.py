@@ -9,7 +9,7 @@ import subprocess
 _HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(_HERE, "csrc")
 SOURCES = ("qtt_kernel.cu", "qtt_api.cu", "qtt_noalloc.cu")
-HEADERS = ("qtt_kernel.cuh", "qtt_device.cuh")
+HEADERS = ("qtt_kernel.cuh", "qtt_device.cuh", "qtt_batch.cuh")
 LIB = os.path.join(_HERE, "libqtt.so")
 INCLUDE = os.path.join(os.path.dirname(_HERE), "include")
 

@@ -688,26 +688,31 @@ qtt_status ensure_batch(qtt_engine* e) {
   if (e->b_ready) return QTT_OK;
   cudaError_t ce = qtt::kernel_setup_b(e->device, &e->bshape.ctas, &e->bshape.smem);
   if (ce != cudaSuccess) return from_cuda(ce);
-  if (e->bshape.ctas > qtt::BKCTAS) return QTT_ERR_UNSUPPORTED;
+  // the K split needs a CTA per row tile (gate/up: 48 tiles of 128 rows)
+  if (e->bshape.ctas > qtt::BKCTAS || e->bshape.ctas < 64) return QTT_ERR_UNSUPPORTED;
   const int nbb = e->dims.backbone_layers, ncp = e->dims.cp_layers;
   const int h0 = (nbb + ncp) * qtt::NLMAPS;
   const int nmaps = h0 + 1 + qtt::NCPHEADS + 4;
   std::vector<CUtensorMap> maps(nmaps);
   bool ok = true;
   auto layer_maps = [&](const TTSLayerWeights& L, CUtensorMap* m) {
-    ok = ok && encode_sw128(L.q_proj_weight, qtt::QSZ, qtt::HID, 16, m + 0);
-    ok = ok && encode_sw128(L.k_proj_weight, qtt::KVSZ, qtt::HID, 16, m + 1);
-    ok = ok && encode_sw128(L.v_proj_weight, qtt::KVSZ, qtt::HID, 16, m + 2);
-    ok = ok && encode_sw128(L.o_proj_weight, qtt::HID, qtt::QSZ, 16, m + 3);
-    ok = ok && encode_sw128(L.gate_proj_weight, qtt::INTER, qtt::HID, 16, m + 4);
-    ok = ok && encode_sw128(L.up_proj_weight, qtt::INTER, qtt::HID, 16, m + 5);
-    ok = ok && encode_sw128(L.down_proj_weight, qtt::HID, qtt::INTER, 16, m + 6);
+    // one box per 128-row tile and 64-column atom (gate/up: 64-row boxes, one of each)
+    constexpr uint32_t R = qtt::BNMAX, RH = qtt::BNMAX / 2;
+    ok = ok && encode_sw128(L.q_proj_weight, qtt::QSZ, qtt::HID, R, m + 0);
+    ok = ok && encode_sw128(L.k_proj_weight, qtt::KVSZ, qtt::HID, R, m + 1);
+    ok = ok && encode_sw128(L.v_proj_weight, qtt::KVSZ, qtt::HID, R, m + 2);
+    ok = ok && encode_sw128(L.o_proj_weight, qtt::HID, qtt::QSZ, R, m + 3);
+    ok = ok && encode_sw128(L.gate_proj_weight, qtt::INTER, qtt::HID, RH, m + 4);
+    ok = ok && encode_sw128(L.up_proj_weight, qtt::INTER, qtt::HID, RH, m + 5);
+    ok = ok && encode_sw128(L.down_proj_weight, qtt::HID, qtt::INTER, R, m + 6);
   };
+  // every row tile is full: 128-row tiles of the heads
+  if (e->dims.vocab % qtt::BNMAX != 0 || e->dims.cp_vocab % qtt::BNMAX != 0) return QTT_ERR_UNSUPPORTED;
   for (int l = 0; l < nbb; ++l) layer_maps(e->h_bb[l], maps.data() + l * qtt::NLMAPS);
   for (int l = 0; l < ncp; ++l) layer_maps(e->h_cp[l], maps.data() + (nbb + l) * qtt::NLMAPS);
-  ok = ok && encode_sw128(e->h_codec_head, e->dims.vocab, qtt::HID, 16, &maps[h0]);
+  ok = ok && encode_sw128(e->h_codec_head, e->dims.vocab, qtt::HID, qtt::BNMAX, &maps[h0]);
   for (int g = 0; g < qtt::NCPHEADS; ++g)
-    ok = ok && encode_sw128(e->h_cp_head[g], e->dims.cp_vocab, qtt::HID, 16, &maps[h0 + 1 + g]);
+    ok = ok && encode_sw128(e->h_cp_head[g], e->dims.cp_vocab, qtt::HID, qtt::BNMAX, &maps[h0 + 1 + g]);
   if (!ok) return QTT_ERR_UNSUPPORTED;
   ce = cudaMalloc(&e->d_bwork, qtt::bwork_bytes());
   if (ce == cudaSuccess) ce = cudaMemset(e->d_bwork, 0, qtt::bwork_bytes());
@@ -750,8 +755,7 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   p.cp_wd_map = nullptr;
   p.dbg_cp_logits = e->b_dbg_cp;
   p.dbg_g0_logits = e->b_dbg_g0;
-  p.dbg_arrivals = nullptr;     // (the stage timeline and profile marks, if set, are kept)
-  return p;
+  return p;   // the stage timeline, profile marks and barrier arrivals, if set, are kept
 }
 
 qtt_status batch_check(qtt_engine* e, int B, const qtt_sampling* sp) {

@@ -33,19 +33,21 @@ constexpr int KSUB = 64;                  // K elements of one 128-byte swizzle 
 constexpr int NSUB = 2;                   // atoms per pipeline step
 constexpr int KSTEP = KSUB * NSUB;        // K elements per pipeline step
 constexpr int WBOX = 16;                  // weight rows per TMA box
-constexpr int WS_BYTES = NSUB * 64 * 128; // weight slot: per atom up to 64 rows of 128 bytes
-constexpr int NWS = 4;
+constexpr int NMAX = BNMAX;               // columns of D (weight rows) per CTA tile
+constexpr int WS_BYTES = NMAX * 128;      // weight slot: one atom of up to 128 rows of 128 bytes
+constexpr int NWS = 4;                    // weight slots (two pipeline steps)
 constexpr int APLANE_BYTES = 64 * 128;    // one plane of an activation atom: 64 token rows
 constexpr int ASUB_BYTES = 2 * APLANE_BYTES;  // hi plane, then lo plane
 constexpr int AS_BYTES = NSUB * ASUB_BYTES;
 constexpr int NAS = 3;
-constexpr int NCHAIN = 1;                 // accumulators per tile
-constexpr int DCOLS = 64;                 // tensor-memory columns of one accumulator (N <= 64)
-constexpr uint32_t TMEM_COLS = 2 * NCHAIN * DCOLS;   // 2 tiles x 64 columns
-constexpr int BATT_SPAN = 96;             // backbone attention: positions per work item (target)
+constexpr int DCOLS = NMAX;               // tensor-memory columns of one 64-token tile's accumulator
+constexpr uint32_t TMEM_COLS = 2 * DCOLS; // two 64-token tiles
+constexpr int KPAD = NMAX;                // row stride of a K-slice partial in global memory
+constexpr int BKBANK = 64;                // K-split counters per bank (row tiles of a stage)
 // An M = 128 MMA reads the whole slot: rows 0..63 (hi plane) and 64..127 (lo plane).
 static_assert(NWS * WS_BYTES + NAS * AS_BYTES <= NSLOTS * SLOT_BYTES, "batched rings fit the ring region");
-constexpr int YLO_STRIDE = DCOLS + 1;     // epilogue staging of the lo lanes: [2 tiles][64 tokens][65]
+static_assert(TBMAX * (NMAX + 1) * 4 <= NAS * AS_BYTES, "epilogue staging fits the activation ring");
+static_assert(2 * BKBANK <= BKCTAS, "K-split counter banks");
 // mbarriers in sm.bbar (all with one expected arrival)
 enum : int {
   BB_WFULL = 0,                  // weight slot filled (producer expect_tx + TMA bytes)
@@ -78,31 +80,31 @@ __device__ __forceinline__ int bmap_abuf(const Params& p, int buf, bool box128) 
   return (p.n_bb + p.n_cp) * NLMAPS + 1 + NCPHEADS + 2 * buf + (box128 ? 1 : 0);
 }
 
-// Work of a CTA in a GEMM stage. Rows are grouped into row blocks of `nb` blocks of 16 rows
-// (gate/up: 16 intermediate columns, i.e. 16 gate + 16 up rows per block), N <= 64 columns of D;
-// for o_proj and down the K steps are split too: CTA c < R * nk takes row block
-// c / nk and K steps [ks0, ks1) of slice c % nk, and the last CTA of a row block to finish sums
-// the slices' partial results (fixed order) and runs the epilogue.
+// Work of a CTA in a GEMM stage: a row tile of up to 8 blocks of 16 weight rows (gate/up: 4
+// blocks of 16 intermediate channels = 16 gate + 16 up rows each), N <= 128 columns of D, and a
+// K slice: the R row tiles times nk K slices cover the grid (CTA c < R * nk takes row tile c / nk
+// and K steps [ks0, ks1) of slice c % nk). The nk CTAs of a row tile write their slices' D to
+// global memory, wait for each other (counter) and then each sums the slices (slice order) for
+// its share of the tile's epilogue items.
 struct BSplit {
   int b0, nb;        // first 16-row block, blocks (0: idle in this stage)
-  int rb, kspl, nk;  // row block, K slice, K slices per row block
+  int rb, kspl, nk;  // row tile, K slice, K slices per row tile
   int ks0, ks1;      // K steps of this CTA
 };
-__device__ __forceinline__ BSplit bg_split(const Params& p, const BGemm& g, int cta, int G) {
-  int total;
+__device__ __forceinline__ int bg_blocks(const Params& p, const BGemm& g) {
   switch (g.kind) {
-    case BK_QKV: total = QKV_ROWS / WBOX; break;
-    case BK_GU: total = INTER / WBOX; break;
-    case BK_HEAD: total = (g.hidx == 0 ? p.vocab : p.cp_vocab) / WBOX; break;
-    default: total = HID / WBOX; break;
+    case BK_QKV: return QKV_ROWS / WBOX;
+    case BK_GU: return INTER / WBOX;
+    case BK_HEAD: return (g.hidx == 0 ? p.vocab : p.cp_vocab) / WBOX;
+    default: return HID / WBOX;
   }
-  // o_proj and down (1024 rows, K = 2048 / 3072): 16 row blocks of 64 rows, K split over the
-  // other CTAs; the rest: ceil(blocks / CTAs) blocks per CTA, no split
-  const bool ksplit = g.kind == BK_O || g.kind == BK_D;
-  const int bpc = ksplit ? 4 : (total + G - 1) / G;
-  const int R = total / bpc;
-  const int nks = (g.kind == BK_O ? QSZ : g.kind == BK_D ? INTER : HID) / (KSUB * NSUB);
-  int nk = ksplit ? G / R : 1;
+}
+__device__ __forceinline__ BSplit bg_split(const Params& p, const BGemm& g, int cta, int G) {
+  const int total = bg_blocks(p, g);
+  const int bpc = g.kind == BK_GU ? NMAX / (2 * WBOX) : NMAX / WBOX;
+  const int R = (total + bpc - 1) / bpc;
+  const int nks = bg_K(g.kind) / KSTEP;
+  int nk = G / R;
   nk = nk < 1 ? 1 : (nk > nks ? nks : nk);
   BSplit s;
   s.nk = nk;
@@ -110,7 +112,7 @@ __device__ __forceinline__ BSplit bg_split(const Params& p, const BGemm& g, int 
     s.rb = cta / nk;
     s.kspl = cta - s.rb * nk;
     s.b0 = s.rb * bpc;
-    s.nb = bpc;
+    s.nb = min(bpc, total - s.b0);
     s.ks0 = split_lo(nks, nk, s.kspl);
     s.ks1 = split_lo(nks, nk, s.kspl + 1);
   } else {
@@ -120,31 +122,56 @@ __device__ __forceinline__ BSplit bg_split(const Params& p, const BGemm& g, int 
 }
 __device__ __forceinline__ int bg_N(int kind, int nb) { return (kind == BK_GU ? 2 : 1) * WBOX * nb; }
 
-// Tensor map and row of weight box i of a stage (gate/up: boxes 0..nb-1 gate, nb..2nb-1 up).
-__device__ __forceinline__ void bg_wbox(const Params& p, const BGemm& g, int b0, int nb, int i, const uint8_t*& map,
-                                        int& y) {
+// Weight boxes of a CTA tile: one box of NMAX rows (gate/up: a box of NMAX / 2 gate rows and one
+// of NMAX / 2 up rows) per atom; every row tile of every stage is full (the host checks that the
+// head vocabularies are multiples of NMAX). Returns the tensor map and first row of box i.
+__device__ __forceinline__ int bg_nbox(int kind) { return kind == BK_GU ? 2 : 1; }
+__device__ __forceinline__ void bg_wbox(const Params& p, const BGemm& g, int b0, int i, const uint8_t*& map, int& y) {
   const int base = g.li * NLMAPS;
+  const int r = WBOX * b0;
   switch (g.kind) {
-    case BK_QKV: {
-      const int r = WBOX * (b0 + i);
+    case BK_QKV: {   // a 128-row tile lies inside one of q (2048 rows), k, v (1024 rows each)
       const int m = r < QSZ ? 0 : (r < QSZ + KVSZ ? 1 : 2);
       y = r - (m == 0 ? 0 : (m == 1 ? QSZ : QSZ + KVSZ));
       map = bmap(p, base + m);
       break;
     }
-    case BK_O: map = bmap(p, base + 3); y = WBOX * (b0 + i); break;
-    case BK_GU:
-      if (i < nb) {
-        map = bmap(p, base + 4);
-        y = WBOX * (b0 + i);
-      } else {
-        map = bmap(p, base + 5);
-        y = WBOX * (b0 + i - nb);
-      }
-      break;
-    case BK_D: map = bmap(p, base + 6); y = WBOX * (b0 + i); break;
-    default: map = bmap(p, bmap_head(p, g.hidx)); y = WBOX * (b0 + i); break;
+    case BK_O: map = bmap(p, base + 3); y = r; break;
+    case BK_GU: map = bmap(p, base + 4 + i); y = r; break;   // intermediate channels r .. r + 63
+    case BK_D: map = bmap(p, base + 6); y = r; break;
+    default: map = bmap(p, bmap_head(p, g.hidx)); y = r; break;
   }
+}
+
+// Profiling trace (dbg_marks set): marks[(gemm * G + cta) * BT_EVENTS + event] = %globaltimer
+// for GEMM stages gemm < dbg_marks_len / (G * BT_EVENTS) of the launch, every CTA.
+enum BTrace : int {
+  BT_START = 0,     // consumers: stage start (GO)
+  BT_DREADY,        // consumers: D complete
+  BT_STAGED,        // consumers: D staged in shared memory, accumulator freed
+  BT_PART,          // consumers: K-slice partial stored and fenced
+  BT_COUNT,         // consumers: every slice of the row tile stored
+  BT_REDUCED,       // consumers: slices summed
+  BT_EPI,           // consumers: epilogue done (barrier arrival)
+  BT_BARRIER,       // consumers: barrier passed
+  BT_W0,            // MMA: first weight step ready
+  BT_A0,            // MMA: first activation slot ready
+  BT_MMA_END,       // MMA: last MMA issued
+  BT_GO,            // activation loader: GO seen
+  BT_A_END,         // activation loader: last box issued
+  BT_P0,            // producer: first weight box issued
+  BT_P_END,         // producer: last weight box issued
+  BT_LAST,          // MMA: the last K step's weights and activations ready
+  BT_PH1,           // consumers: lo lanes staged
+  BT_ALAST,         // activation loader: last step's slot free (loads issued next)
+  BT_S0,            // MMA: first step's MMAs and commits issued
+  BT_W1,            // MMA: second step's weights ready
+  BT_EVENTS = 24
+};
+__device__ __forceinline__ void btrace(const Params& p, int gemm, int cta, int G, int ev) {
+  if (p.dbg_marks == nullptr) return;
+  const long long i = (static_cast<long long>(gemm) * G + cta) * BT_EVENTS + ev;
+  if (i < p.dbg_marks_len) p.dbg_marks[i] = globaltimer_ns();
 }
 
 // The GEMM stages of the launch's program, in order; f returns false to stop.
@@ -173,40 +200,46 @@ __device__ void b_walk(const Params& p, F&& f) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Producer warp (one thread): weight boxes of every GEMM stage into the 8-slot ring.
+// Producer warp (one thread): weight boxes of every GEMM stage into the 4-slot ring, one slot
+// per 128-byte swizzle atom (64 K columns of the CTA's N rows), two slots per K step.
 // ------------------------------------------------------------------------------------------
 __device__ void b_producer(const Params& p, Smem& sm, int cta, int G) {
   uint8_t* wring = reinterpret_cast<uint8_t*>(sm.ring);
   uint32_t m = 0;
   int* err = p.w.err;
+  int gidx = 0;
   b_walk(p, [&](const BGemm& g) -> bool {
     const BSplit sp = bg_split(p, g, cta, G);
-    const int b0 = sp.b0, nb = sp.nb;
-    if (nb == 0) return true;
-    const int N = bg_N(g.kind, nb), nbox = N / WBOX;
-    for (int ks = sp.ks0; ks < sp.ks1; ++ks, ++m) {
-      const uint32_t slot = m % NWS, round = m / NWS;
-      if (!mbar_spin(&sm.bbar[BB_WEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
-        if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
-        return false;
-      }
-      mbar_arrive_expect_tx(&sm.bbar[BB_WFULL + slot], static_cast<uint32_t>(NSUB * N * 128));
-      for (int i = 0; i < nbox; ++i) {
-        const uint8_t* map;
-        int y;
-        bg_wbox(p, g, b0, nb, i, map, y);
-        if (ks == sp.ks0) tensormap_acquire(map);   // the host's copy of the map, before its first use
-        for (int a = 0; a < NSUB; ++a)
-          tma_load_2d(wring + slot * WS_BYTES + a * (N * 128) + i * (WBOX * 128), map, ks * KSTEP + a * KSUB, y,
+    const int gi = gidx++;
+    if (sp.nb == 0) return true;
+    const int N = bg_N(g.kind, sp.nb), nbox = bg_nbox(g.kind), brows = N / nbox;
+    bool first = true;
+    for (int ks = sp.ks0; ks < sp.ks1; ++ks)
+      for (int a = 0; a < NSUB; ++a, ++m) {
+        const uint32_t slot = m % NWS, round = m / NWS;
+        if (!mbar_wait(&sm.bbar[BB_WEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
+          if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+          return false;
+        }
+        mbar_arrive_expect_tx(&sm.bbar[BB_WFULL + slot], static_cast<uint32_t>(N * 128));
+        for (int i = 0; i < nbox; ++i) {
+          const uint8_t* map;
+          int y;
+          bg_wbox(p, g, sp.b0, i, map, y);
+          if (first) tensormap_acquire(map);   // the host's copy of the map, before its first use
+          tma_load_2d(wring + slot * WS_BYTES + i * (brows * 128), map, ks * KSTEP + a * KSUB, y,
                       &sm.bbar[BB_WFULL + slot]);
+        }
+        if (first) btrace(p, gi, cta, G, BT_P0);
+        first = false;
       }
-    }
+    btrace(p, gi, cta, G, BT_P_END);
     return true;
   });
   // drain: no box may still be landing in shared memory when the CTA exits
   int zero = 0;
   for (uint32_t i = (m > NWS ? m - NWS : 0u); i < m; ++i)
-    mbar_spin(&sm.bbar[BB_WFULL + i % NWS], (i / NWS) & 1u, &zero);
+    mbar_wait(&sm.bbar[BB_WFULL + i % NWS], (i / NWS) & 1u, &zero);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -218,25 +251,29 @@ __device__ void b_aloader(const Params& p, Smem& sm, int cta, int G) {
   uint32_t na = 0, n = 0;
   int* err = p.w.err;
   for (int b = 0; b < 2; ++b) tensormap_acquire(bmap(p, bmap_abuf(p, b, false)));
+  int gidx = 0;
   b_walk(p, [&](const BGemm& g) -> bool {
     const BSplit sp = bg_split(p, g, cta, G);
+    const int gi = gidx++;
     if (sp.nb == 0) return true;
     const int ntiles = (g.T + 63) >> 6;
     const uint8_t* amap = bmap(p, bmap_abuf(p, bg_abuf(g.kind), false));
     // the consumers arrive on GO after the stage's grid barrier: the A planes are complete
-    if (!mbar_spin(&sm.bbar[BB_GO], n & 1u, &sm.abort)) {
+    if (!mbar_wait(&sm.bbar[BB_GO], n & 1u, &sm.abort)) {
       if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_FULL_TIMEOUT);
       return false;
     }
     ++n;
+    btrace(p, gi, cta, G, BT_GO);
     fence_proxy_async_global();
     for (int ks = sp.ks0; ks < sp.ks1; ++ks)
       for (int j = 0; j < ntiles; ++j, ++na) {
         const uint32_t slot = na % NAS, round = na / NAS;
-        if (!mbar_spin(&sm.bbar[BB_AEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
+        if (!mbar_wait(&sm.bbar[BB_AEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
           if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
           return false;
         }
+        if (ks == sp.ks1 - 1 && j == ntiles - 1) btrace(p, gi, cta, G, BT_ALAST);
         mbar_arrive_expect_tx(&sm.bbar[BB_AFULL + slot], static_cast<uint32_t>(AS_BYTES));
         for (int a = 0; a < NSUB; ++a) {
           uint8_t* dst = aring + slot * AS_BYTES + a * ASUB_BYTES;
@@ -244,11 +281,12 @@ __device__ void b_aloader(const Params& p, Smem& sm, int cta, int G) {
           tma_load_2d(dst + APLANE_BYTES, amap, ks * KSTEP + a * KSUB, TBMAX + 64 * j, &sm.bbar[BB_AFULL + slot]);
         }
       }
+    btrace(p, gi, cta, G, BT_A_END);
     return true;
   });
   int zero = 0;
   for (uint32_t i = (na > NAS ? na - NAS : 0u); i < na; ++i)
-    mbar_spin(&sm.bbar[BB_AFULL + i % NAS], (i / NAS) & 1u, &zero);
+    mbar_wait(&sm.bbar[BB_AFULL + i % NAS], (i / NAS) & 1u, &zero);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -266,91 +304,66 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
       *reinterpret_cast<volatile int*>(&sm.abort) = 1;
     }
   };
+  int gidx = 0;
   b_walk(p, [&](const BGemm& g) -> bool {
     const BSplit sp = bg_split(p, g, cta, G);
+    const int gi = gidx++;
     if (sp.nb == 0) return true;
     const int N = bg_N(g.kind, sp.nb), nks = sp.ks1 - sp.ks0, ntiles = (g.T + 63) >> 6;
     const uint32_t idesc = umma_idesc_bf16(128, N);
-    // profiling (CTA 0, dbg_marks set), dbg_marks[8192 + 8 n]: accumulator free, first
-    // activation slot ready, last MMA issued; the consumers add GO, D ready, epilogue done,
-    // barrier passed
-    const bool prof = p.dbg_marks != nullptr && cta == 0 && static_cast<int>(8192 + 8 * n + 7) < p.dbg_marks_len;
-    unsigned long long tw = 0, ta = 0, t_first = 0;
-    long long cyc_fence = 0, cyc_mma = 0, cyc_commit = 0;
     // the previous stage's epilogue has read D
-    if (!mbar_spin(&sm.bbar[BB_ACCEMPTY], (n & 1u) ^ 1u, &sm.abort)) {
+    if (!mbar_wait(&sm.bbar[BB_ACCEMPTY], (n & 1u) ^ 1u, &sm.abort)) {
       fail_mma(DEV_ERR_FULL_TIMEOUT);
       return false;
     }
     tc_fence_after();
-    const unsigned long long t_start = prof ? globaltimer_ns() : 0ull;
     for (int ks = 0; ks < nks; ++ks) {   // ks: index within this CTA's K slice
-      const uint32_t ws = m % NWS, wr = m / NWS;
-      unsigned long long t0 = prof ? globaltimer_ns() : 0ull;
-      if (!mbar_spin(&sm.bbar[BB_WFULL + ws], wr & 1u, &sm.abort)) {
+      const uint32_t ws0 = m % NWS, ws1 = (m + 1) % NWS;
+      if (!mbar_wait(&sm.bbar[BB_WFULL + ws0], (m / NWS) & 1u, &sm.abort) ||
+          !mbar_wait(&sm.bbar[BB_WFULL + ws1], ((m + 1) / NWS) & 1u, &sm.abort)) {
         fail_mma(DEV_ERR_FULL_TIMEOUT);
         return false;
       }
-      if (prof && ks > 0) tw += globaltimer_ns() - t0;
-      const uint32_t wa = wbase + ws * WS_BYTES;
+      if (ks == 0) btrace(p, gi, cta, G, BT_W0);
+      if (ks == 1) btrace(p, gi, cta, G, BT_W1);
+      // descriptors built once per step; a K offset adds (bytes >> 4) to the start-address field
+      const uint64_t db0 = umma_desc_sw128(wbase + ws0 * WS_BYTES), db1 = umma_desc_sw128(wbase + ws1 * WS_BYTES);
       for (int j = 0; j < ntiles; ++j, ++ua) {
         const uint32_t as = ua % NAS, ar = ua / NAS;
-        t0 = prof ? globaltimer_ns() : 0ull;
-        if (!mbar_spin(&sm.bbar[BB_AFULL + as], ar & 1u, &sm.abort)) {
+        if (!mbar_wait(&sm.bbar[BB_AFULL + as], ar & 1u, &sm.abort)) {
           fail_mma(DEV_ERR_FULL_TIMEOUT);
           return false;
         }
-        if (prof) {
-          if (ks > 0) ta += globaltimer_ns() - t0;
-          if (t_first == 0ull) t_first = globaltimer_ns();
-        }
-        long long c0 = prof ? clock64() : 0;
+        if (ks == 0 && j == 0) btrace(p, gi, cta, G, BT_A0);
+        if (ks == nks - 1 && j == ntiles - 1) btrace(p, gi, cta, G, BT_LAST);
         tc_fence_after();
-        long long c1 = prof ? clock64() : 0;
-        const uint32_t aa = abase + as * AS_BYTES;
         // one M = 128 MMA covers both planes: A rows 0..63 = hi, 64..127 = lo of the tile's tokens
-        const uint32_t dt = tmem + j * NCHAIN * DCOLS;
+        const uint64_t da = umma_desc_sw128(abase + as * AS_BYTES);
+        const uint32_t dt = tmem + j * DCOLS;
 #pragma unroll
         for (int a = 0; a < NSUB; ++a)
 #pragma unroll
           for (int kk = 0; kk < KSUB / 16; ++kk)   // the first MMA of the slice overwrites D
-            tc_mma_bf16(dt, umma_desc_sw128(aa + a * ASUB_BYTES + kk * 32),
-                        umma_desc_sw128(wa + a * (N * 128) + kk * 32), idesc, (ks | a | kk) != 0 ? 1u : 0u);
-        long long c2 = prof ? clock64() : 0;
+            tc_mma_bf16(dt, da + static_cast<uint64_t>((a * ASUB_BYTES + kk * 32) >> 4),
+                        (a == 0 ? db0 : db1) + static_cast<uint64_t>((kk * 32) >> 4), idesc,
+                        (ks | a | kk) != 0 ? 1u : 0u);
         any = true;
         tc_commit(&sm.bbar[BB_AEMPTY + as]);
-        long long c3 = prof ? clock64() : 0;
-        if (prof) {
-          cyc_fence += c1 - c0;
-          cyc_mma += c2 - c1;
-          cyc_commit += c3 - c2;
-        }
       }
-      long long c4 = prof ? clock64() : 0;
-      tc_commit(&sm.bbar[BB_WEMPTY + ws]);
-      if (prof) cyc_commit += clock64() - c4;
-      ++m;
+      tc_commit(&sm.bbar[BB_WEMPTY + ws0]);
+      tc_commit(&sm.bbar[BB_WEMPTY + ws1]);
+      if (ks == 0) btrace(p, gi, cta, G, BT_S0);
+      m += 2;
     }
+    btrace(p, gi, cta, G, BT_MMA_END);
     tc_commit(&sm.bbar[BB_ACCFULL]);
-    if (prof) {
-      p.dbg_marks[8192 + 8 * n + 0] = t_start;
-      p.dbg_marks[8192 + 8 * n + 1] = t_first;
-      p.dbg_marks[8192 + 8 * n + 2] = globaltimer_ns();
-      p.dbg_marks[8192 + 8 * n + 7] = (tw << 32) | (ta & 0xFFFFFFFFull);
-      if (static_cast<int>(12288 + 4 * n + 3) < p.dbg_marks_len) {
-        p.dbg_marks[12288 + 4 * n + 0] = cyc_fence;
-        p.dbg_marks[12288 + 4 * n + 1] = cyc_mma;
-        p.dbg_marks[12288 + 4 * n + 2] = cyc_commit;
-        p.dbg_marks[12288 + 4 * n + 3] = nks;
-      }
-    }
     ++n;
     return true;
   });
   if (any) {   // every issued MMA done before the accumulator is freed
     int zero = 0;
     tc_commit(&sm.bbar[BB_DRAIN]);
-    mbar_spin(&sm.bbar[BB_DRAIN], 0u, &zero);
+    mbar_wait(&sm.bbar[BB_DRAIN], 0u, &zero);
   }
 }
 
@@ -372,9 +385,6 @@ __device__ __forceinline__ float b_rstd(const unsigned long long* ssq, int t, fl
   const double s = static_cast<double>(static_cast<long long>(__ldcg(ssq + t))) * (1.0 / 4294967296.0);
   return rms_scale(s, HID, eps);
 }
-
-// Columns [c, c + 16) of D for this thread's token lane.
-__device__ __forceinline__ void b_ld16(uint32_t taddr, int c, float (&v)[16]) { tmem_ld16(taddr + c, v); }
 
 // Columns [c, c + 16) of D for token t: hi lanes (chains added) + the lo lanes staged in smem.
 // hilo_store of 16 consecutive columns (col0 a multiple of 16): 32-byte stores per plane.
@@ -417,124 +427,164 @@ __device__ __forceinline__ void st16_f32(float* dst, const float (&v)[16]) {
   for (int i = 0; i < 16; i += 4) __stcg(reinterpret_cast<float4*>(dst + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
 }
 
-// Columns [c, c + 16) of D for the thread's token. TMEM mode: the hi lanes (chains added) + the
-// lo lanes staged in shared memory. Summed mode (K split): the row of the slices' sum.
-struct BAcc {
-  uint32_t taddr;      // this thread's hi lane, tile base column
-  const float* lo;     // staged lo lane row of this token
-  const float* y;      // summed row of this token, or nullptr
-  __device__ __forceinline__ void ld16(int c, float (&v)[16]) const {
-    if (y != nullptr) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = y[c + i];
-      return;
-    }
-    b_ld16(taddr, c, v);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] += lo[c + i];
-  }
+// Inputs of one epilogue item that do not depend on D, loaded before D is ready.
+struct EpiSt {
+  float a[16], b[16];
+  float rs;
 };
 
-// Consumer side of one GEMM stage: release the activation loader, wait for D, stage the lo
-// lanes (warps 2, 3 of each 64-token tile) in shared memory, then on the hi lanes (warps 0, 1 of
-// tile 0 and 4, 5 of tile 1, all lanes taking part in the tensor-memory loads):
-//   * one K slice: the epilogue epi(t, acc, b0, nb, N) directly;
-//   * K split: the slice's partial D rows to global memory; the last CTA of the row block
-//     (counter) sums the slices in slice order and runs the epilogue.
-// Then free D and the grid barrier.
-template <class EPI>
-__device__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, EPI&& epi) {
-  const BSplit sp = bg_split(p, g, cs.cta, cs.G);
-  const bool prof = p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0 &&
-                    static_cast<int>(8192 + 8 * gemm_n + 7) < p.dbg_marks_len;
-  if (sp.nb == 0) return grid_sync(p, sm, cs);
-  const int N = bg_N(g.kind, sp.nb);
-  if (prof) p.dbg_marks[8192 + 8 * gemm_n + 3] = globaltimer_ns();
-  if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_GO]);
-  bool freed = false;
-  if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
-    if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
-  } else {
-    if (prof) p.dbg_marks[8192 + 8 * gemm_n + 4] = globaltimer_ns();
-    tc_fence_after();
-    const int q = cs.warp & 3, j = cs.warp >> 2;   // lane quarter, 64-token tile
-    float* ylo = sm.xs;                            // [2][64][YLO_STRIDE]
-    const uint32_t tq = sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * NCHAIN * DCOLS;
-    if (j < 2 && q >= 2 && 64 * j + 32 * (q - 2) < g.T) {
-      float* row = ylo + (j * 64 + 32 * (q - 2) + cs.lane) * YLO_STRIDE;
-      for (int c = 0; c < N; c += 16) {
-        float v[16];
-        b_ld16(tq, c, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) row[c + i] = v[i];
-      }
-    }
-    named_sync(1, NCT);
-    const bool mine = j < 2 && q < 2 && 64 * j + 32 * q < g.T;
-    const int t = 64 * j + 32 * q + cs.lane;
-    const BAcc dacc{tq, ylo + (j * 64 + 32 * q + cs.lane) * YLO_STRIDE, nullptr};
-    if (sp.nk == 1) {
-      if (mine) epi(t, dacc, sp.b0, sp.nb, N);
-      tc_fence_before();
-    } else {
-      if (mine) {
-        float* dst = p.bw.kpart + (static_cast<size_t>(cs.cta) * TBMAX + t) * DCOLS;
-        for (int c = 0; c < N; c += 16) {
-          float v[16];
-          dacc.ld16(c, v);
-#pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            __stcg(reinterpret_cast<float4*>(dst + c + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
-        }
-      }
-      tc_fence_before();
-      named_sync(1, NCT);
-      if (cs.tid == 0) {
-        mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
-        __threadfence();
-        const uint32_t old = atomicAdd(p.bw.kcnt + sp.rb, 1u);
-        const bool last = old == static_cast<uint32_t>(sp.nk - 1);
-        if (last) atomicExch(p.bw.kcnt + sp.rb, 0u);
-        sm.bcast[0] = last ? 1 : 0;
-        __threadfence();
-      }
-      freed = true;
-      named_sync(1, NCT);
-      if (sm.bcast[0]) {
-        float* y = sm.xs;   // [T][YLO_STRIDE]: the slices' sum (the lo staging is no longer read)
-        const float* base = p.bw.kpart + static_cast<size_t>(sp.rb * sp.nk) * TBMAX * DCOLS;
-        const int n4 = N / 4;
-        for (int e = cs.tid; e < g.T * n4; e += NCT) {
-          const int tt = e / n4, c = 4 * (e - tt * n4);
-          const float* src = base + static_cast<size_t>(tt) * DCOLS + c;
-          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int k0 = 0; k0 < sp.nk; k0 += 4) {   // four slices' loads in flight, added in order
-            float4 v[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (k0 + k < sp.nk)
-                v[k] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(k0 + k) * TBMAX * DCOLS));
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (k0 + k < sp.nk) {
-                a.x += v[k].x; a.y += v[k].y; a.z += v[k].z; a.w += v[k].w;
-              }
-          }
-          float* d = y + tt * YLO_STRIDE + c;
-          d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
-        }
-        named_sync(1, NCT);
-        if (mine) epi(t, BAcc{0u, nullptr, y + t * YLO_STRIDE}, sp.b0, sp.nb, N);
+// Bounded wait until *cnt >= target (thread 0 of the CTA), as in grid_sync.
+__device__ bool b_wait_count(const Params& p, Smem& sm, const uint32_t* cnt, uint32_t target) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (ld_acquire_gpu(cnt) >= target) return true;
+    if ((it & 31u) == 31u) {
+      if (ld_volatile_i32(p.w.err) != 0 || aborted(sm)) return false;
+      if (globaltimer_ns() - t0 > QTT_WAIT_NS) {
+        set_error(p.w.err, DEV_ERR_GRID_TIMEOUT);
+        return false;
       }
     }
   }
-  named_sync(1, NCT);
-  if (prof) p.dbg_marks[8192 + 8 * gemm_n + 5] = globaltimer_ns();
-  if (cs.tid == 0 && !freed) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);
-  const bool ok = grid_sync(p, sm, cs);
-  if (prof) p.dbg_marks[8192 + 8 * gemm_n + 6] = globaltimer_ns();
+}
+
+// Consumer side of one GEMM stage. Epilogue items are (token t, 16 output columns c); the
+// callbacks are pre(t, r0, st), issued right after the stage starts (inputs that do not depend
+// on D), and run(t, r0, y, y2, st) with y = D[t][16 columns] (gate/up: y = gate, y2 = up) and
+// r0 the first output column (row of W; gate/up: intermediate channel).
+//   1. release the activation loader (GO), prefetch the first item's inputs;
+//   2. wait for D; stage it in shared memory as hi + lo rows: the lo lanes (TMEM lanes 64..127,
+//      warps of lane quarters 2, 3) write, then the hi lanes add; D is freed;
+//   3. K split: the slice's D rows to global memory, count, wait for the row tile's other slices,
+//      and sum the nk slices (slice order) for this CTA's share of the items;
+//   4. the epilogue of this CTA's items (all of them without a K split); the grid barrier.
+template <class PRE, class RUN>
+__device__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, PRE&& pre, RUN&& run) {
+  const BSplit sp = bg_split(p, g, cs.cta, cs.G);
+  const bool tr = p.dbg_marks != nullptr && cs.tid == 0;
+  const int gi = cs.gi;
+  const uint32_t bank = static_cast<uint32_t>(cs.gi & 1) * BKBANK;
+  // the other counter bank was last used by the previous GEMM stage, whose barrier has passed
+  if (cs.cta == 0 && cs.tid < BKBANK) __stcg(p.bw.kcnt + (bank ^ BKBANK) + cs.tid, 0u);
+  cs.gi++;
+  if (sp.nb == 0) return grid_sync(p, sm, cs);
+  const int N = bg_N(g.kind, sp.nb);
+  const bool gu = g.kind == BK_GU;
+  const int NO = gu ? N / 2 : N, nci = NO / 16, items = g.T * nci;
+  const int i0 = split_lo(items, sp.nk, sp.kspl), i1 = split_lo(items, sp.nk, sp.kspl + 1);
+  const int r0b = WBOX * sp.b0;
+  if (tr) btrace(p, gi, cs.cta, cs.G, BT_START);
+  if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_GO]);
+  EpiSt st;
+  if (i0 + cs.tid < i1) {
+    const int i = i0 + cs.tid;
+    pre(i / nci, r0b + 16 * (i % nci), st);
+  }
+  bool ok = true;
+  float* Y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sm.ring) + NWS * WS_BYTES);   // [T][N + 1]
+  const int YST = N + 1;
+  if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
+    if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
+    ok = false;
+  } else {
+    if (tr) btrace(p, gi, cs.cta, cs.G, BT_DREADY);
+    tc_fence_after();
+    // 2. D -> Y (the activation ring is idle until the next stage's GO)
+    const int ntiles = (g.T + 63) >> 6, nch = N / 16;
+    const int q = cs.warp & 3, wq = cs.warp >> 2, half = q & 1;
+    for (int ph = 0; ph < 2; ++ph) {
+      if ((q >> 1) == (ph == 0 ? 1 : 0)) {
+        for (int job = wq; job < ntiles * nch; job += NCW / 4) {
+          const int j = job / nch, c = job - j * nch;
+          if (64 * j + 32 * half < g.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
+            float v[16];
+            tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * DCOLS + 16 * c, v);
+            const int t = 64 * j + 32 * half + cs.lane;
+            if (t < g.T) {
+              float* yr = Y + t * YST + 16 * c;
+              if (ph == 0) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) yr[i] = v[i];
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) yr[i] += v[i];
+              }
+            }
+          }
+        }
+      }
+      if (ph == 1) tc_fence_before();
+      named_sync(1, NCT);
+      if (ph == 0 && tr) btrace(p, gi, cs.cta, cs.G, BT_PH1);
+    }
+    if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
+    if (tr) btrace(p, gi, cs.cta, cs.G, BT_STAGED);
+    // 3. K split
+    if (sp.nk > 1) {
+      float* part = p.bw.kpart + static_cast<size_t>(cs.cta) * TBMAX * KPAD;
+      const int n4 = N / 4;
+      for (int e = cs.tid; e < g.T * n4; e += NCT) {
+        const int t = e / n4, c4 = e - t * n4;
+        const float* yr = Y + t * YST + 4 * c4;
+        __stcg(reinterpret_cast<float4*>(part + t * KPAD + 4 * c4), make_float4(yr[0], yr[1], yr[2], yr[3]));
+      }
+      // bar.sync orders the CTA's stores before thread 0, whose release add publishes them at
+      // gpu scope (the pattern of grid_sync)
+      named_sync(1, NCT);
+      uint32_t* cnt = p.bw.kcnt + bank + sp.rb;
+      if (cs.tid == 0) {
+        if (tr) btrace(p, gi, cs.cta, cs.G, BT_PART);
+        red_release_gpu_add(cnt, 1u);
+        sm.bcast[0] = b_wait_count(p, sm, cnt, static_cast<uint32_t>(sp.nk)) ? 1 : 0;
+        if (tr) btrace(p, gi, cs.cta, cs.G, BT_COUNT);
+      }
+      named_sync(1, NCT);
+      if (!sm.bcast[0]) {
+        *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+        ok = false;
+      } else {
+        const int ppi = gu ? 8 : 4;   // float4 pieces per item
+        const float* base = p.bw.kpart + static_cast<size_t>(sp.rb * sp.nk) * TBMAX * KPAD;
+        for (int e = cs.tid; e < (i1 - i0) * ppi; e += NCT) {
+          const int it = i0 + e / ppi, pc = e % ppi;
+          const int t = it / nci, c = it - t * nci;
+          const int col = (pc < 4 ? 16 * c : NO + 16 * c) + 4 * (pc & 3);
+          const float* src = base + static_cast<size_t>(t) * KPAD + col;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int k0 = 0; k0 < sp.nk; k0 += 8) {   // eight slices' loads in flight, added in slice order
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              if (k0 + k < sp.nk) v[k] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(k0 + k) * TBMAX * KPAD));
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              if (k0 + k < sp.nk) {
+                acc.x += v[k].x; acc.y += v[k].y; acc.z += v[k].z; acc.w += v[k].w;
+              }
+          }
+          float* yr = Y + t * YST + col;
+          yr[0] = acc.x; yr[1] = acc.y; yr[2] = acc.z; yr[3] = acc.w;
+        }
+        named_sync(1, NCT);
+        if (tr) btrace(p, gi, cs.cta, cs.G, BT_REDUCED);
+      }
+    }
+    // 4. epilogue items
+    if (ok) {
+      for (int i = i0 + cs.tid; i < i1; i += NCT) {
+        const int t = i / nci, c = i - t * nci, r0 = r0b + 16 * c;
+        if (i != i0 + cs.tid) pre(t, r0, st);
+        const float* yr = Y + t * YST + 16 * c;
+        run(t, r0, yr, gu ? yr + NO : yr, st);
+      }
+    }
+  }
+  fence_proxy_async_smem();   // Y aliases the activation ring: before the next stage's TMA writes
+  if (tr) btrace(p, gi, cs.cta, cs.G, BT_EPI);
+  const bool ok2 = grid_sync(p, sm, cs);
+  if (tr) btrace(p, gi, cs.cta, cs.G, BT_BARRIER);
   gemm_n++;
-  return ok;
+  return ok && ok2;
 }
 
 // Sums-of-squares buffer written by the next producing stage (INPUT, O, down); that stage also
@@ -606,63 +656,318 @@ __device__ bool b_norm(const Params& p, Smem& sm, Cons& cs, const float* h, int 
   return grid_sync(p, sm, cs);
 }
 
-// Attention of one layer for every utterance. Code predictor: one item per (utterance, KV
-// head), NT = 2 tokens in the first pass. Backbone: (utterance, KV head, chunk) items over each
-// active utterance's own context, combined by the last item of a head.
+// ------------------------------------------------------------------------------------------
+// Attention as warp work items. A warp owns one (utterance, KV head, chunk of context
+// positions) item; its lanes are WG = 2 position groups of WL = 16 lanes, lane (g, u) holding
+// the head dimensions [8u, 8u + 8) of positions g, g + 2, g + 4, ... of the chunk, so one warp
+// load reads 2 whole cached rows and a score needs 4 shuffles. Both q heads of the KV head
+// (GQA 2:1) are done together; each position group keeps an online softmax, the groups are
+// merged with shuffles at the end, and the result is either the output (single chunk) or a
+// partial record merged by the head's last chunk to finish (counter), as in flash decoding.
+// ------------------------------------------------------------------------------------------
+constexpr unsigned WFULL = 0xffffffffu;
+constexpr int WD = 8;          // head dimensions per lane
+constexpr int WL = HD / WD;    // lanes per position
+constexpr int WG = 32 / WL;    // position groups per warp
+static_assert(WL == 16 && WG == 2, "warp attention layout");
+
+__device__ __forceinline__ float bf16_at(const uint32_t* w, int i) { return (i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]); }
+
+// q/k RMSNorm (fused_decode_tts.cu:183-197) + RoPE at position pos on the dimensions
+// [8u, 8u + 8) in x; the rotation partner d +- 64 is in lane u ^ 8 of the same group.
+__device__ __forceinline__ void w_norm_rope(float (&x)[WD], const bf16* nw, const Params& p, int pos, int u) {
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < WD; ++i) ss = fma(static_cast<double>(x[i]), static_cast<double>(x[i]), ss);
+#pragma unroll
+  for (int o = 1; o < WL; o <<= 1) ss += __shfl_xor_sync(WFULL, ss, o);
+  const float rstd = rms_scale(ss, HD, p.eps);
+  const uint4 w4 = *reinterpret_cast<const uint4*>(nw + WD * u);
+  const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+  for (int i = 0; i < WD; ++i) x[i] = x[i] * rstd * bf16_at(w, i);
+  const uint4 c4 = *reinterpret_cast<const uint4*>(p.cos_tab + static_cast<size_t>(pos) * HD + WD * u);
+  const uint4 s4 = *reinterpret_cast<const uint4*>(p.sin_tab + static_cast<size_t>(pos) * HD + WD * u);
+  const uint32_t c[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+  float y[WD];
+#pragma unroll
+  for (int i = 0; i < WD; ++i) y[i] = __shfl_xor_sync(WFULL, x[i], WL / 2);
+#pragma unroll
+  for (int i = 0; i < WD; ++i)
+    x[i] = u < WL / 2 ? x[i] * bf16_at(c, i) - y[i] * bf16_at(sn, i) : x[i] * bf16_at(c, i) + y[i] * bf16_at(sn, i);
+}
+
+// Dimensions [8u, 8u + 8) of cached row j: 4 words of packed bf16 pairs (backbone) or 8 fp32
+// words (code predictor).
+template <bool CP>
+struct WRow {
+  uint32_t w[CP ? 8 : 4];
+  __device__ __forceinline__ void load(const uint8_t* base, int j, int u) {
+    const uint4* r = reinterpret_cast<const uint4*>(base + static_cast<size_t>(j) * HD * (CP ? 4 : 2)) + (CP ? 2 : 1) * u;
+#pragma unroll
+    for (int i = 0; i < (CP ? 2 : 1); ++i) {
+      // code-predictor rows were written by other CTAs earlier in this launch: read through L2
+      const uint4 a = CP ? __ldcg(r + i) : __ldcs(r + i);
+      w[4 * i] = a.x; w[4 * i + 1] = a.y; w[4 * i + 2] = a.z; w[4 * i + 3] = a.w;
+    }
+  }
+  __device__ __forceinline__ float operator[](int i) const { return CP ? __uint_as_float(w[i]) : bf16_at(w, i); }
+};
+
+// Online softmax state of one q head on this lane's dimensions.
+struct WSoft {
+  float m, l, acc[WD];
+  __device__ __forceinline__ void init() {
+    m = -INFINITY;
+    l = 0.f;
+#pragma unroll
+    for (int i = 0; i < WD; ++i) acc[i] = 0.f;
+  }
+  template <class V>
+  __device__ __forceinline__ void add(float s, const V& v) {
+    const float mn = fmaxf(m, s);
+    const float f = m == -INFINITY ? 0.f : expf(m - mn);
+    const float e = expf(s - mn);
+    l = fmaf(l, f, e);
+#pragma unroll
+    for (int i = 0; i < WD; ++i) acc[i] = fmaf(acc[i], f, e * v[i]);
+    m = mn;
+  }
+  // merge with another state (m2, l2, a2)
+  __device__ __forceinline__ void merge(float m2, float l2, const float (&a2)[WD]) {
+    const float mn = fmaxf(m, m2);
+    if (mn == -INFINITY) return;
+    const float f = m == -INFINITY ? 0.f : expf(m - mn), f2 = m2 == -INFINITY ? 0.f : expf(m2 - mn);
+    l = l * f + l2 * f2;
+#pragma unroll
+    for (int i = 0; i < WD; ++i) acc[i] = acc[i] * f + a2[i] * f2;
+    m = mn;
+  }
+  // merge the position groups of the warp (lanes u and u + 16); every lane takes part
+  __device__ __forceinline__ void merge_groups() {
+    const float m2 = __shfl_xor_sync(WFULL, m, WL), l2 = __shfl_xor_sync(WFULL, l, WL);
+    const float mn = fmaxf(m, m2);
+    const float f = m == -INFINITY ? 0.f : expf(m - mn), f2 = m2 == -INFINITY ? 0.f : expf(m2 - mn);
+    l = l * f + l2 * f2;
+#pragma unroll
+    for (int i = 0; i < WD; ++i) acc[i] = acc[i] * f + __shfl_xor_sync(WFULL, acc[i], WL) * f2;
+    m = mn;
+  }
+};
+
+// 8 fp32 from global memory through L2 (rows written by other CTAs in this launch).
+__device__ __forceinline__ void ld8_f32(const float* src, float (&v)[WD]) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(src)), b = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Normalised output of q head g (0: a0, 1: a1) on this lane's 8 dimensions as hi/lo planes.
+__device__ __forceinline__ void w_out(bf16* hilo, int tok, int col0, const WSoft& a0, const WSoft& a1, int g) {
+  const float inv = 1.f / (g == 0 ? a0.l : a1.l);
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float v0 = (g == 0 ? a0.acc[2 * i] : a1.acc[2 * i]) * inv;
+    const float v1 = (g == 0 ? a0.acc[2 * i + 1] : a1.acc[2 * i + 1]) * inv;
+    const bf16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
+    const bf16 l0 = __float2bfloat16_rn(v0 - __bfloat162float(h0)), l1 = __float2bfloat16_rn(v1 - __bfloat162float(h1));
+    hi[i] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+    lo[i] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+  }
+  *reinterpret_cast<uint4*>(hilo + static_cast<size_t>(tok) * ABUF_LD + col0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(hilo + static_cast<size_t>(TBMAX + tok) * ABUF_LD + col0) =
+      make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+// One warp item: tokens t < NT of utterance rows qkv + t * QKV_ROWS at positions p0 + t, KV
+// head h, context positions [s0, s1) (chunk c of nch). The writer stores the new K/V rows of
+// the tokens first (q/k norm + RoPE), so every position is read from the cache.
+template <bool CP>
+__device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const LayerW* L, const float* qkv, int NT, int p0, int h,
+                          uint8_t* kb, uint8_t* vb, bf16* hilo, int tok0, int c, int nch, int s0, int s1,
+                          bool writer, float* prt, uint32_t* cnt) {
+  const int g = cs.lane / WL, u = cs.lane % WL;
+  if (writer) {
+    for (int t = 0; t < NT; ++t) {
+      float k[WD], v[WD];
+      ld8_f32(qkv + t * QKV_ROWS + QSZ + h * HD + WD * u, k);
+      ld8_f32(qkv + t * QKV_ROWS + QSZ + KVSZ + h * HD + WD * u, v);
+      w_norm_rope(k, L->k_norm, p, p0 + t, u);
+      if (g == 0) {
+        const size_t row = static_cast<size_t>(p0 + t) * HD + WD * u;
+        if (CP) {
+          float4* kd = reinterpret_cast<float4*>(reinterpret_cast<float*>(kb) + row);
+          float4* vd = reinterpret_cast<float4*>(reinterpret_cast<float*>(vb) + row);
+          kd[0] = make_float4(k[0], k[1], k[2], k[3]);
+          kd[1] = make_float4(k[4], k[5], k[6], k[7]);
+          vd[0] = make_float4(v[0], v[1], v[2], v[3]);
+          vd[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+          uint32_t kw[4], vw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            kw[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(k[2 * i]))) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(k[2 * i + 1]))) << 16);
+            vw[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i]))) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1]))) << 16);
+          }
+          *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(kb) + row) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+          *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(vb) + row) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        }
+      }
+    }
+    __syncwarp();   // the rows just stored are read back by the other lanes of this warp
+  }
+  for (int t = 0; t < NT; ++t) {
+    float q0[WD], q1[WD];
+    ld8_f32(qkv + t * QKV_ROWS + (2 * h) * HD + WD * u, q0);
+    ld8_f32(qkv + t * QKV_ROWS + (2 * h + 1) * HD + WD * u, q1);
+    w_norm_rope(q0, L->q_norm, p, p0 + t, u);
+    w_norm_rope(q1, L->q_norm, p, p0 + t, u);
+    WSoft a0, a1;
+    a0.init();
+    a1.init();
+    const int send = min(s1, p0 + t + 1);
+    constexpr int P = CP ? 2 : 4;   // positions per group per trip: 4 P rows in flight per lane
+    for (int j = s0 + g; j - g < send; j += P * WG) {   // every lane runs the same trip count
+      bool ok[P];
+      WRow<CP> kr[P], vr[P];
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        ok[q] = j + q * WG < send;
+        kr[q].load(kb, ok[q] ? j + q * WG : s0, u);   // s0: a row that exists, score not used
+      }
+#pragma unroll
+      for (int q = 0; q < P; ++q) vr[q].load(vb, ok[q] ? j + q * WG : s0, u);
+      float d0[P], d1[P];
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        d0[q] = 0.f;
+        d1[q] = 0.f;
+#pragma unroll
+        for (int i = 0; i < WD; ++i) {
+          d0[q] = fmaf(q0[i], kr[q][i], d0[q]);
+          d1[q] = fmaf(q1[i], kr[q][i], d1[q]);
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < WL; o <<= 1)
+#pragma unroll
+        for (int q = 0; q < P; ++q) {
+          d0[q] += __shfl_xor_sync(WFULL, d0[q], o);
+          d1[q] += __shfl_xor_sync(WFULL, d1[q], o);
+        }
+#pragma unroll
+      for (int q = 0; q < P; ++q)
+        if (ok[q]) {
+          a0.add(d0[q] * p.attn_scale, vr[q]);
+          a1.add(d1[q] * p.attn_scale, vr[q]);
+        }
+    }
+    a0.merge_groups();
+    a1.merge_groups();
+    if (nch == 1) {
+      if (g < 2) w_out(hilo, tok0 + t, (2 * h + g) * HD + WD * u, a0, a1, g);
+      continue;
+    }
+    // partial record {m, l, -, -, acc[128]} of (token t, q head 2h + g, chunk c)
+    if (g < 2) {
+      float* rec = prt + ((static_cast<size_t>(t) * NQH + 2 * h + g) * MAX_ATT_CHUNKS + c) * PRT_STRIDE;
+      float4* r4 = reinterpret_cast<float4*>(rec + 4 + WD * u);
+      if (g == 0) {
+        __stcg(r4, make_float4(a0.acc[0], a0.acc[1], a0.acc[2], a0.acc[3]));
+        __stcg(r4 + 1, make_float4(a0.acc[4], a0.acc[5], a0.acc[6], a0.acc[7]));
+        if (u == 0) __stcg(reinterpret_cast<float2*>(rec), make_float2(a0.m, a0.l));
+      } else {
+        __stcg(r4, make_float4(a1.acc[0], a1.acc[1], a1.acc[2], a1.acc[3]));
+        __stcg(r4 + 1, make_float4(a1.acc[4], a1.acc[5], a1.acc[6], a1.acc[7]));
+        if (u == 0) __stcg(reinterpret_cast<float2*>(rec), make_float2(a1.m, a1.l));
+      }
+    }
+    __threadfence();
+    __syncwarp();
+    uint32_t last = 0;
+    if (cs.lane == 0) last = atomicAdd(cnt, 1u) == static_cast<uint32_t>(nch - 1) ? 1u : 0u;
+    last = __shfl_sync(WFULL, last, 0);
+    if (!last) continue;
+    __threadfence();
+    // merge the nch records: group g takes chunks g, g + 2, ... of both heads
+    a0.init();
+    a1.init();
+    for (int cc = g; cc - g < nch; cc += WG) {
+      if (cc < nch) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float* rec = prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + cc) * PRT_STRIDE;
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec));
+          float a2[WD];
+          ld8_f32(rec + 4 + WD * u, a2);
+          if (hh == 0)
+            a0.merge(ml.x, ml.y, a2);
+          else
+            a1.merge(ml.x, ml.y, a2);
+        }
+      }
+    }
+    a0.merge_groups();
+    a1.merge_groups();
+    if (g < 2) w_out(hilo, tok0 + t, (2 * h + g) * HD + WD * u, a0, a1, g);
+    if (cs.lane == 0) atomicExch(cnt, 0u);
+  }
+}
+
+// Attention of one layer for every utterance, output as the o_proj operand planes. Code
+// predictor: one warp item per (utterance, KV head) over its <= 17 positions, 2 tokens in the
+// first pass. Backbone: (utterance, KV head, chunk) items, chunk length chosen so that the
+// items of all active utterances spread over every consumer warp of the grid.
 __device__ bool b_attention(const Params& p, Smem& sm, Cons& cs, int li, bool cp, int pass) {
   const BState bst = bstate(sm);
   const int B = p.nb;
+  const int NW = cs.G * NCW, gw = cs.cta * NCW + cs.warp;
   if (cp) {
     const int l = li - p.n_bb;
     const LayerW* L = p.cp_layers + l;
     const int NT = pass == 0 ? 2 : 1, p0 = pass == 0 ? 0 : pass + 1;
-    for (int item = cs.cta; item < B * NKVH; item += cs.G) {
+    for (int item = gw; item < B * NKVH; item += NW) {
       const int s = item / NKVH, h = item - s * NKVH;
-      AttIO io;
-      io.qkv = p.bw.qkv + static_cast<size_t>(s * NT) * QKV_ROWS;
       const size_t off = (static_cast<size_t>(l) * NKVH + h) * p.cp_max_seq * HD;
-      io.kb = reinterpret_cast<uint8_t*>(p.bs[s].cpk + off);
-      io.vb = reinterpret_cast<uint8_t*>(p.bs[s].cpv + off);
-      io.out = nullptr;
-      io.hilo = p.bw.abuf[1];
-      io.tok0 = s * NT;
-      io.prt = nullptr;
-      io.cnt = nullptr;
-      const bool ok = NT == 2 ? att_item<2, true, false>(p, sm, cs, L, io, p0, h, 0, 1, 0, p0 + 2, true)
-                              : att_item<1, true, false>(p, sm, cs, L, io, p0, h, 0, 1, 0, p0 + 1, true);
-      if (!ok) return false;
+      watt_item<true>(p, cs, L, p.bw.qkv + static_cast<size_t>(s * NT) * QKV_ROWS, NT, p0, h,
+                      reinterpret_cast<uint8_t*>(p.bs[s].cpk + off), reinterpret_cast<uint8_t*>(p.bs[s].cpv + off),
+                      p.bw.abuf[1], s * NT, 0, 1, 0, p0 + NT, true, nullptr, nullptr);
     }
   } else {
     const LayerW* L = p.bb_layers + li;
-    int total = 0;
+    int tot = 0;
     for (int s = 0; s < B; ++s)
-      if (bst.act[s]) total += NKVH * min(MAX_ATT_CHUNKS, (bst.pos[s] + 1 + BATT_SPAN - 1) / BATT_SPAN);
-    for (int item = cs.cta; item < total; item += cs.G) {
+      if (bst.act[s]) tot += bst.pos[s] + 1;
+    // chunk length: the smallest (in steps of 1/8) for which every item gets its own warp
+    int CL = max(16, (tot * NKVH + NW - 1) / NW);
+    auto nch_of = [&](int S) { return min(MAX_ATT_CHUNKS, (S + CL - 1) / CL); };
+    int total = 0;
+    for (int it = 0; it < 64; ++it) {
+      total = 0;
+      for (int s = 0; s < B; ++s)
+        if (bst.act[s]) total += NKVH * nch_of(bst.pos[s] + 1);
+      if (total <= NW) break;
+      CL += max(1, CL / 8);
+    }
+    for (int item = gw; item < total; item += NW) {
       int idx = item, s = 0, nch = 1;
       for (; s < B; ++s) {
         if (!bst.act[s]) continue;
-        nch = min(MAX_ATT_CHUNKS, (bst.pos[s] + 1 + BATT_SPAN - 1) / BATT_SPAN);
+        nch = nch_of(bst.pos[s] + 1);
         if (idx < NKVH * nch) break;
         idx -= NKVH * nch;
       }
       const int h = idx / nch, c = idx - h * nch;
       const int S = bst.pos[s] + 1, chunk = (S + nch - 1) / nch;
       const int s0 = c * chunk, s1 = min(S, s0 + chunk);
-      if (chunk > ATT_CHMAX) {
-        fail(p, sm, DEV_ERR_BAD_POSITION);
-        return false;
-      }
-      AttIO io;
-      io.qkv = p.bw.qkv + static_cast<size_t>(s) * QKV_ROWS;
       const size_t off = (static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq * HD;
-      io.kb = reinterpret_cast<uint8_t*>(p.bs[s].k + off);
-      io.vb = reinterpret_cast<uint8_t*>(p.bs[s].v + off);
-      io.out = nullptr;
-      io.hilo = p.bw.abuf[1];
-      io.tok0 = s;
-      io.prt = p.bw.prt + static_cast<size_t>(s) * NQH * MAX_ATT_CHUNKS * PRT_STRIDE;
-      io.cnt = p.bw.att_cnt + s * NKVH + h;
-      if (!att_item<1, false, false>(p, sm, cs, L, io, bst.pos[s], h, c, nch, s0, s1, c == 0)) return false;
+      watt_item<false>(p, cs, L, p.bw.qkv + static_cast<size_t>(s) * QKV_ROWS, 1, bst.pos[s], h,
+                       reinterpret_cast<uint8_t*>(p.bs[s].k + off), reinterpret_cast<uint8_t*>(p.bs[s].v + off),
+                       p.bw.abuf[1], s, c, nch, s0, s1, s1 == S,
+                       p.bw.prt + static_cast<size_t>(s) * NQH * MAX_ATT_CHUNKS * PRT_STRIDE,
+                       p.bw.att_cnt + s * NKVH + h);
     }
   }
   return grid_sync(p, sm, cs);
@@ -676,18 +981,15 @@ __device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int l
   // ---- QKV (deferred input norm)
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
-          const float rs = t < T ? b_rstd(ssq, t, eps) : 0.f;
-          for (int c0 = 0; c0 < N; c0 += 16) {
-            float v[16];
-            acc.ld16(c0, v);
-            if (t < T) {
+    if (!b_gemm(
+            p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn,
+            [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
+            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
+              float v[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] *= rs;
-              st16_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + WBOX * b0 + c0, v);
-            }
-          }
-        }))
+              for (int i = 0; i < 16; ++i) v[i] = y[i] * st.rs;
+              st16_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
+            }))
       return false;
   }
   // ---- attention -> A planes of o_proj
@@ -695,82 +997,71 @@ __device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int l
   // ---- o_proj + residual -> hmid, A planes of gate/up (post-attention norm), sums of squares
   {
     unsigned long long* ssq = b_ssq_next(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_O, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
-          double ss = 0.0;
-          for (int c0 = 0; c0 < N; c0 += 16) {
-            float v[16];
-            acc.ld16(c0, v);
-            if (t < T) {
-              const int r0 = WBOX * b0 + c0;
-              float res[16], wn[16], a[16];
-              ld16_f32(hin + t * HID + r0, res);
-              ld16_bf16(L->post_norm + r0, wn);
+    if (!b_gemm(
+            p, sm, cs, BGemm{BK_O, li, 0, T}, gn,
+            [&](int t, int r0, EpiSt& st) {
+              ld16_f32(hin + t * HID + r0, st.a);
+              ld16_bf16(L->post_norm + r0, st.b);
+            },
+            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
+              double ss = 0.0;
+              float v[16], a[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                v[i] += res[i];
-                a[i] = v[i] * wn[i];
+                v[i] = y[i] + st.a[i];
+                a[i] = v[i] * st.b[i];
                 ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
               }
               st16_f32(p.bw.hmid + t * HID + r0, v);
               hilo_store16(p.bw.abuf[0], t, r0, a);
-            }
-          }
-          if (t < T) b_ssq_add(ssq, t, ss);
-        }))
+              b_ssq_add(ssq, t, ss);
+            }))
       return false;
   }
   // ---- gate/up + SiLU (deferred post-attention norm) -> A planes of down
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_GU, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
-          const float rs = t < T ? b_rstd(ssq, t, eps) : 0.f;
-          for (int c0 = 0; c0 < WBOX * nb; c0 += 16) {
-            float gv[16], uv[16];
-            acc.ld16(c0, gv);
-            acc.ld16(WBOX * nb + c0, uv);
-            if (t < T) {
+    if (!b_gemm(
+            p, sm, cs, BGemm{BK_GU, li, 0, T}, gn,
+            [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
+            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
               float m[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                const float gg = gv[i] * rs, uu = uv[i] * rs;
+                const float gg = y[i] * st.rs, uu = y2[i] * st.rs;
                 m[i] = (gg / (1.0f + expf(-gg))) * uu;
               }
-              hilo_store16(p.bw.abuf[1], t, WBOX * b0 + c0, m);
-            }
-          }
-        }))
+              hilo_store16(p.bw.abuf[1], t, r0, m);
+            }))
       return false;
   }
   // ---- down + residual -> layer output, A planes of the next layer (its input norm), sums
   {
     unsigned long long* ssq = b_ssq_next(p, cs);
-    if (!b_gemm(p, sm, cs, BGemm{BK_D, li, 0, T}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
-          double ss = 0.0;
-          for (int c0 = 0; c0 < N; c0 += 16) {
-            float v[16];
-            acc.ld16(c0, v);
-            if (t < T) {
-              const int r0 = WBOX * b0 + c0;
-              float res[16], a[16];
-              ld16_f32(p.bw.hmid + t * HID + r0, res);
+    if (!b_gemm(
+            p, sm, cs, BGemm{BK_D, li, 0, T}, gn,
+            [&](int t, int r0, EpiSt& st) {
+              ld16_f32(p.bw.hmid + t * HID + r0, st.a);
+              if (next_norm) ld16_bf16(next_norm + r0, st.b);
+            },
+            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
+              double ss = 0.0;
+              float v[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                v[i] += res[i];
+                v[i] = y[i] + st.a[i];
                 if (!cp) v[i] = round_bf16(v[i]);
                 ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
               }
               st16_f32(hout + t * HID + r0, v);
               if (next_norm) {
-                float wn[16];
-                ld16_bf16(next_norm + r0, wn);
+                float a[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) a[i] = v[i] * wn[i];
+                for (int i = 0; i < 16; ++i) a[i] = v[i] * st.b[i];
                 hilo_store16(p.bw.abuf[0], t, r0, a);
               }
-            }
-          }
-          if (t < T) b_ssq_add(ssq, t, ss);
-        }))
+              b_ssq_add(ssq, t, ss);
+            }))
       return false;
   }
   return true;
@@ -799,22 +1090,20 @@ __device__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hi
   unsigned long long* amax = p.bw.amax + slot * TBMAX;
   if (cs.cta == 0)
     for (int t = cs.tid; t < TBMAX; t += NCT) __stcg(p.bw.amax + (slot ^ 1) * TBMAX + t, 0ull);
-  return b_gemm(p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, [&](int t, const BAcc& acc, int b0, int nb, int N) {
-    SampleCfg c = cfg;
-    if (t < p.nb && hidx == 0) {
-      c.seen = (c.penalty != 1.f) ? p.bs[t].st->seen : nullptr;
-      c.mask_eos = (p.mode == MODE_B_HEAD) ? (p.sp.min_new_tokens > 0 ? 1 : 0)
-                                           : ((bst.step[t] + 1 < p.sp.min_new_tokens) ? 1 : 0);
-    }
-    unsigned long long best = 0ull;
-    for (int c0 = 0; c0 < N; c0 += 16) {
-      float v[16];
-      acc.ld16(c0, v);
-      if (t < p.nb) {
+  return b_gemm(
+      p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, [&](int t, int r0, EpiSt& st) {},
+      [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
+        SampleCfg c = cfg;
+        if (hidx == 0) {
+          c.seen = (c.penalty != 1.f) ? p.bs[t].st->seen : nullptr;
+          c.mask_eos = (p.mode == MODE_B_HEAD) ? (p.sp.min_new_tokens > 0 ? 1 : 0)
+                                               : ((bst.step[t] + 1 < p.sp.min_new_tokens) ? 1 : 0);
+        }
+        unsigned long long best = 0ull;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int row = WBOX * b0 + c0 + i;
-          const float lg = round_bf16(v[i]);
+          const int row = r0 + i;
+          const float lg = round_bf16(y[i]);
           if (hidx > 0 && p.dbg_cp_logits != nullptr)   // parity tests: [B][15][cp_vocab]
             p.dbg_cp_logits[(static_cast<size_t>(t) * NCPHEADS + hidx - 1) * p.cp_vocab + row] = lg;
           if (hidx == 0 && p.dbg_g0_logits != nullptr && p.mode == MODE_B_FRAME)   // [B][vocab]
@@ -826,10 +1115,8 @@ __device__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hi
             best = k > best ? k : best;
           }
         }
-      }
-    }
-    if (t < p.nb && !c.do_sample && best != 0ull) atomicMax(amax + t, best);
-  });
+        if (!c.do_sample && best != 0ull) atomicMax(amax + t, best);
+      });
 }
 
 // Token of utterance s from head slot `slot` (greedy) or bw.tok (sampled, column col).
@@ -1104,6 +1391,7 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     cs.warp = warp;
     cs.lane = tid & 31;
     cs.dk = 0;
+    cs.gi = 0;
     bool ok;
     if (p.mode == MODE_B_FRAME)
       ok = b_frame(p, sm, cs);

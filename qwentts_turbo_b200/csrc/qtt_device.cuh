@@ -68,31 +68,6 @@ __device__ __forceinline__ bool mbar_test_parity(uint64_t* bar, uint32_t parity)
       : "memory");
   return ok != 0;
 }
-// Non-blocking probe of the phase (test_wait returns at once; try_wait may suspend the thread).
-__device__ __forceinline__ bool mbar_probe_parity(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded spin with test_wait (for the single-thread pipeline roles of the batched kernel).
-__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_probe_parity(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_probe_parity(bar, parity)) return true;
-    if ((it & 255u) == 255u) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > QTT_WAIT_NS) return false;
-    }
-  }
-}
-
 // Bounded wait for the phase with the given parity; also gives up when *abort is set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_test_parity(bar, parity)) return true;

@@ -380,6 +380,7 @@ struct Cons {
   uint32_t slot, round, bar_target;
   int cta, G, tid, warp, lane;
   int dk;   // fused MLP stages completed in this launch (selects the fixed-point output buffer)
+  int gi;   // batched kernel: GEMM stages completed in this launch (selects the K-split counter bank)
 };
 
 // A layer's input or output hidden state in global memory: fp32 (first layer of a stack,
@@ -428,9 +429,10 @@ __device__ __forceinline__ void fail(const Params& p, Smem& sm, int code) {
   *reinterpret_cast<volatile int*>(&sm.abort) = 1;
 }
 
-// Profiling stamp of CTA 0 for the current stage (no-op unless dbg_marks is set).
+// Profiling stamp of CTA 0 for the current stage (no-op unless dbg_marks is set; the batched
+// kernel, p.nb > 0, uses dbg_marks for its own trace).
 __device__ __forceinline__ void stage_mark(const Params& p, const Cons& cs, int id) {
-  if (p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0) {
+  if (p.dbg_marks != nullptr && p.nb == 0 && cs.cta == 0 && cs.tid == 0) {
     const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
     if (static_cast<int>(k * 3 + id) < p.dbg_marks_len) p.dbg_marks[k * 3 + id] = globaltimer_ns();
   }
@@ -1957,7 +1959,7 @@ size_t bwork_bytes() {
   n += sizeof(uint32_t) * TBMAX * NKVH;                              // att_cnt
   n += sizeof(int32_t) * BMAX * NGROUPS;                             // tok
   n += sizeof(uint32_t) * BKCTAS;                                    // kcnt
-  n += sizeof(float) * BKCTAS * TBMAX * 64 + 256;                    // kpart
+  n += sizeof(float) * BKCTAS * TBMAX * KPAD + 256;                  // kpart
   n += 2 * sizeof(bf16) * 2 * TBMAX * ABUF_LD;                      // abuf
   n += sizeof(float) * TBMAX * HID * 3;                              // x, hb[2]
   n += sizeof(float) * TBMAX * QKV_ROWS;                             // qkv
@@ -1988,7 +1990,7 @@ void bwork_carve(void* base, BWork* w) {
   w->qkv = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * QKV_ROWS;
   w->hmid = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * HID;
   w->logits = reinterpret_cast<float*>(c); c += sizeof(float) * BMAX * VMAX;
-  w->kpart = reinterpret_cast<float*>(c); c += sizeof(float) * BKCTAS * TBMAX * 64;
+  w->kpart = reinterpret_cast<float*>(c); c += sizeof(float) * BKCTAS * TBMAX * KPAD;
   w->prt = reinterpret_cast<float*>(c);
 }
 
@@ -2012,7 +2014,9 @@ cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes) {
 cudaError_t launch_b(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(p.w.bar, 0, sizeof(uint32_t), stream);
   if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(p.bw.ssq, 0, sizeof(unsigned long long) * 5 * TBMAX, stream);   // ssq + amax
+  // ssq, amax, att_cnt, tok and the K-split counters are contiguous at the start of the workspace
+  const size_t head = reinterpret_cast<const char*>(p.bw.kcnt + BKCTAS) - reinterpret_cast<const char*>(p.bw.ssq);
+  e = cudaMemsetAsync(p.bw.ssq, 0, head, stream);
   if (e != cudaSuccess) return e;
   void* args[] = {const_cast<Params*>(&p)};
   return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(qtt_batch_kernel), dim3(num_ctas), dim3(NTHREADS_B),

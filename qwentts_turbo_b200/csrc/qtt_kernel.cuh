@@ -153,7 +153,8 @@ struct BWork {
   float* kpart;            // [BKCTAS][TBMAX][64] K-split GEMM partials, one block per CTA
   uint32_t* kcnt;          // [BKCTAS] last-arriver counters of K-split row blocks
 };
-constexpr int BKCTAS = 160;               // most CTAs a batched launch may have
+constexpr int BKCTAS = 160;
+constexpr int BNMAX = 128;                 // batched GEMM: weight rows per CTA tile (one TMA box per atom)               // most CTAs a batched launch may have
 size_t bwork_bytes();
 void bwork_carve(void* base, BWork* w);
 
