@@ -174,29 +174,39 @@ __device__ __forceinline__ void btrace(const Params& p, int gemm, int cta, int G
   if (i < p.dbg_marks_len) p.dbg_marks[i] = globaltimer_ns();
 }
 
-// The GEMM stages of the launch's program, in order; f returns false to stop.
+// The GEMM stages of the launch's program, in order, by index (one call site for the role
+// loops keeps their code compact): a frame is 15 code-predictor passes of n_cp layers x 4 GEMMs +
+// a head, then n_bb backbone layers x 4 + the codec head; a prefill step the n_bb layers; the first
+// token the codec head.
+__device__ __forceinline__ int b_ngemm(const Params& p) {
+  if (p.mode == MODE_B_FRAME) return NCPHEADS * (4 * p.n_cp + 1) + 4 * p.n_bb + 1;
+  if (p.mode == MODE_B_PREFILL) return 4 * p.n_bb;
+  return 1;
+}
+__device__ __forceinline__ BGemm b_gemm_at(const Params& p, int i) {
+  const int B = p.nb;
+  if (p.mode == MODE_B_FRAME) {
+    const int per = 4 * p.n_cp + 1;
+    if (i < NCPHEADS * per) {
+      const int g = i / per, r = i - g * per;
+      if (r == 4 * p.n_cp) return BGemm{BK_HEAD, 0, 1 + g, B};
+      return BGemm{r & 3, p.n_bb + (r >> 2), 0, g == 0 ? 2 * B : B};
+    }
+    i -= NCPHEADS * per;
+  } else if (p.mode != MODE_B_PREFILL) {
+    return BGemm{BK_HEAD, 0, 0, B};
+  }
+  if (i == 4 * p.n_bb) return BGemm{BK_HEAD, 0, 0, B};
+  return BGemm{i & 3, i >> 2, 0, B};
+}
+static_assert(BK_QKV == 0 && BK_O == 1 && BK_GU == 2 && BK_D == 3, "GEMM kinds in layer order");
+
+// Calls f(gemm index, stage) for every GEMM stage of the launch; f returns false to stop.
 template <class F>
 __device__ void b_walk(const Params& p, F&& f) {
-  const int B = p.nb;
-  auto layer = [&](int li, int T) -> bool {
-    return f(BGemm{BK_QKV, li, 0, T}) && f(BGemm{BK_O, li, 0, T}) && f(BGemm{BK_GU, li, 0, T}) &&
-           f(BGemm{BK_D, li, 0, T});
-  };
-  if (p.mode == MODE_B_FRAME) {
-    for (int g = 0; g < NCPHEADS; ++g) {
-      for (int l = 0; l < p.n_cp; ++l)
-        if (!layer(p.n_bb + l, g == 0 ? 2 * B : B)) return;
-      if (!f(BGemm{BK_HEAD, 0, 1 + g, B})) return;
-    }
-    for (int l = 0; l < p.n_bb; ++l)
-      if (!layer(l, B)) return;
-    f(BGemm{BK_HEAD, 0, 0, B});
-  } else if (p.mode == MODE_B_PREFILL) {
-    for (int l = 0; l < p.n_bb; ++l)
-      if (!layer(l, B)) return;
-  } else {
-    f(BGemm{BK_HEAD, 0, 0, B});
-  }
+  const int n = b_ngemm(p);
+  for (int i = 0; i < n; ++i)
+    if (!f(i, b_gemm_at(p, i))) return;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -207,10 +217,8 @@ __device__ void b_producer(const Params& p, Smem& sm, int cta, int G) {
   uint8_t* wring = reinterpret_cast<uint8_t*>(sm.ring);
   uint32_t m = 0;
   int* err = p.w.err;
-  int gidx = 0;
-  b_walk(p, [&](const BGemm& g) -> bool {
+  b_walk(p, [&](int gi, const BGemm& g) -> bool {
     const BSplit sp = bg_split(p, g, cta, G);
-    const int gi = gidx++;
     if (sp.nb == 0) return true;
     const int N = bg_N(g.kind, sp.nb), nbox = bg_nbox(g.kind), brows = N / nbox;
     bool first = true;
@@ -251,10 +259,8 @@ __device__ void b_aloader(const Params& p, Smem& sm, int cta, int G) {
   uint32_t na = 0, n = 0;
   int* err = p.w.err;
   for (int b = 0; b < 2; ++b) tensormap_acquire(bmap(p, bmap_abuf(p, b, false)));
-  int gidx = 0;
-  b_walk(p, [&](const BGemm& g) -> bool {
+  b_walk(p, [&](int gi, const BGemm& g) -> bool {
     const BSplit sp = bg_split(p, g, cta, G);
-    const int gi = gidx++;
     if (sp.nb == 0) return true;
     const int ntiles = (g.T + 63) >> 6;
     const uint8_t* amap = bmap(p, bmap_abuf(p, bg_abuf(g.kind), false));
@@ -304,10 +310,8 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
       *reinterpret_cast<volatile int*>(&sm.abort) = 1;
     }
   };
-  int gidx = 0;
-  b_walk(p, [&](const BGemm& g) -> bool {
+  b_walk(p, [&](int gi, const BGemm& g) -> bool {
     const BSplit sp = bg_split(p, g, cta, G);
-    const int gi = gidx++;
     if (sp.nb == 0) return true;
     const int N = bg_N(g.kind, sp.nb), nks = sp.ks1 - sp.ks0, ntiles = (g.T + 63) >> 6;
     const uint32_t idesc = umma_idesc_bf16(128, N);
@@ -458,131 +462,161 @@ __device__ bool b_wait_count(const Params& p, Smem& sm, const uint32_t* cnt, uin
 //   3. K split: the slice's D rows to global memory, count, wait for the row tile's other slices,
 //      and sum the nk slices (slice order) for this CTA's share of the items;
 //   4. the epilogue of this CTA's items (all of them without a K split); the grid barrier.
-template <class PRE, class RUN>
-__device__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, PRE&& pre, RUN&& run) {
-  const BSplit sp = bg_split(p, g, cs.cta, cs.G);
-  const bool tr = p.dbg_marks != nullptr && cs.tid == 0;
-  const int gi = cs.gi;
-  const uint32_t bank = static_cast<uint32_t>(cs.gi & 1) * BKBANK;
+// Steps 1-3 and the barrier are shared code (b_gemm_begin / b_gemm_mid / b_gemm_end): the stage
+// kinds differ only in the item callbacks, so the kernel keeps one copy of the pipeline.
+struct BStage {
+  BSplit sp;
+  int gi, N, NO, nci, i0, i1, r0b, T;
+  bool gu;
+  float* Y;   // staged D, [T][N + 1] in the (idle) activation ring
+};
+
+__device__ __noinline__ bool b_gemm_begin(const Params& p, Smem& sm, Cons& cs, const BGemm& g, BStage& S) {
+  S.sp = bg_split(p, g, cs.cta, cs.G);
+  S.gi = cs.gi;
   // the other counter bank was last used by the previous GEMM stage, whose barrier has passed
+  const uint32_t bank = static_cast<uint32_t>(cs.gi & 1) * BKBANK;
   if (cs.cta == 0 && cs.tid < BKBANK) __stcg(p.bw.kcnt + (bank ^ BKBANK) + cs.tid, 0u);
   cs.gi++;
-  if (sp.nb == 0) return grid_sync(p, sm, cs);
-  const int N = bg_N(g.kind, sp.nb);
-  const bool gu = g.kind == BK_GU;
-  const int NO = gu ? N / 2 : N, nci = NO / 16, items = g.T * nci;
-  const int i0 = split_lo(items, sp.nk, sp.kspl), i1 = split_lo(items, sp.nk, sp.kspl + 1);
-  const int r0b = WBOX * sp.b0;
-  if (tr) btrace(p, gi, cs.cta, cs.G, BT_START);
+  if (S.sp.nb == 0) return false;
+  S.T = g.T;
+  S.N = bg_N(g.kind, S.sp.nb);
+  S.gu = g.kind == BK_GU;
+  S.NO = S.gu ? S.N / 2 : S.N;
+  S.nci = S.NO / 16;
+  const int items = g.T * S.nci;
+  S.i0 = split_lo(items, S.sp.nk, S.sp.kspl);
+  S.i1 = split_lo(items, S.sp.nk, S.sp.kspl + 1);
+  S.r0b = WBOX * S.sp.b0;
+  S.Y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sm.ring) + NWS * WS_BYTES);
+  if (p.dbg_marks != nullptr && cs.tid == 0) btrace(p, S.gi, cs.cta, cs.G, BT_START);
   if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_GO]);
-  EpiSt st;
-  if (i0 + cs.tid < i1) {
-    const int i = i0 + cs.tid;
-    pre(i / nci, r0b + 16 * (i % nci), st);
-  }
-  bool ok = true;
-  float* Y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sm.ring) + NWS * WS_BYTES);   // [T][N + 1]
-  const int YST = N + 1;
+  return true;
+}
+
+// Steps 2-3; false on abort.
+__device__ __noinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, const BStage& S, uint32_t gemm_n) {
+  const bool tr = p.dbg_marks != nullptr && cs.tid == 0;
+  const BSplit& sp = S.sp;
+  float* Y = S.Y;
+  const int N = S.N, YST = N + 1;
   if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
     if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
-    ok = false;
-  } else {
-    if (tr) btrace(p, gi, cs.cta, cs.G, BT_DREADY);
-    tc_fence_after();
-    // 2. D -> Y (the activation ring is idle until the next stage's GO)
-    const int ntiles = (g.T + 63) >> 6, nch = N / 16;
-    const int q = cs.warp & 3, wq = cs.warp >> 2, half = q & 1;
-    for (int ph = 0; ph < 2; ++ph) {
-      if ((q >> 1) == (ph == 0 ? 1 : 0)) {
-        for (int job = wq; job < ntiles * nch; job += NCW / 4) {
-          const int j = job / nch, c = job - j * nch;
-          if (64 * j + 32 * half < g.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
-            float v[16];
-            tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * DCOLS + 16 * c, v);
-            const int t = 64 * j + 32 * half + cs.lane;
-            if (t < g.T) {
-              float* yr = Y + t * YST + 16 * c;
-              if (ph == 0) {
+    return false;
+  }
+  if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_DREADY);
+  tc_fence_after();
+  // D -> Y (the activation ring is idle until the next stage's GO)
+  const int ntiles = (S.T + 63) >> 6, nch = N / 16;
+  const int q = cs.warp & 3, wq = cs.warp >> 2, half = q & 1;
+  for (int ph = 0; ph < 2; ++ph) {
+    if ((q >> 1) == (ph == 0 ? 1 : 0)) {
+      for (int job = wq; job < ntiles * nch; job += NCW / 4) {
+        const int j = job / nch, c = job - j * nch;
+        if (64 * j + 32 * half < S.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
+          float v[16];
+          tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * DCOLS + 16 * c, v);
+          const int t = 64 * j + 32 * half + cs.lane;
+          if (t < S.T) {
+            float* yr = Y + t * YST + 16 * c;
+            if (ph == 0) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) yr[i] = v[i];
-              } else {
+              for (int i = 0; i < 16; ++i) yr[i] = v[i];
+            } else {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) yr[i] += v[i];
-              }
+              for (int i = 0; i < 16; ++i) yr[i] += v[i];
             }
           }
         }
       }
-      if (ph == 1) tc_fence_before();
-      named_sync(1, NCT);
-      if (ph == 0 && tr) btrace(p, gi, cs.cta, cs.G, BT_PH1);
     }
-    if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
-    if (tr) btrace(p, gi, cs.cta, cs.G, BT_STAGED);
-    // 3. K split
-    if (sp.nk > 1) {
-      float* part = p.bw.kpart + static_cast<size_t>(cs.cta) * TBMAX * KPAD;
-      const int n4 = N / 4;
-      for (int e = cs.tid; e < g.T * n4; e += NCT) {
-        const int t = e / n4, c4 = e - t * n4;
-        const float* yr = Y + t * YST + 4 * c4;
-        __stcg(reinterpret_cast<float4*>(part + t * KPAD + 4 * c4), make_float4(yr[0], yr[1], yr[2], yr[3]));
-      }
-      // bar.sync orders the CTA's stores before thread 0, whose release add publishes them at
-      // gpu scope (the pattern of grid_sync)
-      named_sync(1, NCT);
-      uint32_t* cnt = p.bw.kcnt + bank + sp.rb;
-      if (cs.tid == 0) {
-        if (tr) btrace(p, gi, cs.cta, cs.G, BT_PART);
-        red_release_gpu_add(cnt, 1u);
-        sm.bcast[0] = b_wait_count(p, sm, cnt, static_cast<uint32_t>(sp.nk)) ? 1 : 0;
-        if (tr) btrace(p, gi, cs.cta, cs.G, BT_COUNT);
-      }
-      named_sync(1, NCT);
-      if (!sm.bcast[0]) {
-        *reinterpret_cast<volatile int*>(&sm.abort) = 1;
-        ok = false;
-      } else {
-        const int ppi = gu ? 8 : 4;   // float4 pieces per item
-        const float* base = p.bw.kpart + static_cast<size_t>(sp.rb * sp.nk) * TBMAX * KPAD;
-        for (int e = cs.tid; e < (i1 - i0) * ppi; e += NCT) {
-          const int it = i0 + e / ppi, pc = e % ppi;
-          const int t = it / nci, c = it - t * nci;
-          const int col = (pc < 4 ? 16 * c : NO + 16 * c) + 4 * (pc & 3);
-          const float* src = base + static_cast<size_t>(t) * KPAD + col;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int k0 = 0; k0 < sp.nk; k0 += 8) {   // eight slices' loads in flight, added in slice order
-            float4 v[8];
+    if (ph == 1) tc_fence_before();
+    named_sync(1, NCT);
+    if (ph == 0 && tr) btrace(p, S.gi, cs.cta, cs.G, BT_PH1);
+  }
+  if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
+  if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_STAGED);
+  if (sp.nk == 1) return true;
+  // K split
+  float* part = p.bw.kpart + static_cast<size_t>(cs.cta) * TBMAX * KPAD;
+  const int n4 = N / 4;
+  for (int e = cs.tid; e < S.T * n4; e += NCT) {
+    const int t = e / n4, c4 = e - t * n4;
+    const float* yr = Y + t * YST + 4 * c4;
+    __stcg(reinterpret_cast<float4*>(part + t * KPAD + 4 * c4), make_float4(yr[0], yr[1], yr[2], yr[3]));
+  }
+  // bar.sync orders the CTA's stores before thread 0, whose release add publishes them at gpu
+  // scope (the pattern of grid_sync)
+  named_sync(1, NCT);
+  uint32_t* cnt = p.bw.kcnt + static_cast<uint32_t>(S.gi & 1) * BKBANK + sp.rb;
+  if (cs.tid == 0) {
+    if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_PART);
+    red_release_gpu_add(cnt, 1u);
+    sm.bcast[0] = b_wait_count(p, sm, cnt, static_cast<uint32_t>(sp.nk)) ? 1 : 0;
+    if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_COUNT);
+  }
+  named_sync(1, NCT);
+  if (!sm.bcast[0]) {
+    *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+    return false;
+  }
+  const int ppi = S.gu ? 8 : 4;   // float4 pieces per item
+  const float* base = p.bw.kpart + static_cast<size_t>(sp.rb * sp.nk) * TBMAX * KPAD;
+  for (int e = cs.tid; e < (S.i1 - S.i0) * ppi; e += NCT) {
+    const int it = S.i0 + e / ppi, pc = e % ppi;
+    const int t = it / S.nci, c = it - t * S.nci;
+    const int col = (pc < 4 ? 16 * c : S.NO + 16 * c) + 4 * (pc & 3);
+    const float* src = base + static_cast<size_t>(t) * KPAD + col;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < sp.nk; k0 += 8) {   // eight slices' loads in flight, added in slice order
+      float4 v[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              if (k0 + k < sp.nk) v[k] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(k0 + k) * TBMAX * KPAD));
+      for (int k = 0; k < 8; ++k)
+        if (k0 + k < sp.nk) v[k] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(k0 + k) * TBMAX * KPAD));
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              if (k0 + k < sp.nk) {
-                acc.x += v[k].x; acc.y += v[k].y; acc.z += v[k].z; acc.w += v[k].w;
-              }
-          }
-          float* yr = Y + t * YST + col;
-          yr[0] = acc.x; yr[1] = acc.y; yr[2] = acc.z; yr[3] = acc.w;
+      for (int k = 0; k < 8; ++k)
+        if (k0 + k < sp.nk) {
+          acc.x += v[k].x; acc.y += v[k].y; acc.z += v[k].z; acc.w += v[k].w;
         }
-        named_sync(1, NCT);
-        if (tr) btrace(p, gi, cs.cta, cs.G, BT_REDUCED);
-      }
     }
-    // 4. epilogue items
-    if (ok) {
-      for (int i = i0 + cs.tid; i < i1; i += NCT) {
-        const int t = i / nci, c = i - t * nci, r0 = r0b + 16 * c;
-        if (i != i0 + cs.tid) pre(t, r0, st);
-        const float* yr = Y + t * YST + 16 * c;
-        run(t, r0, yr, gu ? yr + NO : yr, st);
-      }
+    float* yr = Y + t * YST + col;
+    yr[0] = acc.x; yr[1] = acc.y; yr[2] = acc.z; yr[3] = acc.w;
+  }
+  named_sync(1, NCT);
+  if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_REDUCED);
+  return true;
+}
+
+__device__ __noinline__ bool b_gemm_end(const Params& p, Smem& sm, Cons& cs, int gi, bool planes) {
+  fence_proxy_async_smem();   // Y aliases the activation ring: before the next stage's TMA writes
+  if (planes) fence_proxy_async_global();   // the epilogue wrote the next GEMM's operand planes
+  if (p.dbg_marks != nullptr && cs.tid == 0) btrace(p, gi, cs.cta, cs.G, BT_EPI);
+  const bool ok = grid_sync(p, sm, cs);
+  if (p.dbg_marks != nullptr && cs.tid == 0) btrace(p, gi, cs.cta, cs.G, BT_BARRIER);
+  return ok;
+}
+
+template <class PRE, class RUN>
+__device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, PRE&& pre,
+                                       RUN&& run) {
+  BStage S;
+  if (!b_gemm_begin(p, sm, cs, g, S)) return grid_sync(p, sm, cs);
+  EpiSt st;
+  if (S.i0 + cs.tid < S.i1) {
+    const int i = S.i0 + cs.tid;
+    pre(i / S.nci, S.r0b + 16 * (i % S.nci), st);
+  }
+  const bool ok = b_gemm_mid(p, sm, cs, S, gemm_n);
+  if (ok) {
+    const int YST = S.N + 1;
+    for (int i = S.i0 + cs.tid; i < S.i1; i += NCT) {
+      const int t = i / S.nci, c = i - t * S.nci, r0 = S.r0b + 16 * c;
+      if (i != S.i0 + cs.tid) pre(t, r0, st);
+      const float* yr = S.Y + t * YST + 16 * c;
+      run(t, r0, yr, S.gu ? yr + S.NO : yr, st);
     }
   }
-  fence_proxy_async_smem();   // Y aliases the activation ring: before the next stage's TMA writes
-  if (tr) btrace(p, gi, cs.cta, cs.G, BT_EPI);
-  const bool ok2 = grid_sync(p, sm, cs);
-  if (tr) btrace(p, gi, cs.cta, cs.G, BT_BARRIER);
+  const bool ok2 = b_gemm_end(p, sm, cs, S.gi, g.kind == BK_O || g.kind == BK_GU || g.kind == BK_D);
   gemm_n++;
   return ok && ok2;
 }
@@ -602,6 +636,13 @@ __device__ __forceinline__ const unsigned long long* b_ssq_cur(const Params& p, 
 }
 __device__ __forceinline__ void b_ssq_add(unsigned long long* ssq, int t, double ss) {
   atomicAdd(ssq + t, static_cast<unsigned long long>(__double2ll_rn(ss * 4294967296.0)));
+}
+
+// End of a stage whose generic-proxy stores (a GEMM operand's hi/lo planes) are read by TMA
+// (the async proxy) after the barrier: every writer orders its stores for that proxy first.
+__device__ __forceinline__ bool b_sync_planes(const Params& p, Smem& sm, Cons& cs) {
+  fence_proxy_async_global();
+  return grid_sync(p, sm, cs);
 }
 
 // Elementwise stages over T tokens x HID columns: CTA c owns 8-column units
@@ -633,12 +674,12 @@ __device__ bool b_input(const Params& p, Smem& sm, Cons& cs, int T, const bf16* 
     }
     b_ssq_add(ssq, t, ss);
   });
-  return grid_sync(p, sm, cs);
+  return b_sync_planes(p, sm, cs);
 }
 
 // NORM: head input A = bf16(RMSNorm(h)) (lo plane 0) for head tokens i < B taken from stack
 // token tmul * i + toff; hstate (backbone): the fp32 normed hidden of each active utterance.
-__device__ bool b_norm(const Params& p, Smem& sm, Cons& cs, const float* h, int tmul, int toff, const bf16* w,
+__device__ __noinline__ bool b_norm(const Params& p, Smem& sm, Cons& cs, const float* h, int tmul, int toff, const bf16* w,
                        bool hstate) {
   const unsigned long long* ssq = b_ssq_cur(p, cs);
   const BState bst = bstate(sm);
@@ -653,7 +694,7 @@ __device__ bool b_norm(const Params& p, Smem& sm, Cons& cs, const float* h, int 
       if (hstate && bst.act[i]) p.bs[i].st->h[k0 + j] = nv;
     }
   });
-  return grid_sync(p, sm, cs);
+  return b_sync_planes(p, sm, cs);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -673,21 +714,19 @@ static_assert(WL == 16 && WG == 2, "warp attention layout");
 
 __device__ __forceinline__ float bf16_at(const uint32_t* w, int i) { return (i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]); }
 
-// q/k RMSNorm (fused_decode_tts.cu:183-197) + RoPE at position pos on the dimensions
-// [8u, 8u + 8) in x; the rotation partner d +- 64 is in lane u ^ 8 of the same group.
-__device__ __forceinline__ void w_norm_rope(float (&x)[WD], const bf16* nw, const Params& p, int pos, int u) {
+// q/k RMSNorm (fused_decode_tts.cu:183-197) + RoPE on the dimensions [8u, 8u + 8) in x, with
+// the norm weights w4 and the position's cos / sin rows c4 / s4 (bf16, already loaded); the
+// rotation partner d +- 64 is in lane u ^ 8 of the same group.
+__device__ __forceinline__ void w_norm_rope(float (&x)[WD], uint4 w4, uint4 c4, uint4 s4, float eps, int u) {
   double ss = 0.0;
 #pragma unroll
   for (int i = 0; i < WD; ++i) ss = fma(static_cast<double>(x[i]), static_cast<double>(x[i]), ss);
 #pragma unroll
   for (int o = 1; o < WL; o <<= 1) ss += __shfl_xor_sync(WFULL, ss, o);
-  const float rstd = rms_scale(ss, HD, p.eps);
-  const uint4 w4 = *reinterpret_cast<const uint4*>(nw + WD * u);
+  const float rstd = rms_scale(ss, HD, eps);
   const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
   for (int i = 0; i < WD; ++i) x[i] = x[i] * rstd * bf16_at(w, i);
-  const uint4 c4 = *reinterpret_cast<const uint4*>(p.cos_tab + static_cast<size_t>(pos) * HD + WD * u);
-  const uint4 s4 = *reinterpret_cast<const uint4*>(p.sin_tab + static_cast<size_t>(pos) * HD + WD * u);
   const uint32_t c[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
   float y[WD];
 #pragma unroll
@@ -787,14 +826,24 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
                           uint8_t* kb, uint8_t* vb, bf16* hilo, int tok0, int c, int nch, int s0, int s1,
                           bool writer, float* prt, uint32_t* cnt) {
   const int g = cs.lane / WL, u = cs.lane % WL;
-  if (writer) {
-    for (int t = 0; t < NT; ++t) {
-      float k[WD], v[WD];
+  for (int t = 0; t < NT; ++t) {
+    // one round trip: raw q (both heads), k, v, the norm weights and the position's RoPE rows
+    const int pos = p0 + t;
+    float q0[WD], q1[WD], k[WD], v[WD];
+    ld8_f32(qkv + t * QKV_ROWS + (2 * h) * HD + WD * u, q0);
+    ld8_f32(qkv + t * QKV_ROWS + (2 * h + 1) * HD + WD * u, q1);
+    if (writer) {
       ld8_f32(qkv + t * QKV_ROWS + QSZ + h * HD + WD * u, k);
       ld8_f32(qkv + t * QKV_ROWS + QSZ + KVSZ + h * HD + WD * u, v);
-      w_norm_rope(k, L->k_norm, p, p0 + t, u);
+    }
+    const uint4 c4 = *reinterpret_cast<const uint4*>(p.cos_tab + static_cast<size_t>(pos) * HD + WD * u);
+    const uint4 s4 = *reinterpret_cast<const uint4*>(p.sin_tab + static_cast<size_t>(pos) * HD + WD * u);
+    const uint4 wq = *reinterpret_cast<const uint4*>(L->q_norm + WD * u);
+    const uint4 wk = writer ? *reinterpret_cast<const uint4*>(L->k_norm + WD * u) : make_uint4(0, 0, 0, 0);
+    if (writer) {   // the token's new K/V row, read back below like every other row
+      w_norm_rope(k, wk, c4, s4, p.eps, u);
       if (g == 0) {
-        const size_t row = static_cast<size_t>(p0 + t) * HD + WD * u;
+        const size_t row = static_cast<size_t>(pos) * HD + WD * u;
         if (CP) {
           float4* kd = reinterpret_cast<float4*>(reinterpret_cast<float*>(kb) + row);
           float4* vd = reinterpret_cast<float4*>(reinterpret_cast<float*>(vb) + row);
@@ -815,15 +864,10 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
           *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(vb) + row) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
         }
       }
+      __syncwarp();   // the row just stored is read back by the other lanes of this warp
     }
-    __syncwarp();   // the rows just stored are read back by the other lanes of this warp
-  }
-  for (int t = 0; t < NT; ++t) {
-    float q0[WD], q1[WD];
-    ld8_f32(qkv + t * QKV_ROWS + (2 * h) * HD + WD * u, q0);
-    ld8_f32(qkv + t * QKV_ROWS + (2 * h + 1) * HD + WD * u, q1);
-    w_norm_rope(q0, L->q_norm, p, p0 + t, u);
-    w_norm_rope(q1, L->q_norm, p, p0 + t, u);
+    w_norm_rope(q0, wq, c4, s4, p.eps, u);
+    w_norm_rope(q1, wq, c4, s4, p.eps, u);
     WSoft a0, a1;
     a0.init();
     a1.init();
@@ -920,7 +964,7 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
 // predictor: one warp item per (utterance, KV head) over its <= 17 positions, 2 tokens in the
 // first pass. Backbone: (utterance, KV head, chunk) items, chunk length chosen so that the
 // items of all active utterances spread over every consumer warp of the grid.
-__device__ bool b_attention(const Params& p, Smem& sm, Cons& cs, int li, bool cp, int pass) {
+__device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, int li, bool cp, int pass) {
   const BState bst = bstate(sm);
   const int B = p.nb;
   const int NW = cs.G * NCW, gw = cs.cta * NCW + cs.warp;
@@ -970,15 +1014,37 @@ __device__ bool b_attention(const Params& p, Smem& sm, Cons& cs, int li, bool cp
                        p.bw.att_cnt + s * NKVH + h);
     }
   }
-  return grid_sync(p, sm, cs);
+  return b_sync_planes(p, sm, cs);
+}
+
+// Backbone layer li: bulk L2 prefetch of every active utterance's cached K and V rows
+// [0, position) of the layer, spread over the CTAs (thread 0 each), issued at the start of the QKV
+// stage so that the attention stage after it reads them from L2. Skipped when the layer's rows
+// exceed KV_PREFETCH_MAX bytes (they would evict each other).
+constexpr long long KV_PREFETCH_MAX = 64ll << 20;
+__device__ void b_prefetch_kv(const Params& p, Smem& sm, const Cons& cs, int li) {
+  if (cs.tid != 0) return;
+  const BState bst = bstate(sm);
+  long long tot = 0;
+  for (int s = 0; s < p.nb; ++s)
+    if (bst.act[s]) tot += 2ll * NKVH * bst.pos[s] * HD * 2;
+  if (tot > KV_PREFETCH_MAX) return;
+  for (int it = cs.cta; it < p.nb * 2 * NKVH; it += cs.G) {
+    const int s = it / (2 * NKVH), r = it - s * 2 * NKVH, h = r >> 1;
+    if (!bst.act[s] || bst.pos[s] == 0) continue;
+    const bf16* base = (r & 1) ? p.bs[s].v : p.bs[s].k;
+    prefetch_l2_bulk(base + (static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq * HD,
+                     static_cast<uint32_t>(bst.pos[s]) * HD * 2);
+  }
 }
 
 // One decoder layer of the batch: QKV | attention | O | gate/up | down.
-__device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int pass, int T,
+__device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int pass, int T,
                         const float* hin, float* hout, const bf16* next_norm) {
   const LayerW* L = (cp ? p.cp_layers + (li - p.n_bb) : p.bb_layers + li);
   const float eps = p.eps;
-  // ---- QKV (deferred input norm)
+  // ---- QKV (deferred input norm); backbone: the layer's cached K/V rows start moving to L2
+  if (!cp) b_prefetch_kv(p, sm, cs, li);
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
     if (!b_gemm(
@@ -1085,7 +1151,8 @@ __device__ const float* b_stack(const Params& p, Smem& sm, Cons& cs, uint32_t& g
 // Head GEMM over the NORM stage's A planes: bf16 logits; greedy heads fold the masked argmax of
 // each token into amax[slot][t]; sampled heads store the logits for the sampler. The other slot
 // is cleared for the next head (two barriers away).
-__device__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hidx, const SampleCfg& cfg, int slot) {
+__device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hidx, const SampleCfg& cfg,
+                                    int slot) {
   const BState bst = bstate(sm);
   unsigned long long* amax = p.bw.amax + slot * TBMAX;
   if (cs.cta == 0)
@@ -1131,7 +1198,7 @@ __device__ __forceinline__ int b_token(const Params& p, const SampleCfg& cfg, in
 // Tokens of a head for every utterance, after its barrier, into bw.tok[s][col]: greedy from the
 // packed argmax (CTA 0 copies them; the next stage reads the slot directly), sampled by one CTA
 // per utterance followed by a barrier. frame_of: the Philox frame counter is step + frame_of.
-__device__ bool b_tokens(const Params& p, Smem& sm, Cons& cs, int hidx, const SampleCfg& cfg, int slot, int frame_of,
+__device__ __noinline__ bool b_tokens(const Params& p, Smem& sm, Cons& cs, int hidx, const SampleCfg& cfg, int slot, int frame_of,
                          int col) {
   const BState bst = bstate(sm);
   if (!cfg.do_sample) {
@@ -1233,8 +1300,11 @@ __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
         const int step = bst.step[s];
         const bf16* extra =
             step < p.bs[s].n_trailing ? p.bs[s].trailing + static_cast<size_t>(step) * HID : p.bs[s].pad;
+        // greedy heads publish their tokens in bw.tok without a barrier (CTA 0, for the frame
+        // results): the last head's token comes from its argmax slot, complete at its barrier
         int toks[NCPHEADS];
-        for (int q = 0; q < NCPHEADS; ++q) toks[q] = __ldcg(p.bw.tok + s * NGROUPS + q + 1);
+        for (int q = 0; q < NCPHEADS - 1; ++q) toks[q] = __ldcg(p.bw.tok + s * NGROUPS + q + 1);
+        toks[NCPHEADS - 1] = b_token(p, cpc, slot ^ 1, s, NCPHEADS);
 #pragma unroll 1
         for (int i = 0; i < 8; ++i) {
           const int k = k0 + i;

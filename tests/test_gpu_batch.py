@@ -140,6 +140,41 @@ def test_batch_matches_batch1_engine(dev_small):
     assert same >= 60, f"{same}/64 codes equal"
 
 
+def _batch_run(dev, embeds, trailing, pads, sp, n, debug):
+    B = len(embeds)
+    eng = Engine(dev, max_streams=B, max_seq=512, max_frames=16)
+    try:
+        if debug:   # the debug logit outputs change the heads' timing, not their results
+            cp = torch.zeros(B, 15, 2048, dtype=torch.float32, device="cuda")
+            g0 = torch.zeros(B, 3072, dtype=torch.float32, device="cuda")
+            eng.batch_set_debug_outputs(cp, g0)
+        eng.batch_prefill([e.cuda() for e in embeds], sp)
+        tr, pd = [t.cuda() for t in trailing], [x.cuda() for x in pads]
+        for _ in range(n):   # one launch per frame, state read back in between as a caller would
+            eng.batch_frames(1, tr, pd, sp)
+            _ = [eng.state(s) for s in range(B)]
+        eng.check()
+        return [eng.codes(s)[:n].cpu() for s in range(B)], [eng.hidden(s).cpu() for s in range(B)]
+    finally:
+        eng.batch_set_debug_outputs(None, None)
+        eng.close()
+
+
+def test_batch_runs_bit_identical(dev_small):
+    """Two runs of the same frames give bit-identical codes and hidden states, with and without
+    the debug outputs: every cross-CTA sum has a fixed order and every stage reads only data
+    published before its barrier (a stale read shows up here as a difference)."""
+    embeds, trailing, pads = _inputs([17, 30, 41], 5, 21)
+    sp = _greedy_sp(repetition_penalty=1.3)
+    a = _batch_run(dev_small, embeds, trailing, pads, sp, 4, False)
+    b = _batch_run(dev_small, embeds, trailing, pads, sp, 4, False)
+    c = _batch_run(dev_small, embeds, trailing, pads, sp, 4, True)
+    for s in range(3):
+        for other in (b, c):
+            assert torch.equal(a[0][s], other[0][s]), s
+            assert torch.equal(a[1][s], other[1][s]), s
+
+
 def test_batch_argument_errors(dev_small):
     eng = Engine(dev_small, max_streams=2, max_seq=64, max_frames=4)
     try:
