@@ -15,13 +15,15 @@
 //     below plane 0). After the stage's grid barrier the activation-loader warp streams them with
 //     2-D TMA boxes (64 columns x 64 tokens per plane; one slot per 64-token tile and K step of
 //     128 = two 128-byte swizzle atoms) into a 3-slot ring, independently of the MMA issue.
-//   * D: fp32 in tensor memory, N = 16..64 columns. An activation slot holds a 64-token tile's
-//     hi plane in rows 0..63 and its lo plane in rows 64..127, so one M = 128 tcgen05.mma per
-//     K sub-step of 16 gives D lane t = W hi[t] and lane 64 + t = W lo[t]; the epilogue adds
-//     them: D = W (hi + lo), ~16 mantissa bits of the activations, close to an fp32 GEMV.
-// The epilogue warps read D with tcgen05.ld (warp 4j + q owns tile j's token lanes 32q..32q+31,
-// one thread per token), apply the deferred RMSNorm scale and the stage's elementwise work, and
-// write the next GEMM's A planes. Sums of squares for the next RMSNorm are accumulated per token with
+//   * D: fp32 in tensor memory, N <= 128 columns. An activation slot holds a 64-token tile's hi
+//     plane in rows 0..63 and its lo plane in rows 64..127; per K sub-step of 16 one M = 128
+//     tcgen05.mma starts its A at the hi rows and a second one at the lo rows, both with the same
+//     weights, so TMEM lanes 0..63 hold D = W (hi + lo): ~16 mantissa bits of the activations,
+//     close to an fp32 GEMV.
+// The consumer warps of lane quarters 0 and 1 read D with tcgen05.ld (one thread per token) into
+// the K slice's partial; the row tile's slices are summed in a fixed order, the epilogue applies
+// the deferred RMSNorm scale and the stage's elementwise work, and writes the next GEMM's A
+// planes. Sums of squares for the next RMSNorm are accumulated per token with
 // 64-bit fixed-point atomics (order independent).
 //
 // Stages of a code-predictor pass: INPUT (embedding rows -> x, A planes, sums of squares) |
@@ -162,7 +164,6 @@ enum BTrace : int {
   BT_P0,            // producer: first weight box issued
   BT_P_END,         // producer: last weight box issued
   BT_LAST,          // MMA: the last K step's weights and activations ready
-  BT_PH1,           // consumers: lo lanes staged
   BT_ALAST,         // activation loader: last step's slot free (loads issued next)
   BT_S0,            // MMA: first step's MMAs and commits issued
   BT_W1,            // MMA: second step's weights ready
@@ -341,16 +342,21 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
         if (ks == 0 && j == 0) btrace(p, gi, cta, G, BT_A0);
         if (ks == nks - 1 && j == ntiles - 1) btrace(p, gi, cta, G, BT_LAST);
         tc_fence_after();
-        // one M = 128 MMA covers both planes: A rows 0..63 = hi, 64..127 = lo of the tile's tokens
+        // hi and lo planes along K: an M = 128 MMA whose A starts at the hi rows, then one whose A
+        // starts at the lo rows (8 KB further), both with the same W; TMEM lanes 0..63 collect
+        // hi.W + lo.W of the tile's 64 tokens, lanes 64..127 are not used (the A rows behind the
+        // lo plane stay inside the ring region)
         const uint64_t da = umma_desc_sw128(abase + as * AS_BYTES);
         const uint32_t dt = tmem + j * DCOLS;
 #pragma unroll
         for (int a = 0; a < NSUB; ++a)
 #pragma unroll
-          for (int kk = 0; kk < KSUB / 16; ++kk)   // the first MMA of the slice overwrites D
-            tc_mma_bf16(dt, da + static_cast<uint64_t>((a * ASUB_BYTES + kk * 32) >> 4),
-                        (a == 0 ? db0 : db1) + static_cast<uint64_t>((kk * 32) >> 4), idesc,
+          for (int kk = 0; kk < KSUB / 16; ++kk) {   // the first MMA of the slice overwrites D
+            const uint64_t dw = (a == 0 ? db0 : db1) + static_cast<uint64_t>((kk * 32) >> 4);
+            tc_mma_bf16(dt, da + static_cast<uint64_t>((a * ASUB_BYTES + kk * 32) >> 4), dw, idesc,
                         (ks | a | kk) != 0 ? 1u : 0u);
+            tc_mma_bf16(dt, da + static_cast<uint64_t>((a * ASUB_BYTES + APLANE_BYTES + kk * 32) >> 4), dw, idesc, 1u);
+          }
         any = true;
         tc_commit(&sm.bbar[BB_AEMPTY + as]);
       }
@@ -457,10 +463,10 @@ __device__ bool b_wait_count(const Params& p, Smem& sm, const uint32_t* cnt, uin
 // on D), and run(t, r0, y, y2, st) with y = D[t][16 columns] (gate/up: y = gate, y2 = up) and
 // r0 the first output column (row of W; gate/up: intermediate channel).
 //   1. release the activation loader (GO), prefetch the first item's inputs;
-//   2. wait for D; stage it in shared memory as hi + lo rows: the lo lanes (TMEM lanes 64..127,
-//      warps of lane quarters 2, 3) write, then the hi lanes add; D is freed;
-//   3. K split: the slice's D rows to global memory, count, wait for the row tile's other slices,
-//      and sum the nk slices (slice order) for this CTA's share of the items;
+//   2. wait for D; the warps of TMEM lane quarters 0 and 1 copy its rows (tokens) to the K slice's
+//      partial in global memory (a single slice: to shared memory); D is freed;
+//   3. K split: count, wait for the row tile's other slices, and sum the nk slices (slice order)
+//      for this CTA's share of the items;
 //   4. the epilogue of this CTA's items (all of them without a K split); the grid barrier.
 // Steps 1-3 and the barrier are shared code (b_gemm_begin / b_gemm_mid / b_gemm_end): the stage
 // kinds differ only in the item callbacks, so the kernel keeps one copy of the pipeline.
@@ -506,48 +512,41 @@ __device__ __noinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, con
   }
   if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_DREADY);
   tc_fence_after();
-  // D -> Y (the activation ring is idle until the next stage's GO)
+  // D rows (TMEM lanes 0..63 of each 64-token tile, read by the warps of lane quarters 0 and 1)
+  // -> this K slice's partial in global memory, or Y when the stage has a single slice (the
+  // activation ring is idle until the next stage's GO)
   const int ntiles = (S.T + 63) >> 6, nch = N / 16;
-  const int q = cs.warp & 3, wq = cs.warp >> 2, half = q & 1;
-  for (int ph = 0; ph < 2; ++ph) {
-    if ((q >> 1) == (ph == 0 ? 1 : 0)) {
-      for (int job = wq; job < ntiles * nch; job += NCW / 4) {
-        const int j = job / nch, c = job - j * nch;
-        if (64 * j + 32 * half < S.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
-          float v[16];
-          tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * DCOLS + 16 * c, v);
-          const int t = 64 * j + 32 * half + cs.lane;
-          if (t < S.T) {
+  const int q = cs.warp & 3, wq = cs.warp >> 2;
+  float* part = p.bw.kpart + static_cast<size_t>(cs.cta) * TBMAX * KPAD;
+  if (q < 2) {
+    for (int job = wq; job < ntiles * nch; job += NCW / 4) {
+      const int j = job / nch, c = job - j * nch;
+      if (64 * j + 32 * q < S.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
+        float v[16];
+        tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * DCOLS + 16 * c, v);
+        const int t = 64 * j + 32 * q + cs.lane;
+        if (t < S.T) {
+          if (sp.nk > 1) {
+            float4* d4 = reinterpret_cast<float4*>(part + t * KPAD + 16 * c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) __stcg(d4 + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+          } else {
             float* yr = Y + t * YST + 16 * c;
-            if (ph == 0) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) yr[i] = v[i];
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) yr[i] += v[i];
-            }
+            for (int i = 0; i < 16; ++i) yr[i] = v[i];
           }
         }
       }
     }
-    if (ph == 1) tc_fence_before();
-    named_sync(1, NCT);
-    if (ph == 0 && tr) btrace(p, S.gi, cs.cta, cs.G, BT_PH1);
   }
+  tc_fence_before();
+  // bar.sync orders the CTA's partial stores before thread 0, whose release add publishes them at
+  // gpu scope (the pattern of grid_sync)
+  named_sync(1, NCT);
   if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
   if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_STAGED);
   if (sp.nk == 1) return true;
   // K split
-  float* part = p.bw.kpart + static_cast<size_t>(cs.cta) * TBMAX * KPAD;
-  const int n4 = N / 4;
-  for (int e = cs.tid; e < S.T * n4; e += NCT) {
-    const int t = e / n4, c4 = e - t * n4;
-    const float* yr = Y + t * YST + 4 * c4;
-    __stcg(reinterpret_cast<float4*>(part + t * KPAD + 4 * c4), make_float4(yr[0], yr[1], yr[2], yr[3]));
-  }
-  // bar.sync orders the CTA's stores before thread 0, whose release add publishes them at gpu
-  // scope (the pattern of grid_sync)
-  named_sync(1, NCT);
   uint32_t* cnt = p.bw.kcnt + static_cast<uint32_t>(S.gi & 1) * BKBANK + sp.rb;
   if (cs.tid == 0) {
     if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_PART);
@@ -762,14 +761,27 @@ struct WSoft {
 #pragma unroll
     for (int i = 0; i < WD; ++i) acc[i] = 0.f;
   }
-  template <class V>
-  __device__ __forceinline__ void add(float s, const V& v) {
-    const float mn = fmaxf(m, s);
-    const float f = m == -INFINITY ? 0.f : expf(m - mn);
-    const float e = expf(s - mn);
-    l = fmaf(l, f, e);
+  // the P scores s[q] (valid where ok[q]) of one trip with one running-max update
+  template <int P, class V>
+  __device__ __forceinline__ void add_trip(const float (&s)[P], const bool (&ok)[P], const V (&v)[P]) {
+    float mt = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < WD; ++i) acc[i] = fmaf(acc[i], f, e * v[i]);
+    for (int q = 0; q < P; ++q)
+      if (ok[q]) mt = fmaxf(mt, s[q]);
+    const float mn = fmaxf(m, mt);
+    if (mn == -INFINITY) return;
+    const float f = m == -INFINITY ? 0.f : expf(m - mn);
+    l *= f;
+#pragma unroll
+    for (int i = 0; i < WD; ++i) acc[i] *= f;
+#pragma unroll
+    for (int q = 0; q < P; ++q)
+      if (ok[q]) {
+        const float e = expf(s[q] - mn);
+        l += e;
+#pragma unroll
+        for (int i = 0; i < WD; ++i) acc[i] = fmaf(e, v[q][i], acc[i]);
+      }
     m = mn;
   }
   // merge with another state (m2, l2, a2)
@@ -902,11 +914,12 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
           d1[q] += __shfl_xor_sync(WFULL, d1[q], o);
         }
 #pragma unroll
-      for (int q = 0; q < P; ++q)
-        if (ok[q]) {
-          a0.add(d0[q] * p.attn_scale, vr[q]);
-          a1.add(d1[q] * p.attn_scale, vr[q]);
-        }
+      for (int q = 0; q < P; ++q) {
+        d0[q] *= p.attn_scale;
+        d1[q] *= p.attn_scale;
+      }
+      a0.add_trip(d0, ok, vr);
+      a1.add_trip(d1, ok, vr);
     }
     a0.merge_groups();
     a1.merge_groups();
