@@ -994,28 +994,54 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
     }
   } else {
     const LayerW* L = p.bb_layers + li;
-    int tot = 0;
-    for (int s = 0; s < B; ++s)
-      if (bst.act[s]) tot += bst.pos[s] + 1;
-    // chunk length: the smallest (in steps of 1/8) for which every item gets its own warp
-    int CL = max(16, (tot * NKVH + NW - 1) / NW);
-    auto nch_of = [&](int S) { return min(MAX_ATT_CHUNKS, (S + CL - 1) / CL); };
-    int total = 0;
-    for (int it = 0; it < 64; ++it) {
-      total = 0;
-      for (int s = 0; s < B; ++s)
-        if (bst.act[s]) total += NKVH * nch_of(bst.pos[s] + 1);
-      if (total <= NW) break;
-      CL += max(1, CL / 8);
-    }
-    for (int item = gw; item < total; item += NW) {
-      int idx = item, s = 0, nch = 1;
-      for (; s < B; ++s) {
-        if (!bst.act[s]) continue;
-        nch = nch_of(bst.pos[s] + 1);
-        if (idx < NKVH * nch) break;
-        idx -= NKVH * nch;
+    // the plan, computed by warp 0 (lane l: utterances l and l + 32) into sm.hist: item offset
+    // of each utterance [0, 64), chunks per KV head [64, 128), item count [128]; the chunk length is
+    // the smallest (in steps of 1/8) for which every item gets its own warp
+    int* plan = sm.hist;
+    if (cs.warp == 0) {
+      const int sa = cs.lane, sb = cs.lane + 32;
+      const int Sa = sa < B && bst.act[sa] ? bst.pos[sa] + 1 : 0, Sb = sb < B && bst.act[sb] ? bst.pos[sb] + 1 : 0;
+      int tot = Sa + Sb;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(WFULL, tot, o);
+      int CL = max(16, (tot * NKVH + NW - 1) / NW), na = 0, nb = 0;
+      for (int it = 0; it < 64; ++it) {
+        na = Sa ? min(MAX_ATT_CHUNKS, (Sa + CL - 1) / CL) : 0;
+        nb = Sb ? min(MAX_ATT_CHUNKS, (Sb + CL - 1) / CL) : 0;
+        int n = na + nb;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(WFULL, n, o);
+        if (NKVH * n <= NW) break;
+        CL += max(1, CL / 8);
       }
+      // exclusive prefix sums of NKVH * chunks: utterances 0..31 then 32..63
+      int xa = NKVH * na, xb = NKVH * nb;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int ya = __shfl_up_sync(WFULL, xa, o), yb = __shfl_up_sync(WFULL, xb, o);
+        if (cs.lane >= o) {
+          xa += ya;
+          xb += yb;
+        }
+      }
+      const int totala = __shfl_sync(WFULL, xa, 31);
+      plan[sa] = xa - NKVH * na;
+      plan[sb] = totala + xb - NKVH * nb;
+      plan[64 + sa] = na;
+      plan[64 + sb] = nb;
+      if (cs.lane == 31) plan[128] = totala + xb;
+    }
+    named_sync(1, NCT);
+    const int total = plan[128];
+    for (int item = gw; item < total; item += NW) {
+      int lo = 0, hi = B - 1;   // the last utterance whose offset <= item (binary search)
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (plan[mid] <= item) lo = mid; else hi = mid - 1;
+      }
+      int s = lo;
+      while (plan[64 + s] == 0) --s;   // skip inactive utterances sharing the offset
+      const int nch = plan[64 + s], idx = item - plan[s];
       const int h = idx / nch, c = idx - h * nch;
       const int S = bst.pos[s] + 1, chunk = (S + nch - 1) / nch;
       const int s0 = c * chunk, s1 = min(S, s0 + chunk);
@@ -1030,34 +1056,12 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
   return b_sync_planes(p, sm, cs);
 }
 
-// Backbone layer li: bulk L2 prefetch of every active utterance's cached K and V rows
-// [0, position) of the layer, spread over the CTAs (thread 0 each), issued at the start of the QKV
-// stage so that the attention stage after it reads them from L2. Skipped when the layer's rows
-// exceed KV_PREFETCH_MAX bytes (they would evict each other).
-constexpr long long KV_PREFETCH_MAX = 64ll << 20;
-__device__ void b_prefetch_kv(const Params& p, Smem& sm, const Cons& cs, int li) {
-  if (cs.tid != 0) return;
-  const BState bst = bstate(sm);
-  long long tot = 0;
-  for (int s = 0; s < p.nb; ++s)
-    if (bst.act[s]) tot += 2ll * NKVH * bst.pos[s] * HD * 2;
-  if (tot > KV_PREFETCH_MAX) return;
-  for (int it = cs.cta; it < p.nb * 2 * NKVH; it += cs.G) {
-    const int s = it / (2 * NKVH), r = it - s * 2 * NKVH, h = r >> 1;
-    if (!bst.act[s] || bst.pos[s] == 0) continue;
-    const bf16* base = (r & 1) ? p.bs[s].v : p.bs[s].k;
-    prefetch_l2_bulk(base + (static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq * HD,
-                     static_cast<uint32_t>(bst.pos[s]) * HD * 2);
-  }
-}
-
 // One decoder layer of the batch: QKV | attention | O | gate/up | down.
 __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int pass, int T,
                         const float* hin, float* hout, const bf16* next_norm) {
   const LayerW* L = (cp ? p.cp_layers + (li - p.n_bb) : p.bb_layers + li);
   const float eps = p.eps;
-  // ---- QKV (deferred input norm); backbone: the layer's cached K/V rows start moving to L2
-  if (!cp) b_prefetch_kv(p, sm, cs, li);
+  // ---- QKV (deferred input norm)
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
     if (!b_gemm(
