@@ -46,6 +46,8 @@ constexpr int DCOLS = NMAX;               // tensor-memory columns of one 64-tok
 constexpr uint32_t TMEM_COLS = 2 * DCOLS; // two 64-token tiles
 constexpr int KPAD = NMAX;                // row stride of a K-slice partial in global memory
 constexpr int BKBANK = 64;                // K-split counters per bank (row tiles of a stage)
+constexpr int BT_STRIDE = 20;             // row stride (floats) of a warp's partial-store tile in sm.att
+static_assert(6 * 32 * BT_STRIDE * 4 <= ATT_STAGE_BYTES, "partial-store tiles fit sm.att");
 // An M = 128 MMA reads the whole slot: rows 0..63 (hi plane) and 64..127 (lo plane).
 static_assert(NWS * WS_BYTES + NAS * AS_BYTES <= NSLOTS * SLOT_BYTES, "batched rings fit the ring region");
 static_assert(TBMAX * (NMAX + 1) * 4 <= NAS * AS_BYTES, "epilogue staging fits the activation ring");
@@ -525,16 +527,25 @@ __device__ __noinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, con
         float v[16];
         tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * DCOLS + 16 * c, v);
         const int t = 64 * j + 32 * q + cs.lane;
-        if (t < S.T) {
-          if (sp.nk > 1) {
-            float4* d4 = reinterpret_cast<float4*>(part + t * KPAD + 16 * c);
+        if (sp.nk > 1) {
+          // through a per-warp tile in shared memory, so that each store instruction writes 8
+          // whole 64-byte row pieces (4 lanes per token) instead of 32 scattered 16-byte ones
+          float* tile = reinterpret_cast<float*>(sm.att) + (wq * 2 + q) * 32 * BT_STRIDE;
+          float4* mine = reinterpret_cast<float4*>(tile + cs.lane * BT_STRIDE);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) __stcg(d4 + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
-          } else {
-            float* yr = Y + t * YST + 16 * c;
+          for (int i = 0; i < 4; ++i) mine[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          __syncwarp();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) yr[i] = v[i];
+          for (int k = 0; k < 4; ++k) {
+            const int r = 8 * k + (cs.lane >> 2), tt = 64 * j + 32 * q + r;
+            const float4 x = reinterpret_cast<const float4*>(tile + r * BT_STRIDE)[cs.lane & 3];
+            if (tt < S.T) __stcg(reinterpret_cast<float4*>(part + tt * KPAD + 16 * c) + (cs.lane & 3), x);
           }
+          __syncwarp();   // the tile is rewritten by the warp's next job
+        } else if (t < S.T) {
+          float* yr = Y + t * YST + 16 * c;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) yr[i] = v[i];
         }
       }
     }
