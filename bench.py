@@ -153,14 +153,16 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic_per_frame(name="qtt_decode_kernel_frame_c3.txt"):
-    """DRAM bytes per frame launch from the committed ncu summary (or None)."""
+def ncu_traffic_per_frame(algorithmic_bytes, name="qtt_decode_kernel_frame_c3.txt"):
+    """DRAM bytes per launch of this run: the DRAM / algorithmic ratio of the committed ncu capture
+    (one frame launch at an early position) times this run's algorithmic bytes per launch, since
+    the KV part grows with the position. None when the summary is absent."""
     p = os.path.join(ROOT, "profiles", name)
     try:
         with open(p) as f:
             for line in f:
-                if line.startswith("dram_bytes_per_frame:"):
-                    return int(float(line.split(":", 1)[1].split()[0]))
+                if line.startswith("dram_over_algorithmic:"):
+                    return float(line.split(":", 1)[1].split()[0]) * algorithmic_bytes
     except OSError:
         pass
     return None
@@ -344,7 +346,7 @@ def run_c3(args, rank, world, local_rank, K, W):
     frame_s = ms / 1000.0 / K
     achieved = bytes_per_frame / frame_s / 1e9
     peak, peak_src = measured_hbm_peak()
-    traffic = ncu_traffic_per_frame()
+    traffic = ncu_traffic_per_frame(bytes_per_frame)
     value = world * K / (ms / 1000.0)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
@@ -486,7 +488,7 @@ def run_c4(args, rank, world, local_rank, K, W):
         "frames_per_s_per_gpu": B * K / (ms / 1000.0),
         "batch_frame_ms": ms / K,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_src, "traffic": ncu_traffic_per_frame("qtt_batch_kernel_frame_c4.txt"),
+                     "peak_source": peak_src, "traffic": ncu_traffic_per_frame(bytes_per_frame, "qtt_batch_kernel_frame_c4.txt"),
                      "algorithmic_bytes_per_launch": bytes_per_frame,
                      "tensor_tflops": tflops,
                      "kernel": "qtt_batch_kernel (1 launch per frame of all utterances)"},
