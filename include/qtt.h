@@ -223,6 +223,16 @@ qtt_status qtt_get_hidden(qtt_engine* e, int s, float* out, cudaStream_t stream)
 /* Device pointer of the stream's code buffer int32 [max_frames][16]. */
 qtt_status qtt_codes_ptr(qtt_engine* e, int s, int32_t** codes);
 
+/* Tensor-core prefill of utterance s: the same result as qtt_prefill (KV cache rows of the
+ * context, decode state h, first group-0 token; the stream's state reset first), but the context
+ * is processed in chunks of up to 128 positions per launch, every projection a dense tcgen05 GEMM
+ * over the chunk and a causal attention per position. Replaces the reference's PyTorch prefill and
+ * KV handoff (generator.py:209-225,245-257); qtt_prefill is the token-by-token
+ * counterpart of the reference's megakernel loop. Needs the batched path's conditions (see
+ * qtt_batch_prefill). */
+qtt_status qtt_prefill_tc(qtt_engine* e, int s, const void* embeds, int len, const qtt_sampling* sampling,
+                          cudaStream_t stream);
+
 /* Batched decode (no counterpart in the reference, which decodes one utterance at a time:
  * generator.py:77-176 is the per-utterance loop these replace for B utterances). Streams
  * 0..B-1 of the engine (B <= 64 and <= max_streams) advance together: every launch streams the

@@ -804,6 +804,37 @@ extern "C" qtt_status qtt_batch_prefill(qtt_engine* e, int B, const void* const*
   return from_cuda(qtt::launch_b(p, e->bshape.ctas, e->bshape.smem, stream));
 }
 
+extern "C" qtt_status qtt_prefill_tc(qtt_engine* e, int s, const void* embeds, int len, const qtt_sampling* sp,
+                                     cudaStream_t stream) {
+  QTT_STREAM_CHECK(e, s);
+  if (!embeds || !aligned16(embeds) || len < 1 || len >= e->max_seq || len > e->base.rope_rows)
+    return QTT_ERR_INVALID_ARG;
+  qtt_status r = batch_check(e, 1, sp);
+  if (r != QTT_OK) return r;
+  r = qtt_reset(e, s, stream);
+  if (r != QTT_OK) return r;
+  // the launch's utterance 0 is stream s
+  qtt::BStream b = e->h_bs[s];
+  b.trailing = nullptr;
+  b.n_trailing = 0;
+  b.pad = nullptr;
+  b.len = len;
+  b.emb = static_cast<const bf16*>(embeds);
+  // pageable source: the copy is staged before the call returns
+  cudaError_t ce = cudaMemcpyAsync(e->d_bs, &b, sizeof(qtt::BStream), cudaMemcpyHostToDevice, stream);
+  if (ce != cudaSuccess) return from_cuda(ce);
+  qtt::Params p = batch_params(e, 1, sp);
+  p.mode = qtt::MODE_B_PREFILL_DENSE;
+  for (int p0 = 0; p0 < len; p0 += qtt::TBMAX) {
+    p.b_step = p0;
+    p.b_ntok = len - p0 < qtt::TBMAX ? len - p0 : qtt::TBMAX;
+    ce = qtt::launch_b(p, e->bshape.ctas, e->bshape.smem, stream);
+    if (ce != cudaSuccess) return from_cuda(ce);
+  }
+  p.mode = qtt::MODE_B_HEAD;
+  return from_cuda(qtt::launch_b(p, e->bshape.ctas, e->bshape.smem, stream));
+}
+
 extern "C" qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const void* const* trailing,
                                        const int* n_trailing, const void* const* pad, const qtt_sampling* sp,
                                        cudaStream_t stream) {

@@ -183,11 +183,11 @@ __device__ __forceinline__ void btrace(const Params& p, int gemm, int cta, int G
 // token the codec head.
 __device__ __forceinline__ int b_ngemm(const Params& p) {
   if (p.mode == MODE_B_FRAME) return NCPHEADS * (4 * p.n_cp + 1) + 4 * p.n_bb + 1;
-  if (p.mode == MODE_B_PREFILL) return 4 * p.n_bb;
+  if (p.mode == MODE_B_PREFILL || p.mode == MODE_B_PREFILL_DENSE) return 4 * p.n_bb;
   return 1;
 }
 __device__ __forceinline__ BGemm b_gemm_at(const Params& p, int i) {
-  const int B = p.nb;
+  const int B = p.mode == MODE_B_PREFILL_DENSE ? p.b_ntok : p.nb;   // tokens of the GEMMs
   if (p.mode == MODE_B_FRAME) {
     const int per = 4 * p.n_cp + 1;
     if (i < NCPHEADS * per) {
@@ -196,7 +196,7 @@ __device__ __forceinline__ BGemm b_gemm_at(const Params& p, int i) {
       return BGemm{r & 3, p.n_bb + (r >> 2), 0, g == 0 ? 2 * B : B};
     }
     i -= NCPHEADS * per;
-  } else if (p.mode != MODE_B_PREFILL) {
+  } else if (p.mode != MODE_B_PREFILL && p.mode != MODE_B_PREFILL_DENSE) {
     return BGemm{BK_HEAD, 0, 0, B};
   }
   if (i == 4 * p.n_bb) return BGemm{BK_HEAD, 0, 0, B};
@@ -1005,63 +1005,109 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
     }
   } else {
     const LayerW* L = p.bb_layers + li;
-    // the plan, computed by warp 0 (lane l: utterances l and l + 32) into sm.hist: item offset
-    // of each utterance [0, 64), chunks per KV head [64, 128), item count [128]; the chunk length is
-    // the smallest (in steps of 1/8) for which every item gets its own warp
+    // Items run over "rows": the utterances of a frame / prefill step, or the T context tokens of
+    // one utterance in a dense prefill (row v at position p0 + v, all rows sharing its cache).
+    const bool dense = p.mode == MODE_B_PREFILL_DENSE;
+    const int NV = dense ? p.b_ntok : B, p0d = p.b_step;
+    if (dense) {
+      // the chunk's new K/V rows first (q/k norm of k + RoPE, bf16), so that every row reads them
+      // from the cache after the barrier: item (token t, KV head h)
+      const int g = cs.lane / WL, u = cs.lane % WL;
+      for (int item = gw; item < NV * NKVH; item += NW) {
+        const int t = item / NKVH, h = item - t * NKVH, pos = p0d + t;
+        const float* row = p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS;
+        float k[WD], v[WD];
+        ld8_f32(row + QSZ + h * HD + WD * u, k);
+        ld8_f32(row + QSZ + KVSZ + h * HD + WD * u, v);
+        const uint4 c4 = *reinterpret_cast<const uint4*>(p.cos_tab + static_cast<size_t>(pos) * HD + WD * u);
+        const uint4 s4 = *reinterpret_cast<const uint4*>(p.sin_tab + static_cast<size_t>(pos) * HD + WD * u);
+        const uint4 wk = *reinterpret_cast<const uint4*>(L->k_norm + WD * u);
+        w_norm_rope(k, wk, c4, s4, p.eps, u);
+        if (g == 0) {
+          const size_t off = ((static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq + pos) * HD + WD * u;
+          uint32_t kw[4], vw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            kw[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(k[2 * i]))) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(k[2 * i + 1]))) << 16);
+            vw[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i]))) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1]))) << 16);
+          }
+          *reinterpret_cast<uint4*>(p.bs[0].k + off) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+          *reinterpret_cast<uint4*>(p.bs[0].v + off) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        }
+      }
+      if (!grid_sync(p, sm, cs)) return false;
+    }
+    auto row_len = [&](int v) -> int {   // context length of row v (0: inactive)
+      if (dense) return p0d + v + 1;
+      return bst.act[v] ? bst.pos[v] + 1 : 0;
+    };
+    // the plan, computed by warp 0 (lane l: rows l, l + 32, l + 64, l + 96) into sm.hist: item
+    // offset of each row [0, 128), chunks per KV head [128, 256), item count in sm.bcast[1]; the
+    // chunk length is the smallest (in steps of 1/8) for which every item gets its own warp
     int* plan = sm.hist;
     if (cs.warp == 0) {
-      const int sa = cs.lane, sb = cs.lane + 32;
-      const int Sa = sa < B && bst.act[sa] ? bst.pos[sa] + 1 : 0, Sb = sb < B && bst.act[sb] ? bst.pos[sb] + 1 : 0;
-      int tot = Sa + Sb;
+      int Sx[4], nx[4];
+      int tot = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int v = cs.lane + 32 * k;
+        Sx[k] = v < NV ? row_len(v) : 0;
+        tot += Sx[k];
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(WFULL, tot, o);
-      int CL = max(16, (tot * NKVH + NW - 1) / NW), na = 0, nb = 0;
+      int CL = max(16, (tot * NKVH + NW - 1) / NW);
       for (int it = 0; it < 64; ++it) {
-        na = Sa ? min(MAX_ATT_CHUNKS, (Sa + CL - 1) / CL) : 0;
-        nb = Sb ? min(MAX_ATT_CHUNKS, (Sb + CL - 1) / CL) : 0;
-        int n = na + nb;
+        int n = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          nx[k] = Sx[k] ? min(MAX_ATT_CHUNKS, (Sx[k] + CL - 1) / CL) : 0;
+          n += nx[k];
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(WFULL, n, o);
         if (NKVH * n <= NW) break;
         CL += max(1, CL / 8);
       }
-      // exclusive prefix sums of NKVH * chunks: utterances 0..31 then 32..63
-      int xa = NKVH * na, xb = NKVH * nb;
+      // exclusive prefix sums of NKVH * chunks over rows 0..127 (four 32-row blocks)
+      int base = 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int ya = __shfl_up_sync(WFULL, xa, o), yb = __shfl_up_sync(WFULL, xb, o);
-        if (cs.lane >= o) {
-          xa += ya;
-          xb += yb;
+      for (int k = 0; k < 4; ++k) {
+        int x = NKVH * nx[k];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(WFULL, x, o);
+          if (cs.lane >= o) x += y;
         }
+        plan[cs.lane + 32 * k] = base + x - NKVH * nx[k];
+        plan[128 + cs.lane + 32 * k] = nx[k];
+        base += __shfl_sync(WFULL, x, 31);
       }
-      const int totala = __shfl_sync(WFULL, xa, 31);
-      plan[sa] = xa - NKVH * na;
-      plan[sb] = totala + xb - NKVH * nb;
-      plan[64 + sa] = na;
-      plan[64 + sb] = nb;
-      if (cs.lane == 31) plan[128] = totala + xb;
+      if (cs.lane == 0) sm.bcast[1] = base;
     }
     named_sync(1, NCT);
-    const int total = plan[128];
+    const int total = sm.bcast[1];
     for (int item = gw; item < total; item += NW) {
-      int lo = 0, hi = B - 1;   // the last utterance whose offset <= item (binary search)
+      int lo = 0, hi = NV - 1;   // the last row whose offset <= item (binary search)
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (plan[mid] <= item) lo = mid; else hi = mid - 1;
       }
-      int s = lo;
-      while (plan[64 + s] == 0) --s;   // skip inactive utterances sharing the offset
-      const int nch = plan[64 + s], idx = item - plan[s];
+      int v = lo;
+      while (plan[128 + v] == 0) --v;   // skip inactive rows sharing the offset
+      const int nch = plan[128 + v], idx = item - plan[v];
       const int h = idx / nch, c = idx - h * nch;
-      const int S = bst.pos[s] + 1, chunk = (S + nch - 1) / nch;
+      const int S = row_len(v), chunk = (S + nch - 1) / nch;
       const int s0 = c * chunk, s1 = min(S, s0 + chunk);
+      const int su = dense ? 0 : v;   // the utterance whose cache the row reads
       const size_t off = (static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq * HD;
-      watt_item<false>(p, cs, L, p.bw.qkv + static_cast<size_t>(s) * QKV_ROWS, 1, bst.pos[s], h,
-                       reinterpret_cast<uint8_t*>(p.bs[s].k + off), reinterpret_cast<uint8_t*>(p.bs[s].v + off),
-                       p.bw.abuf[1], s, c, nch, s0, s1, s1 == S,
-                       p.bw.prt + static_cast<size_t>(s) * NQH * MAX_ATT_CHUNKS * PRT_STRIDE,
-                       p.bw.att_cnt + s * NKVH + h);
+      watt_item<false>(p, cs, L, p.bw.qkv + static_cast<size_t>(v) * QKV_ROWS, 1, S - 1, h,
+                       reinterpret_cast<uint8_t*>(p.bs[su].k + off), reinterpret_cast<uint8_t*>(p.bs[su].v + off),
+                       p.bw.abuf[1], v, c, nch, s0, s1, !dense && s1 == S,
+                       p.bw.prt + static_cast<size_t>(v) * NQH * MAX_ATT_CHUNKS * PRT_STRIDE,
+                       p.bw.att_cnt + v * NKVH + h);
     }
   }
   return b_sync_planes(p, sm, cs);
@@ -1398,6 +1444,37 @@ __device__ bool b_prefill(const Params& p, Smem& sm, Cons& cs) {
   return true;
 }
 
+// Dense prefill of one utterance (bs[0]): context positions [p0, p0 + T) in one program, every
+// projection a T-token tensor-core GEMM, the positions' K/V rows written before a causal
+// attention over the cache (replaces the reference's PyTorch prefill and KV handoff,
+// generator.py:209-225,245-257). After the last chunk the final norm of the last position is
+// the decode state h, and the position is the context length.
+__device__ bool b_prefill_dense(const Params& p, Smem& sm, Cons& cs) {
+  uint32_t gn = 0;
+  const int p0 = p.b_step, T = p.b_ntok;
+  const bf16* emb = p.bs[0].emb;
+  if (!b_input(p, sm, cs, T, p.bb_layers[0].in_norm, [&](int t, int k0, float (&v)[8]) {
+        const bf16* row = emb + static_cast<size_t>(p0 + t) * HID + k0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(row[j]);
+      }))
+    return false;
+  const float* last = b_stack(p, sm, cs, gn, false, 0, T);
+  if (!last) return false;
+  if (p0 + T == p.bs[0].len) {
+    const unsigned long long* ssq = b_ssq_cur(p, cs);
+    b_elementwise(cs, 1, [&](int, int k0) {
+      const int t = T - 1;
+      const float rs = b_rstd(ssq, t, p.eps);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        p.bs[0].st->h[k0 + j] = __ldcg(last + t * HID + k0 + j) * rs * __bfloat162float(p.bb_norm[k0 + j]);
+    });
+  }
+  if (cs.cta == 0 && cs.tid == 0) p.bs[0].st->position = p0 + T;
+  return true;
+}
+
 // First group-0 token of every utterance from its decode state h (generator.py:115-120).
 __device__ bool b_first_token(const Params& p, Smem& sm, Cons& cs) {
   uint32_t gn = 0;
@@ -1458,7 +1535,7 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
         act = (p.b_step < p.bs[s].len) ? 1 : 0;
       else
         act = 1;
-      if (p.mode == MODE_B_PREFILL) pos = p.b_step;
+      if (p.mode == MODE_B_PREFILL || p.mode == MODE_B_PREFILL_DENSE) pos = p.b_step;
       if (g0 < 0 || g0 >= p.vocab) g0 = 0;
     }
     sm.bstate[s] = pos;
@@ -1495,6 +1572,8 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
       ok = b_frame(p, sm, cs);
     else if (p.mode == MODE_B_PREFILL)
       ok = b_prefill(p, sm, cs);
+    else if (p.mode == MODE_B_PREFILL_DENSE)
+      ok = b_prefill_dense(p, sm, cs);
     else
       ok = b_first_token(p, sm, cs);
     if (!ok) *reinterpret_cast<volatile int*>(&sm.abort) = 1;

@@ -163,6 +163,7 @@ enum Mode : int {
   MODE_B_FRAME = 3,        // batched: one frame of every utterance
   MODE_B_PREFILL = 4,      // batched: backbone step b_step of every utterance with b_step < len
   MODE_B_HEAD = 5,         // batched: first group-0 token of every utterance after its prefill
+  MODE_B_PREFILL_DENSE = 6,  // one utterance's context positions [b_step, b_step + b_ntok) at once
 };
 enum Flags : int { FLAG_HEAD_SAMPLE = 1, FLAG_EAGER_REFILL = 2 };
 
@@ -196,7 +197,8 @@ struct Params {
   int nb;                  // utterances of the batched launch
   const BStream* bs;       // [nb]
   BWork bw;
-  int b_step;              // MODE_B_PREFILL: context index of this step
+  int b_step;              // MODE_B_PREFILL: context index of this step; DENSE: first position
+  int b_ntok;              // MODE_B_PREFILL_DENSE: positions of this launch (<= TBMAX)
   // caches [layer][kv head][max_seq][128]
   bf16* bb_k;
   bf16* bb_v;

@@ -203,6 +203,15 @@ class Engine:
                                        _stream_handle(stream)), "qtt_frames")
 
     # ---- batched decode (streams 0..B-1 advance together, tcgen05 GEMMs) ----------------------
+    def prefill_tc(self, s: int, embeds: torch.Tensor, sampling: _lib.QttSampling, stream=None):
+        """Prefill stream s with the tensor-core path (chunks of up to 128 context positions per
+        launch); same results as ``prefill``."""
+        embeds = embeds.contiguous()
+        assert embeds.is_cuda and embeds.dtype == torch.bfloat16 and embeds.dim() == 2
+        self._keep_tc = embeds
+        _lib.check(self.lib.qtt_prefill_tc(self.h, s, _ptr(embeds), embeds.shape[0], ctypes.byref(sampling),
+                                           _stream_handle(stream)), "qtt_prefill_tc")
+
     def batch_prefill(self, embeds: list, sampling: _lib.QttSampling, stream=None):
         """Prefill utterances 0..B-1 (``embeds[s]``: bf16 [len_s, 1024] on the engine's GPU) and
         sample each one's first group-0 token."""

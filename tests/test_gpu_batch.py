@@ -77,6 +77,42 @@ def test_batch_prefill_matches_oracle(dev_small, orc_small):
         eng.close()
 
 
+def test_prefill_tc_matches_oracle(dev_small, orc_small):
+    """Tensor-core prefill in chunks of up to 128 positions (contexts of 9, 150 and 300 positions:
+    one to three chunks): the decode state equals the oracle's causal prefill, the cached K/V rows
+    equal the oracle's up to bf16 rounding, and the first group-0 token equals the token-by-token
+    prefill's unless the top two logits are within two bf16 ulps."""
+    embeds, _, _ = _inputs([9, 150, 300], 0, 61)
+    sp = _greedy_sp()
+    eng = Engine(dev_small, max_streams=2, max_seq=512, max_frames=16)
+    try:
+        for e in embeds:
+            L = e.shape[0]
+            eng.prefill_tc(0, e.cuda(), sp)
+            eng.check()
+            ref = orc_small.prefill(e.to(F64))
+            assert eng.state(0)["position"] == L
+            got = eng.hidden(0).cpu().to(F64)
+            rel = float((got - ref).norm() / ref.norm())
+            assert rel <= HID_REL, f"L={L}: hidden rel {rel:.3g}"
+            k, v = eng.kv(0)
+            for a, b in ((k, orc_small.bk), (v, orc_small.bv)):
+                a = a[:, :, :L].cpu().to(F64)
+                b = b[:, :, :L]
+                krel = float((a - b).norm() / b.norm())
+                assert krel <= HID_REL, f"L={L}: cache rel {krel:.3g}"
+            g0_tc = eng.state(0)["g0"]
+            eng.prefill(1, e.cuda(), sp)
+            eng.check()
+            lo = orc_small.head_logits(orc_small.codec_head, ref).double()
+            lo[orc_small.suppress_mask(orc_small.d.eos_token_id)] = float("-inf")
+            top = torch.sort(lo, descending=True)[0]
+            if float(top[0] - top[1]) > TIE_TOL:
+                assert g0_tc == eng.state(1)["g0"], f"L={L}"
+    finally:
+        eng.close()
+
+
 def test_batch_small_teacher_forced(dev_small, orc_small):
     """2+2-layer model with random norm weights, 3 utterances of different contexts, greedy with
     repetition penalty, 8 frames (trailing rows, then the pad row)."""
