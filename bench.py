@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--workload", choices=("c4", "c3"), default="c4")
     ap.add_argument("--batch", type=int, default=64, help="utterances per GPU (c4)")
     ap.add_argument("--bs1-steps", type=int, default=100, help="frames of the batch-1 side measurement (c4)")
+    ap.add_argument("--serve-requests", type=int, default=128,
+                    help="utterances per GPU of the continuous-batching measurement (c4; 0 = skip)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -503,6 +505,69 @@ def run_c4(args, rank, world, local_rank, K, W):
     return line
 
 
+def run_serving(args, rank, world, local_rank):
+    """Continuous batching (qwentts_turbo_b200.serving) of args.serve_requests utterances per GPU
+    with uneven lengths (contexts U[CTX_LO, CTX_HI], frame limits U[50, 300], sampled as C4) on
+    args.batch slots, against static batching of the same utterances (a batch is refilled only
+    once all of its utterances ended). Every joining utterance is prefilled with the tensor-core
+    prefill in its slot; the device-timed region covers the prefills, the frames and the host's
+    scheduling between chunks. Returns useful codec frames/s (whole job) of both policies."""
+    import torch.distributed as dist
+
+    from qwentts_turbo_b200.dist import max_over_ranks
+    from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
+    from qwentts_turbo_b200.serving import ContinuousBatcher, Utterance
+    from qwentts_turbo_b200.weights import synthetic_weights
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    n, B, chunk = args.serve_requests, args.batch, 4
+    lim_lo, lim_hi = 50, 300
+    max_seq = CTX_HI + lim_hi + 8
+    dm = DeviceModel(synthetic_weights(), rope_rows=max_seq)
+    eng = Engine(dm, max_streams=B, max_seq=max_seq, max_frames=lim_hi)
+    g = torch.Generator().manual_seed(40 + rank)
+    ctx = torch.randint(CTX_LO, CTX_HI + 1, (n,), generator=g).tolist()
+    lims = torch.randint(lim_lo, lim_hi + 1, (n,), generator=g).tolist()
+    utts = [Utterance(torch.randn(L, 1024, generator=g).to(torch.bfloat16).cuda(),
+                      torch.randn(N_TRAILING, 1024, generator=g).to(torch.bfloat16).cuda(),
+                      torch.randn(1024, generator=g).to(torch.bfloat16).cuda(), lim, 100_000 * rank + i)
+            for i, (L, lim) in enumerate(zip(ctx, lims))]
+    sp = sampling_struct(do_sample=True, temperature=0.9, top_k=50, repetition_penalty=1.2,
+                         min_new_tokens=1 << 30, seed=1234 + rank)
+    stream = torch.cuda.current_stream()
+
+    def timed(policy, items):
+        cb = ContinuousBatcher(eng, sp, slots=B, chunk=chunk, policy=policy)
+        for u in items:
+            cb.submit(u)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        done = cb.run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        eng.check()
+        frames = sum(f.codes.shape[0] for f in done.values())
+        assert frames == sum(u.max_frames for u in items), "an utterance ended before its frame limit"
+        return max_over_ranks(e0.elapsed_time(e1)), frames, cb.launches
+
+    timed("continuous", utts[:min(n, 8)])      # warm-up (first launches, allocations)
+    ms_c, frames, launches_c = timed("continuous", utts)
+    ms_s, _, launches_s = timed("static", utts)
+    eng.close()
+    if rank != 0:
+        return None
+    return {"workload": f"{n} utterances per GPU, contexts U[{CTX_LO},{CTX_HI}], frame limits U[{lim_lo},{lim_hi}], "
+                        f"sampled (T 0.9, top-k 50, repetition 1.2), {B} slots, {chunk} frames per state read",
+            "frames": frames * world, "continuous_frames_per_s": world * frames / (ms_c / 1000.0),
+            "static_frames_per_s": world * frames / (ms_s / 1000.0), "continuous_s": ms_c / 1000.0,
+            "static_s": ms_s / 1000.0, "calls_continuous": launches_c, "calls_static": launches_s,
+            "prefill": "qtt_prefill_tc of each joining utterance in its slot (inside the timed region)"}
+
+
 def run_ours(args, rank, world, local_rank):
     if args.workload == "c3":
         line = run_c3(args, rank, world, local_rank, args.steps, args.warmup)
@@ -515,6 +580,10 @@ def run_ours(args, rank, world, local_rank):
                                "frames_per_s": bs1["value"] / world, "frame_latency_us": bs1["frame_latency_us"],
                                "rtf": bs1["rtf"], "e2e_frames_per_s": bs1["e2e"]["value"] / world,
                                "hbm_frac": bs1["roofline"]["frac"], "steps": args.bs1_steps}
+        if args.serve_requests > 0:
+            serving = run_serving(args, rank, world, local_rank)
+            if line is not None:
+                line["serving"] = serving
     if line is None:
         return
     if world == 1 and not args.no_cpu_baseline:

@@ -241,12 +241,25 @@ qtt_status qtt_prefill_tc(qtt_engine* e, int s, const void* embeds, int len, con
  * bf16 [lens[s]][1024]) and samples its first group-0 token (as qtt_prefill per stream).
  * qtt_batch_frames: n_frames frames of every stream that has not reached EOS (as qtt_frames per
  * stream; trailing[s] device bf16 [n_trailing[s]][1024] or NULL when n_trailing[s] == 0,
- * pad[s] device bf16 [1024]). Sampling draws of stream s use Philox stream sp->philox_stream + s.
+ * pad[s] device bf16 [1024]). Sampling draws of stream s use Philox stream sp->philox_stream + s
+ * unless qtt_set_stream_params gave the stream its own.
  * The pointer and length arrays are host arrays of B entries. */
 qtt_status qtt_batch_prefill(qtt_engine* e, int B, const void* const* embeds, const int* lens,
                              const qtt_sampling* sp, cudaStream_t stream);
 qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const void* const* trailing, const int* n_trailing,
                             const void* const* pad, const qtt_sampling* sp, cudaStream_t stream);
+/* Continuous batching (no counterpart in the reference, whose generate() call takes one
+ * utterance, its max_new_tokens and torch's global generator: generator.py:77-127). Settings of
+ * stream s for the batched launches and qtt_prefill_tc that follow, kept across resets:
+ * philox_stream >= 0 is the Philox stream of all the stream's draws (-1: the default above, and
+ * sp->philox_stream in qtt_prefill_tc), so an utterance's codes do not depend on the stream it
+ * runs in; frame_limit > 0 stops the stream after that many frames (as max_new_tokens),
+ * 0 = max_frames, < 0 parks it (no frames until set again). */
+qtt_status qtt_set_stream_params(qtt_engine* e, int s, int philox_stream, int frame_limit);
+/* States of streams 0..B-1 with one device->host copy: out[4 * s + 0..3] = position, frames,
+ * group-0 token of the next frame, done (EOS reached). Host array of 4 * B ints; synchronizes
+ * `stream`. */
+qtt_status qtt_batch_states(qtt_engine* e, int B, int32_t* out, cudaStream_t stream);
 /* Diagnostics of the batched path (parity tests): the first n of its scratch device pointers,
  * in this order: GEMM operand planes 0 and 1 (bf16 [2][128][3072] each: plane 0 = hi, plane 1 =
  * lo, row = token), sampled-head logits (fp32 [64][3072]), frame tokens (int32 [64][16]), stack

@@ -103,6 +103,8 @@ SIGNATURES = {
     "qtt_set_refill_policy": (_I, [_P, _I]),
     "qtt_batch_prefill": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_I), ctypes.POINTER(QttSampling), _P]),
     "qtt_prefill_tc": (_I, [_P, _I, _P, _I, ctypes.POINTER(QttSampling), _P]),
+    "qtt_set_stream_params": (_I, [_P, _I, _I, _I]),
+    "qtt_batch_states": (_I, [_P, _I, ctypes.POINTER(_I), _P]),
     "qtt_batch_frames": (_I, [_P, _I, _I, ctypes.POINTER(_P), ctypes.POINTER(_I), ctypes.POINTER(_P),
                               ctypes.POINTER(QttSampling), _P]),
     "qtt_batch_debug_buffers": (_I, [_P, ctypes.POINTER(_P), _I]),

@@ -274,6 +274,8 @@ struct StreamBufs {
   bf16* v = nullptr;
   qtt::StreamState* st = nullptr;
   int32_t* codes = nullptr;
+  int philox = -1;        // qtt_set_stream_params: own Philox stream (-1: the launch's default)
+  int frame_limit = 0;    // > 0: frame limit, 0: max_frames, < 0: parked
 };
 
 struct qtt_engine {
@@ -287,6 +289,9 @@ struct qtt_engine {
   void* d_bmaps = nullptr;
   qtt::BStream* d_bs = nullptr;
   float* d_cpkv = nullptr;
+  qtt::StreamState** d_stptr = nullptr;   // qtt_batch_states: state pointers, gathered words, pinned copy
+  int32_t* d_states = nullptr;
+  int32_t* h_states = nullptr;
   std::vector<qtt::BStream> h_bs;
   float* b_dbg_cp = nullptr;   // batched debug logits [B][15][cp_vocab], [B][vocab]
   float* b_dbg_g0 = nullptr;
@@ -353,6 +358,9 @@ void engine_free(qtt_engine* e) {
   cudaFree(e->d_bmaps);
   cudaFree(e->d_bs);
   cudaFree(e->d_cpkv);
+  cudaFree(e->d_stptr);
+  cudaFree(e->d_states);
+  cudaFreeHost(e->h_states);
   cudaFree(e->d_work);
   cudaFree(e->cp_k);
   cudaFree(e->cp_v);
@@ -729,6 +737,13 @@ qtt_status ensure_batch(qtt_engine* e) {
   const size_t cpkv = 2 * kCpKvFloats * ncp * e->max_streams;
   if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_cpkv), sizeof(float) * cpkv);
   if (ce == cudaSuccess) ce = cudaMemset(e->d_cpkv, 0, sizeof(float) * cpkv);
+  std::vector<qtt::StreamState*> stp(e->max_streams);
+  for (int s = 0; s < e->max_streams; ++s) stp[s] = e->streams[s].st;
+  if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_stptr), sizeof(void*) * e->max_streams);
+  if (ce == cudaSuccess)
+    ce = cudaMemcpy(e->d_stptr, stp.data(), sizeof(void*) * e->max_streams, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_states), sizeof(int32_t) * 4 * e->max_streams);
+  if (ce == cudaSuccess) ce = cudaMallocHost(reinterpret_cast<void**>(&e->h_states), sizeof(int32_t) * 4 * e->max_streams);
   if (ce != cudaSuccess) return from_cuda(ce);
   e->h_bs.assign(e->max_streams, qtt::BStream{});
   for (int s = 0; s < e->max_streams; ++s) {
@@ -756,6 +771,22 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   p.dbg_cp_logits = e->b_dbg_cp;
   p.dbg_g0_logits = e->b_dbg_g0;
   return p;   // the stage timeline, profile marks and barrier arrivals, if set, are kept
+}
+
+// Draw stream and frame limit of engine stream s for a batched launch (qtt_set_stream_params).
+void stream_params(const qtt_engine* e, int s, int default_philox, qtt::BStream& b) {
+  const StreamBufs& sb = e->streams[s];
+  b.philox = sb.philox >= 0 ? sb.philox : default_philox;
+  b.frame_limit = sb.frame_limit < 0 ? 0 : (sb.frame_limit > 0 && sb.frame_limit < e->max_frames ? sb.frame_limit
+                                                                                                  : e->max_frames);
+}
+
+__global__ void batch_states_kernel(qtt::StreamState* const* st, int B, int32_t* out) {
+  for (int i = threadIdx.x; i < 4 * B; i += blockDim.x) {
+    const qtt::StreamState* x = st[i >> 2];
+    const int f = i & 3;
+    out[i] = f == 0 ? x->position : f == 1 ? x->step : f == 2 ? x->g0 : x->done;
+  }
 }
 
 qtt_status batch_check(qtt_engine* e, int B, const qtt_sampling* sp) {
@@ -789,6 +820,7 @@ extern "C" qtt_status qtt_batch_prefill(qtt_engine* e, int B, const void* const*
     b.pad = nullptr;
     b.len = lens[s];
     b.emb = static_cast<const bf16*>(embeds[s]);
+    stream_params(e, s, sp->philox_stream + s, b);
   }
   // pageable source: the copy is staged before the call returns
   cudaError_t ce = cudaMemcpyAsync(e->d_bs, e->h_bs.data(), sizeof(qtt::BStream) * B, cudaMemcpyHostToDevice, stream);
@@ -820,6 +852,7 @@ extern "C" qtt_status qtt_prefill_tc(qtt_engine* e, int s, const void* embeds, i
   b.pad = nullptr;
   b.len = len;
   b.emb = static_cast<const bf16*>(embeds);
+  stream_params(e, s, sp->philox_stream, b);
   // pageable source: the copy is staged before the call returns
   cudaError_t ce = cudaMemcpyAsync(e->d_bs, &b, sizeof(qtt::BStream), cudaMemcpyHostToDevice, stream);
   if (ce != cudaSuccess) return from_cuda(ce);
@@ -850,6 +883,7 @@ extern "C" qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const
     b.pad = static_cast<const bf16*>(pad[s]);
     b.emb = nullptr;
     b.len = 0;
+    stream_params(e, s, sp->philox_stream + s, b);
   }
   cudaError_t ce = cudaMemcpyAsync(e->d_bs, e->h_bs.data(), sizeof(qtt::BStream) * B, cudaMemcpyHostToDevice, stream);
   if (ce != cudaSuccess) return from_cuda(ce);
@@ -859,6 +893,30 @@ extern "C" qtt_status qtt_batch_frames(qtt_engine* e, int B, int n_frames, const
     ce = qtt::launch_b(p, e->bshape.ctas, e->bshape.smem, stream);
     if (ce != cudaSuccess) return from_cuda(ce);
   }
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_set_stream_params(qtt_engine* e, int s, int philox_stream, int frame_limit) {
+  QTT_STREAM_CHECK(e, s);
+  if (philox_stream < -1) return QTT_ERR_INVALID_ARG;
+  e->streams[s].philox = philox_stream;
+  e->streams[s].frame_limit = frame_limit;
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_batch_states(qtt_engine* e, int B, int32_t* out, cudaStream_t stream) {
+  if (!e || !out || B < 1 || B > e->max_streams) return QTT_ERR_INVALID_ARG;
+  qtt_status r = set_device(e);
+  if (r != QTT_OK) return r;
+  r = ensure_batch(e);
+  if (r != QTT_OK) return r;
+  batch_states_kernel<<<1, 256, 0, stream>>>(e->d_stptr, B, e->d_states);
+  cudaError_t ce = cudaGetLastError();
+  if (ce == cudaSuccess)
+    ce = cudaMemcpyAsync(e->h_states, e->d_states, sizeof(int32_t) * 4 * B, cudaMemcpyDeviceToHost, stream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(stream);
+  if (ce != cudaSuccess) return from_cuda(ce);
+  std::memcpy(out, e->h_states, sizeof(int32_t) * 4 * B);
   return QTT_OK;
 }
 

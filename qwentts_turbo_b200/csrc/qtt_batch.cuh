@@ -1288,7 +1288,7 @@ __device__ __noinline__ bool b_tokens(const Params& p, Smem& sm, Cons& cs, int h
                                            : ((bst.step[s] + 1 < p.sp.min_new_tokens) ? 1 : 0);
     }
     Sampling sp = p.sp;
-    sp.philox_stream = p.sp.philox_stream + s;
+    sp.philox_stream = p.bs[s].philox;
     const int fr = p.mode == MODE_B_HEAD ? 0 : bst.step[s] + frame_of;
     c.u24 = draw_u24(sp, fr, hidx);
     const int tk = sample(p.bw.logits + static_cast<size_t>(s) * VMAX, sm, cs, c);
@@ -1528,7 +1528,7 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
       const int done = ld_volatile_i32(&st->done);
       if (p.mode == MODE_B_FRAME)
         act = (!done && g0 != p.sp.eos && g0 >= 0 && g0 < p.vocab && pos >= 0 && pos < p.bb_max_seq &&
-               pos < p.rope_rows && step >= 0 && step < p.max_frames)
+               pos < p.rope_rows && step >= 0 && step < p.bs[s].frame_limit)
                   ? 1
                   : 0;
       else if (p.mode == MODE_B_PREFILL)

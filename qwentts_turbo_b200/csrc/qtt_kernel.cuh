@@ -136,6 +136,8 @@ struct BStream {
   int len;                 // prefill: context length
   const bf16* pad;         // [HID]
   const bf16* emb;         // prefill: context embeddings [len][HID]
+  int philox;              // Philox stream of this utterance's draws
+  int frame_limit;         // frames: the utterance stops once it has this many (<= max_frames)
 };
 // Batched scratch (one per engine).
 struct BWork {

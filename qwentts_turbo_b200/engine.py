@@ -130,6 +130,10 @@ class Engine:
             pass
 
     @property
+    def device(self) -> torch.device:
+        return torch.device("cuda", self.model.device)
+
+    @property
     def num_ctas(self) -> int:
         return self.lib.qtt_engine_num_ctas(self.h)
 
@@ -237,6 +241,17 @@ class Engine:
         pp = (ctypes.c_void_p * B)(*[_ptr(x) for x in pads])
         _lib.check(self.lib.qtt_batch_frames(self.h, B, n, tp, nt, pp, ctypes.byref(sampling), _stream_handle(stream)),
                    "qtt_batch_frames")
+
+    def set_stream_params(self, s: int, philox_stream: int = -1, frame_limit: int = 0):
+        """Stream s's own Philox stream (-1: the launch's default) and frame limit (> 0: stop after
+        that many frames, 0: max_frames, < 0: parked) for the batched launches that follow."""
+        _lib.check(self.lib.qtt_set_stream_params(self.h, s, philox_stream, frame_limit), "qtt_set_stream_params")
+
+    def batch_states(self, B: int, stream=None) -> list:
+        """[position, frames, g0, done] of streams 0..B-1 (one device-to-host copy; synchronizes)."""
+        out = (ctypes.c_int * (4 * B))()
+        _lib.check(self.lib.qtt_batch_states(self.h, B, out, _stream_handle(stream)), "qtt_batch_states")
+        return [list(out[4 * s:4 * s + 4]) for s in range(B)]
 
     def batch_set_debug_outputs(self, cp_logits: torch.Tensor | None, g0_logits: torch.Tensor | None):
         """Parity tests: batched frames also write each head's logits into cp_logits fp32
