@@ -264,7 +264,7 @@ def run_c3(args, rank, world, local_rank, K, W):
     torch.cuda.set_device(dev)
     max_seq = CTX + W + K + 8
     weights = synthetic_weights()
-    dm = DeviceModel(weights, rope_rows=max_seq)
+    dm = DeviceModel(weights, device=dev, rope_rows=max_seq)
     del weights
     eng = Engine(dm, max_streams=1, max_seq=max_seq, max_frames=W + K + 1)
     embeds, trailing, pad = c3_inputs(CTX, N_TRAILING, seed=4 + rank)
@@ -388,7 +388,7 @@ def run_c4(args, rank, world, local_rank, K, W):
     B = args.batch
     max_seq = CTX_HI + W + K + 8
     weights = synthetic_weights()
-    dm = DeviceModel(weights, rope_rows=max_seq)
+    dm = DeviceModel(weights, device=dev, rope_rows=max_seq)
     del weights
     eng = Engine(dm, max_streams=B, max_seq=max_seq, max_frames=W + K + 1)
     g = torch.Generator().manual_seed(4 + rank)
@@ -524,7 +524,7 @@ def run_serving(args, rank, world, local_rank):
     n, B, chunk = args.serve_requests, args.batch, 4
     lim_lo, lim_hi = 50, 300
     max_seq = CTX_HI + lim_hi + 8
-    dm = DeviceModel(synthetic_weights(), rope_rows=max_seq)
+    dm = DeviceModel(synthetic_weights(), device=dev, rope_rows=max_seq)
     eng = Engine(dm, max_streams=B, max_seq=max_seq, max_frames=lim_hi)
     g = torch.Generator().manual_seed(40 + rank)
     ctx = torch.randint(CTX_LO, CTX_HI + 1, (n,), generator=g).tolist()
@@ -602,7 +602,7 @@ def main():
     if world > 1 and args.impl == "ours":
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     args.gpus = world
     try:
@@ -610,10 +610,19 @@ def main():
             run_reference(args, rank)
         else:
             run_ours(args, rank, world, local_rank)
-    finally:
+    except BaseException:
         if world > 1 and args.impl == "ours":
-            import torch.distributed as dist
-            dist.destroy_process_group()
+            # the other ranks may be waiting in a collective this rank never reaches: exit at once
+            # (torchrun then stops them) instead of waiting in destroy_process_group
+            import traceback
+            traceback.print_exc()
+            sys.stdout.flush()
+            sys.stderr.flush()
+            os._exit(1)
+        raise
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
