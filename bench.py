@@ -54,7 +54,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("c4", "c3"), default="c4")
+    ap.add_argument("--workload", choices=("c4", "c3", "prefill"), default="c4")
     ap.add_argument("--batch", type=int, default=64, help="utterances per GPU (c4)")
     ap.add_argument("--bs1-steps", type=int, default=100, help="frames of the batch-1 side measurement (c4)")
     ap.add_argument("--serve-requests", type=int, default=128,
@@ -65,6 +65,15 @@ def parse_args():
 
 
 def workload_config(args):
+    if args.workload == "prefill":
+        return {
+            "workload": f"tensor-core backbone prefill of one {CTX}-position context per step (qtt_prefill_tc: "
+                        "chunks of up to 128 positions per launch + the first group-0 token), greedy",
+            "model": "Qwen3-TTS-12Hz-0.6B backbone (random-init bf16)",
+            "global_batch": args.gpus, "batch_per_gpu": 1, "ctx": CTX, "seq_len": CTX,
+            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU",
+            "l2": "inputs larger than L2: 881 MB of backbone weights streamed per launch (L2 126 MB)",
+        }
     if args.workload == "c3":
         return {
             "workload": "C3: bs1 frame loop (15-step code predictor + combine + 28-layer backbone step + codec "
@@ -568,7 +577,103 @@ def run_serving(args, rank, world, local_rank):
             "prefill": "qtt_prefill_tc of each joining utterance in its slot (inside the timed region)"}
 
 
+def run_prefill(args, rank, world, local_rank, K, W):
+    """Tensor-core prefill (qtt_prefill_tc) of a CTX-position context, one utterance per step;
+    returns rank 0's JSON fields (metric: context positions per second)."""
+    import torch.distributed as dist
+
+    from qwentts_turbo_b200.config import DEFAULT_DIMS
+    from qwentts_turbo_b200.dist import max_over_ranks
+    from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
+    from qwentts_turbo_b200.weights import synthetic_weights
+    from qwentts_turbo_b200.workloads import c3_inputs
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    L = CTX
+    dm = DeviceModel(synthetic_weights(), device=dev, rope_rows=L + 16)
+    eng = Engine(dm, max_streams=1, max_seq=L + 16, max_frames=4)
+    embeds, _, _ = c3_inputs(L, 1, 4 + rank)
+    emb_h = embeds.pin_memory()
+    emb_d = embeds.cuda()
+    sp = sampling_struct(do_sample=False, min_new_tokens=100)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(W):
+        eng.prefill_tc(0, emb_d, sp)
+    eng.check()
+    ref_g0 = eng.state(0)["g0"]
+    clocks = ClockSampler(dev)
+    time.sleep(0.3)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(stream)
+    for _ in range(K):
+        eng.prefill_tc(0, emb_d, sp)
+    e1.record(stream)
+    barrier()
+    t1 = time.time()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks.stop()
+    eng.check()
+    # end to end: the context from pinned host memory, the prefill, the first token read back
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(K):
+        emb_d.copy_(emb_h, non_blocking=True)
+        eng.prefill_tc(0, emb_d, sp, stream)
+        assert eng.state(0, stream)["g0"] == ref_g0, "e2e prefill gave another first token"
+    e3.record(stream)
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    eng.close()
+    if rank != 0:
+        return None
+    d = DEFAULT_DIMS
+    row = 2 * 2 * d.n_kv_heads * d.head_dim * d.backbone_layers    # bf16 K + V of one position, all layers
+    wb = d.backbone_layers * d.layer_bytes() + 2 * d.hidden         # backbone layers + final norm
+    chunks = [(p0, min(128, L - p0)) for p0 in range(0, L, 128)]
+    # per chunk launch: the weights once, the chunk's embeddings, its K/V rows written and the
+    # cache rows [0, p0 + T) read once
+    alg = [wb + T * 2 * d.hidden + T * row + (p0 + T) * row for p0, T in chunks]
+    step_s = ms / 1000.0 / K
+    achieved = sum(alg) / step_s / 1e9    # over the whole step (head launch and resets included)
+    peak, peak_src = measured_hbm_peak()
+    flops = sum(4.0 * (wb / 2) * T for _, T in chunks)   # hi and lo operand planes
+    return {
+        "metric": "prefill_positions_per_s", "value": world * L * K / (ms / 1000.0), "unit": "positions/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, seeded N(0,1) context)", "config": workload_config(args),
+        "prefill_ms_per_utterance": ms / K,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src,
+                     "traffic": ncu_traffic_per_frame(sum(alg) / len(alg), "qtt_batch_kernel_prefill_dense.txt"),
+                     "algorithmic_bytes_per_launch": sum(alg) / len(alg),
+                     "launches_per_step": len(chunks) + 1, "tensor_tflops": flops / step_s / 1e12,
+                     "kernel": "qtt_batch_kernel, dense prefill program (achieved over the whole step: "
+                               "the first-token launch and the stream reset are included)"},
+        "e2e": {"value": world * L * K / (ms_e2e / 1000.0), "unit": "positions/s",
+                "h2d_bytes_per_step": L * 2 * d.hidden + 80, "d2h_bytes_per_step": 16,
+                "path": "pinned H2D of the context, qtt_prefill_tc, qtt_get_state (first token)"},
+        "gpu_launches": K * (len(chunks) + 1),
+        "clocks": clocks.summary(t0, t1),
+    }
+
+
 def run_ours(args, rank, world, local_rank):
+    if args.workload == "prefill":
+        line = run_prefill(args, rank, world, local_rank, args.steps, args.warmup)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
     if args.workload == "c3":
         line = run_c3(args, rank, world, local_rank, args.steps, args.warmup)
     else:

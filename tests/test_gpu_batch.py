@@ -211,6 +211,35 @@ def test_batch_runs_bit_identical(dev_small):
             assert torch.equal(a[1][s], other[1][s]), s
 
 
+def test_batch_eos_stops_one_utterance(dev_small):
+    """EOS in the batched path: utterance 0 stops at the first frame whose group-0 token is the
+    EOS id (as generator.py:125-127), its row goes idle, and the other utterance's codes are the
+    same as in a run without that EOS (as long as its own tokens do not hit the id)."""
+    embeds, trailing, pads = _inputs([20, 35], 4, 91)
+    base = _greedy_sp()
+    eng = Engine(dev_small, max_streams=2, max_seq=512, max_frames=16)
+    try:
+        ed, td, pd = [e.cuda() for e in embeds], [t.cuda() for t in trailing], [x.cuda() for x in pads]
+        eng.batch_prefill(ed, base)
+        eng.batch_frames(6, td, pd, base)
+        eng.check()
+        ref = [eng.codes(s)[:6].cpu().tolist() for s in range(2)]
+        eos = ref[0][3][0]   # below the suppressed band: the logit masks stay the same (see the batch-1 test)
+        stop0 = next(i for i in range(4) if ref[0][i][0] == eos)
+        stop1 = next((i for i in range(6) if ref[1][i][0] == eos), 6)
+        sp = sampling_struct(do_sample=False, min_new_tokens=0, eos_token_id=eos)
+        eng.batch_prefill(ed, sp)
+        eng.batch_frames(6, td, pd, sp)
+        eng.check()
+        st = eng.batch_states(2)
+        assert st[0][1] == stop0 and st[0][2] == eos
+        assert st[1][1] == stop1
+        assert eng.codes(0)[:stop0].cpu().tolist() == ref[0][:stop0]
+        assert eng.codes(1)[:stop1].cpu().tolist() == ref[1][:stop1]
+    finally:
+        eng.close()
+
+
 def test_batch_argument_errors(dev_small):
     eng = Engine(dev_small, max_streams=2, max_seq=64, max_frames=4)
     try:

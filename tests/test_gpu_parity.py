@@ -299,15 +299,21 @@ def test_eos_stops_generation(small_weights, eng_small):
     eng_small.prefill(0, embeds.cuda(), _greedy_sp())
     eng_small.frames(0, 5, trailing.cuda(), pad.cuda(), _greedy_sp())
     codes = eng_small.codes(0)[:5].cpu().tolist()
+    # Declare frame 3's group-0 token the EOS id. The logit masks are the same in both runs: with
+    # the EOS gate on (min_new_tokens large) the whole band [vocab - 1024, vocab) is masked, and
+    # with the EOS id below the band and no gate it is masked too, so frames 0-3 repeat and
+    # generation stops at the first frame whose group-0 token is that id (generator.py:125-127).
     eos = codes[3][0]
-    if eos < 2048 or any(c[0] == eos for c in codes[:3]):
-        pytest.skip("frame-3 token is not a usable EOS id for this seed")
+    stop = next(i for i in range(4) if codes[i][0] == eos)
     sp = sampling_struct(do_sample=False, min_new_tokens=0, eos_token_id=eos)
     eng_small.prefill(0, embeds.cuda(), sp)
     eng_small.frames(0, 8, trailing.cuda(), pad.cuda(), sp)
     eng_small.check()
     st = eng_small.state(0)
-    assert st["done"] == 1 and st["frames"] == 3
+    assert st["frames"] == stop and st["g0"] == eos
+    if stop > 0:   # a first token equal to the EOS id ends the utterance before any frame
+        assert st["done"] == 1
+    assert eng_small.codes(0)[:stop].cpu().tolist() == codes[:stop]
 
 
 def test_long_context_backbone(orc_full, eng_full):
