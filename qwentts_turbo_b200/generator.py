@@ -7,8 +7,11 @@ suppression, repetition penalty, EOS gate and sampling, then the next frame. The
 checks for EOS every ``frame_chunk`` frames.
 
 Backends: only ``"megakernel"`` (the sm_100a engine) exists; there is no PyTorch/CPU path.
-Prefill: the reference runs the HF talker over the context (generator.py:209-225); here the
-context is run through the same engine token by token (same layer math, causal).
+Prefill: the reference runs the HF talker over the context (generator.py:209-225) and copies its
+cache into the megakernel (generator.py:245-257). Here ``prefill="tensor_core"`` (default) runs the
+context through ``qtt_prefill_tc`` (chunks of up to 128 positions per launch, tcgen05 GEMMs, K/V
+written straight into the engine's cache); ``prefill="tokenwise"`` runs it token by token
+through the batch-1 decode kernel (same layer math, causal).
 """
 from __future__ import annotations
 
@@ -27,7 +30,10 @@ class NativeTTSGenerator:
 
     def __init__(self, model_path=None, model=None, backend="megakernel", cp_backend="megakernel",
                  weights: dict | None = None, dims: ModelDims = DEFAULT_DIMS, max_seq_len: int = 4096,
-                 max_frames: int = 4096, device: int = 0, frame_chunk: int = 32):
+                 max_frames: int = 4096, device: int = 0, frame_chunk: int = 32, prefill: str = "tensor_core"):
+        if prefill not in ("tensor_core", "tokenwise"):
+            raise ValueError("prefill must be 'tensor_core' or 'tokenwise'")
+        self.prefill = prefill
         if backend != "megakernel" or cp_backend != "megakernel":
             raise ValueError("qwentts_turbo_b200 only has the sm_100a engine: use backend='megakernel', "
                              "cp_backend='megakernel'")
@@ -78,7 +84,10 @@ class NativeTTSGenerator:
 
     def _run_one(self, embeds, trailing, pad, sp, max_tokens):
         eng = self.engine
-        eng.prefill(0, embeds, sp)
+        if self.prefill == "tensor_core":
+            eng.prefill_tc(0, embeds, sp)
+        else:
+            eng.prefill(0, embeds, sp)
         produced, st = 0, None
         while produced < max_tokens:
             n = min(self.frame_chunk, max_tokens - produced)

@@ -358,9 +358,15 @@ def test_generate_api(small_weights, orc_small):
     assert len(out) == 5 and all(len(f) == 16 for f in out)
     eng = gen.engine
     sp = sampling_struct(do_sample=False, min_new_tokens=100)
-    eng.prefill(0, embeds.cuda(), sp)
+    eng.prefill_tc(0, embeds.cuda(), sp)     # the default prefill="tensor_core"
     eng.frames(0, 5, trailing.cuda(), pad.cuda(), sp)
     assert eng.codes(0)[:5].cpu().tolist() == out
+    gen.prefill = "tokenwise"
+    out_tw = gen.generate(embeds[None], mask, trailing[None], pad[None, None], max_tokens=5, min_new_tokens=100)
+    eng.prefill(0, embeds.cuda(), sp)
+    eng.frames(0, 5, trailing.cuda(), pad.cuda(), sp)
+    assert eng.codes(0)[:5].cpu().tolist() == out_tw
+    gen.prefill = "tensor_core"
     ref = orc_small.generate(embeds.double(), trailing.double(), pad.double(), max_tokens=1, min_new_tokens=100)
     assert out[0][0] == ref[0][0]
     z3 = torch.zeros(1, 3, 1024, dtype=torch.bfloat16)
