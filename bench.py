@@ -45,6 +45,7 @@ FALLBACK_HBM_GBS = 6650.0
 
 
 CTX_LO, CTX_HI = 100, 400     # C4 prefill contexts
+C5_CTX, C5_FRAMES = (100, 600), (200, 600)   # C5 contexts and frame counts per utterance
 CTX_MID = (CTX_LO + CTX_HI) // 2
 
 
@@ -54,7 +55,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("c4", "c3", "prefill"), default="c4")
+    ap.add_argument("--workload", choices=("c4", "c3", "prefill", "c5"), default="c4")
     ap.add_argument("--batch", type=int, default=64, help="utterances per GPU (c4)")
     ap.add_argument("--bs1-steps", type=int, default=100, help="frames of the batch-1 side measurement (c4)")
     ap.add_argument("--serve-requests", type=int, default=128,
@@ -65,6 +66,17 @@ def parse_args():
 
 
 def workload_config(args):
+    if args.workload == "c5":
+        return {
+            "workload": f"C5 per GPU: {args.batch} utterances decoded together, contexts U[{C5_CTX[0]},{C5_CTX[1]}], "
+                        f"frame counts U[{C5_FRAMES[0]},{C5_FRAMES[1]}] (each utterance stops at its own count), "
+                        "T 0.9 / top-k 50 / repetition 1.2 with a Philox stream per utterance, EOS masked",
+            "model": "Qwen3-TTS-12Hz-0.6B (random-init bf16)",
+            "global_batch": args.gpus * args.batch, "batch_per_gpu": args.batch,
+            "ctx": f"U[{C5_CTX[0]},{C5_CTX[1]}]", "seq_len": C5_CTX[1] + C5_FRAMES[1],
+            "parallelism": f"data parallel x{args.gpus} (independent utterances)" if args.gpus > 1 else "single GPU",
+            "l2": "inputs larger than L2: 3.31 GB of weights + KV streamed per frame (L2 126 MB)",
+        }
     if args.workload == "prefill":
         return {
             "workload": f"tensor-core backbone prefill of one {CTX}-position context per step (qtt_prefill_tc: "
@@ -668,7 +680,93 @@ def run_prefill(args, rank, world, local_rank, K, W):
     }
 
 
+def run_c5(args, rank, world, local_rank):
+    """C5 on each GPU: args.batch utterances with their own context lengths and frame counts, all
+    decoded together until the last one reaches its count (the kernel stops each utterance at its
+    own count, qtt_set_stream_params). One device-timed call of qtt_batch_frames over max(count)
+    frames; value = useful frames (sum of the counts, all ranks) / max-over-ranks time."""
+    import torch.distributed as dist
+
+    from qwentts_turbo_b200.config import frame_weight_bytes, kv_read_bytes_per_frame
+    from qwentts_turbo_b200.dist import max_over_ranks
+    from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
+    from qwentts_turbo_b200.weights import synthetic_weights
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    B = args.batch
+    max_seq = C5_CTX[1] + C5_FRAMES[1] + 8
+    dm = DeviceModel(synthetic_weights(), device=dev, rope_rows=max_seq)
+    eng = Engine(dm, max_streams=B, max_seq=max_seq, max_frames=C5_FRAMES[1])
+    g = torch.Generator().manual_seed(500 + rank)
+    ctx = torch.randint(C5_CTX[0], C5_CTX[1] + 1, (B,), generator=g).tolist()
+    counts = torch.randint(C5_FRAMES[0], C5_FRAMES[1] + 1, (B,), generator=g).tolist()
+    embeds = [torch.randn(L, 1024, generator=g).to(torch.bfloat16).cuda() for L in ctx]
+    trailing = [torch.randn(N_TRAILING, 1024, generator=g).to(torch.bfloat16).cuda() for _ in range(B)]
+    pads = [torch.randn(1024, generator=g).to(torch.bfloat16).cuda() for _ in range(B)]
+    sp = sampling_struct(do_sample=True, temperature=0.9, top_k=50, repetition_penalty=1.2,
+                         min_new_tokens=1 << 30, seed=1234 + rank)
+    stream = torch.cuda.current_stream()
+
+    def prefill_all():
+        for s in range(B):
+            eng.set_stream_params(s, 1000 * rank + s, counts[s])
+            eng.prefill_tc(s, embeds[s], sp)
+
+    # warm-up: a short run of the same launches
+    prefill_all()
+    eng.batch_frames(args.warmup, trailing, pads, sp)
+    eng.check()
+    prefill_all()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(stream)
+    eng.batch_frames(max(counts), trailing, pads, sp)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.time()
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local)
+    clocks.stop()
+    eng.check()
+    st = eng.batch_states(B)
+    assert [x[1] for x in st] == counts, "an utterance did not reach its frame count"
+    eng.close()
+    if rank != 0:
+        return None
+    frames = sum(counts)
+    launches = max(counts)
+    wbytes = frame_weight_bytes()
+    kv = sum(kv_read_bytes_per_frame(ctx[s] + f) for s in range(B) for f in range(counts[s]))
+    alg = (launches * wbytes + kv) / launches
+    achieved = alg / (ms_local / 1000.0 / launches) / 1e9
+    peak, peak_src = measured_hbm_peak()
+    return {
+        "metric": METRIC, "value": world * frames / (ms / 1000.0), "unit": UNIT, "n_gpus": world,
+        "steps": launches, "warmup": args.warmup, "ms_per_step": ms / launches, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, seeded N(0,1) inputs)", "config": workload_config(args),
+        "frames_per_gpu": frames, "occupancy": frames / (B * launches),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "traffic": None, "algorithmic_bytes_per_launch": alg,
+                     "kernel": "qtt_batch_kernel (1 launch per frame of the utterances still running)"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(t0, t1),
+    }
+
+
 def run_ours(args, rank, world, local_rank):
+    if args.workload == "c5":
+        line = run_c5(args, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
     if args.workload == "prefill":
         line = run_prefill(args, rank, world, local_rank, args.steps, args.warmup)
         if line is not None:
