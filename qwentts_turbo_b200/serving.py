@@ -140,9 +140,18 @@ class ContinuousBatcher:
                 reason = "context"   # no progress over a whole chunk: the stream's cache is full
             self.slot_frames[s] = frames
             if reason is not None:
-                out.append(Finished(self.slot_uid[s], self.eng.codes(s)[:frames].clone(), reason))
+                out.append(Finished(self.slot_uid[s], self._codes(s, frames), reason))
                 self._release(s)
         return out
+
+    def _codes(self, s: int, frames: int) -> torch.Tensor:
+        """Copy of slot s's codes, made on the batcher's stream so that it precedes the next
+        utterance's frames in that slot."""
+        c = self.eng.codes(s)[:frames]
+        if self.stream is None:
+            return c.clone()
+        with torch.cuda.stream(self.stream):
+            return c.clone()
 
     def run(self) -> dict:
         """Decode everything submitted; returns {uid: Finished}."""
