@@ -461,10 +461,10 @@ __device__ bool b_wait_count(const Params& p, Smem& sm, const uint32_t* cnt, uin
 }
 
 // Consumer side of one GEMM stage. Epilogue items are (token t, 16 output columns c); the
-// callbacks are pre(t, r0, st), issued right after the stage starts (inputs that do not depend
-// on D), and run(t, r0, y, y2, st) with y = D[t][16 columns] (gate/up: y = gate, y2 = up) and
-// r0 the first output column (row of W; gate/up: intermediate channel).
-//   1. release the activation loader (GO), prefetch the first item's inputs;
+// callbacks are pre(t, r0, st) (the item's inputs that do not depend on D) and
+// run(t, r0, y, y2, st) with y = D[t][16 columns] (gate/up: y = gate, y2 = up) and r0 the first
+// output column (row of W; gate/up: intermediate channel).
+//   1. release the activation loader (GO);
 //   2. wait for D; the warps of TMEM lane quarters 0 and 1 copy its rows (tokens) to the K slice's
 //      partial in global memory (a single slice: to shared memory); D is freed;
 //   3. K split: count, wait for the row tile's other slices, and sum the nk slices (slice order)
@@ -611,17 +611,15 @@ __device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, cons
                                        RUN&& run) {
   BStage S;
   if (!b_gemm_begin(p, sm, cs, g, S)) return grid_sync(p, sm, cs);
+  // The items' inputs that do not depend on D are loaded after b_gemm_mid returns: held across
+  // the call they made the epilogues spill, which cost more than their load latency.
   EpiSt st;
-  if (S.i0 + cs.tid < S.i1) {
-    const int i = S.i0 + cs.tid;
-    pre(i / S.nci, S.r0b + 16 * (i % S.nci), st);
-  }
   const bool ok = b_gemm_mid(p, sm, cs, S, gemm_n);
   if (ok) {
     const int YST = S.N + 1;
     for (int i = S.i0 + cs.tid; i < S.i1; i += NCT) {
       const int t = i / S.nci, c = i - t * S.nci, r0 = S.r0b + 16 * c;
-      if (i != S.i0 + cs.tid) pre(t, r0, st);
+      pre(t, r0, st);
       const float* yr = S.Y + t * YST + 16 * c;
       run(t, r0, yr, S.gu ? yr + S.NO : yr, st);
     }
