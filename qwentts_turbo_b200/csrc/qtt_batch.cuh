@@ -1259,12 +1259,21 @@ __device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_
 }
 
 // Token of utterance s from head slot `slot` (greedy) or bw.tok (sampled, column col).
+// A token outside the head's vocabulary (an argmax slot no CTA wrote) sets DEV_ERR_BAD_TOKEN and
+// reads as 0, so that the embedding rows gathered with it stay inside their tables.
 __device__ __forceinline__ int b_token(const Params& p, const SampleCfg& cfg, int slot, int s, int col) {
+  int tok;
   if (!cfg.do_sample) {
     const unsigned long long k = __ldcg(p.bw.amax + slot * TBMAX + s);
-    return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+    tok = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+  } else {
+    tok = __ldcg(p.bw.tok + s * NGROUPS + col);
   }
-  return __ldcg(p.bw.tok + s * NGROUPS + col);
+  if (tok < 0 || tok >= cfg.V) {
+    set_error(p.w.err, DEV_ERR_BAD_TOKEN);
+    tok = 0;
+  }
+  return tok;
 }
 
 // Tokens of a head for every utterance, after its barrier, into bw.tok[s][col]: greedy from the
