@@ -25,7 +25,7 @@ Rounding points kept from the reference:
 * the 16-embedding combine is a chain of bf16 adds (generator.py:356-362), then one more
   bf16 add of the trailing-text row or the pad embedding (generator.py:146-149).
 
-Deliberate definitions where the reference has none on device (documented in DESIGN.md):
+Deliberate definitions where the reference has none on device:
 * sampling draws come from Philox4x32-10 (Salmon et al., SC'11) keyed by the stream seed,
   counter (frame, group, stream, 0); the categorical draw is an inverse CDF over the
   bf16 probabilities in vocabulary order, accumulated in exact 2^-60 fixed point, so the

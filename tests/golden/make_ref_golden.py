@@ -2,7 +2,7 @@
 (hamza1brh/qwenTTS-turbo qwentts_turbo/csrc/*.cu, compiled for sm_100a by oracle/Makefile into
 oracle/_ref/). Needs a GPU; run from the repo root:
 
-    make -C oracle && python tests/golden/make_ref_golden.py gpurun_out/ref_megakernel_golden.npz
+    make -C oracle && python tests/golden/make_ref_golden.py <output.npz>
 
 Inputs are regenerated from seeds on the CPU side of the test (qwentts_turbo_b200.workloads):
 spec weights (seed 0 backbone, seed 1 code predictor), C1 KV cache + embedding (seed 2,
