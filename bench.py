@@ -256,11 +256,11 @@ def run_reference(args, rank):
         return
     budget = 60.0
     c4 = args.workload == "c4"
-    fps, cores, timed, el = cpu_frames_per_s(budget, warmup=min(args.warmup, 2), max_frames=args.steps,
+    fps, cores, timed, el = cpu_frames_per_s(budget, warmup=args.warmup, max_frames=args.steps,
                                              sampled=c4, ctx=CTX_MID if c4 else CTX)
     line = {
         "impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus, "steps": timed,
-        "warmup": min(args.warmup, 2), "ms_per_step": 1000.0 * el / timed, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * el / timed, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args),
         "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
@@ -403,6 +403,7 @@ def run_c4(args, rank, world, local_rank, K, W):
     from qwentts_turbo_b200.dist import gather_codes, max_over_ranks
     from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
     from qwentts_turbo_b200.weights import synthetic_weights
+    from qwentts_turbo_b200.workloads import c4_inputs
 
     dev = local_rank
     torch.cuda.set_device(dev)
@@ -412,11 +413,7 @@ def run_c4(args, rank, world, local_rank, K, W):
     dm = DeviceModel(weights, device=dev, rope_rows=max_seq)
     del weights
     eng = Engine(dm, max_streams=B, max_seq=max_seq, max_frames=W + K + 1)
-    g = torch.Generator().manual_seed(4 + rank)
-    ctx = torch.randint(CTX_LO, CTX_HI + 1, (B,), generator=g).tolist()
-    embeds = [torch.randn(L, 1024, generator=g).to(torch.bfloat16) for L in ctx]
-    trailing = [torch.randn(N_TRAILING, 1024, generator=g).to(torch.bfloat16) for _ in range(B)]
-    pads = [torch.randn(1024, generator=g).to(torch.bfloat16) for _ in range(B)]
+    ctx, embeds, trailing, pads = c4_inputs(B, CTX_LO, CTX_HI, N_TRAILING, seed=4 + rank)
     embeds_d = [e.cuda() for e in embeds]
     trailing_d = [t.cuda() for t in trailing]
     pads_d = [x.cuda() for x in pads]

@@ -92,8 +92,13 @@ void launch_cp_decode_with_embedding(const void* input_embedding, const CPLayerW
  * launch itself. Device-side errors (timeouts) are reported by qtt_stream_check(). */
 int qtt_last_launch_status(void);
 
-/* Synchronises `stream` and returns the device error recorded by drop-in launches on it
- * (then clears it). */
+/* Identifies the sources the library was built from: 16 hex digits of a SHA-256 over
+ * csrc/*.cu, csrc/*.cuh and this header, stamped at build time (no counterpart in the
+ * reference). A host can compare it with the hash of the sources it ships. */
+const char* qtt_build_id(void);
+
+/* Synchronises `stream` and returns the device error recorded by drop-in launches on it and by
+ * qtt_backbone_step_noalloc on the current device (then clears them). */
 int qtt_stream_check(cudaStream_t stream);
 
 /* ------------------------------------------------------------------------------------------
@@ -117,10 +122,14 @@ typedef enum qtt_status {
  * allocator owns the device memory): the scratch lives in a fixed 684 KB device array inside the
  * library instead of a per-stream cudaMalloc. Same arguments as the drop-in launcher minus the
  * unused g_* scratch pointers and cache_len (= position + 1). The first call on a device takes
- * the array's device address (cudaGetSymbolAddress) with that device current; make it before any
- * stream capture. Calls share the array: calls that overlap on the GPU race, so keep them on one
- * stream. max_seq_len above 8192 (or above what the device's CTA count supports) returns
- * QTT_ERR_UNSUPPORTED. Returns the status of the argument checks and the launch. */
+ * the array's device address (cudaGetSymbolAddress) with that device current; with lazy module
+ * loading (the CUDA default) that is also when the driver places the array in device memory, a
+ * one-time allocation: make the first call at start-up as a warm-up, before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race, so keep them on one stream.
+ * max_seq_len above 8192 (or above what the device's CTA count supports), or a GPU with fewer
+ * than 128 SMs, returns QTT_ERR_UNSUPPORTED. Returns the status of the argument checks and the
+ * launch; a device-side error of the step (a bounded wait that timed out) is returned by
+ * qtt_stream_check(stream). */
 qtt_status qtt_backbone_step_noalloc(const void* input_embedding, const TTSLayerWeights* layer_weights,
                                      const void* final_norm_weight, const void* cos_table,
                                      const void* sin_table, void* k_cache, void* v_cache, void* hidden_buffer,
@@ -282,6 +291,13 @@ qtt_status qtt_set_debug_timeline(qtt_engine* e, unsigned long long* stamps, int
  * cta] for stages k in [arrival_stage0, arrival_stage0 + arrival_stages). Zeros turn it off. */
 qtt_status qtt_set_debug_profile(qtt_engine* e, unsigned long long* marks, int n_marks,
                                  unsigned long long* arrivals, int arrival_stage0, int arrival_stages);
+/* Error-path test hook (no counterpart in the reference): when barrier = k > 0, the batch-1
+ * launches that follow (qtt_frames, qtt_prefill, qtt_backbone_step, qtt_cp_step) lose one
+ * arrival at their k-th grid barrier (the last CTA does not arrive), and every
+ * grid-barrier wait gives up after wait_ns nanoseconds (0: the built-in 2 s). Such a launch ends
+ * early with the error word set; qtt_check then returns QTT_ERR_TIMEOUT and the engine stays
+ * usable. barrier = 0 turns it off. */
+qtt_status qtt_set_debug_barrier_fault(qtt_engine* e, int barrier, unsigned long long wait_ns);
 /* Weight-ring refill policy of the persistent kernel: 0 (default) refills a freed slot only
  * after the consumers' next grid barrier, keeping refill traffic out of the barrier; 1 refills
  * as soon as a slot is free. */

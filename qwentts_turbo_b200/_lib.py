@@ -26,6 +26,7 @@ STATUS = {
 }
 QTT_OK = 0
 QTT_ERR_INVALID_ARG = 1
+QTT_ERR_TIMEOUT = 4
 QTT_ERR_UNSUPPORTED = 5
 
 
@@ -77,6 +78,7 @@ SIGNATURES = {
     "launch_tts_decode": (None, [_I] + _LAUNCH_ARGS),
     "launch_cp_decode_with_embedding": (None, _LAUNCH_ARGS),
     "qtt_last_launch_status": (_I, []),
+    "qtt_build_id": (ctypes.c_char_p, []),
     "qtt_stream_check": (_I, [_P]),
     "qtt_status_string": (ctypes.c_char_p, [_I]),
     "qtt_engine_create": (_I, [ctypes.POINTER(QttWeights), ctypes.POINTER(QttDims), _I, _I, _I, _I,
@@ -101,6 +103,7 @@ SIGNATURES = {
     "qtt_get_hidden": (_I, [_P, _I, _P, _P]),
     "qtt_check": (_I, [_P, _P]),
     "qtt_set_refill_policy": (_I, [_P, _I]),
+    "qtt_set_debug_barrier_fault": (_I, [_P, _I, ctypes.c_uint64]),
     "qtt_batch_prefill": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_I), ctypes.POINTER(QttSampling), _P]),
     "qtt_prefill_tc": (_I, [_P, _I, _P, _I, ctypes.POINTER(QttSampling), _P]),
     "qtt_set_stream_params": (_I, [_P, _I, _I, _I]),

@@ -1,7 +1,14 @@
 """Build libqtt.so in-tree for sm_100a with nvcc (no JIT cache, so the library travels with
-the source tree)."""
+the source tree).
+
+Every build stamps the hash of its sources (``source_hash()``: csrc/*.cu, csrc/*.cuh and
+include/qtt.h) into the library, exported as ``qtt_build_id()``, and writes it beside the library
+(``libqtt.so.buildid``). The library is rebuilt whenever the sources' hash differs from the stamp,
+and ``check_build_id()`` tells whether a prebuilt library matches the sources next to it.
+"""
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -28,19 +35,45 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def _stale() -> bool:
-    if not os.path.exists(LIB):
-        return True
-    t = os.path.getmtime(LIB)
+def source_hash() -> str:
+    """16 hex digits of the SHA-256 over the library's sources (name and content, in order)."""
+    h = hashlib.sha256()
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [os.path.join(INCLUDE, "qtt.h")]
-    return any(os.path.getmtime(d) > t for d in deps)
+    for d in deps:
+        h.update(os.path.basename(d).encode())
+        with open(d, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
+
+
+def _stamp_path() -> str:
+    return LIB + ".buildid"
+
+
+def _stale() -> bool:
+    if not os.path.exists(LIB) or not os.path.exists(_stamp_path()):
+        return True
+    with open(_stamp_path()) as f:
+        return f.read().strip() != source_hash()
+
+
+def check_build_id(lib) -> None:
+    """Raises RuntimeError when the loaded library (a ctypes handle) was not built from the
+    sources in this tree."""
+    got = lib.qtt_build_id().decode()
+    want = source_hash()
+    if got != want:
+        raise RuntimeError(f"libqtt.so was built from other sources (build id {got}, sources {want}); "
+                           "rebuild it with qwentts_turbo_b200.build.build_library(force=True)")
 
 
 def build_library(force: bool = False, verbose: bool = False) -> str:
     """Compile csrc/*.cu into qwentts_turbo_b200/libqtt.so (skipped when up to date)."""
     if not force and not _stale():
         return LIB
-    cmd = [_nvcc()] + NVCC_FLAGS + ["-I", INCLUDE] + [os.path.join(CSRC, s) for s in SOURCES] + ["-o", LIB + ".tmp"]
+    bid = source_hash()
+    cmd = ([_nvcc()] + NVCC_FLAGS + [f'-DQTT_BUILD_ID="{bid}"', "-I", INCLUDE] +
+           [os.path.join(CSRC, s) for s in SOURCES] + ["-o", LIB + ".tmp"])
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -49,6 +82,8 @@ def build_library(force: bool = False, verbose: bool = False) -> str:
     if verbose:
         print(r.stdout + r.stderr)
     os.replace(LIB + ".tmp", LIB)
+    with open(_stamp_path(), "w") as f:
+        f.write(bid + "\n")
     return LIB
 
 

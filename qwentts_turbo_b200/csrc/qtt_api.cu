@@ -243,17 +243,26 @@ extern "C" void launch_cp_decode_with_embedding(const void* input_embedding, con
 
 extern "C" int qtt_last_launch_status(void) { return g_last_status; }
 
+#ifndef QTT_BUILD_ID
+#define QTT_BUILD_ID "unstamped"
+#endif
+extern "C" const char* qtt_build_id(void) { return QTT_BUILD_ID; }
+
 extern "C" int qtt_stream_check(cudaStream_t stream) {
   cudaError_t e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) return from_cuda(e);
   int dev = 0;
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return from_cuda(e);
+  // steps of qtt_backbone_step_noalloc keep their error word in the library's fixed scratch
+  int noalloc_code = 0;
+  e = qtt::noalloc_take_error(dev, &noalloc_code);
+  if (e != cudaSuccess) return from_cuda(e);
   qtt::Work w;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_compat.find(std::make_pair(dev, stream));
-    if (it == g_compat.end()) return QTT_OK;
+    if (it == g_compat.end()) return from_dev(noalloc_code);
     w = it->second.w;
   }
   int code = 0;
@@ -263,7 +272,7 @@ extern "C" int qtt_stream_check(cudaStream_t stream) {
     const int zero = 0;
     cudaMemcpy(w.err, &zero, sizeof(int), cudaMemcpyHostToDevice);
   }
-  return from_dev(code);
+  return from_dev(code != 0 ? code : noalloc_code);
 }
 
 // ==========================================================================================
@@ -770,6 +779,8 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   p.cp_wd_map = nullptr;
   p.dbg_cp_logits = e->b_dbg_cp;
   p.dbg_g0_logits = e->b_dbg_g0;
+  p.dbg_skip_barrier = 0;   // the barrier-fault test hook applies to the batch-1 kernel only
+  p.dbg_wait_ns = 0ull;
   return p;   // the stage timeline, profile marks and barrier arrivals, if set, are kept
 }
 
@@ -1018,6 +1029,13 @@ extern "C" qtt_status qtt_set_debug_profile(qtt_engine* e, unsigned long long* m
   e->base.dbg_arrivals = arrival_stages > 0 ? arrivals : nullptr;
   e->base.dbg_arr_stage0 = arrival_stage0;
   e->base.dbg_arr_n = arrival_stages;
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_set_debug_barrier_fault(qtt_engine* e, int barrier, unsigned long long wait_ns) {
+  if (!e || barrier < 0) return QTT_ERR_INVALID_ARG;
+  e->base.dbg_skip_barrier = barrier;
+  e->base.dbg_wait_ns = wait_ns;
   return QTT_OK;
 }
 

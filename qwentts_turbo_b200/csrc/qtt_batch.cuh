@@ -7,9 +7,10 @@
 // or the first group-0 token after the prefill (MODE_B_HEAD). The weights are streamed once
 // per program for the whole batch. Every projection is a GEMM
 //     D[tokens x rows] = A[tokens x K] * W[rows x K]^T
-//   * W: this CTA's rows of the matrix in blocks of 16. The producer warp streams them as 2-D
-//     TMA boxes of 16 rows x 64 columns with the 128-byte swizzle (two per K step of 128) into a
-//     4-slot ring and runs ahead across grid barriers (weights do not depend on activations).
+//   * W: this CTA's row tile of the matrix (128 rows; gate/up: 64 gate + 64 up rows). The
+//     producer warp streams it as 2-D TMA boxes of 128 rows x 64 columns (gate/up: two boxes of
+//     64 rows) with the 128-byte swizzle, two per K step of 128, into a 4-slot ring and runs
+//     ahead across grid barriers (weights do not depend on activations).
 //   * A: the activations of all tokens as two bf16 planes, hi = bf16(v) and lo = bf16(v - hi),
 //     written to global memory by the stage that produced them (row = token, plane 1 TBMAX rows
 //     below plane 0). After the stage's grid barrier the activation-loader warp streams them with

@@ -460,7 +460,10 @@ __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
   if (cs.tid == 0 && !aborted(sm)) {
     // bar.sync above orders this CTA's stores before thread 0; the release add publishes them
     // at gpu scope and the acquire load below orders the other CTAs' stores before ours.
-    red_release_gpu_add(p.w.bar, 1u);
+    const bool skip = p.dbg_skip_barrier > 0 && cs.cta == cs.G - 1 &&
+                      cs.bar_target == static_cast<uint32_t>(p.dbg_skip_barrier) * static_cast<uint32_t>(cs.G);
+    if (!skip) red_release_gpu_add(p.w.bar, 1u);
+    const uint64_t limit = p.dbg_wait_ns != 0ull ? p.dbg_wait_ns : QTT_WAIT_NS;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 0;; ++it) {
       const uint32_t v = ld_acquire_gpu(p.w.bar);
@@ -470,7 +473,7 @@ __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
           *reinterpret_cast<volatile int*>(&sm.abort) = 1;
           break;
         }
-        if (globaltimer_ns() - t0 > QTT_WAIT_NS) {
+        if (globaltimer_ns() - t0 > limit) {
           fail(p, sm, DEV_ERR_GRID_TIMEOUT);
           break;
         }
@@ -1922,6 +1925,9 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
     p.w.amax[0] = 0ull;
     p.w.amax[1] = 0ull;
   }
+  // attention combine counters (the first attention stage follows a grid barrier): a launch that
+  // was abandoned part-way (a bounded wait that timed out) may have left them non-zero
+  if (blockIdx.x == 0 && tid < NKVH) p.w.att_cnt[tid] = 0u;
   Cons cs;
   cs.slot = 0;
   cs.round = 0;

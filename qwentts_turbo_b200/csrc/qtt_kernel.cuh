@@ -238,6 +238,11 @@ struct Params {
   unsigned long long* dbg_arrivals;
   int dbg_arr_stage0;
   int dbg_arr_n;
+  // error-path tests: when dbg_skip_barrier = k > 0, the last CTA does not arrive at the launch's
+  // k-th grid barrier, and grid-barrier waits give up after dbg_wait_ns (0: QTT_WAIT_NS), so the
+  // launch ends with DEV_ERR_GRID_TIMEOUT without a fault or a hang
+  int dbg_skip_barrier;
+  unsigned long long dbg_wait_ns;
 };
 
 // Host side: configure the kernel once per device and report the launch shape.
@@ -247,5 +252,8 @@ cudaError_t launch(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_
 // Batched kernel: the same for qtt_batch_kernel (also clears the sums-of-squares and argmax words).
 cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes);
 cudaError_t launch_b(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream);
+// Error code of the last qtt_backbone_step_noalloc on device `dev` (0: none, or the path is
+// unused there); clears it. Defined with the fixed scratch in qtt_noalloc.cu.
+cudaError_t noalloc_take_error(int dev, int* code);
 
 }  // namespace qtt

@@ -10,17 +10,20 @@
 //
 // Where the scratch lives: a file-scope __device__ array (below) of kNoAllocScratchBytes. The
 // array is part of the library's device image, so every GPU that loads libqtt.so holds it
-// until the process exits. In host code the array's name is only a host-side stand-in, never
-// a device address: the device address comes from cudaGetSymbolAddress, taken once per device
-// on the first call with that device current (so the first call on a device should come
-// before any stream capture) and passed to the kernel.
+// until the process exits. Under lazy module loading (CUDA_MODULE_LOADING=LAZY, the default
+// since CUDA 12.2) the driver places the array in device memory only when it is first used:
+// the first call on each device, which takes its address. That first call is therefore a
+// one-time driver allocation; make it at start-up (a warm-up step) and before any stream
+// capture. In host code the array's name is only a host-side stand-in, never a device
+// address: the device address comes from cudaGetSymbolAddress, taken once per device on the
+// first call with that device current, and is passed to the kernel.
 //
 // Sharing: every call on a device uses the same array, which keeps the last call's contents.
 // The barrier counter, the error word and the attention combine counters are cleared before
 // every launch. Calls whose executions overlap on the GPU (different streams, no ordering
 // between them) race on the array; order them on one stream. The return value covers the
-// argument checks and the launch; a device-side wait timeout in this path is recorded only in
-// the scratch's error word.
+// argument checks and the launch; a device-side error of the step (a bounded wait that timed
+// out) is kept in the array's error word and returned, then cleared, by qtt_stream_check().
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -77,6 +80,29 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+namespace qtt {
+// Device error code left in the fixed scratch by the last no-alloc step on `dev` (0 when the
+// path was never used there), then cleared. The caller has synchronised the step's stream.
+// Copies to and from a __device__ symbol allocate nothing.
+cudaError_t noalloc_take_error(int dev, int* code) {
+  *code = 0;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_setup.find(dev);
+    if (it == g_setup.end()) return cudaSuccess;
+    scratch = it->second.scratch;
+  }
+  Work w;
+  work_carve(scratch, &w);
+  const size_t off = static_cast<size_t>(reinterpret_cast<char*>(w.err) - static_cast<char*>(scratch));
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_noalloc_scratch, sizeof(int), off, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess || *code == 0) return e;
+  const int zero = 0;
+  return cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(int), off, cudaMemcpyHostToDevice);
+}
+}  // namespace qtt
+
 extern "C" qtt_status qtt_backbone_step_noalloc(const void* input_embedding, const TTSLayerWeights* layer_weights,
                                                 const void* final_norm_weight, const void* cos_table,
                                                 const void* sin_table, void* k_cache, void* v_cache,
@@ -94,7 +120,8 @@ extern "C" qtt_status qtt_backbone_step_noalloc(const void* input_embedding, con
   DeviceSetup ds;
   qtt_status st = device_setup(dev, &ds);
   if (st != QTT_OK) return st;
-  if (max_seq_len > (ds.ctas / qtt::NKVH) * qtt::ATT_CHMAX) return QTT_ERR_UNSUPPORTED;
+  // the persistent kernel's per-stage weight shares assume at least 128 CTAs (one per SM)
+  if (ds.ctas < 128 || max_seq_len > (ds.ctas / qtt::NKVH) * qtt::ATT_CHMAX) return QTT_ERR_UNSUPPORTED;
   qtt::Params p;
   std::memset(&p, 0, sizeof(p));
   qtt::work_carve(ds.scratch, &p.w);

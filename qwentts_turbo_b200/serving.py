@@ -17,9 +17,18 @@ sums (a last-bit difference, which can flip a near-tie).
 from __future__ import annotations
 
 import collections
+import ctypes
 from dataclasses import dataclass
 
 import torch
+
+
+def _with_stream(sp, philox: int):
+    """Copy of a qtt_sampling struct with another Philox stream."""
+    out = type(sp)()
+    ctypes.pointer(out)[0] = sp
+    out.philox_stream = philox
+    return out
 
 
 @dataclass
@@ -50,10 +59,12 @@ class ContinuousBatcher:
     engine: an ``Engine`` (or anything with its batched methods); sampling: the ``qtt_sampling``
     of every launch; chunk: frames per batched call between two state reads (a slot freed inside
     a chunk idles for the rest of it); policy: "continuous" refills a slot as soon as it is free,
-    "static" only once every slot is free (request-level batching, the comparison point)."""
+    "static" only once every slot is free (request-level batching, the comparison point);
+    prefill: "tensor_core" (qtt_prefill_tc, chunks of up to 128 positions per launch) or
+    "tokenwise" (qtt_prefill, the batch-1 kernel token by token) for each joining utterance."""
 
     def __init__(self, engine, sampling, slots: int | None = None, chunk: int = 4, stream=None,
-                 policy: str = "continuous"):
+                 policy: str = "continuous", prefill: str = "tensor_core"):
         self.eng = engine
         self.sp = sampling
         self.slots = min(64, engine.max_streams) if slots is None else slots
@@ -63,6 +74,9 @@ class ContinuousBatcher:
             raise ValueError("chunk must be >= 1")
         if policy not in ("continuous", "static"):
             raise ValueError("policy must be 'continuous' or 'static'")
+        if prefill not in ("tensor_core", "tokenwise"):
+            raise ValueError("prefill must be 'tensor_core' or 'tokenwise'")
+        self.prefill = prefill
         self.policy = policy
         self.chunk = chunk
         self.stream = stream
@@ -100,7 +114,10 @@ class ContinuousBatcher:
                         else utt.trailing.to(dev, torch.bfloat16).contiguous(),
                         utt.pad.to(dev, torch.bfloat16).reshape(1024).contiguous(), limit, philox)
         self.eng.set_stream_params(s, philox, limit)
-        self.eng.prefill_tc(s, utt.embeds, self.sp, self.stream)
+        if self.prefill == "tensor_core":
+            self.eng.prefill_tc(s, utt.embeds, self.sp, self.stream)
+        else:   # the first token's draw uses the launch's Philox stream: the utterance's own
+            self.eng.prefill(s, utt.embeds, _with_stream(self.sp, philox), self.stream)
         self.launches += 1
         self.slot_uid[s], self.slot_utt[s], self.slot_limit[s], self.slot_frames[s] = uid, utt, limit, -1
 

@@ -44,3 +44,13 @@ def test_library_loads_and_binds(lib_path):
     assert set(_lib.SIGNATURES) <= set(declared_functions())
     assert lib.qtt_status_string(0) == b"ok"
     assert lib.qtt_last_launch_status() == 0
+
+
+def test_library_build_id_matches_sources(lib_path):
+    """The library identifies the sources it was built from (a stale prebuilt library is
+    detectable on any machine it travels to)."""
+    from qwentts_turbo_b200 import _lib
+    from qwentts_turbo_b200.build import check_build_id, source_hash
+    lib = _lib.load(lib_path)
+    assert lib.qtt_build_id().decode() == source_hash()
+    check_build_id(lib)

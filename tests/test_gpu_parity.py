@@ -62,7 +62,7 @@ def dev_full(full_weights):
 
 @pytest.fixture(scope="module")
 def eng_full(dev_full):
-    e = Engine(dev_full, max_streams=2, max_seq=2304, max_frames=64)
+    e = Engine(dev_full, max_streams=2, max_seq=2304, max_frames=320)
     yield e
     e.close()
 
@@ -252,6 +252,27 @@ def test_c3_teacher_forced_greedy(orc_full, eng_full):
     assert max(r["h_rel"] for r in recs) <= HID_REL
 
 
+def test_c3_teacher_forced_300_frames(orc_full, eng_full):
+    """The whole C3 run (200-token context, 64 trailing rows, 300 greedy
+    frames) teacher-forced against the fp64 oracle. A frame is identical when all 16 of its tokens
+    equal the oracle's picks; a frame whose differing tokens are all near-ties (the oracle's top
+    two logits within two bf16 ulps, so the bf16 rounding of an fp32 sum decides) is counted
+    separately. Asserted: no token differs outside a near-tie, identical + near-tie frames >= 99%,
+    and the logits of every frame within the north_star tolerance."""
+    embeds, trailing, pad = c3_inputs(ctx=200, n_trailing=64)
+    n = 300
+    recs = run_teacher_forced(eng_full, orc_full, embeds, trailing, pad, _greedy_sp(), n)
+    full, bad = _frame_stats(recs)
+    tie_frames = n - full - len({b[0] for b in bad})
+    print(f"C3 300 frames: {full}/{n} identical ({full / n:.4f}), {tie_frames} with near-tie "
+          f"differences only, {len(bad)} other differences")
+    assert not bad, bad
+    assert (full + tie_frames) / n >= 0.99
+    assert max(r["cp_logits_viol"] for r in recs) <= 0
+    assert max(r["g0_logits_viol"] for r in recs) <= 0
+    assert max(r["h_rel"] for r in recs) <= HID_REL
+
+
 def test_teacher_forced_sampling(orc_full, eng_full):
     """Temperature 0.9 / top-k 50 / repetition penalty 1.2 with Philox draws, code predictor
     sampled too: the device sampler must pick exactly what the oracle's sampler picks from the
@@ -328,6 +349,36 @@ def test_long_context_backbone(orc_full, eng_full):
     assert_hidden_close(out, ref, "long context")
 
 
+def test_bounded_wait_timeout_reports_and_recovers(eng_small):
+    """Error path of the bounded device waits, without a fault: a frame whose 5th grid barrier
+    loses one arrival (the qtt_set_debug_barrier_fault test hook, waits limited to 20 ms) ends with
+    QTT_ERR_TIMEOUT from qtt_check and leaves the decode state as it was; the engine then decodes
+    the same frames as a run that never failed."""
+    embeds, trailing, pad = c3_inputs(ctx=40, n_trailing=5, seed=21)
+    sp = _greedy_sp()
+    tr, pd = trailing.cuda(), pad.cuda()
+    eng_small.prefill(0, embeds.cuda(), sp)
+    eng_small.frames(0, 3, tr, pd, sp)
+    eng_small.check()
+    ref = eng_small.codes(0)[:3].cpu().clone()
+    eng_small.prefill(0, embeds.cuda(), sp)
+    eng_small.check()
+    lib = eng_small.lib
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.qtt_set_debug_barrier_fault(eng_small.h, 5, 20_000_000) == 0
+    try:
+        eng_small.frames(0, 1, tr, pd, sp)
+        rc = lib.qtt_check(eng_small.h, stream)
+    finally:
+        assert lib.qtt_set_debug_barrier_fault(eng_small.h, 0, 0) == 0
+    assert rc == _lib.QTT_ERR_TIMEOUT, _lib.STATUS.get(rc)
+    assert lib.qtt_check(eng_small.h, stream) == 0          # the error word was cleared
+    assert eng_small.state(0)["frames"] == 0                # the abandoned frame changed no state
+    eng_small.frames(0, 3, tr, pd, sp)
+    eng_small.check()
+    assert torch.equal(eng_small.codes(0)[:3].cpu(), ref)
+
+
 def test_argument_errors(eng_small):
     lib = eng_small.lib
     out = torch.empty(1024, dtype=torch.float32, device="cuda")
@@ -349,7 +400,8 @@ def test_argument_errors(eng_small):
 
 def test_generate_api(small_weights, orc_small):
     """NativeTTSGenerator.generate (reference signature) returns the engine's frames; batch
-    inputs with padded attention masks decode each utterance on its valid tokens."""
+    inputs with padded attention masks decode each utterance on its valid tokens, all of them
+    together on the batched engine."""
     from qwentts_turbo_b200.generator import NativeTTSGenerator
     gen = NativeTTSGenerator(weights=small_weights, max_seq_len=256, max_frames=64)
     embeds, trailing, pad = c3_inputs(ctx=30, n_trailing=4, seed=31)
@@ -373,6 +425,21 @@ def test_generate_api(small_weights, orc_small):
     m3 = torch.zeros(1, 3, dtype=torch.long)
     emb2 = torch.cat([torch.cat([embeds[None], z3], 1), torch.cat([z3, embeds[None]], 1)])
     mask2 = torch.cat([torch.cat([mask, m3], 1), torch.cat([m3, mask], 1)])
+    # B = 2 runs on the batched engine (qtt_batch_frames, tcgen05): both copies of the utterance
+    # decode to the same codes as that utterance decoded alone on the batched engine, and agree
+    # with the batch-1 engine's codes up to near-tie flips
     both = gen.generate(emb2, mask2, torch.cat([trailing[None]] * 2), pad[None, None], max_tokens=5,
                         min_new_tokens=100)
-    assert both[0] == out and both[1] == out
+    assert gen._bengine is not None
+    alone = gen.generate(embeds[None], mask, trailing[None], pad[None, None], max_tokens=5, min_new_tokens=100,
+                         batched=True)
+    assert both[0] == alone and both[1] == alone
+    same = sum(a == b for fa, fb in zip(alone, out) for a, b in zip(fa, fb))
+    assert same >= 72, f"{same}/80 codes equal to the batch-1 engine's"
+    # sampled, B = 3: utterance b draws from Philox stream b, as a B = 1 batched call would
+    kw = dict(max_tokens=4, min_new_tokens=100, do_sample=True, temperature=0.9, top_k=50, repetition_penalty=1.2,
+              seed=5)
+    three = gen.generate(torch.cat([embeds[None]] * 3), torch.cat([mask] * 3), torch.cat([trailing[None]] * 3),
+                         pad[None, None], **kw)
+    first = gen.generate(embeds[None], mask, trailing[None], pad[None, None], batched=True, **kw)
+    assert three[0] == first and len(three) == 3 and all(len(c) == 4 for c in three)

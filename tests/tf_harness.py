@@ -121,40 +121,44 @@ def run_teacher_forced(eng, orc, embeds, trailing, pad, sp, n_frames, sampling=N
     return out
 
 
-def run_teacher_forced_batch(eng, orc, embeds, trailing, pads, sp, n_frames, sampling=None):
+def run_teacher_forced_batch(eng, orc, embeds, trailing, pads, sp, n_frames, sampling=None, check=None,
+                             prefill=True):
     """The same for the batched path: utterances 0..B-1 of ``eng`` advance together through
-    qtt_batch_frames; each is compared with the oracle holding that utterance's own KV cache
-    (one oracle, its caches swapped per utterance). Returns one list of per-frame dicts per
-    utterance."""
+    qtt_batch_frames; each utterance in ``check`` (default: all) is compared with the oracle
+    holding that utterance's own KV cache (one oracle, its caches swapped per utterance).
+    Returns one list of per-frame dicts per checked utterance, in ``check`` order. With
+    ``prefill=False`` the caller has already prefilled the utterances."""
     B = len(embeds)
-    eng.batch_prefill([e.cuda() for e in embeds], sp)
+    check = list(range(B)) if check is None else list(check)
+    if prefill:
+        eng.batch_prefill([e.cuda() for e in embeds], sp)
     eng.check()
-    caches = []
-    for s in range(B):
+    caches = {}
+    for s in check:
         P = eng.state(s)["position"]
         kc, vc = eng.kv(s)
         orc.reset_backbone()
         orc.set_kv_cache(kc[:, :, :P].cpu().to(orc.dt), vc[:, :, :P].cpu().to(orc.dt))
-        caches.append((orc.bk, orc.bv))
+        caches[s] = (orc.bk, orc.bv)
     d = orc.d
     cp_dbg = torch.zeros(B, 15, d.cp_vocab, dtype=torch.float32, device="cuda")
     g0_dbg = torch.zeros(B, d.vocab, dtype=torch.float32, device="cuda")
     eng.batch_set_debug_outputs(cp_dbg, g0_dbg)
     eos = d.eos_token_id if sampling is None else sampling.get("eos", d.eos_token_id)
     sup = orc.suppress_mask(eos)
-    hists = [[] for _ in range(B)]
-    out = [[] for _ in range(B)]
-    tr = [t.cuda() for t in trailing]
+    hists = {s: [] for s in check}
+    out = {s: [] for s in check}
+    tr = [None if t is None else t.cuda() for t in trailing]
     pd = [x.cuda() for x in pads]
     try:
         for _ in range(n_frames):
-            before = []
-            for s in range(B):
+            before = {}
+            for s in check:
                 st = eng.state(s)
-                before.append((st["position"], st["g0"], st["frames"], eng.hidden(s).cpu().to(orc.dt)))
+                before[s] = (st["position"], st["g0"], st["frames"], eng.hidden(s).cpu().to(orc.dt))
             eng.batch_frames(1, tr, pd, sp)
             eng.check()
-            for s in range(B):
+            for s in check:
                 pos, g0, step, h_e = before[s]
                 codes = eng.codes(s)[step].cpu().tolist()
                 g0_next = eng.state(s)["g0"]
@@ -167,4 +171,4 @@ def run_teacher_forced_batch(eng, orc, embeds, trailing, pads, sp, n_frames, sam
                                              hists[s], sup, eos))
     finally:
         eng.batch_set_debug_outputs(None, None)
-    return out
+    return [out[s] for s in check]
