@@ -62,6 +62,9 @@ def parse_args():
                     help="utterances per GPU of the continuous-batching measurement (c4; 0 = skip)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c5", action="store_true", help="skip the C5 side measurement (c4)")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip the same-GPU timing of the reference's own kernels (oracle/_ref)")
     return ap.parse_args()
 
 
@@ -241,6 +244,58 @@ def cpu_frames_per_s(seconds: float, warmup: int = 1, max_frames: int | None = N
     return timed / el, cores, timed, el
 
 
+def ref_gpu_baseline(dev: int, ctx: int = CTX, frames: int = 20, warmup: int = 3):
+    """Same-GPU baseline leg, outside the product's timed regions: the reference's own decode
+    kernels (fused_decode_tts.cu:834-890, fused_decode_code_predictor.cu:674-730), compiled from
+    its sources into oracle/_ref by oracle/Makefile, on the C3 workload's shapes and the same
+    random-init weights. Per frame one backbone step at position ctx + f and 15 code-predictor
+    steps at positions 0..14, timed with CUDA events on this GPU. Kernels only: the reference's
+    PyTorch code-predictor prefill, its 16 head GEMVs, sampling and combine glue are not counted,
+    so the result is a lower bound of the reference's frame time. None when oracle/_ref is absent."""
+    from oracle import ref_kernels
+    if not ref_kernels.available():
+        return None
+    from qwentts_turbo_b200.megakernel_backbone import extract_backbone_weights
+    from qwentts_turbo_b200.megakernel_code_predictor import extract_code_predictor_weights
+    from qwentts_turbo_b200.weights import synthetic_weights
+    torch.cuda.set_device(dev)
+    w = synthetic_weights()
+    max_seq = ctx + warmup + frames + 8
+    bw = extract_backbone_weights(w, max_seq)
+    cw = extract_code_predictor_weights(w, 64)
+    del w
+    tts = ref_kernels.RefDecoder("tts", bw["layer_weights"], bw["final_norm_weight"], bw["cos_table"],
+                                 bw["sin_table"], bw["num_layers"], max_seq)
+    cp = ref_kernels.RefDecoder("cp", cw["layer_weights"], cw["final_norm_weight"], cw["cos_table"],
+                                cw["sin_table"], cw["num_layers"], 64)
+    g = torch.Generator().manual_seed(4)
+    tts.k[:, :, :ctx] = torch.randn(tts.k[:, :, :ctx].shape, generator=g).to(torch.bfloat16).cuda()
+    tts.v[:, :, :ctx] = torch.randn(tts.v[:, :, :ctx].shape, generator=g).to(torch.bfloat16).cuda()
+    x = torch.randn(1024, generator=g).to(torch.bfloat16).cuda()
+    tts.position = ctx
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    bb_ms, cp_ms = [], []
+    for f in range(warmup + frames):
+        ev[0].record(stream)
+        tts.step(x)
+        ev[1].record(stream)
+        cp.position = 0
+        for _ in range(15):
+            cp.step(x)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        if f >= warmup:
+            bb_ms.append(ev[0].elapsed_time(ev[1]))
+            cp_ms.append(ev[1].elapsed_time(ev[2]))
+    b, c = statistics.median(bb_ms), statistics.median(cp_ms)
+    return {"frame_ms": b + c, "backbone_step_ms": b, "cp_15_steps_ms": c, "frames": frames,
+            "what": "the reference's own CUDA kernels (oracle/_ref, built from its sources for sm_100a) on this "
+                    "GPU: one 28-layer backbone step at the C3 positions + 15 code-predictor steps per frame, "
+                    "median of the timed frames; kernels only (its PyTorch prefill, heads, sampling and combine "
+                    "glue excluded), a lower bound of its frame time"}
+
+
 # ------------------------------------------------------------------------------------------
 def cpu_sample_text(c4, timed, el, cores):
     if c4:
@@ -361,6 +416,8 @@ def run_c3(args, rank, world, local_rank, K, W):
     if rank != 0:
         eng.close()
         return None
+    eng.close()
+    ref_gpu = None if args.no_ref_gpu else ref_gpu_baseline(dev)
 
     # ---- roofline -------------------------------------------------------------------------
     wbytes = frame_weight_bytes()
@@ -389,8 +446,8 @@ def run_c3(args, rank, world, local_rank, K, W):
         "gpu_launches": K,
         "clocks": clocks.summary(t0, t1),
         "codes_gathered": n_codes,
+        "ref_gpu_baseline": ref_gpu,
     }
-    eng.close()
     return line
 
 
@@ -478,13 +535,13 @@ def run_c4(args, rank, world, local_rank, K, W):
             raise _lib.QTTError(rc, "qtt_batch_frames")
         for s in range(B):
             codes_h[f, s].copy_(codes_devs[s][W + f], non_blocking=True)
+    # the run's codes of every rank to rank 0 (NCCL all-gather over NVLink; one rank: a copy)
+    gathered = gather_codes(torch.stack([codes_devs[s][W:W + K] for s in range(B)]).reshape(-1, 16))
     e3.record(stream)
     barrier()
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
     eng.check()
     assert torch.equal(codes_h, codes[:, W:].permute(1, 0, 2).cpu()), "e2e path produced different codes"
-
-    gathered = gather_codes(codes.reshape(-1, 16))
     n_codes = sum(x.shape[0] for x in gathered) if gathered is not None else 0
     if rank != 0:
         eng.close()
@@ -514,7 +571,8 @@ def run_c4(args, rank, world, local_rank, K, W):
                      "kernel": "qtt_batch_kernel (1 launch per frame of all utterances)"},
         "e2e": {"value": world * B * K / (ms_e2e / 1000.0), "unit": UNIT,
                 "h2d_bytes_per_step": B * 2048 + B * bstream_bytes, "d2h_bytes_per_step": B * 64,
-                "path": "qtt_batch_frames C-ABI per frame: pinned H2D of the B text rows, D2H of the B code rows"},
+                "path": "qtt_batch_frames C-ABI per frame: pinned H2D of the B text rows, D2H of the B code rows; "
+                        "the run's codes of all ranks gathered to rank 0 at the end (NCCL all-gather)"},
         "gpu_launches": K,
         "clocks": clocks.summary(t0, t1),
         "codes_gathered": n_codes,
@@ -678,16 +736,23 @@ def run_prefill(args, rank, world, local_rank, K, W):
 
 
 def run_c5(args, rank, world, local_rank):
-    """C5 on each GPU: args.batch utterances with their own context lengths and frame counts, all
-    decoded together until the last one reaches its count (the kernel stops each utterance at its
-    own count, qtt_set_stream_params). One device-timed call of qtt_batch_frames over max(count)
-    frames; value = useful frames (sum of the counts, all ranks) / max-over-ranks time."""
+    """C5 on each GPU: args.batch utterances with their own context
+    lengths U[100,600] and frame counts U[200,600], decoded together until the last one reaches its
+    count (the kernel stops each utterance at its own count, qtt_set_stream_params). One job per
+    rank, timed on the device in three parts with CUDA events:
+      prefill  contexts, text rows and pad rows H2D from pinned host memory + the tensor-core
+               prefill of every utterance (qtt_prefill_tc into its stream),
+      frames   one qtt_batch_frames call of max(count) frames,
+      gather   every utterance's codes to rank 0 (NCCL all-gather over NVLink) and D2H there.
+    value = useful frames of all ranks (the sum of the counts) / max over ranks of the frames part;
+    e2e = the same frames / max over ranks of the whole job. Returns rank 0's fields."""
     import torch.distributed as dist
 
     from qwentts_turbo_b200.config import frame_weight_bytes, kv_read_bytes_per_frame
-    from qwentts_turbo_b200.dist import max_over_ranks
+    from qwentts_turbo_b200.dist import gather_codes, max_over_ranks
     from qwentts_turbo_b200.engine import DeviceModel, Engine, sampling_struct
     from qwentts_turbo_b200.weights import synthetic_weights
+    from qwentts_turbo_b200.workloads import c4_inputs
 
     dev = local_rank
     torch.cuda.set_device(dev)
@@ -695,73 +760,105 @@ def run_c5(args, rank, world, local_rank):
     max_seq = C5_CTX[1] + C5_FRAMES[1] + 8
     dm = DeviceModel(synthetic_weights(), device=dev, rope_rows=max_seq)
     eng = Engine(dm, max_streams=B, max_seq=max_seq, max_frames=C5_FRAMES[1])
-    g = torch.Generator().manual_seed(500 + rank)
-    ctx = torch.randint(C5_CTX[0], C5_CTX[1] + 1, (B,), generator=g).tolist()
+    ctx, embeds, trailing, pads = c4_inputs(B, C5_CTX[0], C5_CTX[1], N_TRAILING, seed=500 + rank)
+    g = torch.Generator().manual_seed(600 + rank)
     counts = torch.randint(C5_FRAMES[0], C5_FRAMES[1] + 1, (B,), generator=g).tolist()
-    embeds = [torch.randn(L, 1024, generator=g).to(torch.bfloat16).cuda() for L in ctx]
-    trailing = [torch.randn(N_TRAILING, 1024, generator=g).to(torch.bfloat16).cuda() for _ in range(B)]
-    pads = [torch.randn(1024, generator=g).to(torch.bfloat16).cuda() for _ in range(B)]
+    # pinned host inputs and their device buffers (allocated before the timed region)
+    emb_h = [e.pin_memory() for e in embeds]
+    tr_h = [t.pin_memory() for t in trailing]
+    pad_h = [x.pin_memory() for x in pads]
+    emb_d = [torch.empty_like(e, device="cuda") for e in embeds]
+    tr_d = [torch.empty_like(t, device="cuda") for t in trailing]
+    pad_d = [torch.empty_like(x, device="cuda") for x in pads]
     sp = sampling_struct(do_sample=True, temperature=0.9, top_k=50, repetition_penalty=1.2,
                          min_new_tokens=1 << 30, seed=1234 + rank)
     stream = torch.cuda.current_stream()
 
-    def prefill_all():
+    def job(n_frames=None):
+        for a, b in zip(emb_d + tr_d + pad_d, emb_h + tr_h + pad_h):
+            a.copy_(b, non_blocking=True)
         for s in range(B):
             eng.set_stream_params(s, 1000 * rank + s, counts[s])
-            eng.prefill_tc(s, embeds[s], sp)
+            eng.prefill_tc(s, emb_d[s], sp)
+        ev[1].record(stream)
+        eng.batch_frames(max(counts) if n_frames is None else n_frames, tr_d, pad_d, sp)
+        ev[2].record(stream)
+        codes = torch.cat([eng.codes(s)[:counts[s]] for s in range(B)])
+        got = gather_codes(codes)
+        if got is not None:
+            got = [x.cpu() for x in got]
+        return got
 
-    # warm-up: a short run of the same launches
-    prefill_all()
-    eng.batch_frames(args.warmup, trailing, pads, sp)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    job(args.warmup)      # warm-up: the same launches, a few frames
     eng.check()
-    prefill_all()
-    torch.cuda.synchronize()
     clocks = ClockSampler(dev)
     time.sleep(0.3)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.time()
-    e0.record(stream)
-    eng.batch_frames(max(counts), trailing, pads, sp)
-    e1.record(stream)
+    ev[0].record(stream)
+    got = job()
+    ev[3].record(stream)
     torch.cuda.synchronize()
     t1 = time.time()
-    ms_local = e0.elapsed_time(e1)
-    ms = max_over_ranks(ms_local)
     clocks.stop()
     eng.check()
     st = eng.batch_states(B)
     assert [x[1] for x in st] == counts, "an utterance did not reach its frame count"
+    t_pre = max_over_ranks(ev[0].elapsed_time(ev[1]))
+    t_fr_local = ev[1].elapsed_time(ev[2])
+    t_fr = max_over_ranks(t_fr_local)
+    t_all = max_over_ranks(ev[0].elapsed_time(ev[3]))
+    frames_local = sum(counts)
+    frames_all = frames_local
+    if world > 1:
+        x = torch.tensor([frames_local], dtype=torch.int64, device="cuda")
+        dist.all_reduce(x)
+        frames_all = int(x.item())
     eng.close()
     if rank != 0:
         return None
-    frames = sum(counts)
+    assert sum(c.shape[0] for c in got) == frames_all, "gathered codes"
     launches = max(counts)
     wbytes = frame_weight_bytes()
     kv = sum(kv_read_bytes_per_frame(ctx[s] + f) for s in range(B) for f in range(counts[s]))
     alg = (launches * wbytes + kv) / launches
-    achieved = alg / (ms_local / 1000.0 / launches) / 1e9
+    achieved = alg / (t_fr_local / 1000.0 / launches) / 1e9
     peak, peak_src = measured_hbm_peak()
+    h2d = sum(2 * 1024 * (c + N_TRAILING + 1) for c in ctx) + 80 * B
     return {
-        "metric": METRIC, "value": world * frames / (ms / 1000.0), "unit": UNIT, "n_gpus": world,
-        "steps": launches, "warmup": args.warmup, "ms_per_step": ms / launches, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (random-init weights, seeded N(0,1) inputs)", "config": workload_config(args),
-        "frames_per_gpu": frames, "occupancy": frames / (B * launches),
+        "workload": f"C5 per GPU: {B} utterances decoded together, contexts U[{C5_CTX[0]},{C5_CTX[1]}], frame counts "
+                    f"U[{C5_FRAMES[0]},{C5_FRAMES[1]}] (each stops at its own count), T 0.9 / top-k 50 / repetition "
+                    "1.2 with a Philox stream per utterance, EOS masked; codes gathered to rank 0",
+        "metric": METRIC, "value": frames_all / (t_fr / 1000.0), "unit": UNIT, "n_gpus": world,
+        "frames": frames_all, "launches_per_gpu": launches, "occupancy": frames_local / (B * launches),
+        "ms_per_launch": t_fr / launches,
+        "e2e": {"value": frames_all / (t_all / 1000.0), "unit": UNIT, "prefill_ms": t_pre, "frames_ms": t_fr,
+                "job_ms": t_all, "h2d_bytes_per_gpu": h2d, "d2h_bytes": frames_all * 64,
+                "path": "pinned H2D of every input, qtt_prefill_tc per utterance, one qtt_batch_frames call, NCCL "
+                        "all-gather of the codes to rank 0 and D2H there"},
+        "limiter": "the batch drains: a launch costs the same with fewer utterances running (the frame is "
+                   "latency-bound), so useful frames per launch fall as utterances reach their counts; the "
+                   "gather is a few MB over NVLink",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_src, "traffic": None, "algorithmic_bytes_per_launch": alg,
-                     "kernel": "qtt_batch_kernel (1 launch per frame of the utterances still running)"},
-        "gpu_launches": launches,
+                     "peak_source": peak_src, "algorithmic_bytes_per_launch": alg},
         "clocks": clocks.summary(t0, t1),
     }
 
 
 def run_ours(args, rank, world, local_rank):
     if args.workload == "c5":
-        line = run_c5(args, rank, world, local_rank)
-        if line is not None:
+        c5 = run_c5(args, rank, world, local_rank)
+        if c5 is not None:
+            line = {k: c5[k] for k in ("metric", "value", "unit", "n_gpus")}
+            line.update({"steps": c5["launches_per_gpu"], "warmup": args.warmup, "ms_per_step": c5["ms_per_launch"],
+                         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                         "data": "synthetic (random-init weights, seeded N(0,1) inputs)",
+                         "config": workload_config(args), "e2e": c5["e2e"], "roofline": c5["roofline"],
+                         "gpu_launches": c5["launches_per_gpu"] + args.batch * 2, "clocks": c5["clocks"],
+                         "occupancy": c5["occupancy"], "limiter": c5["limiter"]})
             print(json.dumps(line), flush=True)
         return
     if args.workload == "prefill":
@@ -779,11 +876,18 @@ def run_ours(args, rank, world, local_rank):
                 line["bs1"] = {"workload": "C3 (batch-1 frame loop, 200-token context, greedy)",
                                "frames_per_s": bs1["value"] / world, "frame_latency_us": bs1["frame_latency_us"],
                                "rtf": bs1["rtf"], "e2e_frames_per_s": bs1["e2e"]["value"] / world,
-                               "hbm_frac": bs1["roofline"]["frac"], "steps": args.bs1_steps}
+                               "hbm_frac": bs1["roofline"]["frac"], "steps": args.bs1_steps,
+                               "ref_gpu_baseline": bs1["ref_gpu_baseline"]}
+                if bs1["ref_gpu_baseline"] is not None:
+                    line["bs1"]["ref_megakernel_frame_ms"] = bs1["ref_gpu_baseline"]["frame_ms"]
         if args.serve_requests > 0:
             serving = run_serving(args, rank, world, local_rank)
             if line is not None:
                 line["serving"] = serving
+        if not args.no_c5:
+            c5 = run_c5(args, rank, world, local_rank)
+            if line is not None:
+                line["c5"] = c5
     if line is None:
         return
     if world == 1 and not args.no_cpu_baseline:

@@ -28,8 +28,21 @@ def violation(a, b):
     return float(((a - b).abs() - (ATOL + RTOL * b.abs()))[fin].max())
 
 
+def bf16_ulp(b):
+    """Spacing of bf16 values at |b| (8 significant bits): the rounding quantum of a bf16 logit."""
+    e = torch.floor(torch.log2(b.abs().clamp_min(2.0 ** -126)))
+    return torch.exp2(e - 7)
+
+
+def violation_ulp(a, b):
+    """As violation(), with one more bf16 ulp of b allowed: both sides round their logits to
+    bf16, so an fp32 difference far below the tolerance can still move a logit by one ulp."""
+    fin = torch.isfinite(b)
+    return float(((a - b).abs() - (ATOL + RTOL * b.abs() + bf16_ulp(b)))[fin].max())
+
+
 def _compare_frame(orc, kv, h_e, g0, pos, step, codes, g0_next, cp_e, g0l_e, h_e2, trailing, pad, sp, sampling,
-                   hist, sup, eos):
+                   hist, sup, eos, peer=None):
     """One teacher-forced frame: the oracle runs from the engine's state before the frame
     (h_e, g0, KV rows), the engine's results are codes / g0_next / cp_e / g0l_e / h_e2. ``kv``:
     (k, v) of the engine's cache after the frame (its new row is copied into the oracle)."""
@@ -62,6 +75,14 @@ def _compare_frame(orc, kv, h_e, g0, pos, step, codes, g0_next, cp_e, g0l_e, h_e
     lo = orc.head_logits(orc.codec_head, h_o).double()
     rec["g0_logits_err"] = float((g0l_e - lo).abs().max())
     rec["g0_logits_viol"] = violation(g0l_e, lo)
+    rec["g0_logits_viol_ulp"] = violation_ulp(g0l_e, lo)
+    if peer is not None:
+        # another implementation's backbone step on the same input and KV rows (the reference's
+        # own kernel): how far its codec-head logits land from the exact math
+        h_p = peer(x, pos, kv).to(orc.dt)
+        lp = bf16_logits(orc.codec_head, h_p)
+        rec["peer_g0_logits_err"] = float((lp - lo).abs().max())
+        rec["peer_g0_logits_viol"] = violation(lp, lo)
     # --- next group 0: greedy from the oracle's logits; sampled from the ENGINE's logits
     min_new = sp.min_new_tokens
     mask_eos = eos if step + 1 < min_new else None
@@ -86,10 +107,17 @@ def _compare_frame(orc, kv, h_e, g0, pos, step, codes, g0_next, cp_e, g0l_e, h_e
     return rec
 
 
-def run_teacher_forced(eng, orc, embeds, trailing, pad, sp, n_frames, sampling=None):
+def bf16_logits(W, h):
+    """Codec-head logits as the reference computes them: bf16 values of W @ bf16(h)."""
+    return O.Qwen3TTSOracle.head_logits(W, h).double()
+
+
+def run_teacher_forced(eng, orc, embeds, trailing, pad, sp, n_frames, sampling=None, peer=None):
     """Returns a list of per-frame dicts. ``sampling``: None for greedy, else dict(temperature,
     top_k, repetition_penalty, seed, stream, cp_temperature, cp_top_k, cp_do_sample,
-    min_new_tokens)."""
+    min_new_tokens). ``peer(x, pos, (k, v))``: optional second implementation of the backbone
+    step, run on each frame's combined input x at position pos over the engine's KV rows; its
+    codec-head logits are compared with the exact math as well (``peer_g0_logits_*``)."""
     eng.prefill(0, embeds.cuda(), sp)
     st = eng.state(0)
     P = st["position"]
@@ -115,14 +143,14 @@ def run_teacher_forced(eng, orc, embeds, trailing, pad, sp, n_frames, sampling=N
             hist.append(g0)
             out.append(_compare_frame(orc, eng.kv(0), h_e, g0, pos, step, codes, g0_next, cp_dbg.cpu().double(),
                                       g0_dbg.cpu().double(), eng.hidden(0).cpu().to(orc.dt), trailing, pad, sp,
-                                      sampling, hist, sup, eos))
+                                      sampling, hist, sup, eos, peer))
     finally:
         eng.set_debug_outputs(None, None)
     return out
 
 
 def run_teacher_forced_batch(eng, orc, embeds, trailing, pads, sp, n_frames, sampling=None, check=None,
-                             prefill=True):
+                             prefill=True, peer=None):
     """The same for the batched path: utterances 0..B-1 of ``eng`` advance together through
     qtt_batch_frames; each utterance in ``check`` (default: all) is compared with the oracle
     holding that utterance's own KV cache (one oracle, its caches swapped per utterance).
@@ -168,7 +196,7 @@ def run_teacher_forced_batch(eng, orc, embeds, trailing, pads, sp, n_frames, sam
                 out[s].append(_compare_frame(orc, eng.kv(s), h_e, g0, pos, step, codes, g0_next,
                                              cp_dbg[s].cpu().double(), g0_dbg[s].cpu().double(),
                                              eng.hidden(s).cpu().to(orc.dt), trailing[s], pads[s], sp, smp,
-                                             hists[s], sup, eos))
+                                             hists[s], sup, eos, peer))
     finally:
         eng.batch_set_debug_outputs(None, None)
     return [out[s] for s in check]
