@@ -293,6 +293,7 @@ struct qtt_engine {
   const void* h_codec_head = nullptr;
   const void* h_cp_head[qtt::NCPHEADS] = {};
   DevShape bshape;
+  int bcl = 0;               // CTAs per cluster of the batched kernel
   bool b_ready = false;
   void* d_bwork = nullptr;
   void* d_bmaps = nullptr;
@@ -703,33 +704,34 @@ constexpr size_t kCpKvFloats = static_cast<size_t>(qtt::NKVH) * kCpMaxSeq * qtt:
 // weight matrix, once per engine.
 qtt_status ensure_batch(qtt_engine* e) {
   if (e->b_ready) return QTT_OK;
-  cudaError_t ce = qtt::kernel_setup_b(e->device, &e->bshape.ctas, &e->bshape.smem);
+  cudaError_t ce = qtt::kernel_setup_b(e->device, &e->bshape.ctas, &e->bshape.smem, &e->bcl);
+  if (ce == cudaErrorInvalidConfiguration) return QTT_ERR_UNSUPPORTED;   // too few clusters fit
   if (ce != cudaSuccess) return from_cuda(ce);
-  // the K split needs a CTA per row tile (gate/up: 48 tiles of 128 rows)
-  if (e->bshape.ctas > qtt::BKCTAS || e->bshape.ctas < 64) return QTT_ERR_UNSUPPORTED;
   const int nbb = e->dims.backbone_layers, ncp = e->dims.cp_layers;
   const int h0 = (nbb + ncp) * qtt::NLMAPS;
   const int nmaps = h0 + 1 + qtt::NCPHEADS + 4;
   std::vector<CUtensorMap> maps(nmaps);
   bool ok = true;
+  // every stage splits its rows into R = 128 / cluster tiles: one box of a tile's N rows per
+  // 64-column atom (gate/up: a box of N/2 gate rows and one of N/2 up rows)
+  const uint32_t R = qtt::BROWS_B / e->bcl;
   auto layer_maps = [&](const TTSLayerWeights& L, CUtensorMap* m) {
-    // one box per 128-row tile and 64-column atom (gate/up: 64-row boxes, one of each)
-    constexpr uint32_t R = qtt::BNMAX, RH = qtt::BNMAX / 2;
-    ok = ok && encode_sw128(L.q_proj_weight, qtt::QSZ, qtt::HID, R, m + 0);
-    ok = ok && encode_sw128(L.k_proj_weight, qtt::KVSZ, qtt::HID, R, m + 1);
-    ok = ok && encode_sw128(L.v_proj_weight, qtt::KVSZ, qtt::HID, R, m + 2);
-    ok = ok && encode_sw128(L.o_proj_weight, qtt::HID, qtt::QSZ, R, m + 3);
-    ok = ok && encode_sw128(L.gate_proj_weight, qtt::INTER, qtt::HID, RH, m + 4);
-    ok = ok && encode_sw128(L.up_proj_weight, qtt::INTER, qtt::HID, RH, m + 5);
-    ok = ok && encode_sw128(L.down_proj_weight, qtt::HID, qtt::INTER, R, m + 6);
+    const uint32_t nq = qtt::QKV_ROWS / R, no = qtt::HID / R, ngu = 2 * qtt::INTER / R, nd = qtt::HID / R;
+    ok = ok && encode_sw128(L.q_proj_weight, qtt::QSZ, qtt::HID, nq, m + 0);
+    ok = ok && encode_sw128(L.k_proj_weight, qtt::KVSZ, qtt::HID, nq, m + 1);
+    ok = ok && encode_sw128(L.v_proj_weight, qtt::KVSZ, qtt::HID, nq, m + 2);
+    ok = ok && encode_sw128(L.o_proj_weight, qtt::HID, qtt::QSZ, no, m + 3);
+    ok = ok && encode_sw128(L.gate_proj_weight, qtt::INTER, qtt::HID, ngu / 2, m + 4);
+    ok = ok && encode_sw128(L.up_proj_weight, qtt::INTER, qtt::HID, ngu / 2, m + 5);
+    ok = ok && encode_sw128(L.down_proj_weight, qtt::HID, qtt::INTER, nd, m + 6);
   };
-  // every row tile is full: 128-row tiles of the heads
-  if (e->dims.vocab % qtt::BNMAX != 0 || e->dims.cp_vocab % qtt::BNMAX != 0) return QTT_ERR_UNSUPPORTED;
+  // the heads split into R full tiles whose row counts the M = 128 MMA takes (multiples of 16)
+  if (e->dims.vocab % (16 * R) != 0 || e->dims.cp_vocab % (16 * R) != 0) return QTT_ERR_UNSUPPORTED;
   for (int l = 0; l < nbb; ++l) layer_maps(e->h_bb[l], maps.data() + l * qtt::NLMAPS);
   for (int l = 0; l < ncp; ++l) layer_maps(e->h_cp[l], maps.data() + (nbb + l) * qtt::NLMAPS);
-  ok = ok && encode_sw128(e->h_codec_head, e->dims.vocab, qtt::HID, qtt::BNMAX, &maps[h0]);
+  ok = ok && encode_sw128(e->h_codec_head, e->dims.vocab, qtt::HID, e->dims.vocab / R, &maps[h0]);
   for (int g = 0; g < qtt::NCPHEADS; ++g)
-    ok = ok && encode_sw128(e->h_cp_head[g], e->dims.cp_vocab, qtt::HID, qtt::BNMAX, &maps[h0 + 1 + g]);
+    ok = ok && encode_sw128(e->h_cp_head[g], e->dims.cp_vocab, qtt::HID, e->dims.cp_vocab / R, &maps[h0 + 1 + g]);
   if (!ok) return QTT_ERR_UNSUPPORTED;
   ce = cudaMalloc(&e->d_bwork, qtt::bwork_bytes());
   if (ce == cudaSuccess) ce = cudaMemset(e->d_bwork, 0, qtt::bwork_bytes());
@@ -772,6 +774,7 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   qtt::Params p = e->base;
   p.bmaps = static_cast<const uint8_t*>(e->d_bmaps);
   p.nb = B;
+  p.bcl = e->bcl;
   p.bs = e->d_bs;
   qtt::bwork_carve(e->d_bwork, &p.bw);
   p.sp = to_dev(sp);

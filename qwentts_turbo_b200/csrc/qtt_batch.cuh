@@ -3,29 +3,34 @@
 // items, sampler, head masks and stage helpers.
 //
 // One cooperative launch of qtt_batch_kernel runs one program for B <= 64 utterances: a frame
-// of every utterance (MODE_B_FRAME), one context step of the backbone prefill (MODE_B_PREFILL)
-// or the first group-0 token after the prefill (MODE_B_HEAD). The weights are streamed once
-// per program for the whole batch. Every projection is a GEMM
+// of every utterance (MODE_B_FRAME), one context step of the backbone prefill (MODE_B_PREFILL),
+// a chunk of one utterance's context (MODE_B_PREFILL_DENSE) or the first group-0 token after the
+// prefill (MODE_B_HEAD). The weights are streamed once per program for the whole batch.
+//
+// The grid is made of thread-block clusters of p.bcl CTAs (4, or 2 when the GPU cannot hold
+// enough clusters of 4). Every projection is a GEMM
 //     D[tokens x rows] = A[tokens x K] * W[rows x K]^T
-//   * W: this CTA's row tile of the matrix (128 rows; gate/up: 64 gate + 64 up rows). The
-//     producer warp streams it as 2-D TMA boxes of 128 rows x 64 columns (gate/up: two boxes of
-//     64 rows) with the 128-byte swizzle, two per K step of 128, into a 4-slot ring and runs
-//     ahead across grid barriers (weights do not depend on activations).
+// split into 128 / bcl row tiles of N rows, one per cluster, and bcl K slices, one per CTA of the
+// cluster (128 CTAs work on every GEMM; the rest of the grid waits at the stage's barrier):
+//   * W: the CTA's rows of the tile over its K slice. The producer warp streams them per K step of
+//     128 as 2-D TMA boxes of N rows x 64 columns with the 128-byte swizzle (gate/up: a box of N/2
+//     gate rows and one of N/2 up rows) into a ring of 4 KB slots (an entry of N / 16 slots per
+//     K step) and runs ahead across grid barriers (weights do not depend on activations).
 //   * A: the activations of all tokens as two bf16 planes, hi = bf16(v) and lo = bf16(v - hi),
 //     written to global memory by the stage that produced them (row = token, plane 1 TBMAX rows
 //     below plane 0). After the stage's grid barrier the activation-loader warp streams them with
-//     2-D TMA boxes (64 columns x 64 tokens per plane; one slot per 64-token tile and K step of
-//     128 = two 128-byte swizzle atoms) into a 3-slot ring, independently of the MMA issue.
-//   * D: fp32 in tensor memory, N <= 128 columns. An activation slot holds a 64-token tile's hi
-//     plane in rows 0..63 and its lo plane in rows 64..127; per K sub-step of 16 one M = 128
-//     tcgen05.mma starts its A at the hi rows and a second one at the lo rows, both with the same
-//     weights, so TMEM lanes 0..63 hold D = W (hi + lo): ~16 mantissa bits of the activations,
-//     close to an fp32 GEMV.
-// The consumer warps of lane quarters 0 and 1 read D with tcgen05.ld (one thread per token) into
-// the K slice's partial; the row tile's slices are summed in a fixed order, the epilogue applies
-// the deferred RMSNorm scale and the stage's elementwise work, and writes the next GEMM's A
-// planes. Sums of squares for the next RMSNorm are accumulated per token with
-// 64-bit fixed-point atomics (order independent).
+//     2-D TMA boxes (64 columns x 64 tokens per plane) into a 3-slot ring: one slot per 64-token
+//     tile and K step, hi rows 0..63 and lo rows 64..127.
+//   * D: one M = 128 tcgen05.mma per K sub-step of 16 reads the whole slot, so TMEM lanes 0..63
+//     hold hi.W and lanes 64..127 lo.W of the tile's 64 tokens (fp32, N columns per token tile):
+//     ~16 mantissa bits of the activations, close to an fp32 GEMV.
+// K-slice exchange: the consumer warps move D to shared memory (the activation ring, idle until
+// the next stage's loads), lo lanes first and the hi lanes added, then signal the cluster's other
+// CTAs on an mbarrier each; every CTA then sums its share of the tile's outputs over the bcl CTAs'
+// partials in rank order, reading them through distributed shared memory, and runs the epilogue:
+// the deferred RMSNorm scale and the stage's elementwise work, the next GEMM's A planes. Sums of
+// squares for the next RMSNorm are accumulated per token with 64-bit fixed-point atomics (order
+// independent), so reruns are bit-identical.
 //
 // Stages of a code-predictor pass: INPUT (embedding rows -> x, A planes, sums of squares) |
 // per layer QKV | attention | O (+ residual) | gate/up | down (+ residual) | NORM | HEAD; a
@@ -35,34 +40,35 @@
 constexpr int KSUB = 64;                  // K elements of one 128-byte swizzle atom row
 constexpr int NSUB = 2;                   // atoms per pipeline step
 constexpr int KSTEP = KSUB * NSUB;        // K elements per pipeline step
-constexpr int WBOX = 16;                  // weight rows per TMA box
-constexpr int NMAX = BNMAX;               // columns of D (weight rows) per CTA tile
-constexpr int WS_BYTES = NMAX * 128;      // weight slot: one atom of up to 128 rows of 128 bytes
-constexpr int NWS = 4;                    // weight slots (two pipeline steps)
+constexpr int BROWS = 128;                // CTAs of a GEMM stage (row tiles x K slices)
+constexpr int WSLOT = 4096;               // weight-ring slot; a K step of an N-row tile is N / 16 slots
+constexpr int NWSLOT = 30;
+constexpr int NWE = 8;                    // weight entries (K steps) in flight
 constexpr int APLANE_BYTES = 64 * 128;    // one plane of an activation atom: 64 token rows
 constexpr int ASUB_BYTES = 2 * APLANE_BYTES;  // hi plane, then lo plane
 constexpr int AS_BYTES = NSUB * ASUB_BYTES;
 constexpr int NAS = 3;
-constexpr int DCOLS = NMAX;               // tensor-memory columns of one 64-token tile's accumulator
-constexpr uint32_t TMEM_COLS = 2 * DCOLS; // two 64-token tiles
-constexpr int KPAD = NMAX;                // row stride of a K-slice partial in global memory
-constexpr int BKBANK = 64;                // K-split counters per bank (row tiles of a stage)
-constexpr int BT_STRIDE = 20;             // row stride (floats) of a warp's partial-store tile in sm.att
-static_assert(6 * 32 * BT_STRIDE * 4 <= ATT_STAGE_BYTES, "partial-store tiles fit sm.att");
-// An M = 128 MMA reads the whole slot: rows 0..63 (hi plane) and 64..127 (lo plane).
-static_assert(NWS * WS_BYTES + NAS * AS_BYTES <= NSLOTS * SLOT_BYTES, "batched rings fit the ring region");
-static_assert(TBMAX * (NMAX + 1) * 4 <= NAS * AS_BYTES, "epilogue staging fits the activation ring");
-static_assert(2 * BKBANK <= BKCTAS, "K-split counter banks");
-// mbarriers in sm.bbar (all with one expected arrival)
+constexpr int WRING_BYTES = NWSLOT * WSLOT;
+constexpr uint32_t TMEM_COLS = 512;       // up to two 64-token tiles of the widest tile
+constexpr int NMAX_B = 192;               // widest tile: 96 gate + 96 up rows (clusters of 4)
+// The batched kernel's rings span sm.ring and the two batch-1 scratch areas behind it (sm.xs,
+// sm.att), which it does not use.
+constexpr int BRING_BYTES = NSLOTS * SLOT_BYTES + NTMAX * INTER * 4 + ATT_STAGE_BYTES;
+static_assert(WRING_BYTES + NAS * AS_BYTES <= BRING_BYTES, "batched rings fit the ring region");
+static_assert(NMAX_B * 2 * KSTEP <= WRING_BYTES, "a K step of the widest tile fits the weight ring");
+static_assert(2 * 64 * NMAX_B * 4 <= NAS * AS_BYTES, "K-slice staging (two planes or two token tiles) fits the activation ring");
+static_assert(2 * NMAX_B <= static_cast<int>(TMEM_COLS), "accumulators of two token tiles fit tensor memory");
+// mbarriers in sm.bbar (one expected arrival except BB_SREADY: one per CTA of the cluster)
 enum : int {
-  BB_WFULL = 0,                  // weight slot filled (producer expect_tx + TMA bytes)
-  BB_WEMPTY = BB_WFULL + NWS,    // weight slot consumed (tcgen05.commit)
-  BB_AFULL = BB_WEMPTY + NWS,    // activation slot filled
+  BB_WFULL = 0,                  // weight entry filled (producer expect_tx + TMA bytes)
+  BB_WEMPTY = BB_WFULL + NWE,    // weight entry consumed (tcgen05.commit)
+  BB_AFULL = BB_WEMPTY + NWE,    // activation slot filled
   BB_AEMPTY = BB_AFULL + NAS,    // activation slot consumed
   BB_ACCFULL = BB_AEMPTY + NAS,  // D complete (tcgen05.commit after the last K step)
-  BB_ACCEMPTY,                   // D read by the epilogue
+  BB_ACCEMPTY,                   // D read by the consumers
   BB_GO,                         // the stage's grid barrier passed: A planes are complete
   BB_DRAIN,                      // every MMA done (exit)
+  BB_SREADY,                     // every CTA of the cluster has staged its K-slice partial
   BB_N
 };
 static_assert(BB_N <= 32, "batched mbarriers");
@@ -84,79 +90,81 @@ __device__ __forceinline__ int bmap_head(const Params& p, int hidx) { return (p.
 __device__ __forceinline__ int bmap_abuf(const Params& p, int buf, bool box128) {
   return (p.n_bb + p.n_cp) * NLMAPS + 1 + NCPHEADS + 2 * buf + (box128 ? 1 : 0);
 }
-
-// Work of a CTA in a GEMM stage: a row tile of up to 8 blocks of 16 weight rows (gate/up: 4
-// blocks of 16 intermediate channels = 16 gate + 16 up rows each), N <= 128 columns of D, and a
-// K slice: the R row tiles times nk K slices cover the grid (CTA c < R * nk takes row tile c / nk
-// and K steps [ks0, ks1) of slice c % nk). The nk CTAs of a row tile write their slices' D to
-// global memory, wait for each other (counter) and then each sums the slices (slice order) for
-// its share of the tile's epilogue items.
-struct BSplit {
-  int b0, nb;        // first 16-row block, blocks (0: idle in this stage)
-  int rb, kspl, nk;  // row tile, K slice, K slices per row tile
-  int ks0, ks1;      // K steps of this CTA
-};
-__device__ __forceinline__ int bg_blocks(const Params& p, const BGemm& g) {
+// Output rows of a stage's weight matrix (gate/up: gate + up rows).
+__device__ __forceinline__ int bg_rows(const Params& p, const BGemm& g) {
   switch (g.kind) {
-    case BK_QKV: return QKV_ROWS / WBOX;
-    case BK_GU: return INTER / WBOX;
-    case BK_HEAD: return (g.hidx == 0 ? p.vocab : p.cp_vocab) / WBOX;
-    default: return HID / WBOX;
+    case BK_QKV: return QKV_ROWS;
+    case BK_GU: return 2 * INTER;
+    case BK_HEAD: return g.hidx == 0 ? p.vocab : p.cp_vocab;
+    default: return HID;
   }
 }
-__device__ __forceinline__ BSplit bg_split(const Params& p, const BGemm& g, int cta, int G) {
-  const int total = bg_blocks(p, g);
-  const int bpc = g.kind == BK_GU ? NMAX / (2 * WBOX) : NMAX / WBOX;
-  const int R = (total + bpc - 1) / bpc;
-  const int nks = bg_K(g.kind) / KSTEP;
-  int nk = G / R;
-  nk = nk < 1 ? 1 : (nk > nks ? nks : nk);
+
+// Work of a CTA in a GEMM stage: cluster rt (< R = 128 / bcl) takes row tile rt of N rows (gate/up:
+// N/2 gate and N/2 up rows of intermediate channels rt * N/2 ...), and its CTA of rank kspl takes K
+// steps [ks0, ks1) of slice kspl; clusters rt >= R have no work in GEMM stages.
+struct BSplit {
+  int rt, R, N, kspl, nk, ks0, ks1;
+  bool act;
+};
+__device__ __forceinline__ BSplit bg_split(const Params& p, const BGemm& g, int cta) {
   BSplit s;
-  s.nk = nk;
-  if (cta < R * nk) {
-    s.rb = cta / nk;
-    s.kspl = cta - s.rb * nk;
-    s.b0 = s.rb * bpc;
-    s.nb = min(bpc, total - s.b0);
-    s.ks0 = split_lo(nks, nk, s.kspl);
-    s.ks1 = split_lo(nks, nk, s.kspl + 1);
-  } else {
-    s.rb = s.kspl = s.b0 = s.nb = s.ks0 = s.ks1 = 0;
-  }
+  s.nk = p.bcl;
+  s.R = BROWS / p.bcl;
+  s.N = bg_rows(p, g) / s.R;
+  s.rt = cta / p.bcl;
+  s.kspl = cta - s.rt * p.bcl;
+  s.act = s.rt < s.R;
+  const int nks = bg_K(g.kind) / KSTEP;
+  s.ks0 = split_lo(nks, s.nk, s.kspl);
+  s.ks1 = split_lo(nks, s.nk, s.kspl + 1);
   return s;
 }
-__device__ __forceinline__ int bg_N(int kind, int nb) { return (kind == BK_GU ? 2 : 1) * WBOX * nb; }
 
-// Weight boxes of a CTA tile: one box of NMAX rows (gate/up: a box of NMAX / 2 gate rows and one
-// of NMAX / 2 up rows) per atom; every row tile of every stage is full (the host checks that the
-// head vocabularies are multiples of NMAX). Returns the tensor map and first row of box i.
+// Weight boxes of a CTA tile: one box of N rows per atom (gate/up: a box of N/2 gate rows and one
+// of N/2 up rows; the host encodes every tensor map with its stage's box height and checks that
+// the head vocabularies split into full tiles). Returns the tensor map and first row of box i.
 __device__ __forceinline__ int bg_nbox(int kind) { return kind == BK_GU ? 2 : 1; }
-__device__ __forceinline__ void bg_wbox(const Params& p, const BGemm& g, int b0, int i, const uint8_t*& map, int& y) {
+__device__ __forceinline__ void bg_wbox(const Params& p, const BGemm& g, const BSplit& sp, int i, const uint8_t*& map,
+                                        int& y) {
   const int base = g.li * NLMAPS;
-  const int r = WBOX * b0;
   switch (g.kind) {
-    case BK_QKV: {   // a 128-row tile lies inside one of q (2048 rows), k, v (1024 rows each)
+    case BK_QKV: {   // a tile lies inside one of q (2048 rows), k, v (1024 rows each)
+      const int r = sp.rt * sp.N;
       const int m = r < QSZ ? 0 : (r < QSZ + KVSZ ? 1 : 2);
       y = r - (m == 0 ? 0 : (m == 1 ? QSZ : QSZ + KVSZ));
       map = bmap(p, base + m);
       break;
     }
-    case BK_O: map = bmap(p, base + 3); y = r; break;
-    case BK_GU: map = bmap(p, base + 4 + i); y = r; break;   // intermediate channels r .. r + 63
-    case BK_D: map = bmap(p, base + 6); y = r; break;
-    default: map = bmap(p, bmap_head(p, g.hidx)); y = r; break;
+    case BK_O: map = bmap(p, base + 3); y = sp.rt * sp.N; break;
+    case BK_GU: map = bmap(p, base + 4 + i); y = sp.rt * (sp.N / 2); break;   // channels of the tile
+    case BK_D: map = bmap(p, base + 6); y = sp.rt * sp.N; break;
+    default: map = bmap(p, bmap_head(p, g.hidx)); y = sp.rt * sp.N; break;
   }
 }
 
-// Profiling trace (dbg_marks set): marks[(gemm * G + cta) * BT_EVENTS + event] = %globaltimer
-// for GEMM stages gemm < dbg_marks_len / (G * BT_EVENTS) of the launch, every CTA.
+// Weight ring: entries (one K step of the CTA's tile, N * 256 bytes = N / 16 slots) are allocated
+// in order and never wrap (an entry that does not fit before the end starts at slot 0); the
+// producer and the MMA thread walk the same sequence of entry sizes, so both compute the same slot.
+struct WRing {
+  uint32_t head;
+  __device__ __forceinline__ uint32_t alloc(uint32_t n) {
+    if (head + n > static_cast<uint32_t>(NWSLOT)) head = 0;
+    const uint32_t f = head;
+    head += n;
+    return f;
+  }
+};
+
+// Profiling trace (dbg_marks set): marks[(gemm * BKCTAS + cta) * BT_EVENTS + event] = %globaltimer
+// for GEMM stages gemm < dbg_marks_len / (BKCTAS * BT_EVENTS) of the launch, every CTA.
 enum BTrace : int {
   BT_START = 0,     // consumers: stage start (GO)
   BT_DREADY,        // consumers: D complete
   BT_STAGED,        // consumers: D staged in shared memory, accumulator freed
-  BT_PART,          // consumers: K-slice partial stored and fenced
-  BT_COUNT,         // consumers: every slice of the row tile stored
-  BT_REDUCED,       // consumers: slices summed
+  BT_PART,          // consumers: cluster signalled
+  BT_COUNT,         // consumers: every K slice of the cluster staged
+  BT_REDUCED,       // consumers: slices summed, epilogue done
   BT_EPI,           // consumers: epilogue done (barrier arrival)
   BT_BARRIER,       // consumers: barrier passed
   BT_W0,            // MMA: first weight step ready
@@ -170,11 +178,17 @@ enum BTrace : int {
   BT_ALAST,         // activation loader: last step's slot free (loads issued next)
   BT_S0,            // MMA: first step's MMAs and commits issued
   BT_W1,            // MMA: second step's weights ready
+  BT_LO_SEEN,       // consumer warp 2: D complete seen
+  BT_LO_DONE,       // consumer warp 2: lo lanes staged
+  BT_PH0,           // consumers: lo lanes of every warp staged
+  BT_HI_DONE,       // consumer warp 0: hi lanes added
+  BT_PH1,           // consumers: hi lanes of every warp added
   BT_EVENTS = 24
 };
 __device__ __forceinline__ void btrace(const Params& p, int gemm, int cta, int G, int ev) {
   if (p.dbg_marks == nullptr) return;
-  const long long i = (static_cast<long long>(gemm) * G + cta) * BT_EVENTS + ev;
+  (void)G;
+  const long long i = (static_cast<long long>(gemm) * BKCTAS + cta) * BT_EVENTS + ev;
   if (i < p.dbg_marks_len) p.dbg_marks[i] = globaltimer_ns();
 }
 
@@ -214,61 +228,83 @@ __device__ void b_walk(const Params& p, F&& f) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Producer warp (one thread): weight boxes of every GEMM stage into the 4-slot ring, one slot
-// per 128-byte swizzle atom (64 K columns of the CTA's N rows), two slots per K step.
+// Producer warp (one thread): weight boxes of every GEMM stage into the weight ring, one entry
+// (N rows x two 64-column atoms) per K step.
 // ------------------------------------------------------------------------------------------
-__device__ void b_producer(const Params& p, Smem& sm, int cta, int G) {
+__device__ __noinline__ void b_producer(const Params& p, Smem& sm, int cta, int G) {
   uint8_t* wring = reinterpret_cast<uint8_t*>(sm.ring);
-  uint32_t m = 0;
+  WRing ring{0u};
+  uint32_t e = 0;                 // entries issued
+  uint8_t efirst[NWE], en[NWE];   // slot range of the entries in flight
   int* err = p.w.err;
+  auto give_up = [&]() {
+    if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+  };
   b_walk(p, [&](int gi, const BGemm& g) -> bool {
-    const BSplit sp = bg_split(p, g, cta, G);
-    if (sp.nb == 0) return true;
-    const int N = bg_N(g.kind, sp.nb), nbox = bg_nbox(g.kind), brows = N / nbox;
+    const BSplit sp = bg_split(p, g, cta);
+    if (!sp.act) return true;
+    const int nbox = bg_nbox(g.kind), brows = sp.N / nbox;
+    const uint32_t n = static_cast<uint32_t>(sp.N) / 16u;
     bool first = true;
-    for (int ks = sp.ks0; ks < sp.ks1; ++ks)
-      for (int a = 0; a < NSUB; ++a, ++m) {
-        const uint32_t slot = m % NWS, round = m / NWS;
-        if (!mbar_wait(&sm.bbar[BB_WEMPTY + slot], (round & 1u) ^ 1u, &sm.abort)) {
-          if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_EMPTY_TIMEOUT);
+    for (int ks = sp.ks0; ks < sp.ks1; ++ks, ++e) {
+      const uint32_t ei = e % NWE;
+      // entry e - NWE (same mbarriers) consumed
+      if (!mbar_wait(&sm.bbar[BB_WEMPTY + ei], ((e / NWE) & 1u) ^ 1u, &sm.abort)) {
+        give_up();
+        return false;
+      }
+      const uint32_t f = ring.alloc(n);
+      // the entries still in flight whose slots overlap [f, f + n)
+      for (uint32_t k = (e >= NWE ? e - NWE + 1 : 0u); k < e; ++k) {
+        const uint32_t ki = k % NWE;
+        if (efirst[ki] < f + n && f < static_cast<uint32_t>(efirst[ki]) + en[ki] &&
+            !mbar_wait(&sm.bbar[BB_WEMPTY + ki], (k / NWE) & 1u, &sm.abort)) {
+          give_up();
           return false;
         }
-        mbar_arrive_expect_tx(&sm.bbar[BB_WFULL + slot], static_cast<uint32_t>(N * 128));
+      }
+      efirst[ei] = static_cast<uint8_t>(f);
+      en[ei] = static_cast<uint8_t>(n);
+      uint8_t* dst = wring + f * WSLOT;
+      mbar_arrive_expect_tx(&sm.bbar[BB_WFULL + ei], static_cast<uint32_t>(sp.N * 2 * 128));
+      for (int a = 0; a < NSUB; ++a)
         for (int i = 0; i < nbox; ++i) {
           const uint8_t* map;
           int y;
-          bg_wbox(p, g, sp.b0, i, map, y);
+          bg_wbox(p, g, sp, i, map, y);
           if (first) tensormap_acquire(map);   // the host's copy of the map, before its first use
-          tma_load_2d(wring + slot * WS_BYTES + i * (brows * 128), map, ks * KSTEP + a * KSUB, y,
-                      &sm.bbar[BB_WFULL + slot]);
+          tma_load_2d(dst + a * (sp.N * 128) + i * (brows * 128), map, ks * KSTEP + a * KSUB, y,
+                      &sm.bbar[BB_WFULL + ei]);
         }
-        if (first) btrace(p, gi, cta, G, BT_P0);
-        first = false;
-      }
+      if (first) btrace(p, gi, cta, G, BT_P0);
+      first = false;
+    }
     btrace(p, gi, cta, G, BT_P_END);
     return true;
   });
   // drain: no box may still be landing in shared memory when the CTA exits
   int zero = 0;
-  for (uint32_t i = (m > NWS ? m - NWS : 0u); i < m; ++i)
-    mbar_wait(&sm.bbar[BB_WFULL + i % NWS], (i / NWS) & 1u, &zero);
+  for (uint32_t i = (e > NWE ? e - NWE : 0u); i < e; ++i)
+    mbar_wait(&sm.bbar[BB_WFULL + i % NWE], (i / NWE) & 1u, &zero);
 }
 
 // ------------------------------------------------------------------------------------------
 // Activation-loader warp (one thread): after each GEMM stage's grid barrier, the A planes of
-// every (K step, 64-token tile) into the 6-slot ring.
+// every (K step, 64-token tile) into the 3-slot ring.
 // ------------------------------------------------------------------------------------------
-__device__ void b_aloader(const Params& p, Smem& sm, int cta, int G) {
-  uint8_t* aring = reinterpret_cast<uint8_t*>(sm.ring) + NWS * WS_BYTES;
+__device__ __noinline__ void b_aloader(const Params& p, Smem& sm, int cta, int G) {
+  uint8_t* aring = reinterpret_cast<uint8_t*>(sm.ring) + WRING_BYTES;
   uint32_t na = 0, n = 0;
   int* err = p.w.err;
   for (int b = 0; b < 2; ++b) tensormap_acquire(bmap(p, bmap_abuf(p, b, false)));
   b_walk(p, [&](int gi, const BGemm& g) -> bool {
-    const BSplit sp = bg_split(p, g, cta, G);
-    if (sp.nb == 0) return true;
+    const BSplit sp = bg_split(p, g, cta);
+    if (!sp.act) return true;
     const int ntiles = (g.T + 63) >> 6;
     const uint8_t* amap = bmap(p, bmap_abuf(p, bg_abuf(g.kind), false));
-    // the consumers arrive on GO after the stage's grid barrier: the A planes are complete
+    // the consumers arrive on GO after the stage's grid barrier: the A planes are complete, and
+    // every CTA of the cluster has read this CTA's staged partials of the previous stage (which
+    // share the ring's space)
     if (!mbar_wait(&sm.bbar[BB_GO], n & 1u, &sm.abort)) {
       if (!*reinterpret_cast<volatile int*>(&sm.abort)) set_error(err, DEV_ERR_FULL_TIMEOUT);
       return false;
@@ -302,10 +338,11 @@ __device__ void b_aloader(const Params& p, Smem& sm, int cta, int G) {
 // ------------------------------------------------------------------------------------------
 // MMA warp (one thread): tcgen05.mma of every GEMM stage.
 // ------------------------------------------------------------------------------------------
-__device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
-  const uint32_t wbase = smem_u32(sm.ring), abase = wbase + NWS * WS_BYTES;
+__device__ __noinline__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
+  const uint32_t wbase = smem_u32(sm.ring), abase = wbase + WRING_BYTES;
   const uint32_t tmem = sm.tmem_base;
-  uint32_t m = 0, ua = 0, n = 0;
+  WRing ring{0u};
+  uint32_t e = 0, ua = 0, n = 0;
   bool any = false;
   int* err = p.w.err;
   auto fail_mma = [&](int code) {
@@ -315,27 +352,28 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
     }
   };
   b_walk(p, [&](int gi, const BGemm& g) -> bool {
-    const BSplit sp = bg_split(p, g, cta, G);
-    if (sp.nb == 0) return true;
-    const int N = bg_N(g.kind, sp.nb), nks = sp.ks1 - sp.ks0, ntiles = (g.T + 63) >> 6;
+    const BSplit sp = bg_split(p, g, cta);
+    if (!sp.act) return true;
+    const int N = sp.N, nks = sp.ks1 - sp.ks0, ntiles = (g.T + 63) >> 6;
     const uint32_t idesc = umma_idesc_bf16(128, N);
-    // the previous stage's epilogue has read D
+    const uint32_t nslots = static_cast<uint32_t>(N) / 16u;
+    // the previous stage's consumers have read D
     if (!mbar_wait(&sm.bbar[BB_ACCEMPTY], (n & 1u) ^ 1u, &sm.abort)) {
       fail_mma(DEV_ERR_FULL_TIMEOUT);
       return false;
     }
     tc_fence_after();
-    for (int ks = 0; ks < nks; ++ks) {   // ks: index within this CTA's K slice
-      const uint32_t ws0 = m % NWS, ws1 = (m + 1) % NWS;
-      if (!mbar_wait(&sm.bbar[BB_WFULL + ws0], (m / NWS) & 1u, &sm.abort) ||
-          !mbar_wait(&sm.bbar[BB_WFULL + ws1], ((m + 1) / NWS) & 1u, &sm.abort)) {
+    for (int ks = 0; ks < nks; ++ks, ++e) {   // ks: index within this CTA's K slice
+      const uint32_t ei = e % NWE;
+      const uint32_t ws = wbase + ring.alloc(nslots) * WSLOT;
+      if (!mbar_wait(&sm.bbar[BB_WFULL + ei], (e / NWE) & 1u, &sm.abort)) {
         fail_mma(DEV_ERR_FULL_TIMEOUT);
         return false;
       }
       if (ks == 0) btrace(p, gi, cta, G, BT_W0);
       if (ks == 1) btrace(p, gi, cta, G, BT_W1);
       // descriptors built once per step; a K offset adds (bytes >> 4) to the start-address field
-      const uint64_t db0 = umma_desc_sw128(wbase + ws0 * WS_BYTES), db1 = umma_desc_sw128(wbase + ws1 * WS_BYTES);
+      const uint64_t db0 = umma_desc_sw128(ws), db1 = umma_desc_sw128(ws + static_cast<uint32_t>(N) * 128u);
       for (int j = 0; j < ntiles; ++j, ++ua) {
         const uint32_t as = ua % NAS, ar = ua / NAS;
         if (!mbar_wait(&sm.bbar[BB_AFULL + as], ar & 1u, &sm.abort)) {
@@ -345,12 +383,10 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
         if (ks == 0 && j == 0) btrace(p, gi, cta, G, BT_A0);
         if (ks == nks - 1 && j == ntiles - 1) btrace(p, gi, cta, G, BT_LAST);
         tc_fence_after();
-        // hi and lo planes along K: an M = 128 MMA whose A starts at the hi rows, then one whose A
-        // starts at the lo rows (8 KB further), both with the same W; TMEM lanes 0..63 collect
-        // hi.W + lo.W of the tile's 64 tokens, lanes 64..127 are not used (the A rows behind the
-        // lo plane stay inside the ring region)
+        // one M = 128 MMA per K sub-step over the whole slot: hi rows 0..63 -> TMEM lanes 0..63,
+        // lo rows 64..127 -> lanes 64..127, the same weights for both
         const uint64_t da = umma_desc_sw128(abase + as * AS_BYTES);
-        const uint32_t dt = tmem + j * DCOLS;
+        const uint32_t dt = tmem + static_cast<uint32_t>(j * N);
 #pragma unroll
         for (int a = 0; a < NSUB; ++a)
 #pragma unroll
@@ -358,15 +394,12 @@ __device__ void b_mma(const Params& p, Smem& sm, int cta, int G) {
             const uint64_t dw = (a == 0 ? db0 : db1) + static_cast<uint64_t>((kk * 32) >> 4);
             tc_mma_bf16(dt, da + static_cast<uint64_t>((a * ASUB_BYTES + kk * 32) >> 4), dw, idesc,
                         (ks | a | kk) != 0 ? 1u : 0u);
-            tc_mma_bf16(dt, da + static_cast<uint64_t>((a * ASUB_BYTES + APLANE_BYTES + kk * 32) >> 4), dw, idesc, 1u);
           }
         any = true;
         tc_commit(&sm.bbar[BB_AEMPTY + as]);
       }
-      tc_commit(&sm.bbar[BB_WEMPTY + ws0]);
-      tc_commit(&sm.bbar[BB_WEMPTY + ws1]);
+      tc_commit(&sm.bbar[BB_WEMPTY + ei]);
       if (ks == 0) btrace(p, gi, cta, G, BT_S0);
-      m += 2;
     }
     btrace(p, gi, cta, G, BT_MMA_END);
     tc_commit(&sm.bbar[BB_ACCFULL]);
@@ -399,232 +432,238 @@ __device__ __forceinline__ float b_rstd(const unsigned long long* ssq, int t, fl
   return rms_scale(s, HID, eps);
 }
 
-// Columns [c, c + 16) of D for token t: hi lanes (chains added) + the lo lanes staged in smem.
-// hilo_store of 16 consecutive columns (col0 a multiple of 16): 32-byte stores per plane.
-__device__ __forceinline__ void hilo_store16(bf16* buf, int t, int col0, const float (&v)[16]) {
-  uint32_t hi[8], lo[8];
+// Epilogue items cover EW consecutive output columns of one token.
+constexpr int EW = 8;
+
+// hilo_store of EW consecutive columns (col0 a multiple of EW): one 16-byte store per plane.
+__device__ __forceinline__ void hilo_store_w(bf16* buf, int t, int col0, const float (&v)[EW]) {
+  uint32_t hi[4], lo[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     const bf16 h0 = __float2bfloat16_rn(v[2 * i]), h1 = __float2bfloat16_rn(v[2 * i + 1]);
     const bf16 l0 = __float2bfloat16_rn(v[2 * i] - __bfloat162float(h0));
     const bf16 l1 = __float2bfloat16_rn(v[2 * i + 1] - __bfloat162float(h1));
     hi[i] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
     lo[i] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
   }
-  uint4* ph = reinterpret_cast<uint4*>(buf + static_cast<size_t>(t) * ABUF_LD + col0);
-  uint4* pl = reinterpret_cast<uint4*>(buf + static_cast<size_t>(TBMAX + t) * ABUF_LD + col0);
-  ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-  ph[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-  pl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-  pl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+  *reinterpret_cast<uint4*>(buf + static_cast<size_t>(t) * ABUF_LD + col0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(buf + static_cast<size_t>(TBMAX + t) * ABUF_LD + col0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
-// 16 consecutive fp32 from global (L2) / bf16 weights as fp32.
-__device__ __forceinline__ void ld16_f32(const float* src, float (&v)[16]) {
+// EW consecutive fp32 from global (L2) / bf16 weights as fp32.
+__device__ __forceinline__ void ldw_f32(const float* src, float (&v)[EW]) {
 #pragma unroll
-  for (int i = 0; i < 16; i += 4) {
+  for (int i = 0; i < EW; i += 4) {
     const float4 a = __ldcg(reinterpret_cast<const float4*>(src + i));
     v[i] = a.x; v[i + 1] = a.y; v[i + 2] = a.z; v[i + 3] = a.w;
   }
 }
-__device__ __forceinline__ void ld16_bf16(const bf16* src, float (&v)[16]) {
-  const uint4 a = reinterpret_cast<const uint4*>(src)[0], b = reinterpret_cast<const uint4*>(src)[1];
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+__device__ __forceinline__ void ldw_bf16(const bf16* src, float (&v)[EW]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(src);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     v[2 * i] = bf16_lo(w[i]);
     v[2 * i + 1] = bf16_hi(w[i]);
   }
 }
-__device__ __forceinline__ void st16_f32(float* dst, const float (&v)[16]) {
+__device__ __forceinline__ void stw_f32(float* dst, const float (&v)[EW]) {
 #pragma unroll
-  for (int i = 0; i < 16; i += 4) __stcg(reinterpret_cast<float4*>(dst + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+  for (int i = 0; i < EW; i += 4) __stcg(reinterpret_cast<float4*>(dst + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
 }
 
-// Inputs of one epilogue item that do not depend on D, loaded before D is ready.
+// Inputs of one epilogue item that do not depend on D.
 struct EpiSt {
-  float a[16], b[16];
+  float a[EW], b[EW];
   float rs;
 };
-
-// Bounded wait until *cnt >= target (thread 0 of the CTA), as in grid_sync.
-__device__ bool b_wait_count(const Params& p, Smem& sm, const uint32_t* cnt, uint32_t target) {
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (ld_acquire_gpu(cnt) >= target) return true;
-    if ((it & 31u) == 31u) {
-      if (ld_volatile_i32(p.w.err) != 0 || aborted(sm)) return false;
-      if (globaltimer_ns() - t0 > QTT_WAIT_NS) {
-        set_error(p.w.err, DEV_ERR_GRID_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
 
 // Consumer side of one GEMM stage. Epilogue items are (token t, 16 output columns c); the
 // callbacks are pre(t, r0, st) (the item's inputs that do not depend on D) and
 // run(t, r0, y, y2, st) with y = D[t][16 columns] (gate/up: y = gate, y2 = up) and r0 the first
 // output column (row of W; gate/up: intermediate channel).
 //   1. release the activation loader (GO);
-//   2. wait for D; the warps of TMEM lane quarters 0 and 1 copy its rows (tokens) to the K slice's
-//      partial in global memory (a single slice: to shared memory); D is freed;
-//   3. K split: count, wait for the row tile's other slices, and sum the nk slices (slice order)
-//      for this CTA's share of the items;
-//   4. the epilogue of this CTA's items (all of them without a K split); the grid barrier.
-// Steps 1-3 and the barrier are shared code (b_gemm_begin / b_gemm_mid / b_gemm_end): the stage
+//   2. wait for D; the consumer warps copy its lo lanes and then add its hi lanes into the K-slice
+//      partial in shared memory; D is freed; every CTA of the cluster is told (mbarrier);
+//   3. once the cluster's partials are staged, each item sums them in rank order (distributed
+//      shared memory), then its epilogue; the grid barrier.
+// Steps 1-2 and the barrier are shared code (b_gemm_begin / b_gemm_mid / b_gemm_end): the stage
 // kinds differ only in the item callbacks, so the kernel keeps one copy of the pipeline.
 struct BStage {
   BSplit sp;
-  int gi, N, NO, nci, i0, i1, r0b, T;
+  int gi, N, NO, nci, i0, i1, r0b, T, smask;
+  int np;            // staged planes: 2 (hi and lo apart, one token tile) or 1 (lo + hi, two tiles)
   bool gu;
-  float* Y;   // staged D, [T][N + 1] in the (idle) activation ring
+  uint32_t s_addr;   // shared address of the K-slice partial [tile][64][N] fp32 (swizzled chunks)
 };
 
-__device__ __noinline__ bool b_gemm_begin(const Params& p, Smem& sm, Cons& cs, const BGemm& g, BStage& S) {
-  S.sp = bg_split(p, g, cs.cta, cs.G);
+// Partial staging layout: row (tile or plane j, token t) of N floats; 16-byte chunk k of the row is
+// stored at chunk k ^ (t & smask), so that the lanes of a warp (one token each) hit different
+// banks. With one token tile the hi and lo products are staged as rows j = 0 and 1 (np = 2); with
+// two tiles, lo + hi of tile j in row j (np = 1).
+__device__ __forceinline__ uint32_t b_part_off(const BStage& S, int j, int t, int k) {
+  return static_cast<uint32_t>(((j * 64 + t) * S.N + 4 * (k ^ (t & S.smask))) * 4);
+}
+
+// Step 1: the stage's tiling (returned by value, so that it stays in registers) and the GO arrival.
+__device__ __forceinline__ BStage b_gemm_begin(const Params& p, Smem& sm, Cons& cs, const BGemm& g) {
+  BStage S;
+  S.sp = bg_split(p, g, cs.cta());
   S.gi = cs.gi;
-  // the other counter bank was last used by the previous GEMM stage, whose barrier has passed
-  const uint32_t bank = static_cast<uint32_t>(cs.gi & 1) * BKBANK;
-  if (cs.cta == 0 && cs.tid < BKBANK) __stcg(p.bw.kcnt + (bank ^ BKBANK) + cs.tid, 0u);
   cs.gi++;
-  if (S.sp.nb == 0) return false;
   S.T = g.T;
-  S.N = bg_N(g.kind, S.sp.nb);
+  S.N = S.sp.N;
   S.gu = g.kind == BK_GU;
   S.NO = S.gu ? S.N / 2 : S.N;
-  S.nci = S.NO / 16;
+  S.nci = S.NO / EW;
   const int items = g.T * S.nci;
   S.i0 = split_lo(items, S.sp.nk, S.sp.kspl);
   S.i1 = split_lo(items, S.sp.nk, S.sp.kspl + 1);
-  S.r0b = WBOX * S.sp.b0;
-  S.Y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sm.ring) + NWS * WS_BYTES);
-  if (p.dbg_marks != nullptr && cs.tid == 0) btrace(p, S.gi, cs.cta, cs.G, BT_START);
-  if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_GO]);
-  return true;
+  S.r0b = S.sp.rt * S.NO;
+  S.smask = (S.N / 4) % 8 == 0 ? 7 : 3;
+  S.np = g.T <= 64 ? 2 : 1;
+  S.s_addr = smem_u32(sm.ring) + WRING_BYTES;
+  if (S.sp.act) {
+    if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_START);
+    if (cs.tid() == 0) mbar_arrive(&sm.bbar[BB_GO]);
+  }
+  return S;
 }
 
-// Steps 2-3; false on abort.
-__device__ __noinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, const BStage& S, uint32_t gemm_n) {
-  const bool tr = p.dbg_marks != nullptr && cs.tid == 0;
-  const BSplit& sp = S.sp;
-  float* Y = S.Y;
-  const int N = S.N, YST = N + 1;
+// Step 2 up to the cluster's partials being staged; false on abort.
+__device__ __noinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, const BStage S, uint32_t gemm_n) {
+  const bool tr = p.dbg_marks != nullptr && cs.tid() == 0;
   if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
     if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
     return false;
   }
-  if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_DREADY);
+  const bool tr2 = p.dbg_marks != nullptr && cs.tid() == 64;   // warp 2 (lo lanes), lane 0
+  if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_DREADY);
+  if (tr2) btrace(p, S.gi, cs.cta(), cs.G(), BT_LO_SEEN);
   tc_fence_after();
-  // D rows (TMEM lanes 0..63 of each 64-token tile, read by the warps of lane quarters 0 and 1)
-  // -> this K slice's partial in global memory, or Y when the stage has a single slice (the
-  // activation ring is idle until the next stage's GO)
-  const int ntiles = (S.T + 63) >> 6, nch = N / 16;
-  const int q = cs.warp & 3, wq = cs.warp >> 2;
-  float* part = p.bw.kpart + static_cast<size_t>(cs.cta) * TBMAX * KPAD;
-  if (q < 2) {
-    for (int job = wq; job < ntiles * nch; job += NCW / 4) {
-      const int j = job / nch, c = job - j * nch;
-      if (64 * j + 32 * q < S.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
-        float v[16];
-        tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + j * DCOLS + 16 * c, v);
-        const int t = 64 * j + 32 * q + cs.lane;
-        if (sp.nk > 1) {
-          // through a per-warp tile in shared memory, so that each store instruction writes 8
-          // whole 64-byte row pieces (4 lanes per token) instead of 32 scattered 16-byte ones
-          float* tile = reinterpret_cast<float*>(sm.att) + (wq * 2 + q) * 32 * BT_STRIDE;
-          float4* mine = reinterpret_cast<float4*>(tile + cs.lane * BT_STRIDE);
+  // D -> partial: TMEM lane quarter q of warp w (w % 4) holds tokens 32 (q & 1) .. of the hi
+  // (q < 2) or lo (q >= 2) products. One token tile: every quarter stores its plane in one pass;
+  // two tiles: lo first, then hi added (the same order for every element).
+  const int ntiles = (S.T + 63) >> 6, nch = S.N / 16;
+  const int q = cs.warp() & 3, wq = cs.warp() >> 2;
+  uint8_t* sbase = reinterpret_cast<uint8_t*>(sm.ring) + WRING_BYTES;
+  const int nphase = S.np == 2 ? 1 : 2;
+  for (int phase = 0; phase < nphase; ++phase) {
+    if (S.np == 2 || (q >= 2) == (phase == 0)) {
+      for (int job = wq; job < ntiles * nch; job += NCW / 4) {
+        const int j = job / nch, c = job - j * nch;
+        if (64 * j + 32 * (q & 1) < S.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
+          float v[16];
+          tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(j * S.N + 16 * c), v);
+          const int t = 32 * (q & 1) + cs.lane();
+          const int row = S.np == 2 ? (q >> 1) : j;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) mine[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int r = 8 * k + (cs.lane >> 2), tt = 64 * j + 32 * q + r;
-            const float4 x = reinterpret_cast<const float4*>(tile + r * BT_STRIDE)[cs.lane & 3];
-            if (tt < S.T) __stcg(reinterpret_cast<float4*>(part + tt * KPAD + 16 * c) + (cs.lane & 3), x);
+          for (int i = 0; i < 4; ++i) {
+            float4* d = reinterpret_cast<float4*>(sbase + b_part_off(S, row, t, 4 * c + i));
+            if (phase == 1) {
+              const float4 lo = *d;
+              *d = make_float4(lo.x + v[4 * i], lo.y + v[4 * i + 1], lo.z + v[4 * i + 2], lo.w + v[4 * i + 3]);
+            } else {
+              *d = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
           }
-          __syncwarp();   // the tile is rewritten by the warp's next job
-        } else if (t < S.T) {
-          float* yr = Y + t * YST + 16 * c;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) yr[i] = v[i];
         }
       }
     }
+    if (tr2 && phase == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_LO_DONE);
+    if (tr && phase == 1) btrace(p, S.gi, cs.cta(), cs.G(), BT_HI_DONE);
+    if (phase + 1 < nphase) named_sync(1, NCT);
+    if (tr && phase == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_PH0);
   }
   tc_fence_before();
-  // bar.sync orders the CTA's partial stores before thread 0, whose release add publishes them at
-  // gpu scope (the pattern of grid_sync)
+  // the CTA barrier orders every thread's partial stores before thread 0, whose release arrivals
+  // (cluster scope, cumulative) publish them to the cluster's readers
   named_sync(1, NCT);
-  if (cs.tid == 0) mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
-  if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_STAGED);
-  if (sp.nk == 1) return true;
-  // K split
-  uint32_t* cnt = p.bw.kcnt + static_cast<uint32_t>(S.gi & 1) * BKBANK + sp.rb;
-  if (cs.tid == 0) {
-    if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_PART);
-    red_release_gpu_add(cnt, 1u);
-    sm.bcast[0] = b_wait_count(p, sm, cnt, static_cast<uint32_t>(sp.nk)) ? 1 : 0;
-    if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_COUNT);
+  if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PH1);
+  if (cs.tid() == 0) {
+    mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
+    if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_STAGED);
+    const uint32_t bar = smem_u32(&sm.bbar[BB_SREADY]);
+    for (int r = 0; r < S.sp.nk; ++r) mbar_arrive_cluster(mapa_shared(bar, static_cast<uint32_t>(r)));
+    if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PART);
   }
-  named_sync(1, NCT);
-  if (!sm.bcast[0]) {
-    *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+  // every CTA of the cluster has staged its partial of this stage
+  if (!mbar_wait_cluster(&sm.bbar[BB_SREADY], gemm_n & 1u, &sm.abort)) {
+    if (!aborted(sm)) fail(p, sm, DEV_ERR_GRID_TIMEOUT);
     return false;
   }
-  const int ppi = S.gu ? 8 : 4;   // float4 pieces per item
-  const float* base = p.bw.kpart + static_cast<size_t>(sp.rb * sp.nk) * TBMAX * KPAD;
-  for (int e = cs.tid; e < (S.i1 - S.i0) * ppi; e += NCT) {
-    const int it = S.i0 + e / ppi, pc = e % ppi;
-    const int t = it / S.nci, c = it - t * S.nci;
-    const int col = (pc < 4 ? 16 * c : S.NO + 16 * c) + 4 * (pc & 3);
-    const float* src = base + static_cast<size_t>(t) * KPAD + col;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k0 = 0; k0 < sp.nk; k0 += 8) {   // eight slices' loads in flight, added in slice order
-      float4 v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (k0 + k < sp.nk) v[k] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(k0 + k) * TBMAX * KPAD));
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (k0 + k < sp.nk) {
-          acc.x += v[k].x; acc.y += v[k].y; acc.z += v[k].z; acc.w += v[k].w;
-        }
-    }
-    float* yr = Y + t * YST + col;
-    yr[0] = acc.x; yr[1] = acc.y; yr[2] = acc.z; yr[3] = acc.w;
-  }
-  named_sync(1, NCT);
-  if (tr) btrace(p, S.gi, cs.cta, cs.G, BT_REDUCED);
+  if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_COUNT);
   return true;
 }
 
+// Partial of CTA rank `base` (a cluster address) for chunks k0, k0 + 1 of token tt: lo + hi
+// (np = 2) or the staged sum of token tile j (np = 1).
+__device__ __forceinline__ void b_part2(const BStage& S, uint32_t base, int j, int tt, int k0, float4 (&a)[2]) {
+  if (S.np == 2) {
+    const float4 l0 = ld_dsmem_f4(base + b_part_off(S, 1, tt, k0)), l1 = ld_dsmem_f4(base + b_part_off(S, 1, tt, k0 + 1));
+    const float4 h0 = ld_dsmem_f4(base + b_part_off(S, 0, tt, k0)), h1 = ld_dsmem_f4(base + b_part_off(S, 0, tt, k0 + 1));
+    a[0] = make_float4(l0.x + h0.x, l0.y + h0.y, l0.z + h0.z, l0.w + h0.w);
+    a[1] = make_float4(l1.x + h1.x, l1.y + h1.y, l1.z + h1.z, l1.w + h1.w);
+  } else {
+    a[0] = ld_dsmem_f4(base + b_part_off(S, j, tt, k0));
+    a[1] = ld_dsmem_f4(base + b_part_off(S, j, tt, k0 + 1));
+  }
+}
+__device__ __forceinline__ void b_acc8(float (&y)[EW], const float4 (&a)[2]) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    y[4 * i] += a[i].x; y[4 * i + 1] += a[i].y; y[4 * i + 2] += a[i].z; y[4 * i + 3] += a[i].w;
+  }
+}
+
+// Sum of the cluster's K-slice partials of item (t, EW columns from chunk 2c) in rank order
+// (y; gate/up: y2 = the matching up columns), read through distributed shared memory. Each rank's
+// partial is lo + hi, formed here (np = 2) or in the staging (np = 1) with the same fp32 add, so
+// the result does not depend on the token count.
+__device__ __forceinline__ void b_reduce_item(const BStage& S, int t, int c, float (&y)[EW], float (&y2)[EW]) {
+  const int tt = t & 63, j = t >> 6;
+#pragma unroll
+  for (int i = 0; i < EW; ++i) {
+    y[i] = 0.f;
+    y2[i] = 0.f;
+  }
+  for (int r = 0; r < S.sp.nk; ++r) {
+    const uint32_t base = mapa_shared(S.s_addr, static_cast<uint32_t>(r));
+    float4 a[2];
+    b_part2(S, base, j, tt, 2 * c, a);
+    b_acc8(y, a);
+    if (S.gu) {
+      b_part2(S, base, j, tt, S.NO / 4 + 2 * c, a);
+      b_acc8(y2, a);
+    }
+  }
+}
+
 __device__ __noinline__ bool b_gemm_end(const Params& p, Smem& sm, Cons& cs, int gi, bool planes) {
-  fence_proxy_async_smem();   // Y aliases the activation ring: before the next stage's TMA writes
+  fence_proxy_async_smem();   // the partials alias the activation ring: before the next stage's TMA writes
   if (planes) fence_proxy_async_global();   // the epilogue wrote the next GEMM's operand planes
-  if (p.dbg_marks != nullptr && cs.tid == 0) btrace(p, gi, cs.cta, cs.G, BT_EPI);
+  if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, gi, cs.cta(), cs.G(), BT_EPI);
   const bool ok = grid_sync(p, sm, cs);
-  if (p.dbg_marks != nullptr && cs.tid == 0) btrace(p, gi, cs.cta, cs.G, BT_BARRIER);
+  if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, gi, cs.cta(), cs.G(), BT_BARRIER);
   return ok;
 }
 
 template <class PRE, class RUN>
 __device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, PRE&& pre,
                                        RUN&& run) {
-  BStage S;
-  if (!b_gemm_begin(p, sm, cs, g, S)) return grid_sync(p, sm, cs);
-  // The items' inputs that do not depend on D are loaded after b_gemm_mid returns: held across
-  // the call they made the epilogues spill, which cost more than their load latency.
-  EpiSt st;
+  const BStage S = b_gemm_begin(p, sm, cs, g);
+  if (!S.sp.act) return grid_sync(p, sm, cs);
   const bool ok = b_gemm_mid(p, sm, cs, S, gemm_n);
   if (ok) {
-    const int YST = S.N + 1;
-    for (int i = S.i0 + cs.tid; i < S.i1; i += NCT) {
-      const int t = i / S.nci, c = i - t * S.nci, r0 = S.r0b + 16 * c;
+    for (int i = S.i0 + cs.tid(); i < S.i1; i += NCT) {
+      const int t = i / S.nci, c = i - t * S.nci, r0 = S.r0b + EW * c;
+      float y[EW], y2[EW];
+      b_reduce_item(S, t, c, y, y2);
+      EpiSt st;
       pre(t, r0, st);
-      const float* yr = S.Y + t * YST + 16 * c;
-      run(t, r0, yr, S.gu ? yr + S.NO : yr, st);
+      run(t, r0, y, y2, st);
     }
   }
+  if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_REDUCED);
   const bool ok2 = b_gemm_end(p, sm, cs, S.gi, g.kind == BK_O || g.kind == BK_GU || g.kind == BK_D);
   gemm_n++;
   return ok && ok2;
@@ -636,8 +675,8 @@ __device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, cons
 __device__ __forceinline__ unsigned long long* b_ssq_next(const Params& p, Cons& cs) {
   cs.dk = (cs.dk + 1) % 3;
   unsigned long long* w = p.bw.ssq + cs.dk * TBMAX;
-  if (cs.cta == 0)
-    for (int t = cs.tid; t < TBMAX; t += NCT) __stcg(p.bw.ssq + ((cs.dk + 1) % 3) * TBMAX + t, 0ull);
+  if (cs.cta() == 0)
+    for (int t = cs.tid(); t < TBMAX; t += NCT) __stcg(p.bw.ssq + ((cs.dk + 1) % 3) * TBMAX + t, 0ull);
   return w;
 }
 __device__ __forceinline__ const unsigned long long* b_ssq_cur(const Params& p, const Cons& cs) {
@@ -658,9 +697,9 @@ __device__ __forceinline__ bool b_sync_planes(const Params& p, Smem& sm, Cons& c
 // [split_lo(128, G, c), split_lo(128, G, c + 1)); one thread per (token, unit).
 template <class F>
 __device__ void b_elementwise(Cons& cs, int T, F&& f) {
-  const int u0 = split_lo(HID / 8, cs.G, cs.cta), u1 = split_lo(HID / 8, cs.G, cs.cta + 1);
+  const int u0 = split_lo(HID / 8, cs.G(), cs.cta()), u1 = split_lo(HID / 8, cs.G(), cs.cta() + 1);
   const int nu = u1 - u0;
-  for (int e = cs.tid; e < T * nu; e += NCT) {
+  for (int e = cs.tid(); e < T * nu; e += NCT) {
     const int t = e / nu, u = u0 + e - t * nu;
     f(t, 8 * u);
   }
@@ -847,7 +886,7 @@ template <bool CP>
 __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const LayerW* L, const float* qkv, int NT, int p0, int h,
                           uint8_t* kb, uint8_t* vb, bf16* hilo, int tok0, int c, int nch, int s0, int s1,
                           bool writer, float* prt, uint32_t* cnt) {
-  const int g = cs.lane / WL, u = cs.lane % WL;
+  const int g = cs.lane() / WL, u = cs.lane() % WL;
   for (int t = 0; t < NT; ++t) {
     // one round trip: raw q (both heads), k, v, the norm weights and the position's RoPE rows
     const int pos = p0 + t;
@@ -954,7 +993,7 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
     __threadfence();
     __syncwarp();
     uint32_t last = 0;
-    if (cs.lane == 0) last = atomicAdd(cnt, 1u) == static_cast<uint32_t>(nch - 1) ? 1u : 0u;
+    if (cs.lane() == 0) last = atomicAdd(cnt, 1u) == static_cast<uint32_t>(nch - 1) ? 1u : 0u;
     last = __shfl_sync(WFULL, last, 0);
     if (!last) continue;
     __threadfence();
@@ -979,7 +1018,7 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
     a0.merge_groups();
     a1.merge_groups();
     if (g < 2) w_out(hilo, tok0 + t, (2 * h + g) * HD + WD * u, a0, a1, g);
-    if (cs.lane == 0) atomicExch(cnt, 0u);
+    if (cs.lane() == 0) atomicExch(cnt, 0u);
   }
 }
 
@@ -990,7 +1029,7 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
 __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, int li, bool cp, int pass) {
   const BState bst = bstate(sm);
   const int B = p.nb;
-  const int NW = cs.G * NCW, gw = cs.cta * NCW + cs.warp;
+  const int NW = cs.G() * NCW, gw = cs.cta() * NCW + cs.warp();
   if (cp) {
     const int l = li - p.n_bb;
     const LayerW* L = p.cp_layers + l;
@@ -1011,7 +1050,7 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
     if (dense) {
       // the chunk's new K/V rows first (q/k norm of k + RoPE, bf16), so that every row reads them
       // from the cache after the barrier: item (token t, KV head h)
-      const int g = cs.lane / WL, u = cs.lane % WL;
+      const int g = cs.lane() / WL, u = cs.lane() % WL;
       for (int item = gw; item < NV * NKVH; item += NW) {
         const int t = item / NKVH, h = item - t * NKVH, pos = p0d + t;
         const float* row = p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS;
@@ -1046,12 +1085,12 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
     // offset of each row [0, 128), chunks per KV head [128, 256), item count in sm.bcast[1]; the
     // chunk length is the smallest (in steps of 1/8) for which every item gets its own warp
     int* plan = sm.hist;
-    if (cs.warp == 0) {
+    if (cs.warp() == 0) {
       int Sx[4], nx[4];
       int tot = 0;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int v = cs.lane + 32 * k;
+        const int v = cs.lane() + 32 * k;
         Sx[k] = v < NV ? row_len(v) : 0;
         tot += Sx[k];
       }
@@ -1078,13 +1117,13 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const int y = __shfl_up_sync(WFULL, x, o);
-          if (cs.lane >= o) x += y;
+          if (cs.lane() >= o) x += y;
         }
-        plan[cs.lane + 32 * k] = base + x - NKVH * nx[k];
-        plan[128 + cs.lane + 32 * k] = nx[k];
+        plan[cs.lane() + 32 * k] = base + x - NKVH * nx[k];
+        plan[128 + cs.lane() + 32 * k] = nx[k];
         base += __shfl_sync(WFULL, x, 31);
       }
-      if (cs.lane == 0) sm.bcast[1] = base;
+      if (cs.lane() == 0) sm.bcast[1] = base;
     }
     named_sync(1, NCT);
     const int total = sm.bcast[1];
@@ -1123,11 +1162,11 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
     if (!b_gemm(
             p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn,
             [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
-            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
-              float v[16];
+            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+              float v[EW];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = y[i] * st.rs;
-              st16_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
+              for (int i = 0; i < EW; ++i) v[i] = y[i] * st.rs;
+              stw_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
             }))
       return false;
   }
@@ -1139,20 +1178,20 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
     if (!b_gemm(
             p, sm, cs, BGemm{BK_O, li, 0, T}, gn,
             [&](int t, int r0, EpiSt& st) {
-              ld16_f32(hin + t * HID + r0, st.a);
-              ld16_bf16(L->post_norm + r0, st.b);
+              ldw_f32(hin + t * HID + r0, st.a);
+              ldw_bf16(L->post_norm + r0, st.b);
             },
-            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
+            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
               double ss = 0.0;
-              float v[16], a[16];
+              float v[EW], a[EW];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < EW; ++i) {
                 v[i] = y[i] + st.a[i];
                 a[i] = v[i] * st.b[i];
                 ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
               }
-              st16_f32(p.bw.hmid + t * HID + r0, v);
-              hilo_store16(p.bw.abuf[0], t, r0, a);
+              stw_f32(p.bw.hmid + t * HID + r0, v);
+              hilo_store_w(p.bw.abuf[0], t, r0, a);
               b_ssq_add(ssq, t, ss);
             }))
       return false;
@@ -1163,14 +1202,14 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
     if (!b_gemm(
             p, sm, cs, BGemm{BK_GU, li, 0, T}, gn,
             [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
-            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
-              float m[16];
+            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+              float m[EW];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < EW; ++i) {
                 const float gg = y[i] * st.rs, uu = y2[i] * st.rs;
                 m[i] = (gg / (1.0f + expf(-gg))) * uu;
               }
-              hilo_store16(p.bw.abuf[1], t, r0, m);
+              hilo_store_w(p.bw.abuf[1], t, r0, m);
             }))
       return false;
   }
@@ -1180,24 +1219,24 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
     if (!b_gemm(
             p, sm, cs, BGemm{BK_D, li, 0, T}, gn,
             [&](int t, int r0, EpiSt& st) {
-              ld16_f32(p.bw.hmid + t * HID + r0, st.a);
-              if (next_norm) ld16_bf16(next_norm + r0, st.b);
+              ldw_f32(p.bw.hmid + t * HID + r0, st.a);
+              if (next_norm) ldw_bf16(next_norm + r0, st.b);
             },
-            [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
+            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
               double ss = 0.0;
-              float v[16];
+              float v[EW];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < EW; ++i) {
                 v[i] = y[i] + st.a[i];
                 if (!cp) v[i] = round_bf16(v[i]);
                 ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
               }
-              st16_f32(hout + t * HID + r0, v);
+              stw_f32(hout + t * HID + r0, v);
               if (next_norm) {
-                float a[16];
+                float a[EW];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) a[i] = v[i] * st.b[i];
-                hilo_store16(p.bw.abuf[0], t, r0, a);
+                for (int i = 0; i < EW; ++i) a[i] = v[i] * st.b[i];
+                hilo_store_w(p.bw.abuf[0], t, r0, a);
               }
               b_ssq_add(ssq, t, ss);
             }))
@@ -1228,11 +1267,11 @@ __device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_
                                     int slot) {
   const BState bst = bstate(sm);
   unsigned long long* amax = p.bw.amax + slot * TBMAX;
-  if (cs.cta == 0)
-    for (int t = cs.tid; t < TBMAX; t += NCT) __stcg(p.bw.amax + (slot ^ 1) * TBMAX + t, 0ull);
+  if (cs.cta() == 0)
+    for (int t = cs.tid(); t < TBMAX; t += NCT) __stcg(p.bw.amax + (slot ^ 1) * TBMAX + t, 0ull);
   return b_gemm(
       p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, [&](int t, int r0, EpiSt& st) {},
-      [&](int t, int r0, const float* y, const float* y2, const EpiSt& st) {
+      [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
         SampleCfg c = cfg;
         if (hidx == 0) {
           c.seen = (c.penalty != 1.f) ? p.bs[t].st->seen : nullptr;
@@ -1241,7 +1280,7 @@ __device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_
         }
         unsigned long long best = 0ull;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < EW; ++i) {
           const int row = r0 + i;
           const float lg = round_bf16(y[i]);
           if (hidx > 0 && p.dbg_cp_logits != nullptr)   // parity tests: [B][15][cp_vocab]
@@ -1284,11 +1323,11 @@ __device__ __noinline__ bool b_tokens(const Params& p, Smem& sm, Cons& cs, int h
                          int col) {
   const BState bst = bstate(sm);
   if (!cfg.do_sample) {
-    if (cs.cta == 0)
-      for (int s = cs.tid; s < p.nb; s += NCT) __stcg(p.bw.tok + s * NGROUPS + col, b_token(p, cfg, slot, s, col));
+    if (cs.cta() == 0)
+      for (int s = cs.tid(); s < p.nb; s += NCT) __stcg(p.bw.tok + s * NGROUPS + col, b_token(p, cfg, slot, s, col));
     return true;
   }
-  for (int s = cs.cta; s < p.nb; s += cs.G) {
+  for (int s = cs.cta(); s < p.nb; s += cs.G()) {
     SampleCfg c = cfg;
     if (hidx == 0) {
       c.seen = (c.penalty != 1.f) ? p.bs[s].st->seen : nullptr;
@@ -1300,7 +1339,7 @@ __device__ __noinline__ bool b_tokens(const Params& p, Smem& sm, Cons& cs, int h
     const int fr = p.mode == MODE_B_HEAD ? 0 : bst.step[s] + frame_of;
     c.u24 = draw_u24(sp, fr, hidx);
     const int tk = sample(p.bw.logits + static_cast<size_t>(s) * VMAX, sm, cs, c);
-    if (cs.tid == 0) __stcg(p.bw.tok + s * NGROUPS + col, tk);
+    if (cs.tid() == 0) __stcg(p.bw.tok + s * NGROUPS + col, tk);
   }
   return grid_sync(p, sm, cs);
 }
@@ -1324,8 +1363,8 @@ __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
   const BState bst = bstate(sm);
   const int B = p.nb;
   uint32_t gn = 0;
-  if (cs.cta == 0)
-    for (int s = cs.tid; s < B; s += NCT) {
+  if (cs.cta() == 0)
+    for (int s = cs.tid(); s < B; s += NCT) {
       if (bst.act[s]) p.bs[s].st->seen[bst.g0[s]] = 1;   // generated_g0.append (generator.py:129)
       else if (ld_volatile_i32(&p.bs[s].st->g0) == p.sp.eos) p.bs[s].st->done = 1;   // generator.py:126
     }
@@ -1405,8 +1444,8 @@ __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
   if (!b_head(p, sm, cs, gn, 0, c, slot)) return false;
   if (!b_tokens(p, sm, cs, 0, c, slot, 1, 0)) return false;
   // ---- frame results: codes, next g0, position, step
-  if (cs.cta == 0)
-    for (int s = cs.tid; s < B; s += NCT) {
+  if (cs.cta() == 0)
+    for (int s = cs.tid(); s < B; s += NCT) {
       if (!bst.act[s]) continue;
       StreamState* st = p.bs[s].st;
       int32_t* out = p.bs[s].codes + static_cast<size_t>(bst.step[s]) * NGROUPS;
@@ -1446,8 +1485,8 @@ __device__ bool b_prefill(const Params& p, Smem& sm, Cons& cs) {
     for (int j = 0; j < 8; ++j)
       p.bs[s].st->h[k0 + j] = __ldcg(last + s * HID + k0 + j) * rs * __bfloat162float(p.bb_norm[k0 + j]);
   });
-  if (cs.cta == 0)
-    for (int s = cs.tid; s < p.nb; s += NCT)
+  if (cs.cta() == 0)
+    for (int s = cs.tid(); s < p.nb; s += NCT)
       if (bst.act[s]) p.bs[s].st->position = i + 1;
   return true;
 }
@@ -1479,7 +1518,7 @@ __device__ bool b_prefill_dense(const Params& p, Smem& sm, Cons& cs) {
         p.bs[0].st->h[k0 + j] = __ldcg(last + t * HID + k0 + j) * rs * __bfloat162float(p.bb_norm[k0 + j]);
     });
   }
-  if (cs.cta == 0 && cs.tid == 0) p.bs[0].st->position = p0 + T;
+  if (cs.cta() == 0 && cs.tid() == 0) p.bs[0].st->position = p0 + T;
   return true;
 }
 
@@ -1497,8 +1536,8 @@ __device__ bool b_first_token(const Params& p, Smem& sm, Cons& cs) {
   const SampleCfg c = b_codec_cfg(p, 1.f);
   if (!b_head(p, sm, cs, gn, 0, c, 0)) return false;
   if (!b_tokens(p, sm, cs, 0, c, 0, 0, 0)) return false;
-  if (cs.cta == 0)
-    for (int s = cs.tid; s < p.nb; s += NCT) {
+  if (cs.cta() == 0)
+    for (int s = cs.tid(); s < p.nb; s += NCT) {
       StreamState* st = p.bs[s].st;
       st->g0 = b_token(p, c, 0, s, 0);
       st->step = 0;
@@ -1516,7 +1555,7 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     return;
   }
   if (tid == 0) {
-    for (int i = 0; i < BB_N; ++i) mbar_init(&sm.bbar[i], 1);
+    for (int i = 0; i < BB_N; ++i) mbar_init(&sm.bbar[i], i == BB_SREADY ? static_cast<uint32_t>(p.bcl) : 1u);
     sm.abort = 0;
     sm.epoch = 0;
     fence_barrier_init();
@@ -1525,6 +1564,8 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     tmem_alloc(&sm.tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
+  // the cluster's mbarriers are initialised before any CTA of the cluster arrives on them
+  cluster_sync_all();
   // per-utterance state: position, step, g0, active
   for (int s = tid; s < BMAX; s += NTHREADS_B) {
     int act = 0, pos = 0, step = 0, g0 = 0;
@@ -1568,11 +1609,6 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     cs.slot = 0;
     cs.round = 0;
     cs.bar_target = 0;
-    cs.cta = blockIdx.x;
-    cs.G = gridDim.x;
-    cs.tid = tid;
-    cs.warp = warp;
-    cs.lane = tid & 31;
     cs.dk = 0;
     cs.gi = 0;
     bool ok;
@@ -1592,4 +1628,6 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     tc_fence_after();
     tmem_dealloc(sm.tmem_base, TMEM_COLS);
   }
+  // no CTA leaves while another CTA of its cluster may still read its shared memory
+  cluster_sync_all();
 }

@@ -188,6 +188,32 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The same load without the wait: the registers are valid only after tmem_wait_ld, which takes
+// them as in/out operands so that no use is scheduled before the wait.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Waits for every tcgen05.ld of this thread; v0 and v1 are tied to the wait.
+__device__ __forceinline__ void tmem_wait_ld(float (&v0)[16], float (&v1)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+f"(v0[0]), "+f"(v0[1]), "+f"(v0[2]), "+f"(v0[3]), "+f"(v0[4]), "+f"(v0[5]), "+f"(v0[6]),
+                 "+f"(v0[7]), "+f"(v0[8]), "+f"(v0[9]), "+f"(v0[10]), "+f"(v0[11]), "+f"(v0[12]), "+f"(v0[13]),
+                 "+f"(v0[14]), "+f"(v0[15]), "+f"(v1[0]), "+f"(v1[1]), "+f"(v1[2]), "+f"(v1[3]), "+f"(v1[4]),
+                 "+f"(v1[5]), "+f"(v1[6]), "+f"(v1[7]), "+f"(v1[8]), "+f"(v1[9]), "+f"(v1[10]), "+f"(v1[11]),
+                 "+f"(v1[12]), "+f"(v1[13]), "+f"(v1[14]), "+f"(v1[15])
+               :
+               : "memory");
+}
+
 // Four 32 lanes x 16 columns loads (columns c, c + stride, c + 2 stride, c + 3 stride) with one
 // wait: a[i][k] = column c + i * stride + k.
 __device__ __forceinline__ void tmem_ld16x4(uint32_t taddr, uint32_t stride, float (&a)[4][16]) {
@@ -231,6 +257,61 @@ __device__ __forceinline__ void cp_async_wait_all() {
 
 __device__ __forceinline__ void prefetch_l2_bulk(const void* gsrc, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------- thread-block clusters
+// Rank of this CTA in its cluster, the address of the same shared-memory location in CTA `rank`
+// of the cluster, and loads from there (distributed shared memory). No TMA multicast anywhere.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t caddr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(caddr)
+               : "memory");
+  return v;
+}
+// One arrival (release at cluster scope) on an mbarrier of a CTA of this cluster; caddr comes from
+// mapa_shared. Orders this thread's earlier writes (and those it has synchronised with through a
+// CTA barrier) before the arrival for the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+// Parity test with acquire at cluster scope (the arrivals came from other CTAs of the cluster).
+__device__ __forceinline__ bool mbar_test_parity_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_test_parity_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_test_parity_cluster(bar, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > QTT_WAIT_NS) return false;
+    }
+  }
+}
+// Every thread of every CTA of the cluster (kernel start and end only).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- named barrier

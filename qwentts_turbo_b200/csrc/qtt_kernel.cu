@@ -376,11 +376,17 @@ __device__ void producer_main(const Params& p, Smem& sm, int cta, int G) {
 // ------------------------------------------------------------------------------------------
 // Consumers
 // ------------------------------------------------------------------------------------------
+// A consumer thread's state. Its indices come from special registers (no memory access); only the
+// counters below are kept in the struct.
 struct Cons {
   uint32_t slot, round, bar_target;
-  int cta, G, tid, warp, lane;
   int dk;   // fused MLP stages completed in this launch (selects the fixed-point output buffer)
-  int gi;   // batched kernel: GEMM stages completed in this launch (selects the K-split counter bank)
+  int gi;   // batched kernel: GEMM stages completed in this launch (trace index)
+  __device__ __forceinline__ int cta() const { return static_cast<int>(blockIdx.x); }
+  __device__ __forceinline__ int G() const { return static_cast<int>(gridDim.x); }
+  __device__ __forceinline__ int tid() const { return static_cast<int>(threadIdx.x); }
+  __device__ __forceinline__ int warp() const { return static_cast<int>(threadIdx.x) >> 5; }
+  __device__ __forceinline__ int lane() const { return static_cast<int>(threadIdx.x) & 31; }
 };
 
 // A layer's input or output hidden state in global memory: fp32 (first layer of a stack,
@@ -432,44 +438,50 @@ __device__ __forceinline__ void fail(const Params& p, Smem& sm, int code) {
 // Profiling stamp of CTA 0 for the current stage (no-op unless dbg_marks is set; the batched
 // kernel, p.nb > 0, uses dbg_marks for its own trace).
 __device__ __forceinline__ void stage_mark(const Params& p, const Cons& cs, int id) {
-  if (p.dbg_marks != nullptr && p.nb == 0 && cs.cta == 0 && cs.tid == 0) {
-    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+  if (p.dbg_marks != nullptr && p.nb == 0 && cs.cta() == 0 && cs.tid() == 0) {
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
     if (static_cast<int>(k * 3 + id) < p.dbg_marks_len) p.dbg_marks[k * 3 + id] = globaltimer_ns();
   }
 }
 
 // Profiling stamps of CTA 0 inside a stage's RMSNorm prologue (input loaded, norm reduced).
 __device__ __forceinline__ void prologue_mark(const Params& p, const Cons& cs, int id) {
-  if (p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0) {
-    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+  if (p.dbg_marks != nullptr && cs.cta() == 0 && cs.tid() == 0) {
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
     if (static_cast<int>(8 * 1024 + 4 * k + id) < p.dbg_marks_len) p.dbg_marks[8 * 1024 + 4 * k + id] = globaltimer_ns();
   }
 }
 
-// Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded).
-__device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
+// Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded). Not
+// inlined: its spin loop keeps its few values in registers instead of sharing the caller's.
+__device__ __noinline__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
   named_sync(1, NCT);
-  if (cs.tid == 0) {
+  if (cs.tid() == 0) {
     stage_mark(p, cs, 2);
     if (p.dbg_arrivals != nullptr) {
-      const int k = static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G)) - p.dbg_arr_stage0;
-      if (k >= 0 && k < p.dbg_arr_n) p.dbg_arrivals[k * cs.G + cs.cta] = globaltimer_ns();
+      const int k = static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G())) - p.dbg_arr_stage0;
+      if (k >= 0 && k < p.dbg_arr_n) p.dbg_arrivals[k * cs.G() + cs.cta()] = globaltimer_ns();
     }
   }
-  cs.bar_target += static_cast<uint32_t>(cs.G);
-  if (cs.tid == 0 && !aborted(sm)) {
+  cs.bar_target += static_cast<uint32_t>(cs.G());
+  if (cs.tid() == 0 && !aborted(sm)) {
     // bar.sync above orders this CTA's stores before thread 0; the release add publishes them
     // at gpu scope and the acquire load below orders the other CTAs' stores before ours.
-    const bool skip = p.dbg_skip_barrier > 0 && cs.cta == cs.G - 1 &&
-                      cs.bar_target == static_cast<uint32_t>(p.dbg_skip_barrier) * static_cast<uint32_t>(cs.G);
+    const bool skip = p.dbg_skip_barrier > 0 && cs.cta() == cs.G() - 1 &&
+                      cs.bar_target == static_cast<uint32_t>(p.dbg_skip_barrier) * static_cast<uint32_t>(cs.G());
     if (!skip) red_release_gpu_add(p.w.bar, 1u);
     const uint64_t limit = p.dbg_wait_ns != 0ull ? p.dbg_wait_ns : QTT_WAIT_NS;
+    // the spin compares against register copies: the acquire load clobbers memory, so a value
+    // read through cs or p would be reloaded from the stack on every iteration
+    const uint32_t target = cs.bar_target;
+    uint32_t* const bar = p.w.bar;
+    const int* const errw = p.w.err;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 0;; ++it) {
-      const uint32_t v = ld_acquire_gpu(p.w.bar);
-      if (static_cast<int>(v - cs.bar_target) >= 0) break;
+      const uint32_t v = ld_acquire_gpu(bar);
+      if (static_cast<int>(v - target) >= 0) break;
       if ((it & 31u) == 31u) {
-        if (ld_volatile_i32(p.w.err) != 0) {
+        if (ld_volatile_i32(errw) != 0) {
           *reinterpret_cast<volatile int*>(&sm.abort) = 1;
           break;
         }
@@ -479,9 +491,9 @@ __device__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
         }
       }
     }
-    *reinterpret_cast<volatile int*>(&sm.epoch) = static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
-    if (p.dbg_timeline != nullptr && cs.cta == 0) {
-      const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+    *reinterpret_cast<volatile int*>(&sm.epoch) = static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G()));
+    if (p.dbg_timeline != nullptr && cs.cta() == 0) {
+      const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
       if (k < static_cast<uint32_t>(p.dbg_timeline_len)) p.dbg_timeline[k] = globaltimer_ns();
     }
   }
@@ -496,7 +508,7 @@ __device__ __forceinline__ void block_sum_d(Smem& sm, Cons& cs, double (&v)[NT])
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     const double s = warp_sum_d(v[t]);
-    if (cs.lane == 0) sm.dred[t * NCW + cs.warp] = s;
+    if (cs.lane() == 0) sm.dred[t * NCW + cs.warp()] = s;
   }
   named_sync(1, NCT);
 #pragma unroll
@@ -515,7 +527,7 @@ __device__ __forceinline__ void block_sum(Smem& sm, Cons& cs, float (&v)[NT]) {
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     const float s = warp_sum(v[t]);
-    if (cs.lane == 0) sm.red[t * NCW + cs.warp] = s;
+    if (cs.lane() == 0) sm.red[t * NCW + cs.warp()] = s;
   }
   named_sync(1, NCT);
 #pragma unroll
@@ -542,14 +554,14 @@ __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4
 template <int NT, bool FROM_SMEM, bool DEFER = false>
 __device__ void load_rmsnorm(const Params& p, Smem& sm, Cons& cs, const float* src, const bf16* w, float eps,
                              float* dst) {
-  const bool act = cs.tid < HID / 4;
+  const bool act = cs.tid() < HID / 4;
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
   if (act) {
-    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
+    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid());
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      const float4* s4 = reinterpret_cast<const float4*>(src + t * HID) + cs.tid;
+      const float4* s4 = reinterpret_cast<const float4*>(src + t * HID) + cs.tid();
       x[t] = FROM_SMEM ? *s4 : __ldcg(s4);
     }
   }
@@ -562,10 +574,10 @@ __device__ void load_rmsnorm_h(const Params& p, Smem& sm, Cons& cs, const HIn& h
                                float* dst) {
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
-  if (cs.tid < HID / 4) {
-    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
+  if (cs.tid() < HID / 4) {
+    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid());
 #pragma unroll
-    for (int t = 0; t < NT; ++t) x[t] = h_ld4<BB>(h, t * HID + 4 * cs.tid);
+    for (int t = 0; t < NT; ++t) x[t] = h_ld4<BB>(h, t * HID + 4 * cs.tid());
   }
   rmsnorm_finish<NT, DEFER>(p, sm, cs, x, wv, eps, dst);
 }
@@ -573,7 +585,7 @@ __device__ void load_rmsnorm_h(const Params& p, Smem& sm, Cons& cs, const HIn& h
 template <int NT, bool DEFER>
 __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4 (&x)[NT], uint2 wv, float eps,
                                float* dst) {
-  const bool act = cs.tid < HID / 4;
+  const bool act = cs.tid() < HID / 4;
   if constexpr (DEFER) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
@@ -584,11 +596,11 @@ __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4
         a = fma(static_cast<double>(x[t].z), static_cast<double>(x[t].z), a);
         a = fma(static_cast<double>(x[t].w), static_cast<double>(x[t].w), a);
         const float w0 = bf16_lo(wv.x), w1 = bf16_hi(wv.x), w2 = bf16_lo(wv.y), w3 = bf16_hi(wv.y);
-        reinterpret_cast<float4*>(dst + t * HID)[cs.tid] =
+        reinterpret_cast<float4*>(dst + t * HID)[cs.tid()] =
             make_float4(x[t].x * w0, x[t].y * w1, x[t].z * w2, x[t].w * w3);
       }
       a = warp_sum_d(a);
-      if (cs.lane == 0) sm.dred[t * NCW + cs.warp] = a;
+      if (cs.lane() == 0) sm.dred[t * NCW + cs.warp()] = a;
     }
     prologue_mark(p, cs, 0);
     named_sync(1, NCT);
@@ -622,7 +634,7 @@ __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4
         o.y = x[t].y * rstd * w1;
         o.z = x[t].z * rstd * w2;
         o.w = x[t].w * rstd * w3;
-        reinterpret_cast<float4*>(dst + t * HID)[cs.tid] = o;
+        reinterpret_cast<float4*>(dst + t * HID)[cs.tid()] = o;
       }
     }
     prologue_mark(p, cs, 2);
@@ -633,7 +645,7 @@ __device__ void rmsnorm_finish(const Params& p, Smem& sm, Cons& cs, const float4
 
 // Copy NT vectors of n floats from global (L2, written by other CTAs) into shared memory.
 __device__ __forceinline__ void load_vec(Cons& cs, float* dst, const float* src, int n_total) {
-  for (int i = cs.tid * 4; i < n_total; i += NCT * 4)
+  for (int i = cs.tid() * 4; i < n_total; i += NCT * 4)
     *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(src + i));
 }
 
@@ -648,11 +660,11 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
     return false;
   }
   float* lp = reinterpret_cast<float*>(sm.att);   // [units * NT][LP_STRIDE] lane partials
-  const int part = cs.warp % pl.P;
+  const int part = cs.warp() % pl.P;
   float xr[NT][32];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    const float* xp = xsrc + t * xstride + part * UNIT + 8 * cs.lane;
+    const float* xp = xsrc + t * xstride + part * UNIT + 8 * cs.lane();
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float4 a = *reinterpret_cast<const float4*>(xp + 256 * i);
@@ -673,9 +685,9 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
       rs[t] = rms_scale(a, HID, p.eps);
     }
   }
-  const bool prof = p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0;
+  const bool prof = p.dbg_marks != nullptr && cs.cta() == 0 && cs.tid() == 0;
   unsigned long long waited = 0;
-  const uint32_t kst = cs.bar_target / static_cast<uint32_t>(cs.G);
+  const uint32_t kst = cs.bar_target / static_cast<uint32_t>(cs.G());
   const bool fine = prof && static_cast<int>(4 * 1024 + 4 * kst + 3) < p.dbg_marks_len;
   if (fine) p.dbg_marks[4 * 1024 + 4 * kst + 0] = globaltimer_ns();
   for (int u0 = 0; u0 < pl.units; u0 += SLOT_UNITS) {
@@ -685,13 +697,13 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
     if (prof) waited += globaltimer_ns() - tw;
     if (!got) {
       if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
-    } else if (cs.warp < n) {
-      const uint4* src = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + cs.warp * UNIT_BYTES);
+    } else if (cs.warp() < n) {
+      const uint4* src = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + cs.warp() * UNIT_BYTES);
       // four independent FMA chains (one per 16-byte chunk) keep the dependent chain short
       float ch[NT][4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint4 v = src[cs.lane + 32 * i];
+        const uint4 v = src[cs.lane() + 32 * i];
         const float w[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
                             bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
 #pragma unroll
@@ -705,12 +717,12 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
       // lane partials go to shared memory; the cross-lane sums are done once per stage below
 #pragma unroll
       for (int t = 0; t < NT; ++t)
-        lp[((u0 + cs.warp) * NT + t) * LP_STRIDE + cs.lane] = (ch[t][0] + ch[t][1]) + (ch[t][2] + ch[t][3]);
+        lp[((u0 + cs.warp()) * NT + t) * LP_STRIDE + cs.lane()] = (ch[t][0] + ch[t][1]) + (ch[t][2] + ch[t][3]);
     }
     __syncwarp();
-    if (cs.lane == 0) {
+    if (cs.lane() == 0) {
       *reinterpret_cast<volatile int*>(&sm.free_epoch[cs.slot]) =
-          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
+          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G()));
       mbar_arrive(&sm.empty[cs.slot]);
     }
     if (++cs.slot == NSLOTS) {
@@ -719,14 +731,14 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
     }
   }
   if (prof) {
-    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
     if (static_cast<int>(k) < p.dbg_marks_len / 3 - 1024) p.dbg_marks[3 * 1024 + k] = waited;
   }
   if (fine) p.dbg_marks[4 * 1024 + 4 * kst + 1] = globaltimer_ns();
   named_sync(1, NCT);
   if (fine) p.dbg_marks[4 * 1024 + 4 * kst + 2] = globaltimer_ns();
   // one thread per (unit, token): fixed-order pairwise sum of the 32 lane partials
-  for (int e = cs.tid; e < pl.units * NT; e += NCT) {
+  for (int e = cs.tid(); e < pl.units * NT; e += NCT) {
     const float* row = lp + e * LP_STRIDE;
     float a[16];
 #pragma unroll
@@ -765,7 +777,7 @@ __device__ __forceinline__ void stage_kv_rows(Cons& cs, uint8_t* dst_k, uint8_t*
   constexpr int ROWB = HD * (CP ? 4 : 2);
   constexpr int PIECES = ROWB / 16;
   const int n = (a1 - a0) * PIECES;
-  for (int e = cs.tid; e < 2 * n; e += NCT) {
+  for (int e = cs.tid(); e < 2 * n; e += NCT) {
     const int which = e >= n, r = which ? e - n : e;
     const size_t off = static_cast<size_t>(a0) * ROWB + static_cast<size_t>(r) * 16;
     cp_async16((which ? dst_v : dst_k) + static_cast<size_t>(r) * 16, (which ? vb : kb) + off);
@@ -826,7 +838,7 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
   uint8_t* vst = sm.att + SUB * ROWB;
 
   // 1. one round trip: raw q/k/v rows of this head + the first sub-chunk of cached rows
-  for (int e = cs.tid; e < NT * 4 * (HD / 4); e += NCT) {
+  for (int e = cs.tid(); e < NT * 4 * (HD / 4); e += NCT) {
     const int t = e / (4 * HD / 4), r = e - t * (4 * HD / 4), vec = r / (HD / 4), piece = r - vec * (HD / 4);
     const int row0 = vec < 2 ? (2 * h + vec) * HD : (vec == 2 ? QSZ + h * HD : QSZ + KVSZ + h * HD);
     cp_async16(qraw + (t * 4 + vec) * HD + piece * 4, io.qkv + t * QKV_ROWS + row0 + piece * 4);
@@ -835,19 +847,19 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
     const int a1 = min(min(s1, p0), s0 + SUB);
     if (a1 > s0) stage_kv_rows<CP>(cs, kst, vst, io.kb, io.vb, s0, a1);
   }
-  for (int j = cs.tid; j < J * HD; j += NCT) acc_s[j] = 0.f;
-  if (cs.tid < J) {
-    ml[cs.tid * 4 + 0] = -INFINITY;
-    ml[cs.tid * 4 + 1] = 0.f;
+  for (int j = cs.tid(); j < J * HD; j += NCT) acc_s[j] = 0.f;
+  if (cs.tid() < J) {
+    ml[cs.tid() * 4 + 0] = -INFINITY;
+    ml[cs.tid() * 4 + 1] = 0.f;
   }
   // norm weights and RoPE rows travel with the staged rows (same round trip)
   float nwv[4], cv[4], sv[4];
-  if (cs.warp < NT * 4 && (cs.warp & 3) < 3) {
-    const int pos = p0 + (cs.warp >> 2);
-    const bf16* nw = (cs.warp & 3) < 2 ? L->q_norm : L->k_norm;
+  if (cs.warp() < NT * 4 && (cs.warp() & 3) < 3) {
+    const int pos = p0 + (cs.warp() >> 2);
+    const bf16* nw = (cs.warp() & 3) < 2 ? L->q_norm : L->k_norm;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int d = cs.lane + 32 * i;
+      const int d = cs.lane() + 32 * i;
       nwv[i] = __bfloat162float(nw[d]);
       cv[i] = __bfloat162float(p.cos_tab[static_cast<size_t>(pos) * HD + d]);
       sv[i] = __bfloat162float(p.sin_tab[static_cast<size_t>(pos) * HD + d]);
@@ -858,12 +870,12 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
 
   // 2. q/k RMSNorm per head (fused_decode_tts.cu:183-197) + RoPE; warp j handles vector j%4
   //    of token j/4 with d = lane + 32 i, so each rotation pair (d, d+64) sits in one lane.
-  if (cs.warp < NT * 4) {
-    const int t = cs.warp >> 2, vec = cs.warp & 3;
+  if (cs.warp() < NT * 4) {
+    const int t = cs.warp() >> 2, vec = cs.warp() & 3;
     const float* src = qraw + (t * 4 + vec) * HD;
     float x[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) x[i] = src[cs.lane + 32 * i];
+    for (int i = 0; i < 4; ++i) x[i] = src[cs.lane() + 32 * i];
     if (vec < 3) {
       double ss = 0.0;
 #pragma unroll
@@ -880,17 +892,17 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
       o[3] = y[3] * cv[3] + y[1] * sv[3];
       float* dst = vec < 2 ? qr + (t * 2 + vec) * HD : kn + t * HD;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dst[cs.lane + 32 * i] = (vec == 2 && !CP) ? round_bf16(o[i]) : o[i];
+      for (int i = 0; i < 4; ++i) dst[cs.lane() + 32 * i] = (vec == 2 && !CP) ? round_bf16(o[i]) : o[i];
     } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) vn[t * HD + cs.lane + 32 * i] = CP ? x[i] : round_bf16(x[i]);
+      for (int i = 0; i < 4; ++i) vn[t * HD + cs.lane() + 32 * i] = CP ? x[i] : round_bf16(x[i]);
     }
   }
   named_sync(1, NCT);
 
   // 3. item 0 of each head stores the new K/V rows into the cache.
   if (writer) {
-    for (int e = cs.tid; e < NT * HD; e += NCT) {
+    for (int e = cs.tid(); e < NT * HD; e += NCT) {
       const int t = e / HD, d = e - t * HD;
       const size_t off = static_cast<size_t>(p0 + t) * HD + d;
       if (CP) {
@@ -913,59 +925,59 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
       named_sync(1, NCT);
     }
     // scores: one warp per position, lane holds d = 4 lane .. 4 lane + 3
-    for (int s = sa + cs.warp; s < sb; s += NCW) {
+    for (int s = sa + cs.warp(); s < sb; s += NCW) {
       float k4[4];
       if (s < p0) {
         const uint8_t* row = kst + static_cast<size_t>(s - sa) * ROWB;
         if (CP) {
-          const float4 kk = *reinterpret_cast<const float4*>(row + 16 * cs.lane);
+          const float4 kk = *reinterpret_cast<const float4*>(row + 16 * cs.lane());
           k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
         } else {
-          const uint2 kk = *reinterpret_cast<const uint2*>(row + 8 * cs.lane);
+          const uint2 kk = *reinterpret_cast<const uint2*>(row + 8 * cs.lane());
           k4[0] = bf16_lo(kk.x); k4[1] = bf16_hi(kk.x); k4[2] = bf16_lo(kk.y); k4[3] = bf16_hi(kk.y);
         }
       } else {
-        const float4 kk = *reinterpret_cast<const float4*>(kn + (s - p0) * HD + 4 * cs.lane);
+        const float4 kk = *reinterpret_cast<const float4*>(kn + (s - p0) * HD + 4 * cs.lane());
         k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
       }
 #pragma unroll
       for (int j = 0; j < J; ++j) {
-        const float4 q = *reinterpret_cast<const float4*>(qr + j * HD + 4 * cs.lane);
+        const float4 q = *reinterpret_cast<const float4*>(qr + j * HD + 4 * cs.lane());
         float d = q.x * k4[0];
         d = fmaf(q.y, k4[1], d);
         d = fmaf(q.z, k4[2], d);
         d = fmaf(q.w, k4[3], d);
         d = warp_sum(d) * p.attn_scale;
-        if (cs.lane == 0) sc[j * SUB + (s - sa)] = (s <= p0 + (j >> 1)) ? d : -INFINITY;
+        if (cs.lane() == 0) sc[j * SUB + (s - sa)] = (s <= p0 + (j >> 1)) ? d : -INFINITY;
       }
     }
     named_sync(1, NCT);
     // online softmax statistics: warp j handles (token, q head) j
-    if (cs.warp < J) {
-      float* row = sc + cs.warp * SUB;
+    if (cs.warp() < J) {
+      float* row = sc + cs.warp() * SUB;
       float m = -INFINITY;
-      for (int i = cs.lane; i < len; i += 32) m = fmaxf(m, row[i]);
+      for (int i = cs.lane(); i < len; i += 32) m = fmaxf(m, row[i]);
       m = warp_max(m);
-      const float m_old = ml[cs.warp * 4 + 0];
+      const float m_old = ml[cs.warp() * 4 + 0];
       const float m_new = fmaxf(m_old, m);
       float l = 0.f;
-      for (int i = cs.lane; i < len; i += 32) {
+      for (int i = cs.lane(); i < len; i += 32) {
         const float e = (m_new == -INFINITY) ? 0.f : expf(row[i] - m_new);
         row[i] = e;
         l += e;
       }
       l = warp_sum(l);
-      if (cs.lane == 0) {
+      if (cs.lane() == 0) {
         const float rescale = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-        ml[cs.warp * 4 + 0] = m_new;
-        ml[cs.warp * 4 + 1] = ml[cs.warp * 4 + 1] * rescale + l;
-        ml[cs.warp * 4 + 2] = rescale;
+        ml[cs.warp() * 4 + 0] = m_new;
+        ml[cs.warp() * 4 + 1] = ml[cs.warp() * 4 + 1] * rescale + l;
+        ml[cs.warp() * 4 + 2] = rescale;
       }
     }
     named_sync(1, NCT);
     // P.V: thread -> (d, position residue g mod 3)
     {
-      const int d = cs.tid & (HD - 1), g = cs.tid >> 7;
+      const int d = cs.tid() & (HD - 1), g = cs.tid() >> 7;
       float acc[J];
 #pragma unroll
       for (int j = 0; j < J; ++j) acc[j] = 0.f;
@@ -985,7 +997,7 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
       for (int j = 0; j < J; ++j) accg[(g * J + j) * HD + d] = acc[j];
     }
     named_sync(1, NCT);
-    for (int e = cs.tid; e < J * HD; e += NCT) {
+    for (int e = cs.tid(); e < J * HD; e += NCT) {
       const int j = e / HD, d = e - j * HD;
       const float a = (accg[(0 * J + j) * HD + d] + accg[(1 * J + j) * HD + d]) + accg[(2 * J + j) * HD + d];
       acc_s[e] = acc_s[e] * ml[j * 4 + 2] + a;
@@ -996,7 +1008,7 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
 
   // 5. publish (or finish directly when the head has a single item).
   if (GROUP) {   // head output stays in shared memory: xs[t][hh * HD + d]
-    for (int e = cs.tid; e < J * HD; e += NCT) {
+    for (int e = cs.tid(); e < J * HD; e += NCT) {
       const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
       sm.xs[t * 2 * HD + hh * HD + d] = acc_s[e] / ml[j * 4 + 1];
     }
@@ -1004,20 +1016,20 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
     return true;
   }
   if (nch == 1) {
-    for (int e = cs.tid; e < J * HD; e += NCT) {
+    for (int e = cs.tid(); e < J * HD; e += NCT) {
       const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
       att_store(io, t, (2 * h + hh) * HD + d, acc_s[e] / ml[j * 4 + 1]);
     }
     named_sync(1, NCT);
     return true;
   }
-  for (int e = cs.tid; e < J * PRT_STRIDE; e += NCT) {
+  for (int e = cs.tid(); e < J * PRT_STRIDE; e += NCT) {
     const int j = e / PRT_STRIDE, k = e - j * PRT_STRIDE, t = j >> 1, hh = j & 1;
     const float val = k < 2 ? ml[j * 4 + k] : (k < 4 ? 0.f : acc_s[j * HD + (k - 4)]);
     io.prt[((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + c) * PRT_STRIDE + k] = val;
   }
   named_sync(1, NCT);
-  if (cs.tid == 0) {
+  if (cs.tid() == 0) {
     __threadfence();
     const uint32_t old = atomicAdd(io.cnt, 1u);
     sm.bcast[0] = (old == static_cast<uint32_t>(nch - 1)) ? 1 : 0;
@@ -1030,7 +1042,7 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
     float* recs = reinterpret_cast<float*>(sm.att);   // [J][nch][PRT_STRIDE]
     if (staged) {
       const int pieces = nch * PRT_STRIDE / 4;
-      for (int e = cs.tid; e < J * pieces; e += NCT) {
+      for (int e = cs.tid(); e < J * pieces; e += NCT) {
         const int j = e / pieces, r = e - j * pieces, t = j >> 1, hh = j & 1;
         cp_async16(recs + (j * nch) * PRT_STRIDE + r * 4,
                    io.prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS) * PRT_STRIDE + r * 4);
@@ -1038,7 +1050,7 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
       cp_async_wait_all();
       named_sync(1, NCT);
     }
-    for (int e = cs.tid; e < J * HD; e += NCT) {
+    for (int e = cs.tid(); e < J * HD; e += NCT) {
       const int j = e / HD, d = e - j * HD, t = j >> 1, hh = j & 1;
       float M = -INFINITY, Ls = 0.f, O = 0.f;
       if (staged) {
@@ -1064,7 +1076,7 @@ __device__ bool att_item(const Params& p, Smem& sm, Cons& cs, const LayerW* L, c
       }
       att_store(io, t, (2 * h + hh) * HD + d, O / Ls);
     }
-    if (cs.tid == 0) atomicExch(io.cnt, 0u);
+    if (cs.tid() == 0) atomicExch(io.cnt, 0u);
   }
   named_sync(1, NCT);
 return true;
@@ -1079,7 +1091,7 @@ template <int NT, bool CP, bool GROUP>
 __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int li, int p0) {
   const int S = p0 + NT;
   int nch, chunk;
-  att_split(S, cs.G, p.att_target, nch, chunk);
+  att_split(S, cs.G(), p.att_target, nch, chunk);
   if (GROUP) {
     nch = 1;
     chunk = S;
@@ -1090,12 +1102,12 @@ __device__ bool attention(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
   constexpr int ESZ = CP ? 4 : 2;
   const int max_seq = CP ? p.cp_max_seq : p.bb_max_seq;
   const size_t layer_off = static_cast<size_t>(li) * NKVH * max_seq * HD;
-  const int gph = cs.G / NKVH;
-  const int n_items = GROUP ? (cs.cta < NKVH * gph ? 1 : 0) : NKVH * nch;
-  for (int item = GROUP ? 0 : cs.cta; item < n_items; item += GROUP ? 1 : cs.G) {
-    const int h = GROUP ? cs.cta / gph : item / nch;
+  const int gph = cs.G() / NKVH;
+  const int n_items = GROUP ? (cs.cta() < NKVH * gph ? 1 : 0) : NKVH * nch;
+  for (int item = GROUP ? 0 : cs.cta(); item < n_items; item += GROUP ? 1 : cs.G()) {
+    const int h = GROUP ? cs.cta() / gph : item / nch;
     const int c = GROUP ? 0 : item - h * nch;
-    const bool writer = GROUP ? (cs.cta % gph == 0) : (c == 0);
+    const bool writer = GROUP ? (cs.cta() % gph == 0) : (c == 0);
     const int s0 = c * chunk, s1 = min(S, s0 + chunk);
     AttIO io;
     io.qkv = p.w.qkv;
@@ -1130,10 +1142,10 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
   else
     load_rmsnorm_h<NT, !CP, true>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
-    const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta(), cs.G());
     if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nr = pl.r1 - pl.r0;
-    for (int e = cs.tid; e < NT * nr; e += NCT) {
+    for (int e = cs.tid(); e < NT * nr; e += NCT) {
       const int t = e / nr, r = e - t * nr;
       __stcg(p.w.qkv + t * QKV_ROWS + pl.r0 + r, sm.part[r * NT + t]);
     }
@@ -1146,15 +1158,15 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
 
   // ---- o_proj + residual (the residual rows are fetched with the attention output)
   {
-    const Plan pl = make_plan(SK_O, nullptr, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_O, nullptr, nullptr, 0, cs.cta(), cs.G());
     const int nr = pl.r1 - pl.r0;
     float res = 0.f;
-    if (cs.tid < NT * nr) res = h_ld<!CP>(hin, (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
+    if (cs.tid() < NT * nr) res = h_ld<!CP>(hin, (cs.tid() / nr) * HID + pl.r0 + cs.tid() % nr);
     load_vec(cs, sm.xs, p.w.attn, NT * QSZ);
     named_sync(1, NCT);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, QSZ)) return false;
-    if (cs.tid < NT * nr) {
-      const int t = cs.tid / nr, r = cs.tid % nr;
+    if (cs.tid() < NT * nr) {
+      const int t = cs.tid() / nr, r = cs.tid() % nr;
       __stcg(p.w.hmid + t * HID + pl.r0 + r, (sm.part[(2 * r) * NT + t] + sm.part[(2 * r + 1) * NT + t]) + res);
     }
   }
@@ -1175,12 +1187,12 @@ __device__ bool layer(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, int
 // hacc[(dk + 1) % 3], the buffer of the next fused stage (last read two stages before).
 template <int NT>
 __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, long long*& out) {
-  const Plan pl = make_plan(SK_GUF, nullptr, nullptr, 0, cs.cta, cs.G);
+  const Plan pl = make_plan(SK_GUF, nullptr, nullptr, 0, cs.cta(), cs.G());
   if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
   const int nj = pl.r1 - pl.r0;
   float* mv = sm.xs + NTMAX * HID;   // [NT][WD_BOX_COLS], zero beyond this CTA's columns
-  if (cs.tid < NT * WD_BOX_COLS) {
-    const int t = cs.tid / WD_BOX_COLS, j = cs.tid - t * WD_BOX_COLS;
+  if (cs.tid() < NT * WD_BOX_COLS) {
+    const int t = cs.tid() / WD_BOX_COLS, j = cs.tid() - t * WD_BOX_COLS;
     float m = 0.f;
     if (j < nj) {
       const float g = sm.part[j * NT + t], u = sm.part[(nj + j) * NT + t];
@@ -1204,15 +1216,15 @@ __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
       cs.round++;
     }
   }
-  if (p.dbg_marks != nullptr && cs.cta == 0 && cs.tid == 0) {   // profiling: W_down boxes ready
-    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G);
+  if (p.dbg_marks != nullptr && cs.cta() == 0 && cs.tid() == 0) {   // profiling: W_down boxes ready
+    const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
     if (static_cast<int>(4 * 1024 + 4 * k + 3) < p.dbg_marks_len) p.dbg_marks[4 * 1024 + 4 * k + 3] = globaltimer_ns();
   }
-  const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
+  const int d0 = split_lo(HID, cs.G(), cs.cta()), d1 = split_lo(HID, cs.G(), cs.cta() + 1);
   long long* acc = p.w.hacc + static_cast<size_t>(cs.dk % NHACC) * NTMAX * HID;
   long long* part = reinterpret_cast<long long*>(sm.att);   // [NT][HID] this CTA's fixed-point partials
   if (ok) {
-    for (int r = cs.tid; r < HID; r += NCT) {
+    for (int r = cs.tid(); r < HID; r += NCT) {
       const int box = r / WD_BOX_ROWS;
       const uint8_t* row = sm.ring[box < WD_BOXES_PER_SLOT ? sl[0] : sl[1]] +
                            (box % WD_BOXES_PER_SLOT) * WD_BOX_BYTES + (r % WD_BOX_ROWS) * (WD_BOX_COLS * 2);
@@ -1241,25 +1253,25 @@ __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
     }
   }
   __syncwarp();
-  if (cs.lane == 0) {
+  if (cs.lane() == 0) {
 #pragma unroll
     for (int i = 0; i < WD_SLOTS; ++i) {
       *reinterpret_cast<volatile int*>(&sm.free_epoch[sl[i]]) =
-          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
+          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G()));
       mbar_arrive(&sm.empty[sl[i]]);
     }
   }
   // one TMA bulk reduction adds the CTA's whole partial vector into the layer output
   fence_proxy_async_smem();
   named_sync(1, NCT);
-  if (cs.tid == 0 && ok) {
+  if (cs.tid() == 0 && ok) {
     fence_proxy_async_global();   // the zeroing of acc (generic stores, earlier stages) first
     bulk_reduce_add_u64(acc, part, static_cast<uint32_t>(NT * HID * sizeof(long long)));
     bulk_commit_and_wait_all();
     fence_proxy_async_global();
   }
   long long* nxt = p.w.hacc + static_cast<size_t>((cs.dk + 1) % NHACC) * NTMAX * HID;
-  for (int e = cs.tid; e < NTMAX * (d1 - d0); e += NCT) {
+  for (int e = cs.tid(); e < NTMAX * (d1 - d0); e += NCT) {
     const int t = e / (d1 - d0), r = d0 + e % (d1 - d0);
     __stcg(nxt + t * HID + r, 0ll);
   }
@@ -1281,10 +1293,10 @@ __device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
     return grid_sync(p, sm, cs);
   }
   {
-    const Plan pl = make_plan(SK_GU, nullptr, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_GU, nullptr, nullptr, 0, cs.cta(), cs.G());
     if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nj = pl.r1 - pl.r0;
-    for (int e = cs.tid; e < NT * nj; e += NCT) {
+    for (int e = cs.tid(); e < NT * nj; e += NCT) {
       const int t = e / nj, j = e - t * nj;
       const float g = sm.part[j * NT + t], u = sm.part[(nj + j) * NT + t];
       __stcg(p.w.mlp + t * INTER + pl.r0 + j, (g / (1.0f + expf(-g))) * u);
@@ -1294,15 +1306,15 @@ __device__ bool mlp_tail(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
 
   // ---- down_proj + residual
   {
-    const Plan pl = make_plan(SK_D, nullptr, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_D, nullptr, nullptr, 0, cs.cta(), cs.G());
     const int nr = pl.r1 - pl.r0;
     float res = 0.f;
-    if (cs.tid < NT * nr) res = __ldcg(p.w.hmid + (cs.tid / nr) * HID + pl.r0 + cs.tid % nr);
+    if (cs.tid() < NT * nr) res = __ldcg(p.w.hmid + (cs.tid() / nr) * HID + pl.r0 + cs.tid() % nr);
     load_vec(cs, sm.xs, p.w.mlp, NT * INTER);
     named_sync(1, NCT);
     if (!gemv<NT>(p, pl, sm, cs, sm.xs, INTER)) return false;
-    if (cs.tid < NT * nr) {
-      const int t = cs.tid / nr, r = cs.tid % nr;
+    if (cs.tid() < NT * nr) {
+      const int t = cs.tid() / nr, r = cs.tid() % nr;
       float v = ((sm.part[(3 * r) * NT + t] + sm.part[(3 * r + 1) * NT + t]) + sm.part[(3 * r + 2) * NT + t]) + res;
       if (!CP) v = round_bf16(v);
       __stcg(hout_f + t * HID + pl.r0 + r, v);
@@ -1326,8 +1338,8 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
   float xr[NT][8];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    const float4 a = *reinterpret_cast<const float4*>(x + t * 2 * HD + 8 * cs.lane);
-    const float4 b = *reinterpret_cast<const float4*>(x + t * 2 * HD + 8 * cs.lane + 4);
+    const float4 a = *reinterpret_cast<const float4*>(x + t * 2 * HD + 8 * cs.lane());
+    const float4 b = *reinterpret_cast<const float4*>(x + t * 2 * HD + 8 * cs.lane() + 4);
     xr[t][0] = a.x; xr[t][1] = a.y; xr[t][2] = a.z; xr[t][3] = a.w;
     xr[t][4] = b.x; xr[t][5] = b.y; xr[t][6] = b.z; xr[t][7] = b.w;
   }
@@ -1336,8 +1348,8 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
     if (!mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort)) {
       if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
     } else {
-      for (int r = cs.warp; r < m; r += NCW) {
-        const uint4 v = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + r * OH_ROW_BYTES)[cs.lane];
+      for (int r = cs.warp(); r < m; r += NCW) {
+        const uint4 v = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + r * OH_ROW_BYTES)[cs.lane()];
         const float w[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
                             bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
 #pragma unroll
@@ -1345,14 +1357,14 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
           float a = w[0] * xr[t][0];
 #pragma unroll
           for (int j = 1; j < 8; ++j) a = fmaf(w[j], xr[t][j], a);
-          lp[((u0 + r) * NT + t) * LP_STRIDE + cs.lane] = a;
+          lp[((u0 + r) * NT + t) * LP_STRIDE + cs.lane()] = a;
         }
       }
     }
     __syncwarp();
-    if (cs.lane == 0) {
+    if (cs.lane() == 0) {
       *reinterpret_cast<volatile int*>(&sm.free_epoch[cs.slot]) =
-          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G));
+          static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G()));
       mbar_arrive(&sm.empty[cs.slot]);
     }
     if (++cs.slot == NSLOTS) {
@@ -1361,7 +1373,7 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
     }
   }
   named_sync(1, NCT);
-  for (int e = cs.tid; e < nrows * NT; e += NCT) {
+  for (int e = cs.tid(); e < nrows * NT; e += NCT) {
     const float* row = lp + e * LP_STRIDE;
     float a[16];
 #pragma unroll
@@ -1384,15 +1396,15 @@ __device__ void load_rmsnorm_oh(const Params& p, Smem& sm, Cons& cs, const float
                                 const bf16* w, float eps, float* dst, float* hmid, int d0, int d1) {
   float4 x[NT];
   uint2 wv = make_uint2(0u, 0u);
-  if (cs.tid < HID / 4) {
-    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid);
+  if (cs.tid() < HID / 4) {
+    wv = *reinterpret_cast<const uint2*>(w + 4 * cs.tid());
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       float4 parts[NKVH];
 #pragma unroll
       for (int h = 0; h < NKVH; ++h)
-        parts[h] = __ldcg(reinterpret_cast<const float4*>(opart + (h * NTMAX + t) * HID) + cs.tid);
-      const float4 r = h_ld4<false>(hin, t * HID + 4 * cs.tid);
+        parts[h] = __ldcg(reinterpret_cast<const float4*>(opart + (h * NTMAX + t) * HID) + cs.tid());
+      const float4 r = h_ld4<false>(hin, t * HID + 4 * cs.tid());
       float4 a = parts[0];
 #pragma unroll
       for (int h = 1; h < NKVH; ++h) {
@@ -1403,7 +1415,7 @@ __device__ void load_rmsnorm_oh(const Params& p, Smem& sm, Cons& cs, const float
       const float v4[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int idx = 4 * cs.tid + k;
+        const int idx = 4 * cs.tid() + k;
         if (idx >= d0 && idx < d1) __stcg(hmid + t * HID + idx, v4[k]);
       }
     }
@@ -1422,10 +1434,10 @@ __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
   else
     load_rmsnorm_h<NT, false, true>(p, sm, cs, hin, lw->in_norm, p.eps, sm.xs);
   {
-    const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta, cs.G);
+    const Plan pl = make_plan(SK_QKV, nullptr, nullptr, 0, cs.cta(), cs.G());
     if (!gemv<NT, true>(p, pl, sm, cs, sm.xs, HID)) return false;
     const int nr = pl.r1 - pl.r0;
-    for (int e = cs.tid; e < NT * nr; e += NCT) {
+    for (int e = cs.tid(); e < NT * nr; e += NCT) {
       const int t = e / nr, r = e - t * nr;
       __stcg(p.w.qkv + t * QKV_ROWS + pl.r0 + r, sm.part[r * NT + t]);
     }
@@ -1436,10 +1448,10 @@ __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
   if (!attention<NT, true, true>(p, sm, cs, lw, li, p0)) return false;
   {
     int h, r0, r1;
-    if (oh_rows(cs.cta, cs.G, h, r0, r1)) {
+    if (oh_rows(cs.cta(), cs.G(), h, r0, r1)) {
       const int nr = r1 - r0;
       if (!gemv_oh<NT>(p, sm, cs, nr, sm.xs)) return false;
-      for (int e = cs.tid; e < NT * nr; e += NCT) {
+      for (int e = cs.tid(); e < NT * nr; e += NCT) {
         const int t = e / nr, r = e - t * nr;
         __stcg(p.w.prt + (h * NTMAX + t) * HID + r0 + r, sm.part[r * NT + t]);
       }
@@ -1449,7 +1461,7 @@ __device__ bool layer_cp(const Params& p, Smem& sm, Cons& cs, const LayerW* lw, 
 
   // ---- o = sum of head partials + residual; RMSNorm, MLP
   {
-    const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
+    const int d0 = split_lo(HID, cs.G(), cs.cta()), d1 = split_lo(HID, cs.G(), cs.cta() + 1);
     load_rmsnorm_oh<NT, true>(p, sm, cs, p.w.prt, hin, lw->post_norm, p.eps, sm.xs, p.w.hmid, d0, d1);
   }
   return mlp_tail<NT, true>(p, sm, cs, lw, hout_f, hout);
@@ -1463,8 +1475,8 @@ __device__ bool run_stack(const Params& p, Smem& sm, Cons& cs, int p0, HIn* last
   // layer input already in sm.xs; CTA 0 publishes it for the o_proj residual.
   float* hb0 = p.w.hbuf;
   float* hb1 = p.w.hbuf + NTMAX * HID;
-  if (cs.cta == 0)
-    for (int i = cs.tid; i < NT * HID; i += NCT) __stcg(hb0 + i, sm.xs[i]);
+  if (cs.cta() == 0)
+    for (int i = cs.tid(); i < NT * HID; i += NCT) __stcg(hb0 + i, sm.xs[i]);
   HIn h{hb0, nullptr};
   for (int l = 0; l < n; ++l) {
     float* hout_f = (l & 1) ? hb0 : hb1;
@@ -1530,33 +1542,33 @@ __device__ uint32_t radix_threshold(Smem& sm, Cons& cs, const uint32_t (&key)[SP
 #pragma unroll 1
   for (int pass = 0; pass < 2; ++pass) {
     const int shift = pass == 0 ? 8 : 0;
-    for (int i = cs.tid; i < 256; i += NCT) sm.hist[i] = 0;
+    for (int i = cs.tid(); i < 256; i += NCT) sm.hist[i] = 0;
     named_sync(1, NCT);
 #pragma unroll
     for (int j = 0; j < SPT; ++j) {
       if (pass == 0 || (key[j] >> 8) == (prefix >> 8)) atomicAdd(&sm.hist[(key[j] >> shift) & 0xffu], 1);
     }
     named_sync(1, NCT);
-    if (cs.warp == 0) {
+    if (cs.warp() == 0) {
       // lane l owns bins [8l, 8l+8); find the bin where the count from the top reaches need
       int c8 = 0;
 #pragma unroll
-      for (int b = 0; b < 8; ++b) c8 += sm.hist[8 * cs.lane + b];
+      for (int b = 0; b < 8; ++b) c8 += sm.hist[8 * cs.lane() + b];
       int above = 0;  // count in bins strictly above this lane's range
       int s = c8;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_down_sync(0xffffffffu, s, o);
-        if (cs.lane + o < 32) s += v;
+        if (cs.lane() + o < 32) s += v;
       }
       above = s - c8;  // inclusive suffix minus own
       const bool mine = (above < need) && (s >= need);
       const unsigned ballot = __ballot_sync(0xffffffffu, mine);
       const int src = __ffs(ballot) - 1;
-      if (cs.lane == src) {
+      if (cs.lane() == src) {
         int cnt = above;
-        int bin = 8 * cs.lane + 7;
-        for (; bin > 8 * cs.lane; --bin) {
+        int bin = 8 * cs.lane() + 7;
+        for (; bin > 8 * cs.lane(); --bin) {
           if (cnt + sm.hist[bin] >= need) break;
           cnt += sm.hist[bin];
         }
@@ -1575,7 +1587,7 @@ __device__ uint32_t radix_threshold(Smem& sm, Cons& cs, const uint32_t (&key)[SP
 
 __device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& c) {
   float v[SPT];
-  const int base = cs.tid * SPT;
+  const int base = cs.tid() * SPT;
 #pragma unroll
   for (int j = 0; j < SPT; ++j) {
     const int i = base + j;
@@ -1603,9 +1615,9 @@ __device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& 
         bi = oi;
       }
     }
-    if (cs.lane == 0) {
-      sm.red[cs.warp] = bv;
-      sm.red[NCW + cs.warp] = __int_as_float(bi);
+    if (cs.lane() == 0) {
+      sm.red[cs.warp()] = bv;
+      sm.red[NCW + cs.warp()] = __int_as_float(bi);
     }
     named_sync(1, NCT);
     float best = sm.red[0];
@@ -1636,7 +1648,7 @@ __device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& 
   for (int j = 0; j < SPT; ++j)
     if (base + j < c.V && key[j] >= thr) mx = fmaxf(mx, v[j]);
   mx = warp_max(mx);
-  if (cs.lane == 0) sm.red[cs.warp] = mx;
+  if (cs.lane() == 0) sm.red[cs.warp()] = mx;
   named_sync(1, NCT);
   mx = sm.red[0];
   for (int w = 1; w < NCW; ++w) mx = fmaxf(mx, sm.red[w]);
@@ -1663,13 +1675,13 @@ __device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& 
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const unsigned long long n = __shfl_up_sync(0xffffffffu, incl, o);
-    if (cs.lane >= o) incl += n;
+    if (cs.lane() >= o) incl += n;
   }
-  if (cs.lane == 31) sm.ured[cs.warp] = incl;
+  if (cs.lane() == 31) sm.ured[cs.warp()] = incl;
   named_sync(1, NCT);
   unsigned long long wpre = 0, total = 0;
   for (int w = 0; w < NCW; ++w) {
-    if (w < cs.warp) wpre += sm.ured[w];
+    if (w < cs.warp()) wpre += sm.ured[w];
     total += sm.ured[w];
   }
   named_sync(1, NCT);
@@ -1698,13 +1710,13 @@ __device__ __forceinline__ float head_mask(const SampleCfg& c, int i, float x) {
 __device__ int head(const Params& p, Smem& sm, Cons& cs, const bf16* W, int rows, int t, const SampleCfg& c,
                     int call) {
   float* x = sm.xs + t * HID;
-  for (int i = cs.tid; i < HID; i += NCT) x[i] = round_bf16(x[i]);
+  for (int i = cs.tid(); i < HID; i += NCT) x[i] = round_bf16(x[i]);
   named_sync(1, NCT);
-  const Plan pl = make_plan(SK_HEAD, nullptr, W, rows, cs.cta, cs.G);
+  const Plan pl = make_plan(SK_HEAD, nullptr, W, rows, cs.cta(), cs.G());
   if (!gemv<1>(p, pl, sm, cs, x, HID)) return -2;
   const bool greedy = c.do_sample == 0;
   unsigned long long best = 0ull;
-  for (int r = cs.tid; r < pl.r1 - pl.r0; r += NCT) {
+  for (int r = cs.tid(); r < pl.r1 - pl.r0; r += NCT) {
     const float lg = round_bf16(sm.part[r]);
     __stcg(p.w.logits + pl.r0 + r, lg);
     if (greedy) {
@@ -1718,9 +1730,9 @@ __device__ int head(const Params& p, Smem& sm, Cons& cs, const bf16* W, int rows
       const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
-    if (cs.lane == 0) sm.ured[cs.warp] = best;
+    if (cs.lane() == 0) sm.ured[cs.warp()] = best;
     named_sync(1, NCT);
-    if (cs.tid == 0) {
+    if (cs.tid() == 0) {
       unsigned long long b = 0ull;
       for (int w = 0; w < NCW; ++w) b = sm.ured[w] > b ? sm.ured[w] : b;
       if (b != 0ull) atomicMax(p.w.amax + (call & 1), b);
@@ -1730,7 +1742,7 @@ __device__ int head(const Params& p, Smem& sm, Cons& cs, const bf16* W, int rows
   if (!greedy) return -1;
   const unsigned long long k = __ldcg(p.w.amax + (call & 1));
   named_sync(1, NCT);   // every thread has read the slot before it can be reused
-  if (cs.cta == 0 && cs.tid == 0) p.w.amax[(call + 1) & 1] = 0ull;   // next call's slot
+  if (cs.cta() == 0 && cs.tid() == 0) p.w.amax[(call + 1) & 1] = 0ull;   // next call's slot
   return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
 }
 
@@ -1743,7 +1755,7 @@ __device__ __forceinline__ uint32_t draw_u24(const Sampling& sp, int frame, int 
 
 // Write a bf16 row (as fp32) into NT slot t of sm.xs.
 __device__ __forceinline__ void xs_from_bf16(Cons& cs, float* dst, const bf16* src) {
-  for (int i = cs.tid; i < HID; i += NCT) dst[i] = __bfloat162float(src[i]);
+  for (int i = cs.tid(); i < HID; i += NCT) dst[i] = __bfloat162float(src[i]);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1757,7 +1769,7 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   const int step = ld_volatile_i32(&st->step);
   if (done) return true;
   if (g0 == p.sp.eos) {  // generator.py:126
-    if (cs.cta == 0 && cs.tid == 0) st->done = 1;
+    if (cs.cta() == 0 && cs.tid() == 0) st->done = 1;
     return true;
   }
   if (g0 < 0 || g0 >= p.vocab) {
@@ -1768,12 +1780,12 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
     fail(p, sm, DEV_ERR_BAD_POSITION);
     return false;
   }
-  if (cs.cta == 0 && cs.tid == 0) st->seen[g0] = 1;  // generated_g0.append (generator.py:129)
+  if (cs.cta() == 0 && cs.tid() == 0) st->seen[g0] = 1;  // generated_g0.append (generator.py:129)
 
   int toks[NGROUPS];
   toks[0] = g0;
   // ---- code-predictor pass 0: [bf16(h), codec_embedding[g0]] at positions 0, 1
-  for (int i = cs.tid; i < HID; i += NCT) {
+  for (int i = cs.tid(); i < HID; i += NCT) {
     sm.xs[i] = round_bf16(__ldcg(st->h + i));
     sm.xs[HID + i] = __bfloat162float(p.codec_emb[static_cast<size_t>(g0) * HID + i]);
   }
@@ -1800,14 +1812,14 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
     c.u24 = c.do_sample ? draw_u24(p.sp, step, g + 1) : 0u;
     const int tk = head(p, sm, cs, p.cp_head[g], p.cp_vocab, g == 0 ? 1 : 0, c, g);
     if (tk == -2) return false;
-    if (p.dbg_cp_logits && cs.cta == 0)
-      for (int i = cs.tid; i < p.cp_vocab; i += NCT) p.dbg_cp_logits[g * p.cp_vocab + i] = __ldcg(p.w.logits + i);
+    if (p.dbg_cp_logits && cs.cta() == 0)
+      for (int i = cs.tid(); i < p.cp_vocab; i += NCT) p.dbg_cp_logits[g * p.cp_vocab + i] = __ldcg(p.w.logits + i);
     toks[g + 1] = tk >= 0 ? tk : sample(p.w.logits, sm, cs, c);
   }
   // ---- combine (generator.py:143-149,356-362): sequential bf16 adds
   {
     const bf16* extra = step < p.n_trailing ? p.trailing + static_cast<size_t>(step) * HID : p.pad;
-    for (int i = cs.tid; i < HID; i += NCT) {
+    for (int i = cs.tid(); i < HID; i += NCT) {
       float a = __bfloat162float(p.codec_emb[static_cast<size_t>(g0) * HID + i]);
 #pragma unroll 1
       for (int q = 0; q < NCPHEADS; ++q)
@@ -1818,8 +1830,8 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   }
   // ---- backbone step at position pos
   if (!run_stack<1, false>(p, sm, cs, pos)) return false;
-  if (cs.cta == 0)
-    for (int i = cs.tid; i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
+  if (cs.cta() == 0)
+    for (int i = cs.tid(); i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
   SampleCfg c;
   c.V = p.vocab;
   c.do_sample = p.sp.do_sample;
@@ -1833,10 +1845,10 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   c.u24 = c.do_sample ? draw_u24(p.sp, step + 1, 0) : 0u;
   const int tk = head(p, sm, cs, p.codec_head, p.vocab, 0, c, NCPHEADS);
   if (tk == -2) return false;
-  if (p.dbg_g0_logits && cs.cta == 0)
-    for (int i = cs.tid; i < p.vocab; i += NCT) p.dbg_g0_logits[i] = __ldcg(p.w.logits + i);
+  if (p.dbg_g0_logits && cs.cta() == 0)
+    for (int i = cs.tid(); i < p.vocab; i += NCT) p.dbg_g0_logits[i] = __ldcg(p.w.logits + i);
   const int g0n = tk >= 0 ? tk : sample(p.w.logits, sm, cs, c);
-  if (cs.cta == 0 && cs.tid == 0) {
+  if (cs.cta() == 0 && cs.tid() == 0) {
     int32_t* out = p.codes + static_cast<size_t>(step) * NGROUPS;
     for (int g = 0; g < NGROUPS; ++g) out[g] = toks[g];
     st->g0 = g0n;
@@ -1858,8 +1870,8 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
   HIn last{nullptr, nullptr};
   const bool ok = cp ? run_stack<1, true>(p, sm, cs, pos, &last) : run_stack<1, false>(p, sm, cs, pos, &last);
   if (!ok) return false;
-  if (cs.cta == 0) {
-    for (int i = cs.tid; i < HID; i += NCT) {
+  if (cs.cta() == 0) {
+    for (int i = cs.tid(); i < HID; i += NCT) {
       if (p.out_hidden) p.out_hidden[i] = sm.xs[i];
       if (p.out_raw_hidden) p.out_raw_hidden[i] = __float2bfloat16_rn(cp ? h_ld<false>(last, i) : h_ld<true>(last, i));
     }
@@ -1867,8 +1879,8 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
   if (!cp && (p.flags & FLAG_HEAD_SAMPLE)) {
     // end of prefill: first group-0 token (generator.py:115-120), no repetition history
     StreamState* st = p.st;
-    if (cs.cta == 0)
-      for (int i = cs.tid; i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
+    if (cs.cta() == 0)
+      for (int i = cs.tid(); i < HID; i += NCT) __stcg(st->h + i, sm.xs[i]);
     SampleCfg c;
     c.V = p.vocab;
     c.do_sample = p.sp.do_sample;
@@ -1883,7 +1895,7 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
     const int tk = head(p, sm, cs, p.codec_head, p.vocab, 0, c, 0);
     if (tk == -2) return false;
     const int g0 = tk >= 0 ? tk : sample(p.w.logits, sm, cs, c);
-    if (cs.cta == 0 && cs.tid == 0) {
+    if (cs.cta() == 0 && cs.tid() == 0) {
       st->g0 = g0;
       st->position = pos + 1;
       st->step = 0;
@@ -1932,15 +1944,10 @@ extern "C" __global__ void __launch_bounds__(NTHREADS, 1) qtt_decode_kernel(cons
   cs.slot = 0;
   cs.round = 0;
   cs.bar_target = 0;
-  cs.cta = blockIdx.x;
-  cs.G = gridDim.x;
-  cs.tid = tid;
-  cs.warp = warp;
-  cs.lane = tid & 31;
   cs.dk = 0;
   if (p.bb_wd_map != nullptr || p.cp_wd_map != nullptr) {
     // the first fused MLP stage (several barriers away) accumulates into hacc[0]
-    const int d0 = split_lo(HID, cs.G, cs.cta), d1 = split_lo(HID, cs.G, cs.cta + 1);
+    const int d0 = split_lo(HID, cs.G(), cs.cta()), d1 = split_lo(HID, cs.G(), cs.cta() + 1);
     for (int e = tid; e < NTMAX * (d1 - d0); e += NCT) {
       const int t = e / (d1 - d0), r = d0 + e % (d1 - d0);
       __stcg(p.w.hacc + t * HID + r, 0ll);
@@ -1963,9 +1970,7 @@ size_t bwork_bytes() {
   size_t n = 256;
   n += sizeof(unsigned long long) * 5 * TBMAX;                       // ssq, amax
   n += sizeof(uint32_t) * TBMAX * NKVH;                              // att_cnt
-  n += sizeof(int32_t) * BMAX * NGROUPS;                             // tok
-  n += sizeof(uint32_t) * BKCTAS;                                    // kcnt
-  n += sizeof(float) * BKCTAS * TBMAX * KPAD + 256;                  // kpart
+  n += sizeof(int32_t) * BMAX * NGROUPS + 256;                       // tok
   n += 2 * sizeof(bf16) * 2 * TBMAX * ABUF_LD;                      // abuf
   n += sizeof(float) * TBMAX * HID * 3;                              // x, hb[2]
   n += sizeof(float) * TBMAX * QKV_ROWS;                             // qkv
@@ -1982,7 +1987,6 @@ void bwork_carve(void* base, BWork* w) {
   w->amax = reinterpret_cast<unsigned long long*>(c); c += sizeof(unsigned long long) * 2 * TBMAX;
   w->att_cnt = reinterpret_cast<uint32_t*>(c); c += sizeof(uint32_t) * TBMAX * NKVH;
   w->tok = reinterpret_cast<int32_t*>(c); c += sizeof(int32_t) * BMAX * NGROUPS;
-  w->kcnt = reinterpret_cast<uint32_t*>(c); c += sizeof(uint32_t) * BKCTAS;
   c = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c) + 255) & ~static_cast<uintptr_t>(255));
   for (int i = 0; i < 2; ++i) {
     w->abuf[i] = reinterpret_cast<bf16*>(c);
@@ -1996,37 +2000,70 @@ void bwork_carve(void* base, BWork* w) {
   w->qkv = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * QKV_ROWS;
   w->hmid = reinterpret_cast<float*>(c); c += sizeof(float) * TBMAX * HID;
   w->logits = reinterpret_cast<float*>(c); c += sizeof(float) * BMAX * VMAX;
-  w->kpart = reinterpret_cast<float*>(c); c += sizeof(float) * BKCTAS * TBMAX * KPAD;
   w->prt = reinterpret_cast<float*>(c);
 }
 
-cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes) {
+namespace {
+// Launch configuration of the batched kernel: clusters of `cluster` CTAs. The launch is not
+// cooperative (profilers replay cluster launches only without that attribute); the grid is sized
+// from cudaOccupancyMaxActiveClusters so that every CTA is resident at once, which the grid
+// barrier needs, and every wait is bounded, so a CTA that could not be placed ends the launch with
+// a timeout error rather than a hang.
+cudaLaunchConfig_t batch_config(int num_ctas, int cluster, size_t smem_bytes, cudaStream_t stream,
+                                cudaLaunchAttribute (&attrs)[1]) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_ctas);
+  cfg.blockDim = dim3(NTHREADS_B);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+}  // namespace
+
+cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes, int* cluster) {
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return e;
   const size_t smem = sizeof(Smem);
   e = cudaFuncSetAttribute(qtt_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  int sms = 0, per_sm = 0;
+  int sms = 0;
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qtt_batch_kernel, NTHREADS_B, smem);
-  if (e != cudaSuccess) return e;
-  if (per_sm < 1) return cudaErrorInvalidConfiguration;
-  *num_ctas = sms;
-  *smem_bytes = smem;
-  return cudaSuccess;
+  for (int c = 4; c >= 2; c /= 2) {
+    cudaLaunchAttribute attrs[1];
+    cudaLaunchConfig_t cfg = batch_config(c * (sms / c), c, smem, nullptr, attrs);
+    int ncl = 0;
+    e = cudaOccupancyMaxActiveClusters(&ncl, reinterpret_cast<const void*>(qtt_batch_kernel), &cfg);
+    if (e != cudaSuccess) return e;
+    int ctas = c * ncl;
+    if (ctas > BKCTAS) ctas = (BKCTAS / c) * c;
+    if (ctas > sms) ctas = (sms / c) * c;
+    if (ctas >= BROWS_B) {
+      *num_ctas = ctas;
+      *smem_bytes = smem;
+      *cluster = c;
+      return cudaSuccess;
+    }
+  }
+  return cudaErrorInvalidConfiguration;
 }
 
 cudaError_t launch_b(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(p.w.bar, 0, sizeof(uint32_t), stream);
   if (e != cudaSuccess) return e;
-  // ssq, amax, att_cnt, tok and the K-split counters are contiguous at the start of the workspace
-  const size_t head = reinterpret_cast<const char*>(p.bw.kcnt + BKCTAS) - reinterpret_cast<const char*>(p.bw.ssq);
+  // ssq, amax, att_cnt and tok are contiguous at the start of the workspace
+  const size_t head = reinterpret_cast<const char*>(p.bw.tok + BMAX * NGROUPS) - reinterpret_cast<const char*>(p.bw.ssq);
   e = cudaMemsetAsync(p.bw.ssq, 0, head, stream);
   if (e != cudaSuccess) return e;
-  void* args[] = {const_cast<Params*>(&p)};
-  return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(qtt_batch_kernel), dim3(num_ctas), dim3(NTHREADS_B),
-                                     args, smem_bytes, stream);
+  cudaLaunchAttribute attrs[1];
+  cudaLaunchConfig_t cfg = batch_config(num_ctas, p.bcl, smem_bytes, stream, attrs);
+  return cudaLaunchKernelEx(&cfg, qtt_batch_kernel, p);
 }
 
 cudaError_t kernel_setup(int device, int* num_ctas, size_t* smem_bytes) {

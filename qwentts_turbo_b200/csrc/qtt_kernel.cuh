@@ -152,11 +152,11 @@ struct BWork {
   unsigned long long* ssq; // [3][TBMAX] sums of squares for the next RMSNorm, fixed point 2^-32
   unsigned long long* amax;// [2][TBMAX] packed argmax of greedy heads
   int32_t* tok;            // [BMAX][NGROUPS] tokens of the frame
-  float* kpart;            // [BKCTAS][TBMAX][64] K-split GEMM partials, one block per CTA
-  uint32_t* kcnt;          // [BKCTAS] last-arriver counters of K-split row blocks
 };
-constexpr int BKCTAS = 160;
-constexpr int BNMAX = 128;                 // batched GEMM: weight rows per CTA tile (one TMA box per atom)               // most CTAs a batched launch may have
+// Batched GEMM tiling: 128 CTAs per GEMM stage, as BROWS_B / C row tiles (one per cluster of C
+// CTAs) x C K slices (one per CTA of the cluster).
+constexpr int BROWS_B = 128;
+constexpr int BKCTAS = 160;                // most CTAs a batched launch may have
 size_t bwork_bytes();
 void bwork_carve(void* base, BWork* w);
 
@@ -197,6 +197,7 @@ struct Params {
   // [abuf 0 box 64, abuf 0 box 128, abuf 1 box 64, abuf 1 box 128]
   const uint8_t* bmaps;
   int nb;                  // utterances of the batched launch
+  int bcl;                 // CTAs per thread-block cluster of the batched launch (4 or 2)
   const BStream* bs;       // [nb]
   BWork bw;
   int b_step;              // MODE_B_PREFILL: context index of this step; DENSE: first position
@@ -249,8 +250,10 @@ struct Params {
 cudaError_t kernel_setup(int device, int* num_ctas, size_t* smem_bytes);
 // Host side: zero the barrier counter and cooperatively launch one program.
 cudaError_t launch(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream);
-// Batched kernel: the same for qtt_batch_kernel (also clears the sums-of-squares and argmax words).
-cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes);
+// Batched kernel: the same for qtt_batch_kernel (also clears the sums-of-squares and argmax words),
+// launched as clusters of *cluster CTAs: 4 when at least 128 / 4 clusters of 4 fit on the device,
+// else 2; num_ctas = cluster x the clusters that fit (at most BKCTAS).
+cudaError_t kernel_setup_b(int device, int* num_ctas, size_t* smem_bytes, int* cluster);
 cudaError_t launch_b(const Params& p, int num_ctas, size_t smem_bytes, cudaStream_t stream);
 // Error code of the last qtt_backbone_step_noalloc on device `dev` (0: none, or the path is
 // unused there); clears it. Defined with the fixed scratch in qtt_noalloc.cu.
