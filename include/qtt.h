@@ -172,7 +172,9 @@ typedef struct qtt_weights {
 } qtt_weights;
 
 /* Sampling options of NativeTTSGenerator.generate (generator.py:77-81). Draws are
- * Philox4x32-10 keyed by `seed`, counter (frame, group, philox_stream, 0). top_p must be 1. */
+ * Philox4x32-10 keyed by `seed`, counter (frame, group, philox_stream, 0). top_p < 1 applies the
+ * nucleus filter to group 0 after top-k (generator.py:196-203; the code predictor samples with
+ * top_p = 1 as in generator.py:332,352); NaN or negative top_p is an invalid argument. */
 typedef struct qtt_sampling {
   int do_sample;
   float temperature;

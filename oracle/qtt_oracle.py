@@ -149,6 +149,30 @@ def argmax_first(x: torch.Tensor) -> int:
     return int(torch.nonzero(x == m)[0, 0])
 
 
+def filter_logits(logits: torch.Tensor, temperature: float, top_k: int, top_p: float = 1.0) -> torch.Tensor:
+    """generator.py:188-203: scaled = bf16(l / T), top-k keeps values >= the k-th (ties kept), and
+    top-p (nucleus) on the bf16 tensors the reference uses: the values sorted descending (ties in
+    index order), probs = bf16(softmax), cum = bf16(fp32 running sum), and entry i of the sorted
+    order removed when cum[i - 1] > bf16(top_p) (torch compares a bf16 tensor with a Python float in
+    bf16). Returns the filtered scaled logits (-inf = removed), fp32."""
+    scaled = bf16r(logits.to(torch.float32) / temperature)
+    if top_k > 0:
+        k = min(top_k, scaled.shape[-1])
+        thr = torch.topk(scaled, k)[0][-1]
+        scaled[scaled < thr] = float("-inf")
+    if top_p < 1.0:
+        sorted_logits, sorted_idx = torch.sort(scaled, descending=True, stable=True)
+        e = torch.exp(sorted_logits - sorted_logits[0])
+        probs = bf16r(e / e.sum())
+        cum = bf16r(torch.cumsum(probs, dim=-1))
+        remove = cum > bf16r(torch.tensor(float(top_p)))
+        remove[1:] = remove[:-1].clone()
+        remove[0] = False
+        sorted_logits[remove] = float("-inf")
+        scaled = scaled.scatter(0, sorted_idx, sorted_logits)
+    return scaled
+
+
 def sample_token(logits: torch.Tensor, do_sample: bool, temperature: float, top_k: int,
                  top_p: float = 1.0, suppress_eos_id=None, u24: int | None = None) -> int:
     """generator.py:178-207 with the multinomial draw replaced by :func:`inverse_cdf_pick`.
@@ -160,19 +184,7 @@ def sample_token(logits: torch.Tensor, do_sample: bool, temperature: float, top_
         logits[suppress_eos_id] = float("-inf")
     if not do_sample:
         return argmax_first(logits)
-    scaled = bf16r(logits / temperature)
-    if top_k > 0:
-        k = min(top_k, scaled.shape[-1])
-        thr = torch.topk(scaled, k)[0][-1]
-        scaled[scaled < thr] = float("-inf")
-    if top_p < 1.0:
-        sorted_logits, sorted_idx = torch.sort(scaled, descending=True, stable=True)
-        cum = torch.cumsum(torch.softmax(sorted_logits, dim=-1), dim=-1)
-        remove = cum > top_p
-        remove[1:] = remove[:-1].clone()
-        remove[0] = False
-        sorted_logits[remove] = float("-inf")
-        scaled = scaled.scatter(0, sorted_idx, sorted_logits)
+    scaled = filter_logits(logits, temperature, top_k, top_p)
     mx = scaled.max()
     e = torch.exp(scaled - mx)
     probs = bf16r(e / e.sum())

@@ -328,7 +328,7 @@ qtt_status set_device(const qtt_engine* e) { return from_cuda(cudaSetDevice(e->d
 
 qtt_status check_sampling(const qtt_sampling* sp, const qtt_engine* e) {
   if (!sp) return QTT_ERR_INVALID_ARG;
-  if (sp->top_p < 1.0f) return QTT_ERR_UNSUPPORTED;
+  if (!(sp->top_p >= 0.f)) return QTT_ERR_INVALID_ARG;   // NaN or negative
   if (sp->do_sample && !(sp->temperature > 0.f)) return QTT_ERR_INVALID_ARG;
   if (sp->cp_do_sample && !(sp->cp_temperature > 0.f)) return QTT_ERR_INVALID_ARG;
   if (!(sp->repetition_penalty > 0.f)) return QTT_ERR_INVALID_ARG;
@@ -349,6 +349,7 @@ qtt::Sampling to_dev(const qtt_sampling* sp) {
   s.eos = sp->eos_token_id;
   s.philox_stream = sp->philox_stream;
   s.seed = sp->seed;
+  s.top_p = sp->top_p;
   return s;
 }
 

@@ -37,6 +37,10 @@
 // frame adds COMBINE (the 16-embedding sum + text row) before the backbone layers and the
 // codec head (+ sampler) at the end.
 
+// The batched kernel's grid barrier as a call of its own: its spin loop then keeps its few values
+// in registers rather than sharing the caller's register budget.
+__device__ __noinline__ bool grid_sync_b(const Params& p, Smem& sm, Cons& cs) { return grid_sync(p, sm, cs); }
+
 constexpr int KSUB = 64;                  // K elements of one 128-byte swizzle atom row
 constexpr int NSUB = 2;                   // atoms per pipeline step
 constexpr int KSTEP = KSUB * NSUB;        // K elements per pipeline step
@@ -530,7 +534,7 @@ __device__ __forceinline__ BStage b_gemm_begin(const Params& p, Smem& sm, Cons& 
 }
 
 // Step 2 up to the cluster's partials being staged; false on abort.
-__device__ __noinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, const BStage S, uint32_t gemm_n) {
+__device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, const BStage S, uint32_t gemm_n) {
   const bool tr = p.dbg_marks != nullptr && cs.tid() == 0;
   if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
     if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
@@ -638,11 +642,11 @@ __device__ __forceinline__ void b_reduce_item(const BStage& S, int t, int c, flo
   }
 }
 
-__device__ __noinline__ bool b_gemm_end(const Params& p, Smem& sm, Cons& cs, int gi, bool planes) {
+__device__ __forceinline__ bool b_gemm_end(const Params& p, Smem& sm, Cons& cs, int gi, bool planes) {
   fence_proxy_async_smem();   // the partials alias the activation ring: before the next stage's TMA writes
   if (planes) fence_proxy_async_global();   // the epilogue wrote the next GEMM's operand planes
   if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, gi, cs.cta(), cs.G(), BT_EPI);
-  const bool ok = grid_sync(p, sm, cs);
+  const bool ok = grid_sync_b(p, sm, cs);
   if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, gi, cs.cta(), cs.G(), BT_BARRIER);
   return ok;
 }
@@ -651,15 +655,17 @@ template <class PRE, class RUN>
 __device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, PRE&& pre,
                                        RUN&& run) {
   const BStage S = b_gemm_begin(p, sm, cs, g);
-  if (!S.sp.act) return grid_sync(p, sm, cs);
+  if (!S.sp.act) return grid_sync_b(p, sm, cs);
   const bool ok = b_gemm_mid(p, sm, cs, S, gemm_n);
   if (ok) {
     for (int i = S.i0 + cs.tid(); i < S.i1; i += NCT) {
       const int t = i / S.nci, c = i - t * S.nci, r0 = S.r0b + EW * c;
-      float y[EW], y2[EW];
-      b_reduce_item(S, t, c, y, y2);
+      // the item's inputs that do not depend on D first: their L2 loads overlap the partials'
+      // distributed shared memory loads
       EpiSt st;
       pre(t, r0, st);
+      float y[EW], y2[EW];
+      b_reduce_item(S, t, c, y, y2);
       run(t, r0, y, y2, st);
     }
   }
@@ -690,7 +696,7 @@ __device__ __forceinline__ void b_ssq_add(unsigned long long* ssq, int t, double
 // (the async proxy) after the barrier: every writer orders its stores for that proxy first.
 __device__ __forceinline__ bool b_sync_planes(const Params& p, Smem& sm, Cons& cs) {
   fence_proxy_async_global();
-  return grid_sync(p, sm, cs);
+  return grid_sync_b(p, sm, cs);
 }
 
 // Elementwise stages over T tokens x HID columns: CTA c owns 8-column units
@@ -1075,7 +1081,7 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
           *reinterpret_cast<uint4*>(p.bs[0].v + off) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
         }
       }
-      if (!grid_sync(p, sm, cs)) return false;
+      if (!grid_sync_b(p, sm, cs)) return false;
     }
     auto row_len = [&](int v) -> int {   // context length of row v (0: inactive)
       if (dense) return p0d + v + 1;
@@ -1341,7 +1347,7 @@ __device__ __noinline__ bool b_tokens(const Params& p, Smem& sm, Cons& cs, int h
     const int tk = sample(p.bw.logits + static_cast<size_t>(s) * VMAX, sm, cs, c);
     if (cs.tid() == 0) __stcg(p.bw.tok + s * NGROUPS + col, tk);
   }
-  return grid_sync(p, sm, cs);
+  return grid_sync_b(p, sm, cs);
 }
 
 __device__ SampleCfg b_codec_cfg(const Params& p, float penalty) {
@@ -1350,6 +1356,7 @@ __device__ SampleCfg b_codec_cfg(const Params& p, float penalty) {
   c.do_sample = p.sp.do_sample;
   c.temperature = p.sp.temperature;
   c.top_k = p.sp.top_k;
+  c.top_p = p.sp.top_p;
   c.suppress_from = p.vocab - 1024;
   c.eos = p.sp.eos;
   c.mask_eos = 0;
@@ -1373,6 +1380,7 @@ __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
   cpc.do_sample = p.sp.cp_do_sample;
   cpc.temperature = p.sp.cp_temperature;
   cpc.top_k = p.sp.cp_top_k;
+  cpc.top_p = 1.f;
   cpc.suppress_from = p.cp_vocab;
   cpc.eos = -1;
   cpc.mask_eos = 0;
@@ -1532,7 +1540,7 @@ __device__ bool b_first_token(const Params& p, Smem& sm, Cons& cs) {
       p.bw.abuf[1][static_cast<size_t>(TBMAX + s) * ABUF_LD + k0 + j] = __float2bfloat16_rn(0.f);
     }
   });
-  if (!grid_sync(p, sm, cs)) return false;
+  if (!grid_sync_b(p, sm, cs)) return false;
   const SampleCfg c = b_codec_cfg(p, 1.f);
   if (!b_head(p, sm, cs, gn, 0, c, 0)) return false;
   if (!b_tokens(p, sm, cs, 0, c, 0, 0, 0)) return false;

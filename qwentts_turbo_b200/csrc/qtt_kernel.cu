@@ -452,9 +452,8 @@ __device__ __forceinline__ void prologue_mark(const Params& p, const Cons& cs, i
   }
 }
 
-// Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded). Not
-// inlined: its spin loop keeps its few values in registers instead of sharing the caller's.
-__device__ __noinline__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
+// Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded).
+__device__ __forceinline__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
   named_sync(1, NCT);
   if (cs.tid() == 0) {
     stage_mark(p, cs, 2);
@@ -660,6 +659,7 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
     return false;
   }
   float* lp = reinterpret_cast<float*>(sm.att);   // [units * NT][LP_STRIDE] lane partials
+  uint32_t slot = cs.slot, round = cs.round;   // ring position in registers for the stage
   const int part = cs.warp() % pl.P;
   float xr[NT][32];
 #pragma unroll
@@ -693,12 +693,12 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
   for (int u0 = 0; u0 < pl.units; u0 += SLOT_UNITS) {
     const int n = min(SLOT_UNITS, pl.units - u0);
     unsigned long long tw = prof ? globaltimer_ns() : 0ull;
-    const bool got = mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort);
+    const bool got = mbar_wait(&sm.full[slot], round & 1u, &sm.abort);
     if (prof) waited += globaltimer_ns() - tw;
     if (!got) {
       if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
     } else if (cs.warp() < n) {
-      const uint4* src = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + cs.warp() * UNIT_BYTES);
+      const uint4* src = reinterpret_cast<const uint4*>(sm.ring[slot] + cs.warp() * UNIT_BYTES);
       // four independent FMA chains (one per 16-byte chunk) keep the dependent chain short
       float ch[NT][4];
 #pragma unroll
@@ -721,15 +721,17 @@ __device__ bool gemv(const Params& p, const Plan& pl, Smem& sm, Cons& cs, const 
     }
     __syncwarp();
     if (cs.lane() == 0) {
-      *reinterpret_cast<volatile int*>(&sm.free_epoch[cs.slot]) =
+      *reinterpret_cast<volatile int*>(&sm.free_epoch[slot]) =
           static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G()));
-      mbar_arrive(&sm.empty[cs.slot]);
+      mbar_arrive(&sm.empty[slot]);
     }
-    if (++cs.slot == NSLOTS) {
-      cs.slot = 0;
-      cs.round++;
+    if (++slot == NSLOTS) {
+      slot = 0;
+      round++;
     }
   }
+  cs.slot = slot;
+  cs.round = round;
   if (prof) {
     const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
     if (static_cast<int>(k) < p.dbg_marks_len / 3 - 1024) p.dbg_marks[3 * 1024 + k] = waited;
@@ -1203,19 +1205,22 @@ __device__ bool mlp_fused(const Params& p, Smem& sm, Cons& cs, const LayerW* lw,
   named_sync(1, NCT);
 
   uint32_t sl[WD_SLOTS];
+  uint32_t slot = cs.slot, round = cs.round;   // ring position in registers for the stage
   bool ok = true;
 #pragma unroll
   for (int i = 0; i < WD_SLOTS; ++i) {
-    sl[i] = cs.slot;
-    if (ok && !mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort)) {
+    sl[i] = slot;
+    if (ok && !mbar_wait(&sm.full[slot], round & 1u, &sm.abort)) {
       if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
       ok = false;
     }
-    if (++cs.slot == NSLOTS) {
-      cs.slot = 0;
-      cs.round++;
+    if (++slot == NSLOTS) {
+      slot = 0;
+      round++;
     }
   }
+  cs.slot = slot;
+  cs.round = round;
   if (p.dbg_marks != nullptr && cs.cta() == 0 && cs.tid() == 0) {   // profiling: W_down boxes ready
     const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
     if (static_cast<int>(4 * 1024 + 4 * k + 3) < p.dbg_marks_len) p.dbg_marks[4 * 1024 + 4 * k + 3] = globaltimer_ns();
@@ -1335,6 +1340,7 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
     return false;
   }
   float* lp = reinterpret_cast<float*>(sm.att);
+  uint32_t slot = cs.slot, round = cs.round;   // ring position in registers for the stage
   float xr[NT][8];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
@@ -1345,11 +1351,11 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
   }
   for (int u0 = 0; u0 < nrows; u0 += OH_ROWS_PER_SLOT) {
     const int m = min(OH_ROWS_PER_SLOT, nrows - u0);
-    if (!mbar_wait(&sm.full[cs.slot], cs.round & 1u, &sm.abort)) {
+    if (!mbar_wait(&sm.full[slot], round & 1u, &sm.abort)) {
       if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
     } else {
       for (int r = cs.warp(); r < m; r += NCW) {
-        const uint4 v = reinterpret_cast<const uint4*>(sm.ring[cs.slot] + r * OH_ROW_BYTES)[cs.lane()];
+        const uint4 v = reinterpret_cast<const uint4*>(sm.ring[slot] + r * OH_ROW_BYTES)[cs.lane()];
         const float w[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
                             bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
 #pragma unroll
@@ -1363,15 +1369,17 @@ __device__ bool gemv_oh(const Params& p, Smem& sm, Cons& cs, int nrows, const fl
     }
     __syncwarp();
     if (cs.lane() == 0) {
-      *reinterpret_cast<volatile int*>(&sm.free_epoch[cs.slot]) =
+      *reinterpret_cast<volatile int*>(&sm.free_epoch[slot]) =
           static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G()));
-      mbar_arrive(&sm.empty[cs.slot]);
+      mbar_arrive(&sm.empty[slot]);
     }
-    if (++cs.slot == NSLOTS) {
-      cs.slot = 0;
-      cs.round++;
+    if (++slot == NSLOTS) {
+      slot = 0;
+      round++;
     }
   }
+  cs.slot = slot;
+  cs.round = round;
   named_sync(1, NCT);
   for (int e = cs.tid(); e < nrows * NT; e += NCT) {
     const float* row = lp + e * LP_STRIDE;
@@ -1525,6 +1533,7 @@ struct SampleCfg {
   float penalty;
   const uint8_t* seen; // nullptr = no repetition penalty
   uint32_t u24;
+  float top_p;         // nucleus filter (generator.py:196-203); >= 1: off (the code predictor)
 };
 
 constexpr int SPT = VMAX / NCT;  // 8 entries per thread
@@ -1585,6 +1594,79 @@ __device__ uint32_t radix_threshold(Smem& sm, Cons& cs, const uint32_t (&key)[SP
   return prefix;
 }
 
+// Nucleus (top-p) filter of generator.py:196-203 on the entries the top-k filter kept: sort
+// them by value, descending, ties in index order (a bitonic sort of 4096 keys (bf16 value, index)
+// in sm.att), bf16 softmax over the sorted values, running sum in sorted order (fp32, each value
+// rounded to bf16 as torch.cumsum on a bf16 tensor), and keep the sorted prefix up to and including
+// the first entry whose running sum exceeds bf16(top_p) (the comparison runs in bf16).
+constexpr int NSORT = 4096;
+static_assert(NSORT * 4 <= ATT_STAGE_BYTES && NSORT >= VMAX, "nucleus sort buffer fits sm.att");
+__device__ __noinline__ void nucleus_filter(Smem& sm, Cons& cs, const SampleCfg& c, const float (&v)[SPT],
+                                            const uint32_t (&key)[SPT], bool (&kept)[SPT]) {
+  uint32_t* sk = reinterpret_cast<uint32_t*>(sm.att);
+  const int base = cs.tid() * SPT;
+  auto ckey = [&](int j) {   // larger value first, then smaller index; 0 = not a candidate
+    return (kept[j] && v[j] != -INFINITY) ? ((key[j] << 16) | (0xFFFFu - static_cast<uint32_t>(base + j))) : 0u;
+  };
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) sk[base + j] = ckey(j);
+  for (int i = NCT * SPT + cs.tid(); i < NSORT; i += NCT) sk[i] = 0u;
+  named_sync(1, NCT);
+  for (int k = 2; k <= NSORT; k <<= 1)
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      for (int i = cs.tid(); i < NSORT; i += NCT) {
+        const int l = i ^ jj;
+        if (l > i) {
+          const uint32_t a = sk[i], b = sk[l];
+          // descending order overall: blocks with (i & k) == 0 sort descending
+          const bool desc = (i & k) == 0;
+          if (desc ? (a < b) : (a > b)) {
+            sk[i] = b;
+            sk[l] = a;
+          }
+        }
+      }
+      named_sync(1, NCT);
+    }
+  // thread 0: softmax over the sorted candidates and the running sum in sorted order
+  if (cs.tid() == 0) {
+    auto val = [&](uint32_t k32) {   // the bf16 value of a key
+      const uint32_t b = k32 >> 16;
+      const uint32_t bits = (b & 0x8000u) ? (b & 0x7fffu) : (~b & 0xffffu);
+      return __uint_as_float(bits << 16);
+    };
+    int n = 0;
+    while (n < NSORT && sk[n] != 0u) ++n;
+    uint32_t cut = 0u;
+    if (n > 0) {
+      // bf16 tensors as in the reference: probs = bf16(softmax), cum = bf16(fp32 running sum),
+      // compared with bf16(top_p)
+      const float mx = val(sk[0]);
+      float es = 0.f;
+      for (int i = 0; i < n; ++i) es += expf(val(sk[i]) - mx);
+      const float tp = round_bf16(c.top_p);
+      float cum = 0.f;
+      int last = n - 1;
+      for (int i = 0; i < n; ++i) {
+        cum += round_bf16(__fdiv_rn(expf(val(sk[i]) - mx), es));
+        if (round_bf16(cum) > tp) {
+          last = i;
+          break;
+        }
+      }
+      cut = sk[last];
+    }
+    sm.bcast[3] = static_cast<int>(cut);
+  }
+  named_sync(1, NCT);
+  const uint32_t cut = static_cast<uint32_t>(sm.bcast[3]);
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) kept[j] = kept[j] && ckey(j) >= cut && cut != 0u;
+  named_sync(1, NCT);
+  // sm.att lies in the batched kernel's activation ring, written next by TMA
+  fence_proxy_async_smem();
+}
+
 __device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& c) {
   float v[SPT];
   const int base = cs.tid() * SPT;
@@ -1642,11 +1724,15 @@ __device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& 
   }
   uint32_t thr = 0;
   if (c.top_k > 0 && c.top_k < c.V) thr = radix_threshold(sm, cs, key, c.top_k);
+  bool kept[SPT];
+#pragma unroll
+  for (int j = 0; j < SPT; ++j) kept[j] = base + j < c.V && key[j] >= thr;
+  if (c.top_p < 1.f) nucleus_filter(sm, cs, c, v, key, kept);
   // softmax over kept entries (probabilities rounded to bf16 as torch.softmax on bf16)
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < SPT; ++j)
-    if (base + j < c.V && key[j] >= thr) mx = fmaxf(mx, v[j]);
+    if (kept[j]) mx = fmaxf(mx, v[j]);
   mx = warp_max(mx);
   if (cs.lane() == 0) sm.red[cs.warp()] = mx;
   named_sync(1, NCT);
@@ -1657,7 +1743,7 @@ __device__ int sample(const float* logits, Smem& sm, Cons& cs, const SampleCfg& 
   float es[1] = {0.f};
 #pragma unroll
   for (int j = 0; j < SPT; ++j) {
-    e[j] = (base + j < c.V && key[j] >= thr && v[j] != -INFINITY) ? expf(v[j] - mx) : 0.f;
+    e[j] = (kept[j] && v[j] != -INFINITY) ? expf(v[j] - mx) : 0.f;
     es[0] += e[j];
   }
   block_sum<1>(sm, cs, es);
@@ -1804,6 +1890,7 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
     c.do_sample = p.sp.cp_do_sample;
     c.temperature = p.sp.cp_temperature;
     c.top_k = p.sp.cp_top_k;
+    c.top_p = 1.f;
     c.suppress_from = p.cp_vocab;
     c.eos = -1;
     c.mask_eos = 0;
@@ -1837,6 +1924,7 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   c.do_sample = p.sp.do_sample;
   c.temperature = p.sp.temperature;
   c.top_k = p.sp.top_k;
+  c.top_p = p.sp.top_p;
   c.suppress_from = p.vocab - 1024;
   c.eos = p.sp.eos;
   c.mask_eos = (step + 1 < p.sp.min_new_tokens) ? 1 : 0;
@@ -1886,6 +1974,7 @@ __device__ bool run_step(const Params& p, Smem& sm, Cons& cs, bool cp) {
     c.do_sample = p.sp.do_sample;
     c.temperature = p.sp.temperature;
     c.top_k = p.sp.top_k;
+    c.top_p = p.sp.top_p;
     c.suppress_from = p.vocab - 1024;
     c.eos = p.sp.eos;
     c.mask_eos = p.sp.min_new_tokens > 0 ? 1 : 0;

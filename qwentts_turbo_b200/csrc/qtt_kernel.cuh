@@ -99,6 +99,7 @@ struct Sampling {
   int eos;
   int philox_stream;
   unsigned long long seed;
+  float top_p;             // nucleus filter of the group-0 sampler (>= 1: off)
 };
 
 struct Work {

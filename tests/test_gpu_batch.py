@@ -150,6 +150,23 @@ def test_batch_sampling_teacher_forced(dev_small, orc_small):
         assert max(x["cp_logits_viol"] for x in r) <= 0
 
 
+def test_batch_top_p_teacher_forced(dev_small, orc_small):
+    """Nucleus sampling in the batched path (one CTA per utterance runs the sampler): each
+    utterance's group-0 picks equal the oracle sampler's on the engine's logits."""
+    embeds, trailing, pads = _inputs([15, 28], 4, 71)
+    cfg = dict(temperature=0.9, top_k=50, top_p=0.7, repetition_penalty=1.2, seed=5, stream=1, cp_do_sample=False)
+    sp = sampling_struct(do_sample=True, temperature=0.9, top_k=50, top_p=0.7, repetition_penalty=1.2,
+                         min_new_tokens=10_000, seed=5, philox_stream=1)
+    eng = Engine(dev_small, max_streams=2, max_seq=512, max_frames=16)
+    try:
+        recs = run_teacher_forced_batch(eng, orc_small, embeds, trailing, pads, sp, 5, sampling=cfg)
+    finally:
+        eng.close()
+    for s, r in enumerate(recs):
+        bad = [(f, x["g0_next"], x["g0_pred"]) for f, x in enumerate(r) if x["g0_next"] != x["g0_pred"]]
+        assert len(bad) <= 1, (s, bad)
+
+
 def test_batch_matches_batch1_engine(dev_small):
     """Free-running greedy codes of the batched path equal the batch-1 engine's on the same
     utterances until the first near-tie (checked over the first 2 frames)."""

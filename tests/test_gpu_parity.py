@@ -333,6 +333,21 @@ def test_teacher_forced_sampling(orc_full, eng_full):
     assert max(r["cp_logits_viol"] for r in recs) <= 0
 
 
+@pytest.mark.parametrize("top_k,top_p", [(50, 0.8), (0, 0.6)])
+def test_teacher_forced_top_p(orc_small, eng_small, top_k, top_p):
+    """Nucleus sampling of group 0 (generator.py:196-203) on the device: the sorted-prefix filter
+    after top-k (or over the whole vocabulary with top_k = 0) picks exactly what the oracle's
+    sampler picks from the engine's logits with the same Philox draw."""
+    embeds, trailing, pad = c3_inputs(ctx=40, n_trailing=5, seed=23)
+    cfg = dict(temperature=0.9, top_k=top_k, top_p=top_p, repetition_penalty=1.2, seed=99, stream=2,
+               cp_do_sample=False)
+    sp = sampling_struct(do_sample=True, temperature=0.9, top_k=top_k, top_p=top_p, repetition_penalty=1.2,
+                         min_new_tokens=10_000, seed=99, philox_stream=2)
+    recs = run_teacher_forced(eng_small, orc_small, embeds, trailing, pad, sp, 10, sampling=cfg)
+    bad = [(f, r["g0_next"], r["g0_pred"]) for f, r in enumerate(recs) if r["g0_next"] != r["g0_pred"]]
+    assert len(bad) <= 1, bad
+
+
 def test_small_model_teacher_forced(orc_small, eng_small):
     """2+2-layer model with random norm weights, greedy, 16 frames (trailing rows then pad)."""
     embeds, trailing, pad = c3_inputs(ctx=40, n_trailing=5, seed=21)
@@ -429,9 +444,9 @@ def test_argument_errors(eng_small):
     s = torch.cuda.current_stream().cuda_stream
     assert lib.qtt_backbone_step(eng_small.h, 5, emb.data_ptr(), 0, out.data_ptr(), s) == _lib.QTT_ERR_INVALID_ARG
     assert lib.qtt_backbone_step(eng_small.h, 0, emb.data_ptr(), 512, out.data_ptr(), s) == _lib.QTT_ERR_INVALID_ARG
-    sp = sampling_struct(top_p=0.9)
+    sp = sampling_struct(top_p=float("nan"))
     pad = torch.zeros(1024, dtype=torch.bfloat16, device="cuda")
-    assert lib.qtt_frames(eng_small.h, 0, 1, None, 0, pad.data_ptr(), ctypes.byref(sp), s) == _lib.QTT_ERR_UNSUPPORTED
+    assert lib.qtt_frames(eng_small.h, 0, 1, None, 0, pad.data_ptr(), ctypes.byref(sp), s) == _lib.QTT_ERR_INVALID_ARG
     h = torch.zeros(1024, dtype=torch.float32, device="cuda")
     assert lib.qtt_set_decode_state(eng_small.h, 0, h.data_ptr(), 5000, 0, s) == _lib.QTT_ERR_INVALID_ARG
     # the last cache row is usable

@@ -149,6 +149,38 @@ def test_sampler_matches_reference_semantics(seed):
     assert len(picks) >= min(40, int(kept_ref.sum()))
 
 
+def _ref_top_p_kept(logits_bf16, temperature, top_k, top_p):
+    """Literal restatement of generator.py:188-205 up to the multinomial, on bf16 tensors as the
+    reference runs it (the sort made stable: torch.sort leaves the order of equal values open):
+    the set of ids with nonzero probability after top-k and top-p."""
+    scaled = logits_bf16.clone() / temperature
+    if top_k > 0:
+        topk_vals = torch.topk(scaled, min(top_k, scaled.size(-1)))[0]
+        scaled[scaled < topk_vals[-1]] = float("-inf")
+    if top_p < 1.0:
+        sorted_logits, sorted_idx = torch.sort(scaled, descending=True, stable=True)
+        cumprobs = torch.cumsum(torch.softmax(sorted_logits, dim=-1), dim=-1)
+        remove = cumprobs > top_p
+        remove[1:] = remove[:-1].clone()
+        remove[0] = False
+        sorted_logits[remove] = float("-inf")
+        scaled.scatter_(0, sorted_idx, sorted_logits)
+    return torch.softmax(scaled, dim=-1) > 0
+
+
+@pytest.mark.parametrize("seed,top_k,top_p", [(0, 50, 0.8), (1, 50, 0.5), (2, 0, 0.9), (3, 20, 0.3), (4, 0, 0.97)])
+def test_top_p_matches_reference_semantics(seed, top_k, top_p):
+    """The oracle's nucleus filter keeps exactly the reference's set of ids, and its draws land
+    only there."""
+    g = torch.Generator().manual_seed(seed)
+    logits = (torch.randn(3072, generator=g) * 1.5).to(torch.bfloat16)
+    kept_ref = _ref_top_p_kept(logits, 0.9, top_k, top_p)
+    kept = torch.isfinite(O.filter_logits(logits.float(), 0.9, top_k, top_p))
+    assert torch.equal(kept, kept_ref), (int(kept.sum()), int(kept_ref.sum()))
+    picks = {O.sample_token(logits.float(), True, 0.9, top_k, top_p, None, u24=u) for u in range(0, 1 << 24, 1 << 14)}
+    assert all(bool(kept_ref[p]) for p in picks)
+
+
 def test_inverse_cdf_pick_edges():
     p = torch.tensor([0.0, 0.25, 0.0, 0.5, 0.25]).to(torch.bfloat16).float()
     assert O.inverse_cdf_pick(p, 0) == 1

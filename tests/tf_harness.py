@@ -98,7 +98,8 @@ def _compare_frame(orc, kv, h_e, g0, pos, step, codes, g0_next, cp_e, g0l_e, h_e
         l2[sup] = float("-inf")
         l2 = O.apply_repetition_penalty(l2, hist, sampling["repetition_penalty"])
         u = O.draw_u24(sampling["seed"], step + 1, 0, sampling["stream"])
-        rec["g0_pred"] = O.sample_token(l2, True, sampling["temperature"], sampling["top_k"], 1.0, mask_eos, u)
+        rec["g0_pred"] = O.sample_token(l2, True, sampling["temperature"], sampling["top_k"],
+                                        sampling.get("top_p", 1.0), mask_eos, u)
         rec["g0_gap"] = None
     # --- keep the oracle's cache identical to the engine's
     kc, vc = kv
