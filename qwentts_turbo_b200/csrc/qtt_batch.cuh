@@ -481,9 +481,9 @@ struct EpiSt {
   float rs;
 };
 
-// Consumer side of one GEMM stage. Epilogue items are (token t, 16 output columns c); the
+// Consumer side of one GEMM stage. Epilogue items are (token t, EW output columns c); the
 // callbacks are pre(t, r0, st) (the item's inputs that do not depend on D) and
-// run(t, r0, y, y2, st) with y = D[t][16 columns] (gate/up: y = gate, y2 = up) and r0 the first
+// run(t, r0, y, y2, st) with y = D[t][EW columns] (gate/up: y = gate, y2 = up) and r0 the first
 // output column (row of W; gate/up: intermediate channel).
 //   1. release the activation loader (GO);
 //   2. wait for D; the consumer warps copy its lo lanes and then add its hi lanes into the K-slice
@@ -495,15 +495,15 @@ struct EpiSt {
 struct BStage {
   BSplit sp;
   int gi, N, NO, nci, i0, i1, r0b, T, smask;
-  int np;            // staged planes: 2 (hi and lo apart, one token tile) or 1 (lo + hi, two tiles)
   bool gu;
   uint32_t s_addr;   // shared address of the K-slice partial [tile][64][N] fp32 (swizzled chunks)
 };
 
-// Partial staging layout: row (tile or plane j, token t) of N floats; 16-byte chunk k of the row is
-// stored at chunk k ^ (t & smask), so that the lanes of a warp (one token each) hit different
-// banks. With one token tile the hi and lo products are staged as rows j = 0 and 1 (np = 2); with
-// two tiles, lo + hi of tile j in row j (np = 1).
+// Partial staging layout: row (token tile j, token t) of N floats holding lo + hi; 16-byte chunk k
+// of the row is stored at chunk k ^ (t & smask), so that the lanes of a warp (one token each) hit
+// different banks. The hi and lo products are summed here, before the exchange, so that the other
+// CTAs of the cluster read one plane: when every SM of the cluster reads at once, distributed
+// shared memory moves only ~7 bytes per clock per SM, and the exchange is bound by it.
 __device__ __forceinline__ uint32_t b_part_off(const BStage& S, int j, int t, int k) {
   return static_cast<uint32_t>(((j * 64 + t) * S.N + 4 * (k ^ (t & S.smask))) * 4);
 }
@@ -524,7 +524,6 @@ __device__ __forceinline__ BStage b_gemm_begin(const Params& p, Smem& sm, Cons& 
   S.i1 = split_lo(items, S.sp.nk, S.sp.kspl + 1);
   S.r0b = S.sp.rt * S.NO;
   S.smask = (S.N / 4) % 8 == 0 ? 7 : 3;
-  S.np = g.T <= 64 ? 2 : 1;
   S.s_addr = smem_u32(sm.ring) + WRING_BYTES;
   if (S.sp.act) {
     if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_START);
@@ -545,24 +544,22 @@ __device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, 
   if (tr2) btrace(p, S.gi, cs.cta(), cs.G(), BT_LO_SEEN);
   tc_fence_after();
   // D -> partial: TMEM lane quarter q of warp w (w % 4) holds tokens 32 (q & 1) .. of the hi
-  // (q < 2) or lo (q >= 2) products. One token tile: every quarter stores its plane in one pass;
-  // two tiles: lo first, then hi added (the same order for every element).
+  // (q < 2) or lo (q >= 2) products. The lo quarters store first, then the hi quarters add (the
+  // same order for every element).
   const int ntiles = (S.T + 63) >> 6, nch = S.N / 16;
   const int q = cs.warp() & 3, wq = cs.warp() >> 2;
   uint8_t* sbase = reinterpret_cast<uint8_t*>(sm.ring) + WRING_BYTES;
-  const int nphase = S.np == 2 ? 1 : 2;
-  for (int phase = 0; phase < nphase; ++phase) {
-    if (S.np == 2 || (q >= 2) == (phase == 0)) {
+  for (int phase = 0; phase < 2; ++phase) {
+    if ((q >= 2) == (phase == 0)) {
       for (int job = wq; job < ntiles * nch; job += NCW / 4) {
         const int j = job / nch, c = job - j * nch;
         if (64 * j + 32 * (q & 1) < S.T) {   // warp-uniform: tcgen05.ld is a warp-wide instruction
           float v[16];
           tmem_ld16(sm.tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(j * S.N + 16 * c), v);
           const int t = 32 * (q & 1) + cs.lane();
-          const int row = S.np == 2 ? (q >> 1) : j;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            float4* d = reinterpret_cast<float4*>(sbase + b_part_off(S, row, t, 4 * c + i));
+            float4* d = reinterpret_cast<float4*>(sbase + b_part_off(S, j, t, 4 * c + i));
             if (phase == 1) {
               const float4 lo = *d;
               *d = make_float4(lo.x + v[4 * i], lo.y + v[4 * i + 1], lo.z + v[4 * i + 2], lo.w + v[4 * i + 3]);
@@ -575,7 +572,7 @@ __device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, 
     }
     if (tr2 && phase == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_LO_DONE);
     if (tr && phase == 1) btrace(p, S.gi, cs.cta(), cs.G(), BT_HI_DONE);
-    if (phase + 1 < nphase) named_sync(1, NCT);
+    if (phase == 0) named_sync(1, NCT);
     if (tr && phase == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_PH0);
   }
   tc_fence_before();
@@ -583,11 +580,14 @@ __device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, 
   // (cluster scope, cumulative) publish them to the cluster's readers
   named_sync(1, NCT);
   if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PH1);
-  if (cs.tid() == 0) {
-    mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
-    if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_STAGED);
-    const uint32_t bar = smem_u32(&sm.bbar[BB_SREADY]);
-    for (int r = 0; r < S.sp.nk; ++r) mbar_arrive_cluster(mapa_shared(bar, static_cast<uint32_t>(r)));
+  if (cs.tid() < S.sp.nk) {
+    if (cs.tid() == 0) {
+      mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
+      if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_STAGED);
+    }
+    // lane r signals rank r: the ranks' release arrivals go out together instead of one after
+    // another
+    mbar_arrive_cluster(mapa_shared(smem_u32(&sm.bbar[BB_SREADY]), static_cast<uint32_t>(cs.tid())));
     if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PART);
   }
   // every CTA of the cluster has staged its partial of this stage
@@ -599,18 +599,11 @@ __device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, 
   return true;
 }
 
-// Partial of CTA rank `base` (a cluster address) for chunks k0, k0 + 1 of token tt: lo + hi
-// (np = 2) or the staged sum of token tile j (np = 1).
+// Partial of the CTA of the cluster at `base` (its cluster address) for chunks k0, k0 + 1 of token
+// tt of tile j.
 __device__ __forceinline__ void b_part2(const BStage& S, uint32_t base, int j, int tt, int k0, float4 (&a)[2]) {
-  if (S.np == 2) {
-    const float4 l0 = ld_dsmem_f4(base + b_part_off(S, 1, tt, k0)), l1 = ld_dsmem_f4(base + b_part_off(S, 1, tt, k0 + 1));
-    const float4 h0 = ld_dsmem_f4(base + b_part_off(S, 0, tt, k0)), h1 = ld_dsmem_f4(base + b_part_off(S, 0, tt, k0 + 1));
-    a[0] = make_float4(l0.x + h0.x, l0.y + h0.y, l0.z + h0.z, l0.w + h0.w);
-    a[1] = make_float4(l1.x + h1.x, l1.y + h1.y, l1.z + h1.z, l1.w + h1.w);
-  } else {
-    a[0] = ld_dsmem_f4(base + b_part_off(S, j, tt, k0));
-    a[1] = ld_dsmem_f4(base + b_part_off(S, j, tt, k0 + 1));
-  }
+  a[0] = ld_dsmem_f4(base + b_part_off(S, j, tt, k0));
+  a[1] = ld_dsmem_f4(base + b_part_off(S, j, tt, k0 + 1));
 }
 __device__ __forceinline__ void b_acc8(float (&y)[EW], const float4 (&a)[2]) {
 #pragma unroll
@@ -619,26 +612,27 @@ __device__ __forceinline__ void b_acc8(float (&y)[EW], const float4 (&a)[2]) {
   }
 }
 
-// Sum of the cluster's K-slice partials of item (t, EW columns from chunk 2c) in rank order
-// (y; gate/up: y2 = the matching up columns), read through distributed shared memory. Each rank's
-// partial is lo + hi, formed here (np = 2) or in the staging (np = 1) with the same fp32 add, so
-// the result does not depend on the token count.
+// Sum of the cluster's K-slice partials (each lo + hi) of item (t, EW columns from chunk 2c) in
+// rank order (y; gate/up: y2 = the matching up columns). NK ranks: every rank's loads are issued
+// before the first add, so the item waits for one distributed-shared-memory round trip, not NK.
+template <int NK>
+__device__ __forceinline__ void b_sum_ranks(const BStage& S, int j, int tt, int k0, float (&y)[EW]) {
+  float4 a[NK][2];
+#pragma unroll
+  for (int r = 0; r < NK; ++r) b_part2(S, mapa_shared(S.s_addr, static_cast<uint32_t>(r)), j, tt, k0, a[r]);
+#pragma unroll
+  for (int i = 0; i < EW; ++i) y[i] = 0.f;
+#pragma unroll
+  for (int r = 0; r < NK; ++r) b_acc8(y, a[r]);
+}
 __device__ __forceinline__ void b_reduce_item(const BStage& S, int t, int c, float (&y)[EW], float (&y2)[EW]) {
   const int tt = t & 63, j = t >> 6;
-#pragma unroll
-  for (int i = 0; i < EW; ++i) {
-    y[i] = 0.f;
-    y2[i] = 0.f;
-  }
-  for (int r = 0; r < S.sp.nk; ++r) {
-    const uint32_t base = mapa_shared(S.s_addr, static_cast<uint32_t>(r));
-    float4 a[2];
-    b_part2(S, base, j, tt, 2 * c, a);
-    b_acc8(y, a);
-    if (S.gu) {
-      b_part2(S, base, j, tt, S.NO / 4 + 2 * c, a);
-      b_acc8(y2, a);
-    }
+  if (S.sp.nk == 4) {
+    b_sum_ranks<4>(S, j, tt, 2 * c, y);
+    if (S.gu) b_sum_ranks<4>(S, j, tt, S.NO / 4 + 2 * c, y2);
+  } else {
+    b_sum_ranks<2>(S, j, tt, 2 * c, y);
+    if (S.gu) b_sum_ranks<2>(S, j, tt, S.NO / 4 + 2 * c, y2);
   }
 }
 
