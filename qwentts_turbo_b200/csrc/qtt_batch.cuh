@@ -60,9 +60,14 @@ constexpr int NMAX_B = 192;               // widest tile: 96 gate + 96 up rows (
 constexpr int BRING_BYTES = NSLOTS * SLOT_BYTES + NTMAX * INTER * 4 + ATT_STAGE_BYTES;
 static_assert(WRING_BYTES + NAS * AS_BYTES <= BRING_BYTES, "batched rings fit the ring region");
 static_assert(NMAX_B * 2 * KSTEP <= WRING_BYTES, "a K step of the widest tile fits the weight ring");
-static_assert(2 * 64 * NMAX_B * 4 <= NAS * AS_BYTES, "K-slice staging (two planes or two token tiles) fits the activation ring");
+static_assert(2 * 64 * NMAX_B * 4 <= NAS * AS_BYTES, "K-slice staging of two token tiles fits the activation ring");
+// one token tile, pushed: the own partial plus (cluster - 1) receive slots of up to 64 / cluster + 1
+// rows each (cluster 4; cluster 2 halves the widest tile)
+static_assert((64 + 3 * (64 / 4 + 1)) * NMAX_B * 4 <= NAS * AS_BYTES, "pushed K-slice slices fit the activation ring");
+static_assert((64 + 1 * (64 / 2 + 1)) * (NMAX_B / 2) * 4 <= NAS * AS_BYTES, "pushed K-slice slices fit the activation ring");
 static_assert(2 * NMAX_B <= static_cast<int>(TMEM_COLS), "accumulators of two token tiles fit tensor memory");
-// mbarriers in sm.bbar (one expected arrival except BB_SREADY: one per CTA of the cluster)
+// mbarriers in sm.bbar (one expected arrival except BB_SREADY: one per CTA of the cluster, and
+// BB_RFREE: one per other CTA of the cluster)
 enum : int {
   BB_WFULL = 0,                  // weight entry filled (producer expect_tx + TMA bytes)
   BB_WEMPTY = BB_WFULL + NWE,    // weight entry consumed (tcgen05.commit)
@@ -72,7 +77,9 @@ enum : int {
   BB_ACCEMPTY,                   // D read by the consumers
   BB_GO,                         // the stage's grid barrier passed: A planes are complete
   BB_DRAIN,                      // every MMA done (exit)
-  BB_SREADY,                     // every CTA of the cluster has staged its K-slice partial
+  BB_SREADY,                     // every CTA of the cluster has staged its K-slice partial (pull)
+  BB_RFREE,                      // every other CTA of the cluster may receive this CTA's slices (push)
+  BB_RCV,                        // the other CTAs' slices of this CTA's items arrived (push)
   BB_N
 };
 static_assert(BB_N <= 32, "batched mbarriers");
@@ -496,8 +503,19 @@ struct BStage {
   BSplit sp;
   int gi, N, NO, nci, i0, i1, r0b, T, smask;
   bool gu;
+  bool push;         // one token tile: partial slices pushed to their owners by bulk copies
+  int ra, rb;        // push: partial rows (tokens) [ra, rb) holding this CTA's items
   uint32_t s_addr;   // shared address of the K-slice partial [tile][64][N] fp32 (swizzled chunks)
+  uint32_t r_addr;   // push: receive slots, one per other CTA of the cluster [rb - ra][N] fp32
 };
+
+// Partial rows (tokens) holding the epilogue items of cluster rank r: [*ra, *rb).
+__device__ __forceinline__ void b_rows_of(const BStage& S, int r, int& ra, int& rb) {
+  const int items = S.T * S.nci;
+  const int i0 = split_lo(items, S.sp.nk, r), i1 = split_lo(items, S.sp.nk, r + 1);
+  ra = i0 / S.nci;
+  rb = (i1 + S.nci - 1) / S.nci;
+}
 
 // Partial staging layout: row (token tile j, token t) of N floats holding lo + hi; 16-byte chunk k
 // of the row is stored at chunk k ^ (t & smask), so that the lanes of a warp (one token each) hit
@@ -525,22 +543,48 @@ __device__ __forceinline__ BStage b_gemm_begin(const Params& p, Smem& sm, Cons& 
   S.r0b = S.sp.rt * S.NO;
   S.smask = (S.N / 4) % 8 == 0 ? 7 : 3;
   S.s_addr = smem_u32(sm.ring) + WRING_BYTES;
+  S.push = g.T <= 64;
+  b_rows_of(S, S.sp.kspl, S.ra, S.rb);
+  S.r_addr = S.s_addr + static_cast<uint32_t>(64 * S.N * 4);
   if (S.sp.act) {
     if (p.dbg_marks != nullptr && cs.tid() == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_START);
-    if (cs.tid() == 0) mbar_arrive(&sm.bbar[BB_GO]);
+    if (cs.tid() == 0) {
+      // armed before this CTA frees its receive slots (after its MMAs), so before any slice lands
+      if (S.push)
+        mbar_arrive_expect_tx(&sm.bbar[BB_RCV], static_cast<uint32_t>((S.sp.nk - 1) * (S.rb - S.ra) * S.N * 4));
+      mbar_arrive(&sm.bbar[BB_GO]);
+    }
   }
   return S;
 }
 
-// Step 2 up to the cluster's partials being staged; false on abort.
-__device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, const BStage S, uint32_t gemm_n) {
-  const bool tr = p.dbg_marks != nullptr && cs.tid() == 0;
-  if (!mbar_wait(&sm.bbar[BB_ACCFULL], gemm_n & 1u, &sm.abort)) {
-    if (!aborted(sm)) fail(p, sm, DEV_ERR_FULL_TIMEOUT);
-    return false;
+// Consumer-wide wait for an mbarrier phase: thread 0 polls, the other consumer threads wait at the
+// CTA barrier, so that 384 threads do not poll the mbarrier unit while the loader's and the MMA
+// thread's mbarriers are busy. Thread 0's acquire and the CTA barrier order the phase's data
+// before every consumer's later reads.
+__device__ __forceinline__ bool b_cons_wait(const Params& p, Smem& sm, Cons& cs, uint64_t* bar, uint32_t parity,
+                                            bool cluster, int code) {
+  if (cs.tid() == 0) {
+    const bool ok = cluster ? mbar_wait_cluster(bar, parity, &sm.abort) : mbar_wait(bar, parity, &sm.abort);
+    if (!ok && !aborted(sm)) fail(p, sm, code);
   }
+  named_sync(1, NCT);
+  return !aborted(sm);
+}
+
+// Step 2 up to the cluster's partials being staged; false on abort.
+__device__ __noinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, const BStage S, uint32_t gemm_n) {
+  const bool tr = p.dbg_marks != nullptr && cs.tid() == 0;
+  if (!b_cons_wait(p, sm, cs, &sm.bbar[BB_ACCFULL], gemm_n & 1u, false, DEV_ERR_FULL_TIMEOUT)) return false;
   const bool tr2 = p.dbg_marks != nullptr && cs.tid() == 64;   // warp 2 (lo lanes), lane 0
   if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_DREADY);
+  // push: the MMAs have read this CTA's activation ring, where the other CTAs' slices land; the
+  // warp barrier orders thread 0's arming of BB_RCV before these arrivals
+  if (S.push && cs.warp() == 0) {
+    __syncwarp();
+    if (cs.tid() < S.sp.nk && cs.tid() != S.sp.kspl)
+      mbar_arrive_cluster(mapa_shared(smem_u32(&sm.bbar[BB_RFREE]), static_cast<uint32_t>(cs.tid())));
+  }
   if (tr2) btrace(p, S.gi, cs.cta(), cs.G(), BT_LO_SEEN);
   tc_fence_after();
   // D -> partial: TMEM lane quarter q of warp w (w % 4) holds tokens 32 (q & 1) .. of the hi
@@ -576,8 +620,42 @@ __device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, 
     if (tr && phase == 0) btrace(p, S.gi, cs.cta(), cs.G(), BT_PH0);
   }
   tc_fence_before();
-  // the CTA barrier orders every thread's partial stores before thread 0, whose release arrivals
-  // (cluster scope, cumulative) publish them to the cluster's readers
+  if (S.push) {
+    // the partial's generic stores are read by the bulk copies (async proxy) after the CTA barrier
+    fence_proxy_async_smem();
+    named_sync(1, NCT);
+    if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PH1);
+    if (cs.tid() == 0) {
+      mbar_arrive(&sm.bbar[BB_ACCEMPTY]);   // D is no longer needed
+      if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_STAGED);
+    }
+    const int d = cs.tid();
+    if (d < S.sp.nk && d != S.sp.kspl) {
+      // lane d: the rows of rank d's items, into its receive slot of this CTA, once rank d's MMAs
+      // are done
+      if (!mbar_wait_cluster(&sm.bbar[BB_RFREE], static_cast<uint32_t>(cs.pn) & 1u, &sm.abort)) {
+        if (!aborted(sm)) fail(p, sm, DEV_ERR_GRID_TIMEOUT);
+      } else {
+        int ra, rb;
+        b_rows_of(S, d, ra, rb);
+        const uint32_t row_bytes = static_cast<uint32_t>(S.N * 4), slot_bytes = static_cast<uint32_t>(rb - ra) * row_bytes;
+        const uint32_t sidx = static_cast<uint32_t>(S.sp.kspl < d ? S.sp.kspl : S.sp.kspl - 1);
+        if (slot_bytes != 0u)
+          bulk_s2cluster(mapa_shared(S.r_addr + sidx * slot_bytes, static_cast<uint32_t>(d)),
+                         S.s_addr + static_cast<uint32_t>(ra) * row_bytes, slot_bytes,
+                         mapa_shared(smem_u32(&sm.bbar[BB_RCV]), static_cast<uint32_t>(d)));
+      }
+      if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PART);
+    }
+    // the other CTAs' slices of this CTA's items
+    if (!b_cons_wait(p, sm, cs, &sm.bbar[BB_RCV], static_cast<uint32_t>(cs.pn) & 1u, true, DEV_ERR_GRID_TIMEOUT))
+      return false;
+    cs.pn++;
+    if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_COUNT);
+    return true;
+  }
+  // pull: the CTA barrier orders every thread's partial stores before the lanes whose release
+  // arrivals (cluster scope, cumulative) publish them to the cluster's readers
   named_sync(1, NCT);
   if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PH1);
   if (cs.tid() < S.sp.nk) {
@@ -591,10 +669,7 @@ __device__ __forceinline__ bool b_gemm_mid(const Params& p, Smem& sm, Cons& cs, 
     if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_PART);
   }
   // every CTA of the cluster has staged its partial of this stage
-  if (!mbar_wait_cluster(&sm.bbar[BB_SREADY], gemm_n & 1u, &sm.abort)) {
-    if (!aborted(sm)) fail(p, sm, DEV_ERR_GRID_TIMEOUT);
-    return false;
-  }
+  if (!b_cons_wait(p, sm, cs, &sm.bbar[BB_SREADY], gemm_n & 1u, true, DEV_ERR_GRID_TIMEOUT)) return false;
   if (tr) btrace(p, S.gi, cs.cta(), cs.G(), BT_COUNT);
   return true;
 }
@@ -625,8 +700,39 @@ __device__ __forceinline__ void b_sum_ranks(const BStage& S, int j, int tt, int 
 #pragma unroll
   for (int r = 0; r < NK; ++r) b_acc8(y, a[r]);
 }
+// The same sum when the slices were pushed: this CTA's own partial and the received slices, all
+// in this CTA's shared memory, in rank order.
+template <int NK>
+__device__ __forceinline__ void b_sum_ranks_pushed(const BStage& S, int t, int k0, float (&y)[EW]) {
+  const uint32_t slot = static_cast<uint32_t>((S.rb - S.ra) * S.N * 4);
+  const int sw = t & S.smask;
+  float4 a[NK][2];
+#pragma unroll
+  for (int r = 0; r < NK; ++r) {
+    const bool own = r == S.sp.kspl;
+    const uint32_t base = own ? S.s_addr : S.r_addr + static_cast<uint32_t>(r < S.sp.kspl ? r : r - 1) * slot;
+    const int row = own ? t : t - S.ra;
+    a[r][0] = ld_smem_f4(base + static_cast<uint32_t>((row * S.N + 4 * (k0 ^ sw)) * 4));
+    a[r][1] = ld_smem_f4(base + static_cast<uint32_t>((row * S.N + 4 * ((k0 + 1) ^ sw)) * 4));
+  }
+#pragma unroll
+  for (int i = 0; i < EW; ++i) y[i] = 0.f;
+#pragma unroll
+  for (int r = 0; r < NK; ++r) b_acc8(y, a[r]);
+}
+
 __device__ __forceinline__ void b_reduce_item(const BStage& S, int t, int c, float (&y)[EW], float (&y2)[EW]) {
   const int tt = t & 63, j = t >> 6;
+  if (S.push) {
+    if (S.sp.nk == 4) {
+      b_sum_ranks_pushed<4>(S, t, 2 * c, y);
+      if (S.gu) b_sum_ranks_pushed<4>(S, t, S.NO / 4 + 2 * c, y2);
+    } else {
+      b_sum_ranks_pushed<2>(S, t, 2 * c, y);
+      if (S.gu) b_sum_ranks_pushed<2>(S, t, S.NO / 4 + 2 * c, y2);
+    }
+    return;
+  }
   if (S.sp.nk == 4) {
     b_sum_ranks<4>(S, j, tt, 2 * c, y);
     if (S.gu) b_sum_ranks<4>(S, j, tt, S.NO / 4 + 2 * c, y2);
@@ -690,6 +796,7 @@ __device__ __forceinline__ void b_ssq_add(unsigned long long* ssq, int t, double
 // (the async proxy) after the barrier: every writer orders its stores for that proxy first.
 __device__ __forceinline__ bool b_sync_planes(const Params& p, Smem& sm, Cons& cs) {
   fence_proxy_async_global();
+  fence_proxy_async_smem();   // attention staged rows in the activation ring: before its next TMA writes
   return grid_sync_b(p, sm, cs);
 }
 
@@ -879,14 +986,118 @@ __device__ __forceinline__ void w_out(bf16* hilo, int tok, int col0, const WSoft
       make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
+// Backbone items of one token: the cached rows [s0, ce) pass through this warp's WBUF bytes of
+// the activation ring (idle between GEMM stages) in sub-chunks of WSC positions, double-buffered
+// with cp.async, so that a warp keeps 8 KB of K/V rows in flight instead of the 4 KB its
+// registers hold (the stage is bound by bytes in flight from HBM). Group g takes rows g, g + 2,
+// g + 4, g + 6 of each sub-chunk, as in the register loop.
+constexpr int WSC = 8;                          // positions per sub-chunk
+constexpr int WSUB = 2 * WSC * HD * 2;          // K and V rows of one sub-chunk (bf16): 4 KB
+constexpr int WBUF = 2 * WSUB;                  // two sub-chunks in flight
+static_assert(NCW * WBUF <= NAS * AS_BYTES, "attention staging fits the activation ring");
+// Code-predictor items of one token: the warps 0..3 of every CTA take one item each (512 items on
+// 132 CTAs) and stage all of its <= 16 cached fp32 rows in 24 KB of the activation ring with one
+// round of cp.async.
+constexpr int CPWBUF = 24 * 1024;
+constexpr int CPW_ROWS = CPWBUF / 2 / (HD * 4);   // 24 rows of K, then 24 of V
+static_assert(4 * CPWBUF <= NAS * AS_BYTES && CPW_ROWS >= 16, "code-predictor attention staging fits the activation ring");
+__device__ __forceinline__ void w_stage_sub(uint8_t* dst, const uint8_t* kb, const uint8_t* vb, int j0, int n, int lane,
+                                            uint64_t pol) {
+  const int pieces = n * (HD * 2 / 16);
+  const size_t off = static_cast<size_t>(j0) * HD * 2;
+  for (int e = lane; e < pieces; e += 32) {
+    cp_async16_stream(dst + e * 16, kb + off + e * 16, pol);
+    cp_async16_stream(dst + WSUB / 2 + e * 16, vb + off + e * 16, pol);
+  }
+  cp_async_commit();
+}
+__device__ __forceinline__ void w_scores4(const float (&q0)[WD], const float (&q1)[WD], const WRow<false> (&kr)[4],
+                                          float scale, float (&d0)[4], float (&d1)[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    d0[q] = 0.f;
+    d1[q] = 0.f;
+#pragma unroll
+    for (int i = 0; i < WD; ++i) {
+      d0[q] = fmaf(q0[i], kr[q][i], d0[q]);
+      d1[q] = fmaf(q1[i], kr[q][i], d1[q]);
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < WL; o <<= 1)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      d0[q] += __shfl_xor_sync(WFULL, d0[q], o);
+      d1[q] += __shfl_xor_sync(WFULL, d1[q], o);
+    }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    d0[q] *= scale;
+    d1[q] *= scale;
+  }
+}
+// The first two sub-chunks, issued before the item's q/k/v loads (the cached rows do not depend
+// on them).
+__device__ __forceinline__ void w_stage_first(const uint8_t* kb, const uint8_t* vb, int s0, int ce, uint8_t* wbuf, int lane) {
+  const uint64_t pol = l2_evict_first_policy();
+  const int nsc = (ce - s0 + WSC - 1) / WSC;
+  if (nsc > 0) w_stage_sub(wbuf, kb, vb, s0, min(WSC, ce - s0), lane, pol);
+  if (nsc > 1) w_stage_sub(wbuf + WSUB, kb, vb, s0 + WSC, min(WSC, ce - s0 - WSC), lane, pol);
+}
+__device__ __forceinline__ void w_loop_staged(const uint8_t* kb, const uint8_t* vb, int s0, int ce, uint8_t* wbuf,
+                                              const float (&q0)[WD], const float (&q1)[WD], float scale, int lane,
+                                              WSoft& a0, WSoft& a1) {
+  const int g = lane / WL, u = lane % WL;
+  const uint64_t pol = l2_evict_first_policy();
+  const int nsc = (ce - s0 + WSC - 1) / WSC;
+  for (int i = 0; i < nsc; ++i) {
+    if (i + 1 < nsc)
+      cp_async_wait<1>();
+    else
+      cp_async_wait<0>();
+    __syncwarp();   // every lane's copies of sub-chunk i have landed
+    const uint8_t* b = wbuf + (i & 1) * WSUB;
+    const int n = min(WSC, ce - s0 - i * WSC);
+    bool ok[4];
+    WRow<false> kr[4], vr[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int r = g + 2 * q;
+      ok[q] = r < n;
+      const uint4 k4 = *reinterpret_cast<const uint4*>(b + (ok[q] ? r : 0) * HD * 2 + 16 * u);
+      const uint4 v4 = *reinterpret_cast<const uint4*>(b + WSUB / 2 + (ok[q] ? r : 0) * HD * 2 + 16 * u);
+      kr[q].w[0] = k4.x; kr[q].w[1] = k4.y; kr[q].w[2] = k4.z; kr[q].w[3] = k4.w;
+      vr[q].w[0] = v4.x; vr[q].w[1] = v4.y; vr[q].w[2] = v4.z; vr[q].w[3] = v4.w;
+    }
+    float d0[4], d1[4];
+    w_scores4(q0, q1, kr, scale, d0, d1);
+    a0.add_trip(d0, ok, vr);
+    a1.add_trip(d1, ok, vr);
+    __syncwarp();   // sub-chunk i read by every lane before its buffer is refilled
+    if (i + 2 < nsc) w_stage_sub(wbuf + (i & 1) * WSUB, kb, vb, s0 + (i + 2) * WSC, min(WSC, ce - s0 - (i + 2) * WSC), lane, pol);
+  }
+}
+
 // One warp item: tokens t < NT of utterance rows qkv + t * QKV_ROWS at positions p0 + t, KV
 // head h, context positions [s0, s1) (chunk c of nch). The writer stores the new K/V rows of
 // the tokens first (q/k norm + RoPE), so every position is read from the cache.
 template <bool CP>
 __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const LayerW* L, const float* qkv, int NT, int p0, int h,
                           uint8_t* kb, uint8_t* vb, bf16* hilo, int tok0, int c, int nch, int s0, int s1,
-                          bool writer, float* prt, uint32_t* cnt) {
+                          bool writer, float* prt, uint32_t* cnt, uint8_t* wbuf) {
   const int g = cs.lane() / WL, u = cs.lane() % WL;
+  const bool staged = !CP && wbuf != nullptr && NT == 1;
+  const bool staged_cp = CP && wbuf != nullptr && NT == 1 && writer && p0 - s0 <= CPW_ROWS;
+  if (staged) w_stage_first(kb, vb, s0, writer ? min(s1, p0 + 1) - 1 : min(s1, p0 + 1), wbuf, cs.lane());
+  if (staged_cp) {   // cached rows [s0, p0), before the item's q/k/v loads
+    const int pieces = (p0 - s0) * (HD * 4 / 16);
+    const size_t off = static_cast<size_t>(s0) * HD * 4;
+    for (int e = cs.lane(); e < pieces; e += 32) {
+      cp_async16(wbuf + e * 16, kb + off + e * 16);
+      cp_async16(wbuf + CPWBUF / 2 + e * 16, vb + off + e * 16);
+    }
+    cp_async_commit();
+  }
   for (int t = 0; t < NT; ++t) {
     // one round trip: raw q (both heads), k, v, the norm weights and the position's RoPE rows
     const int pos = p0 + t;
@@ -933,6 +1144,36 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
     a0.init();
     a1.init();
     const int send = min(s1, p0 + t + 1);
+    if (staged) {   // one token (frames): staged rows, then this token's own row
+      const int ce = writer ? send - 1 : send;
+      w_loop_staged(kb, vb, s0, ce, wbuf, q0, q1, p.attn_scale, cs.lane(), a0, a1);
+      if (writer) {   // position send - 1: the row just stored, from registers (bf16 as cached)
+        WRow<false> kr[1], vr[1];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          kr[0].w[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(k[2 * i]))) |
+                       (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(k[2 * i + 1]))) << 16);
+          vr[0].w[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i]))) |
+                       (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1]))) << 16);
+        }
+        bool ok[1] = {g == ((send - 1 - s0) & 1)};
+        float d0[1] = {0.f}, d1[1] = {0.f};
+#pragma unroll
+        for (int i = 0; i < WD; ++i) {
+          d0[0] = fmaf(q0[i], kr[0][i], d0[0]);
+          d1[0] = fmaf(q1[i], kr[0][i], d1[0]);
+        }
+#pragma unroll
+        for (int o = 1; o < WL; o <<= 1) {
+          d0[0] += __shfl_xor_sync(WFULL, d0[0], o);
+          d1[0] += __shfl_xor_sync(WFULL, d1[0], o);
+        }
+        d0[0] *= p.attn_scale;
+        d1[0] *= p.attn_scale;
+        a0.add_trip(d0, ok, vr);
+        a1.add_trip(d1, ok, vr);
+      }
+    } else if (!staged_cp) {
     constexpr int P = CP ? 2 : 4;   // positions per group per trip: 4 P rows in flight per lane
     for (int j = s0 + g; j - g < send; j += P * WG) {   // every lane runs the same trip count
       bool ok[P];
@@ -969,6 +1210,76 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
       }
       a0.add_trip(d0, ok, vr);
       a1.add_trip(d1, ok, vr);
+    }
+    } else if (staged_cp) {   // code predictor, one token: staged rows, then the own row
+      const int n = p0 - s0;
+      cp_async_wait<0>();
+      __syncwarp();   // every lane's copies have landed
+      for (int j = g; j - g < n; j += 2 * WG) {   // every lane runs the same trip count
+        bool ok[2];
+        WRow<true> kr[2], vr[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int r = j + q * WG;
+          ok[q] = r < n;
+          const uint4* kp = reinterpret_cast<const uint4*>(wbuf + (ok[q] ? r : 0) * HD * 4 + 32 * u);
+          const uint4* vp = reinterpret_cast<const uint4*>(wbuf + CPWBUF / 2 + (ok[q] ? r : 0) * HD * 4 + 32 * u);
+          const uint4 k0 = kp[0], k1 = kp[1], v0 = vp[0], v1 = vp[1];
+          kr[q].w[0] = k0.x; kr[q].w[1] = k0.y; kr[q].w[2] = k0.z; kr[q].w[3] = k0.w;
+          kr[q].w[4] = k1.x; kr[q].w[5] = k1.y; kr[q].w[6] = k1.z; kr[q].w[7] = k1.w;
+          vr[q].w[0] = v0.x; vr[q].w[1] = v0.y; vr[q].w[2] = v0.z; vr[q].w[3] = v0.w;
+          vr[q].w[4] = v1.x; vr[q].w[5] = v1.y; vr[q].w[6] = v1.z; vr[q].w[7] = v1.w;
+        }
+        float d0[2], d1[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          d0[q] = 0.f;
+          d1[q] = 0.f;
+#pragma unroll
+          for (int i = 0; i < WD; ++i) {
+            d0[q] = fmaf(q0[i], kr[q][i], d0[q]);
+            d1[q] = fmaf(q1[i], kr[q][i], d1[q]);
+          }
+        }
+#pragma unroll
+        for (int o = 1; o < WL; o <<= 1)
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            d0[q] += __shfl_xor_sync(WFULL, d0[q], o);
+            d1[q] += __shfl_xor_sync(WFULL, d1[q], o);
+          }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          d0[q] *= p.attn_scale;
+          d1[q] *= p.attn_scale;
+        }
+        a0.add_trip(d0, ok, vr);
+        a1.add_trip(d1, ok, vr);
+      }
+      {   // position p0: the row just stored, from registers (fp32 as cached)
+        WRow<true> kr[1], vr[1];
+#pragma unroll
+        for (int i = 0; i < WD; ++i) {
+          kr[0].w[i] = __float_as_uint(k[i]);
+          vr[0].w[i] = __float_as_uint(v[i]);
+        }
+        bool ok[1] = {g == (n & 1)};
+        float d0[1] = {0.f}, d1[1] = {0.f};
+#pragma unroll
+        for (int i = 0; i < WD; ++i) {
+          d0[0] = fmaf(q0[i], kr[0][i], d0[0]);
+          d1[0] = fmaf(q1[i], kr[0][i], d1[0]);
+        }
+#pragma unroll
+        for (int o = 1; o < WL; o <<= 1) {
+          d0[0] += __shfl_xor_sync(WFULL, d0[0], o);
+          d1[0] += __shfl_xor_sync(WFULL, d1[0], o);
+        }
+        d0[0] *= p.attn_scale;
+        d1[0] *= p.attn_scale;
+        a0.add_trip(d0, ok, vr);
+        a1.add_trip(d1, ok, vr);
+      }
     }
     a0.merge_groups();
     a1.merge_groups();
@@ -1034,15 +1345,22 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
     const int l = li - p.n_bb;
     const LayerW* L = p.cp_layers + l;
     const int NT = pass == 0 ? 2 : 1, p0 = pass == 0 ? 0 : pass + 1;
-    for (int item = gw; item < B * NKVH; item += NW) {
+    // items spread over the CTAs first (warp w of CTA c: item c + G w), so that warps 0..3 of
+    // every CTA hold them and each stages its rows in a quarter of the activation ring
+    uint8_t* wb = (NT == 1 && cs.warp() < 4)
+                      ? reinterpret_cast<uint8_t*>(sm.ring) + WRING_BYTES + cs.warp() * CPWBUF
+                      : nullptr;
+    for (int item = cs.cta() + cs.G() * cs.warp(); item < B * NKVH; item += NW) {
       const int s = item / NKVH, h = item - s * NKVH;
       const size_t off = (static_cast<size_t>(l) * NKVH + h) * p.cp_max_seq * HD;
       watt_item<true>(p, cs, L, p.bw.qkv + static_cast<size_t>(s * NT) * QKV_ROWS, NT, p0, h,
                       reinterpret_cast<uint8_t*>(p.bs[s].cpk + off), reinterpret_cast<uint8_t*>(p.bs[s].cpv + off),
-                      p.bw.abuf[1], s * NT, 0, 1, 0, p0 + NT, true, nullptr, nullptr);
+                      p.bw.abuf[1], s * NT, 0, 1, 0, p0 + NT, true, nullptr, nullptr, wb);
     }
   } else {
     const LayerW* L = p.bb_layers + li;
+    // this warp's slice of the activation ring stages the items' cached K/V rows
+    uint8_t* wbuf = reinterpret_cast<uint8_t*>(sm.ring) + WRING_BYTES + cs.warp() * WBUF;
     // Items run over "rows": the utterances of a frame / prefill step, or the T context tokens of
     // one utterance in a dense prefill (row v at position p0 + v, all rows sharing its cache).
     const bool dense = p.mode == MODE_B_PREFILL_DENSE;
@@ -1081,11 +1399,12 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
       if (dense) return p0d + v + 1;
       return bst.act[v] ? bst.pos[v] + 1 : 0;
     };
-    // the plan, computed by warp 0 (lane l: rows l, l + 32, l + 64, l + 96) into sm.hist: item
-    // offset of each row [0, 128), chunks per KV head [128, 256), item count in sm.bcast[1]; the
-    // chunk length is the smallest (in steps of 1/8) for which every item gets its own warp
-    int* plan = sm.hist;
-    if (cs.warp() == 0) {
+    // the plan, computed by warp 0 (lane l: rows l, l + 32, l + 64, l + 96) into sm.bplan: item
+    // offset of each row [0, 128), chunks per KV head [128, 256), item count [256]; the chunk
+    // length is the smallest (in steps of 1/8) for which every item gets its own warp. The rows'
+    // lengths do not change within a launch, so the first backbone layer's plan serves them all.
+    int* plan = sm.bplan;
+    if (cs.warp() == 0 && !sm.bplan_ok) {
       int Sx[4], nx[4];
       int tot = 0;
 #pragma unroll
@@ -1123,10 +1442,13 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
         plan[128 + cs.lane() + 32 * k] = nx[k];
         base += __shfl_sync(WFULL, x, 31);
       }
-      if (cs.lane() == 0) sm.bcast[1] = base;
+      if (cs.lane() == 0) {
+        plan[256] = base;
+        sm.bplan_ok = 1;
+      }
     }
     named_sync(1, NCT);
-    const int total = sm.bcast[1];
+    const int total = plan[256];
     for (int item = gw; item < total; item += NW) {
       int lo = 0, hi = NV - 1;   // the last row whose offset <= item (binary search)
       while (lo < hi) {
@@ -1145,7 +1467,7 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
                        reinterpret_cast<uint8_t*>(p.bs[su].k + off), reinterpret_cast<uint8_t*>(p.bs[su].v + off),
                        p.bw.abuf[1], v, c, nch, s0, s1, !dense && s1 == S,
                        p.bw.prt + static_cast<size_t>(v) * NQH * MAX_ATT_CHUNKS * PRT_STRIDE,
-                       p.bw.att_cnt + v * NKVH + h);
+                       p.bw.att_cnt + v * NKVH + h, wbuf);
     }
   }
   return b_sync_planes(p, sm, cs);
@@ -1428,14 +1750,21 @@ __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
         int toks[NCPHEADS];
         for (int q = 0; q < NCPHEADS - 1; ++q) toks[q] = __ldcg(p.bw.tok + s * NGROUPS + q + 1);
         toks[NCPHEADS - 1] = b_token(p, cpc, slot ^ 1, s, NCPHEADS);
-#pragma unroll 1
+        // the 17 rows' 8 columns as 16-byte loads, all in flight together, then the adds in order
+        uint4 e[NCPHEADS + 1];
+        e[0] = *reinterpret_cast<const uint4*>(p.codec_emb + static_cast<size_t>(bst.g0[s]) * HID + k0);
+#pragma unroll
+        for (int q = 0; q < NCPHEADS; ++q)
+          e[q + 1] = *reinterpret_cast<const uint4*>(p.cp_emb[q] + static_cast<size_t>(toks[q]) * HID + k0);
+        float x[8];   // the caller's text row (no alignment promised beyond bf16)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = __bfloat162float(extra[k0 + i]);
+#pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int k = k0 + i;
-          float a = __bfloat162float(p.codec_emb[static_cast<size_t>(bst.g0[s]) * HID + k]);
-#pragma unroll 1
-          for (int q = 0; q < NCPHEADS; ++q)
-            a = round_bf16(a + __bfloat162float(p.cp_emb[q][static_cast<size_t>(toks[q]) * HID + k]));
-          v[i] = round_bf16(a + __bfloat162float(extra[k]));
+          float a = bf16_at(&e[0].x, i);
+#pragma unroll
+          for (int q = 0; q < NCPHEADS; ++q) a = round_bf16(a + bf16_at(&e[q + 1].x, i));
+          v[i] = round_bf16(a + x[i]);
         }
       }))
     return false;
@@ -1557,9 +1886,12 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     return;
   }
   if (tid == 0) {
-    for (int i = 0; i < BB_N; ++i) mbar_init(&sm.bbar[i], i == BB_SREADY ? static_cast<uint32_t>(p.bcl) : 1u);
+    for (int i = 0; i < BB_N; ++i)
+      mbar_init(&sm.bbar[i], i == BB_SREADY ? static_cast<uint32_t>(p.bcl)
+                                            : (i == BB_RFREE ? static_cast<uint32_t>(p.bcl - 1) : 1u));
     sm.abort = 0;
     sm.epoch = 0;
+    sm.bplan_ok = 0;
     fence_barrier_init();
   }
   if (warp == NCW + 1) {
@@ -1613,6 +1945,7 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     cs.bar_target = 0;
     cs.dk = 0;
     cs.gi = 0;
+    cs.pn = 0;
     bool ok;
     if (p.mode == MODE_B_FRAME)
       ok = b_frame(p, sm, cs);

@@ -92,6 +92,15 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
       : "memory");
 }
 
+// Bulk copy from this CTA's shared memory to the shared memory of a CTA of the cluster (dst_cl
+// and its mbarrier bar_cl are cluster addresses from mapa_shared); the copy completes `bytes`
+// transactions on that mbarrier. 16-byte aligned addresses, size a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cl, uint32_t src, uint32_t bytes, uint32_t bar_cl) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_cl),
+               "r"(src), "r"(bytes), "r"(bar_cl)
+               : "memory");
+}
+
 // 2-D tiled TMA load of one box of a tensor map held in global memory (no multicast). The
 // innermost coordinate x must be a multiple of 16 bytes / element size.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int x, int y, uint64_t* bar) {
@@ -251,6 +260,23 @@ __device__ __forceinline__ void tensormap_acquire(const void* tmap) {
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
 }
+// The same, with an L2 evict-first policy (streamed data that is read once).
+__device__ __forceinline__ void cp_async16_stream(void* smem_dst, const void* gsrc, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+               "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
@@ -277,6 +303,14 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t caddr) {
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "r"(caddr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_smem_f4(uint32_t saddr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(saddr)
                : "memory");
   return v;
 }

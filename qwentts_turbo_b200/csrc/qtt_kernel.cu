@@ -44,6 +44,8 @@ struct __align__(128) Smem {
   uint64_t bbar[32];                 // pipeline mbarriers
   uint32_t tmem_base;                // tensor-memory address of the accumulator
   int bstate[4 * BMAX];              // per utterance: position, step, g0, active
+  int bplan[257];                    // backbone attention plan of the launch (item offsets, chunks, count)
+  int bplan_ok;                      // bplan holds the launch's plan
 };
 
 size_t work_bytes() {
@@ -382,6 +384,7 @@ struct Cons {
   uint32_t slot, round, bar_target;
   int dk;   // fused MLP stages completed in this launch (selects the fixed-point output buffer)
   int gi;   // batched kernel: GEMM stages completed in this launch (trace index)
+  int pn;   // batched kernel: GEMM stages whose K-slice partials were pushed (mbarrier parity)
   __device__ __forceinline__ int cta() const { return static_cast<int>(blockIdx.x); }
   __device__ __forceinline__ int G() const { return static_cast<int>(gridDim.x); }
   __device__ __forceinline__ int tid() const { return static_cast<int>(threadIdx.x); }
@@ -1906,12 +1909,29 @@ __device__ bool run_frame(const Params& p, Smem& sm, Cons& cs) {
   // ---- combine (generator.py:143-149,356-362): sequential bf16 adds
   {
     const bf16* extra = step < p.n_trailing ? p.trailing + static_cast<size_t>(step) * HID : p.pad;
-    for (int i = cs.tid(); i < HID; i += NCT) {
-      float a = __bfloat162float(p.codec_emb[static_cast<size_t>(g0) * HID + i]);
-#pragma unroll 1
+    // 8 columns per thread: the 16 table rows as 16-byte loads, all in flight together, then the
+    // sequential adds (the caller's text row: bf16 loads, no alignment promised)
+    for (int i8 = cs.tid(); i8 < HID / 8; i8 += NCT) {
+      const int i0 = 8 * i8;
+      uint4 e[NCPHEADS + 1];
+      e[0] = *reinterpret_cast<const uint4*>(p.codec_emb + static_cast<size_t>(g0) * HID + i0);
+#pragma unroll
       for (int q = 0; q < NCPHEADS; ++q)
-        a = round_bf16(a + __bfloat162float(p.cp_emb[q][static_cast<size_t>(toks[q + 1]) * HID + i]));
-      sm.xs[i] = round_bf16(a + __bfloat162float(extra[i]));
+        e[q + 1] = *reinterpret_cast<const uint4*>(p.cp_emb[q] + static_cast<size_t>(toks[q + 1]) * HID + i0);
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = __bfloat162float(extra[i0 + i]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t* w0 = &e[0].x;
+        float a = (i & 1) ? bf16_hi(w0[i >> 1]) : bf16_lo(w0[i >> 1]);
+#pragma unroll
+        for (int q = 0; q < NCPHEADS; ++q) {
+          const uint32_t* w = &e[q + 1].x;
+          a = round_bf16(a + ((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1])));
+        }
+        sm.xs[i0 + i] = round_bf16(a + x[i]);
+      }
     }
     named_sync(1, NCT);
   }
