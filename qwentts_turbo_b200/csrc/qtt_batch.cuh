@@ -37,10 +37,6 @@
 // frame adds COMBINE (the 16-embedding sum + text row) before the backbone layers and the
 // codec head (+ sampler) at the end.
 
-// The batched kernel's grid barrier as a call of its own: its spin loop then keeps its few values
-// in registers rather than sharing the caller's register budget.
-__device__ __noinline__ bool grid_sync_b(const Params& p, Smem& sm, Cons& cs) { return grid_sync(p, sm, cs); }
-
 constexpr int KSUB = 64;                  // K elements of one 128-byte swizzle atom row
 constexpr int NSUB = 2;                   // atoms per pipeline step
 constexpr int KSTEP = KSUB * NSUB;        // K elements per pipeline step
@@ -83,6 +79,17 @@ enum : int {
   BB_N
 };
 static_assert(BB_N <= 32, "batched mbarriers");
+
+// The batched kernel's grid barrier as a call of its own: its spin loop then keeps its few values
+// in registers rather than sharing the caller's register budget. go_next: the coming stage is a
+// GEMM, whose activation loads the barrier itself releases (GO) on the CTAs that take part in
+// GEMMs, instead of b_gemm_begin after the consumers' CTA barrier.
+__device__ __noinline__ bool grid_sync_b(const Params& p, Smem& sm, Cons& cs) {
+  uint64_t* go = (cs.go_next && cs.cta() < BROWS_B) ? &sm.bbar[BB_GO] : nullptr;
+  cs.go_sent = cs.go_next;
+  cs.go_next = 0;
+  return grid_sync(p, sm, cs, go);
+}
 
 enum BKind : int { BK_QKV = 0, BK_O = 1, BK_GU = 2, BK_D = 3, BK_HEAD = 4 };
 
@@ -552,9 +559,10 @@ __device__ __forceinline__ BStage b_gemm_begin(const Params& p, Smem& sm, Cons& 
       // armed before this CTA frees its receive slots (after its MMAs), so before any slice lands
       if (S.push)
         mbar_arrive_expect_tx(&sm.bbar[BB_RCV], static_cast<uint32_t>((S.sp.nk - 1) * (S.rb - S.ra) * S.N * 4));
-      mbar_arrive(&sm.bbar[BB_GO]);
+      if (!cs.go_sent) mbar_arrive(&sm.bbar[BB_GO]);
     }
   }
+  cs.go_sent = 0;
   return S;
 }
 
@@ -751,10 +759,12 @@ __device__ __forceinline__ bool b_gemm_end(const Params& p, Smem& sm, Cons& cs, 
   return ok;
 }
 
+// go_after: a GEMM stage follows this one's grid barrier directly.
 template <class PRE, class RUN>
-__device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, PRE&& pre,
-                                       RUN&& run) {
+__device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, bool go_after,
+                                       PRE&& pre, RUN&& run) {
   const BStage S = b_gemm_begin(p, sm, cs, g);
+  cs.go_next = go_after ? 1 : 0;
   if (!S.sp.act) return grid_sync_b(p, sm, cs);
   const bool ok = b_gemm_mid(p, sm, cs, S, gemm_n);
   if (ok) {
@@ -829,6 +839,7 @@ __device__ bool b_input(const Params& p, Smem& sm, Cons& cs, int T, const bf16* 
     }
     b_ssq_add(ssq, t, ss);
   });
+  cs.go_next = 1;   // the stack's first QKV follows
   return b_sync_planes(p, sm, cs);
 }
 
@@ -849,6 +860,7 @@ __device__ __noinline__ bool b_norm(const Params& p, Smem& sm, Cons& cs, const f
       if (hstate && bst.act[i]) p.bs[i].st->h[k0 + j] = nv;
     }
   });
+  cs.go_next = 1;   // a head follows
   return b_sync_planes(p, sm, cs);
 }
 
@@ -1470,6 +1482,7 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
                        p.bw.att_cnt + v * NKVH + h, wbuf);
     }
   }
+  cs.go_next = 1;   // o_proj follows
   return b_sync_planes(p, sm, cs);
 }
 
@@ -1482,7 +1495,7 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
     if (!b_gemm(
-            p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn,
+            p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, false,
             [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
             [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
               float v[EW];
@@ -1498,7 +1511,7 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
   {
     unsigned long long* ssq = b_ssq_next(p, cs);
     if (!b_gemm(
-            p, sm, cs, BGemm{BK_O, li, 0, T}, gn,
+            p, sm, cs, BGemm{BK_O, li, 0, T}, gn, true,
             [&](int t, int r0, EpiSt& st) {
               ldw_f32(hin + t * HID + r0, st.a);
               ldw_bf16(L->post_norm + r0, st.b);
@@ -1522,7 +1535,7 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
   {
     const unsigned long long* ssq = b_ssq_cur(p, cs);
     if (!b_gemm(
-            p, sm, cs, BGemm{BK_GU, li, 0, T}, gn,
+            p, sm, cs, BGemm{BK_GU, li, 0, T}, gn, true,
             [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
             [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
               float m[EW];
@@ -1539,7 +1552,7 @@ __device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32
   {
     unsigned long long* ssq = b_ssq_next(p, cs);
     if (!b_gemm(
-            p, sm, cs, BGemm{BK_D, li, 0, T}, gn,
+            p, sm, cs, BGemm{BK_D, li, 0, T}, gn, next_norm != nullptr,
             [&](int t, int r0, EpiSt& st) {
               ldw_f32(p.bw.hmid + t * HID + r0, st.a);
               if (next_norm) ldw_bf16(next_norm + r0, st.b);
@@ -1592,7 +1605,7 @@ __device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_
   if (cs.cta() == 0)
     for (int t = cs.tid(); t < TBMAX; t += NCT) __stcg(p.bw.amax + (slot ^ 1) * TBMAX + t, 0ull);
   return b_gemm(
-      p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, [&](int t, int r0, EpiSt& st) {},
+      p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, false, [&](int t, int r0, EpiSt& st) {},
       [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
         SampleCfg c = cfg;
         if (hidx == 0) {
@@ -1863,6 +1876,7 @@ __device__ bool b_first_token(const Params& p, Smem& sm, Cons& cs) {
       p.bw.abuf[1][static_cast<size_t>(TBMAX + s) * ABUF_LD + k0 + j] = __float2bfloat16_rn(0.f);
     }
   });
+  cs.go_next = 1;   // the codec head follows
   if (!grid_sync_b(p, sm, cs)) return false;
   const SampleCfg c = b_codec_cfg(p, 1.f);
   if (!b_head(p, sm, cs, gn, 0, c, 0)) return false;
@@ -1946,6 +1960,8 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
     cs.dk = 0;
     cs.gi = 0;
     cs.pn = 0;
+    cs.go_next = 0;
+    cs.go_sent = 0;
     bool ok;
     if (p.mode == MODE_B_FRAME)
       ok = b_frame(p, sm, cs);

@@ -385,6 +385,8 @@ struct Cons {
   int dk;   // fused MLP stages completed in this launch (selects the fixed-point output buffer)
   int gi;   // batched kernel: GEMM stages completed in this launch (trace index)
   int pn;   // batched kernel: GEMM stages whose K-slice partials were pushed (mbarrier parity)
+  int go_next;   // batched kernel: the coming grid barrier precedes a GEMM stage (release its loads there)
+  int go_sent;   // batched kernel: the last grid barrier released the coming GEMM stage's loads
   __device__ __forceinline__ int cta() const { return static_cast<int>(blockIdx.x); }
   __device__ __forceinline__ int G() const { return static_cast<int>(gridDim.x); }
   __device__ __forceinline__ int tid() const { return static_cast<int>(threadIdx.x); }
@@ -455,8 +457,10 @@ __device__ __forceinline__ void prologue_mark(const Params& p, const Cons& cs, i
   }
 }
 
-// Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded).
-__device__ __forceinline__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
+// Grid-wide barrier over the consumer threads of all CTAs (monotonic counter, bounded). go: an
+// mbarrier that thread 0 arrives on as soon as the barrier has passed (the batched kernel's
+// activation loader starts the next GEMM stage's loads there).
+__device__ __forceinline__ bool grid_sync(const Params& p, Smem& sm, Cons& cs, uint64_t* go = nullptr) {
   named_sync(1, NCT);
   if (cs.tid() == 0) {
     stage_mark(p, cs, 2);
@@ -493,6 +497,7 @@ __device__ __forceinline__ bool grid_sync(const Params& p, Smem& sm, Cons& cs) {
         }
       }
     }
+    if (go != nullptr && !aborted(sm)) mbar_arrive(go);
     *reinterpret_cast<volatile int*>(&sm.epoch) = static_cast<int>(cs.bar_target / static_cast<uint32_t>(cs.G()));
     if (p.dbg_timeline != nullptr && cs.cta() == 0) {
       const uint32_t k = cs.bar_target / static_cast<uint32_t>(cs.G());
