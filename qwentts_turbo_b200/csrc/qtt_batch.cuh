@@ -1323,20 +1323,26 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
     // merge the nch records: group g takes chunks g, g + 2, ... of both heads
     a0.init();
     a1.init();
-    for (int cc = g; cc - g < nch; cc += WG) {
-      if (cc < nch) {
+    // up to 2 chunks per group per round, all their loads issued before the first merge
+    for (int cb = g; cb - g < nch; cb += 2 * WG) {
+      float2 ml[2][2];
+      float a2[2][2][WD];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int cc = min(cb + j * WG, nch - 1);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const float* rec = prt + ((static_cast<size_t>(t) * NQH + 2 * h + hh) * MAX_ATT_CHUNKS + cc) * PRT_STRIDE;
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec));
-          float a2[WD];
-          ld8_f32(rec + 4 + WD * u, a2);
-          if (hh == 0)
-            a0.merge(ml.x, ml.y, a2);
-          else
-            a1.merge(ml.x, ml.y, a2);
+          ml[j][hh] = __ldcg(reinterpret_cast<const float2*>(rec));
+          ld8_f32(rec + 4 + WD * u, a2[j][hh]);
         }
       }
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (cb + j * WG < nch) {
+          a0.merge(ml[j][0].x, ml[j][0].y, a2[j][0]);
+          a1.merge(ml[j][1].x, ml[j][1].y, a2[j][1]);
+        }
     }
     a0.merge_groups();
     a1.merge_groups();
@@ -1487,102 +1493,109 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
 }
 
 // One decoder layer of the batch: QKV | attention | O | gate/up | down.
-__device__ __noinline__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int pass, int T,
+// The four GEMM stages of a layer, each a function of its own: one epilogue's callbacks at a time
+// share the register budget, so the item loops run without spilling to local memory.
+__device__ __noinline__ bool b_qkv_stage(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, int T) {
+  const unsigned long long* ssq = b_ssq_cur(p, cs);
+  const float eps = p.eps;
+  return b_gemm(
+      p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, false,
+      [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
+      [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+        float v[EW];
+#pragma unroll
+        for (int i = 0; i < EW; ++i) v[i] = y[i] * st.rs;
+        stw_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
+      });
+}
+
+// o_proj + residual -> hmid, A planes of gate/up (post-attention norm), sums of squares
+__device__ __noinline__ bool b_o_stage(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, int T, const float* hin,
+                                       const bf16* post_norm) {
+  unsigned long long* ssq = b_ssq_next(p, cs);
+  return b_gemm(
+      p, sm, cs, BGemm{BK_O, li, 0, T}, gn, true,
+      [&](int t, int r0, EpiSt& st) {
+        ldw_f32(hin + t * HID + r0, st.a);
+        ldw_bf16(post_norm + r0, st.b);
+      },
+      [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+        double ss = 0.0;
+        float v[EW], a[EW];
+#pragma unroll
+        for (int i = 0; i < EW; ++i) {
+          v[i] = y[i] + st.a[i];
+          a[i] = v[i] * st.b[i];
+          ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+        }
+        stw_f32(p.bw.hmid + t * HID + r0, v);
+        hilo_store_w(p.bw.abuf[0], t, r0, a);
+        b_ssq_add(ssq, t, ss);
+      });
+}
+
+// gate/up + SiLU (deferred post-attention norm) -> A planes of down
+__device__ __noinline__ bool b_gu_stage(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, int T) {
+  const unsigned long long* ssq = b_ssq_cur(p, cs);
+  const float eps = p.eps;
+  return b_gemm(
+      p, sm, cs, BGemm{BK_GU, li, 0, T}, gn, true,
+      [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
+      [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+        float m[EW];
+#pragma unroll
+        for (int i = 0; i < EW; ++i) {
+          const float gg = y[i] * st.rs, uu = y2[i] * st.rs;
+          m[i] = (gg / (1.0f + expf(-gg))) * uu;
+        }
+        hilo_store_w(p.bw.abuf[1], t, r0, m);
+      });
+}
+
+// down + residual -> layer output, A planes of the next layer (its input norm), sums of squares
+__device__ __noinline__ bool b_d_stage(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int T,
+                                       float* hout, const bf16* next_norm) {
+  unsigned long long* ssq = b_ssq_next(p, cs);
+  return b_gemm(
+      p, sm, cs, BGemm{BK_D, li, 0, T}, gn, next_norm != nullptr,
+      [&](int t, int r0, EpiSt& st) {
+        ldw_f32(p.bw.hmid + t * HID + r0, st.a);
+        if (next_norm) ldw_bf16(next_norm + r0, st.b);
+      },
+      [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+        double ss = 0.0;
+        float v[EW];
+#pragma unroll
+        for (int i = 0; i < EW; ++i) {
+          v[i] = y[i] + st.a[i];
+          if (!cp) v[i] = round_bf16(v[i]);
+          ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+        }
+        stw_f32(hout + t * HID + r0, v);
+        if (next_norm) {
+          float a[EW];
+#pragma unroll
+          for (int i = 0; i < EW; ++i) a[i] = v[i] * st.b[i];
+          hilo_store_w(p.bw.abuf[0], t, r0, a);
+        }
+        b_ssq_add(ssq, t, ss);
+      });
+}
+
+__device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int pass, int T,
                         const float* hin, float* hout, const bf16* next_norm) {
   const LayerW* L = (cp ? p.cp_layers + (li - p.n_bb) : p.bb_layers + li);
-  const float eps = p.eps;
-  // ---- QKV (deferred input norm)
-  {
-    const unsigned long long* ssq = b_ssq_cur(p, cs);
-    if (!b_gemm(
-            p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, false,
-            [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
-            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
-              float v[EW];
-#pragma unroll
-              for (int i = 0; i < EW; ++i) v[i] = y[i] * st.rs;
-              stw_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
-            }))
-      return false;
-  }
-  // ---- attention -> A planes of o_proj
+  if (!b_qkv_stage(p, sm, cs, gn, li, T)) return false;
+  // attention -> A planes of o_proj
   if (!b_attention(p, sm, cs, li, cp, pass)) return false;
-  // ---- o_proj + residual -> hmid, A planes of gate/up (post-attention norm), sums of squares
-  {
-    unsigned long long* ssq = b_ssq_next(p, cs);
-    if (!b_gemm(
-            p, sm, cs, BGemm{BK_O, li, 0, T}, gn, true,
-            [&](int t, int r0, EpiSt& st) {
-              ldw_f32(hin + t * HID + r0, st.a);
-              ldw_bf16(L->post_norm + r0, st.b);
-            },
-            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
-              double ss = 0.0;
-              float v[EW], a[EW];
-#pragma unroll
-              for (int i = 0; i < EW; ++i) {
-                v[i] = y[i] + st.a[i];
-                a[i] = v[i] * st.b[i];
-                ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
-              }
-              stw_f32(p.bw.hmid + t * HID + r0, v);
-              hilo_store_w(p.bw.abuf[0], t, r0, a);
-              b_ssq_add(ssq, t, ss);
-            }))
-      return false;
-  }
-  // ---- gate/up + SiLU (deferred post-attention norm) -> A planes of down
-  {
-    const unsigned long long* ssq = b_ssq_cur(p, cs);
-    if (!b_gemm(
-            p, sm, cs, BGemm{BK_GU, li, 0, T}, gn, true,
-            [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
-            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
-              float m[EW];
-#pragma unroll
-              for (int i = 0; i < EW; ++i) {
-                const float gg = y[i] * st.rs, uu = y2[i] * st.rs;
-                m[i] = (gg / (1.0f + expf(-gg))) * uu;
-              }
-              hilo_store_w(p.bw.abuf[1], t, r0, m);
-            }))
-      return false;
-  }
-  // ---- down + residual -> layer output, A planes of the next layer (its input norm), sums
-  {
-    unsigned long long* ssq = b_ssq_next(p, cs);
-    if (!b_gemm(
-            p, sm, cs, BGemm{BK_D, li, 0, T}, gn, next_norm != nullptr,
-            [&](int t, int r0, EpiSt& st) {
-              ldw_f32(p.bw.hmid + t * HID + r0, st.a);
-              if (next_norm) ldw_bf16(next_norm + r0, st.b);
-            },
-            [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
-              double ss = 0.0;
-              float v[EW];
-#pragma unroll
-              for (int i = 0; i < EW; ++i) {
-                v[i] = y[i] + st.a[i];
-                if (!cp) v[i] = round_bf16(v[i]);
-                ss = fma(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
-              }
-              stw_f32(hout + t * HID + r0, v);
-              if (next_norm) {
-                float a[EW];
-#pragma unroll
-                for (int i = 0; i < EW; ++i) a[i] = v[i] * st.b[i];
-                hilo_store_w(p.bw.abuf[0], t, r0, a);
-              }
-              b_ssq_add(ssq, t, ss);
-            }))
-      return false;
-  }
-  return true;
+  if (!b_o_stage(p, sm, cs, gn, li, T, hin, L->post_norm)) return false;
+  if (!b_gu_stage(p, sm, cs, gn, li, T)) return false;
+  return b_d_stage(p, sm, cs, gn, li, cp, T, hout, next_norm);
 }
 
 // Layers of a stack over T tokens whose input (x, A planes, sums of squares) is ready.
 // Returns the buffer holding the last layer's output (nullptr on abort).
-__device__ const float* b_stack(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, bool cp, int pass, int T) {
+__device__ __noinline__ const float* b_stack(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, bool cp, int pass, int T) {
   const int n = cp ? p.n_cp : p.n_bb;
   const LayerW* Ls = cp ? p.cp_layers : p.bb_layers;
   const float* hin = p.bw.x;
@@ -1598,14 +1611,31 @@ __device__ const float* b_stack(const Params& p, Smem& sm, Cons& cs, uint32_t& g
 // Head GEMM over the NORM stage's A planes: bf16 logits; greedy heads fold the masked argmax of
 // each token into amax[slot][t]; sampled heads store the logits for the sampler. The other slot
 // is cleared for the next head (two barriers away).
-__device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hidx, const SampleCfg& cfg,
+__device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int hidx, const SampleCfg cfg,
                                     int slot) {
   const BState bst = bstate(sm);
   unsigned long long* amax = p.bw.amax + slot * TBMAX;
   if (cs.cta() == 0)
     for (int t = cs.tid(); t < TBMAX; t += NCT) __stcg(p.bw.amax + (slot ^ 1) * TBMAX + t, 0ull);
+  float* dbg = hidx > 0 ? p.dbg_cp_logits : (p.mode == MODE_B_FRAME ? p.dbg_g0_logits : nullptr);
+  if (cfg.do_sample)   // sampled heads store the bf16 logits; the sampler applies the masks
+    return b_gemm(
+        p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, false, [&](int t, int r0, EpiSt& st) {},
+        [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+          float lg[EW];
+#pragma unroll
+          for (int i = 0; i < EW; ++i) lg[i] = round_bf16(y[i]);
+          if (dbg != nullptr) {   // parity tests: [B][15][cp_vocab] / [B][vocab]
+            float* d = hidx > 0 ? dbg + (static_cast<size_t>(t) * NCPHEADS + hidx - 1) * p.cp_vocab + r0
+                                : dbg + static_cast<size_t>(t) * p.vocab + r0;
+#pragma unroll
+            for (int i = 0; i < EW; ++i) d[i] = lg[i];
+          }
+          stw_f32(p.bw.logits + static_cast<size_t>(t) * VMAX + r0, lg);
+        });
   return b_gemm(
-      p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, false, [&](int t, int r0, EpiSt& st) {},
+      p, sm, cs, BGemm{BK_HEAD, 0, hidx, p.nb}, gn, false,
+      [&](int t, int r0, EpiSt& st) {},
       [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
         SampleCfg c = cfg;
         if (hidx == 0) {
@@ -1618,18 +1648,16 @@ __device__ __noinline__ bool b_head(const Params& p, Smem& sm, Cons& cs, uint32_
         for (int i = 0; i < EW; ++i) {
           const int row = r0 + i;
           const float lg = round_bf16(y[i]);
-          if (hidx > 0 && p.dbg_cp_logits != nullptr)   // parity tests: [B][15][cp_vocab]
-            p.dbg_cp_logits[(static_cast<size_t>(t) * NCPHEADS + hidx - 1) * p.cp_vocab + row] = lg;
-          if (hidx == 0 && p.dbg_g0_logits != nullptr && p.mode == MODE_B_FRAME)   // [B][vocab]
-            p.dbg_g0_logits[static_cast<size_t>(t) * p.vocab + row] = lg;
-          if (c.do_sample) {
-            __stcg(p.bw.logits + static_cast<size_t>(t) * VMAX + row, lg);
-          } else {
-            const unsigned long long k = argmax_key(head_mask(c, row, lg), row);
-            best = k > best ? k : best;
+          if (dbg != nullptr) {
+            if (hidx > 0)
+              dbg[(static_cast<size_t>(t) * NCPHEADS + hidx - 1) * p.cp_vocab + row] = lg;
+            else
+              dbg[static_cast<size_t>(t) * p.vocab + row] = lg;
           }
+          const unsigned long long k = argmax_key(head_mask(c, row, lg), row);
+          best = k > best ? k : best;
         }
-        if (!c.do_sample && best != 0ull) atomicMax(amax + t, best);
+        if (best != 0ull) atomicMax(amax + t, best);
       });
 }
 
@@ -1695,6 +1723,76 @@ __device__ SampleCfg b_codec_cfg(const Params& p, float penalty) {
   return c;
 }
 
+// Input of code-predictor pass g (T tokens): [bf16(h), codec_embedding[g0]] for the first pass,
+// else the previous head's token's codec embedding g - 1.
+__device__ __noinline__ bool b_cp_input(const Params& p, Smem& sm, Cons& cs, int g, int T, int slot, const SampleCfg& cpc) {
+  const BState bst = bstate(sm);
+  const bf16* w0 = p.cp_layers[0].in_norm;
+  if (g == 0) {
+    // [bf16(h), codec_embedding[g0]] at positions 0, 1 (generator.py:319-325)
+    if (!b_input(p, sm, cs, T, w0, [&](int t, int k0, float (&v)[8]) {
+          const int s = t >> 1;
+          if (t & 1) {
+            const bf16* row = p.codec_emb + static_cast<size_t>(bst.g0[s]) * HID + k0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(row[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = round_bf16(__ldcg(p.bs[s].st->h + k0 + i));
+          }
+        }))
+      return false;
+  } else {
+    // codec embedding g-1 of the previous head's token (generator.py:347-352)
+    const bf16* table = p.cp_emb[g - 1];
+    const int prev = slot ^ 1;
+    if (!b_input(p, sm, cs, T, w0, [&](int t, int k0, float (&v)[8]) {
+          const int tk = b_token(p, cpc, prev, t, g);
+          const bf16* row = table + static_cast<size_t>(tk) * HID + k0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(row[i]);
+        }))
+      return false;
+  }
+  return true;
+}
+
+// COMBINE of a frame: the 16 codec embeddings of each utterance's codes summed in bf16 + its
+// text row (or the pad row); the last code-predictor head's tokens are in argmax slot slot ^ 1.
+__device__ __noinline__ bool b_combine(const Params& p, Smem& sm, Cons& cs, int slot, const SampleCfg& cpc) {
+  const BState bst = bstate(sm);
+  const int B = p.nb;
+  if (!b_input(p, sm, cs, B, p.bb_layers[0].in_norm, [&](int s, int k0, float (&v)[8]) {
+        const int step = bst.step[s];
+        const bf16* extra =
+            step < p.bs[s].n_trailing ? p.bs[s].trailing + static_cast<size_t>(step) * HID : p.bs[s].pad;
+        // greedy heads publish their tokens in bw.tok without a barrier (CTA 0, for the frame
+        // results): the last head's token comes from its argmax slot, complete at its barrier
+        int toks[NCPHEADS];
+#pragma unroll
+        for (int q = 0; q < NCPHEADS - 1; ++q) toks[q] = __ldcg(p.bw.tok + s * NGROUPS + q + 1);
+        toks[NCPHEADS - 1] = b_token(p, cpc, slot ^ 1, s, NCPHEADS);
+        // the 17 rows' 8 columns as 16-byte loads, all in flight together, then the adds in order
+        uint4 e[NCPHEADS + 1];
+        e[0] = *reinterpret_cast<const uint4*>(p.codec_emb + static_cast<size_t>(bst.g0[s]) * HID + k0);
+#pragma unroll
+        for (int q = 0; q < NCPHEADS; ++q)
+          e[q + 1] = *reinterpret_cast<const uint4*>(p.cp_emb[q] + static_cast<size_t>(toks[q]) * HID + k0);
+        float x[8];   // the caller's text row (no alignment promised beyond bf16)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = __bfloat162float(extra[k0 + i]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = bf16_at(&e[0].x, i);
+#pragma unroll
+          for (int q = 0; q < NCPHEADS; ++q) a = round_bf16(a + bf16_at(&e[q + 1].x, i));
+          v[i] = round_bf16(a + x[i]);
+        }
+      }))
+    return false;
+  return true;
+}
+
 __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
   const BState bst = bstate(sm);
   const int B = p.nb;
@@ -1719,33 +1817,7 @@ __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
   int slot = 0;
   for (int g = 0; g < NCPHEADS; ++g) {
     const int T = g == 0 ? 2 * B : B;
-    const bf16* w0 = p.cp_layers[0].in_norm;
-    if (g == 0) {
-      // [bf16(h), codec_embedding[g0]] at positions 0, 1 (generator.py:319-325)
-      if (!b_input(p, sm, cs, T, w0, [&](int t, int k0, float (&v)[8]) {
-            const int s = t >> 1;
-            if (t & 1) {
-              const bf16* row = p.codec_emb + static_cast<size_t>(bst.g0[s]) * HID + k0;
-#pragma unroll
-              for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(row[i]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 8; ++i) v[i] = round_bf16(__ldcg(p.bs[s].st->h + k0 + i));
-            }
-          }))
-        return false;
-    } else {
-      // codec embedding g-1 of the previous head's token (generator.py:347-352)
-      const bf16* table = p.cp_emb[g - 1];
-      const int prev = slot ^ 1;
-      if (!b_input(p, sm, cs, T, w0, [&](int t, int k0, float (&v)[8]) {
-            const int tk = b_token(p, cpc, prev, t, g);
-            const bf16* row = table + static_cast<size_t>(tk) * HID + k0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(row[i]);
-          }))
-        return false;
-    }
+    if (!b_cp_input(p, sm, cs, g, T, slot, cpc)) return false;
     const float* last = b_stack(p, sm, cs, gn, true, g, T);
     if (!last) return false;
     if (!b_norm(p, sm, cs, last, g == 0 ? 2 : 1, g == 0 ? 1 : 0, p.cp_norm, false)) return false;
@@ -1754,33 +1826,7 @@ __device__ bool b_frame(const Params& p, Smem& sm, Cons& cs) {
     slot ^= 1;
   }
   // ---- combine (generator.py:143-149,356-362): sequential bf16 adds + text row
-  if (!b_input(p, sm, cs, B, p.bb_layers[0].in_norm, [&](int s, int k0, float (&v)[8]) {
-        const int step = bst.step[s];
-        const bf16* extra =
-            step < p.bs[s].n_trailing ? p.bs[s].trailing + static_cast<size_t>(step) * HID : p.bs[s].pad;
-        // greedy heads publish their tokens in bw.tok without a barrier (CTA 0, for the frame
-        // results): the last head's token comes from its argmax slot, complete at its barrier
-        int toks[NCPHEADS];
-        for (int q = 0; q < NCPHEADS - 1; ++q) toks[q] = __ldcg(p.bw.tok + s * NGROUPS + q + 1);
-        toks[NCPHEADS - 1] = b_token(p, cpc, slot ^ 1, s, NCPHEADS);
-        // the 17 rows' 8 columns as 16-byte loads, all in flight together, then the adds in order
-        uint4 e[NCPHEADS + 1];
-        e[0] = *reinterpret_cast<const uint4*>(p.codec_emb + static_cast<size_t>(bst.g0[s]) * HID + k0);
-#pragma unroll
-        for (int q = 0; q < NCPHEADS; ++q)
-          e[q + 1] = *reinterpret_cast<const uint4*>(p.cp_emb[q] + static_cast<size_t>(toks[q]) * HID + k0);
-        float x[8];   // the caller's text row (no alignment promised beyond bf16)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = __bfloat162float(extra[k0 + i]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float a = bf16_at(&e[0].x, i);
-#pragma unroll
-          for (int q = 0; q < NCPHEADS; ++q) a = round_bf16(a + bf16_at(&e[q + 1].x, i));
-          v[i] = round_bf16(a + x[i]);
-        }
-      }))
-    return false;
+  if (!b_combine(p, sm, cs, slot, cpc)) return false;
   const float* last = b_stack(p, sm, cs, gn, false, 0, B);
   if (!last) return false;
   if (!b_norm(p, sm, cs, last, 1, 0, p.bb_norm, true)) return false;
