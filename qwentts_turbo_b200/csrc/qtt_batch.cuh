@@ -1048,8 +1048,7 @@ __device__ __forceinline__ void w_scores4(const float (&q0)[WD], const float (&q
     d1[q] *= scale;
   }
 }
-// The first two sub-chunks, issued before the item's q/k/v loads (the cached rows do not depend
-// on them).
+// The first two sub-chunks of a backbone item (issued once the item's q/k/v loads have returned).
 __device__ __forceinline__ void w_stage_first(const uint8_t* kb, const uint8_t* vb, int s0, int ce, uint8_t* wbuf, int lane) {
   const uint64_t pol = l2_evict_first_policy();
   const int nsc = (ce - s0 + WSC - 1) / WSC;
@@ -1100,7 +1099,6 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
   const int g = cs.lane() / WL, u = cs.lane() % WL;
   const bool staged = !CP && wbuf != nullptr && NT == 1;
   const bool staged_cp = CP && wbuf != nullptr && NT == 1 && writer && p0 - s0 <= CPW_ROWS;
-  if (staged) w_stage_first(kb, vb, s0, writer ? min(s1, p0 + 1) - 1 : min(s1, p0 + 1), wbuf, cs.lane());
   if (staged_cp) {   // cached rows [s0, p0), before the item's q/k/v loads
     const int pieces = (p0 - s0) * (HD * 4 / 16);
     const size_t off = static_cast<size_t>(s0) * HD * 4;
@@ -1152,6 +1150,11 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
     }
     w_norm_rope(q0, wq, c4, s4, p.eps, u);
     w_norm_rope(q1, wq, c4, s4, p.eps, u);
+    // Backbone items: the cached rows' copies go out once the item's own loads have returned.
+    // Issued earlier, the stage's burst of cache reads (every warp of the grid at once, ~12 MB)
+    // holds these L2 loads back by several microseconds. (The code predictor's few cached rows are
+    // issued before its loads, at the top of the item.)
+    if (t == 0 && staged) w_stage_first(kb, vb, s0, writer ? min(s1, p0 + 1) - 1 : min(s1, p0 + 1), wbuf, cs.lane());
     WSoft a0, a1;
     a0.init();
     a1.init();
