@@ -1,5 +1,4 @@
 // Host side of libqtt: the drop-in launchers and the engine API declared in include/qtt.h.
-#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -776,6 +775,7 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   p.bmaps = static_cast<const uint8_t*>(e->d_bmaps);
   p.nb = B;
   p.bcl = e->bcl;
+  p.kv_pre = e->bcl == 4 ? 1 : 0;   // a QKV row tile is one head (N = 128) with clusters of 4
   p.bs = e->d_bs;
   qtt::bwork_carve(e->d_bwork, &p.bw);
   p.sp = to_dev(sp);

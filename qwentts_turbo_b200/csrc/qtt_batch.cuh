@@ -493,6 +493,9 @@ __device__ __forceinline__ void stw_f32(float* dst, const float (&v)[EW]) {
 struct EpiSt {
   float a[EW], b[EW];
   float rs;
+  bool valid;    // warp-uniform item loops: the lane holds an item of the CTA
+  uint4 w4, c4, s4;   // QKV with the q/k norms: norm weights, RoPE cos / sin of the token's position
+  void* kv;      // QKV with the K/V write: the token's row in the cache (nullptr: none)
 };
 
 // Consumer side of one GEMM stage. Epilogue items are (token t, EW output columns c); the
@@ -516,12 +519,11 @@ struct BStage {
   uint32_t r_addr;   // push: receive slots, one per other CTA of the cluster [rb - ra][N] fp32
 };
 
-// Partial rows (tokens) holding the epilogue items of cluster rank r: [*ra, *rb).
+// Partial rows (tokens) holding the epilogue items of cluster rank r: [*ra, *rb). The ranks split
+// the tokens, so that all items of a token (a whole head row of QKV) are one CTA's.
 __device__ __forceinline__ void b_rows_of(const BStage& S, int r, int& ra, int& rb) {
-  const int items = S.T * S.nci;
-  const int i0 = split_lo(items, S.sp.nk, r), i1 = split_lo(items, S.sp.nk, r + 1);
-  ra = i0 / S.nci;
-  rb = (i1 + S.nci - 1) / S.nci;
+  ra = split_lo(S.T, S.sp.nk, r);
+  rb = split_lo(S.T, S.sp.nk, r + 1);
 }
 
 // Partial staging layout: row (token tile j, token t) of N floats holding lo + hi; 16-byte chunk k
@@ -544,9 +546,8 @@ __device__ __forceinline__ BStage b_gemm_begin(const Params& p, Smem& sm, Cons& 
   S.gu = g.kind == BK_GU;
   S.NO = S.gu ? S.N / 2 : S.N;
   S.nci = S.NO / EW;
-  const int items = g.T * S.nci;
-  S.i0 = split_lo(items, S.sp.nk, S.sp.kspl);
-  S.i1 = split_lo(items, S.sp.nk, S.sp.kspl + 1);
+  S.i0 = S.nci * split_lo(g.T, S.sp.nk, S.sp.kspl);
+  S.i1 = S.nci * split_lo(g.T, S.sp.nk, S.sp.kspl + 1);
   S.r0b = S.sp.rt * S.NO;
   S.smask = (S.N / 4) % 8 == 0 ? 7 : 3;
   S.s_addr = smem_u32(sm.ring) + WRING_BYTES;
@@ -760,7 +761,9 @@ __device__ __forceinline__ bool b_gemm_end(const Params& p, Smem& sm, Cons& cs, 
 }
 
 // go_after: a GEMM stage follows this one's grid barrier directly.
-template <class PRE, class RUN>
+// UNIFORM: every lane of a warp runs the same trip count (lane l of the warp's 32 consecutive items,
+// st.valid false past the CTA's last item), so that run() may shuffle across the lanes of a token.
+template <bool UNIFORM = false, class PRE, class RUN>
 __device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, const BGemm& g, uint32_t& gemm_n, bool go_after,
                                        PRE&& pre, RUN&& run) {
   const BStage S = b_gemm_begin(p, sm, cs, g);
@@ -768,11 +771,15 @@ __device__ __forceinline__ bool b_gemm(const Params& p, Smem& sm, Cons& cs, cons
   if (!S.sp.act) return grid_sync_b(p, sm, cs);
   const bool ok = b_gemm_mid(p, sm, cs, S, gemm_n);
   if (ok) {
-    for (int i = S.i0 + cs.tid(); i < S.i1; i += NCT) {
+    for (int ib = S.i0 + (UNIFORM ? (cs.tid() & ~31) : cs.tid()); ib < S.i1; ib += NCT) {
+      const int iu = ib + (UNIFORM ? cs.lane() : 0);
+      const bool valid = iu < S.i1;
+      const int i = valid ? iu : S.i0;   // a stand-in item of this CTA past the end
       const int t = i / S.nci, c = i - t * S.nci, r0 = S.r0b + EW * c;
       // the item's inputs that do not depend on D first: their L2 loads overlap the partials'
       // distributed shared memory loads
       EpiSt st;
+      st.valid = valid;
       pre(t, r0, st);
       float y[EW], y2[EW];
       b_reduce_item(S, t, c, y, y2);
@@ -1097,10 +1104,15 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
                           uint8_t* kb, uint8_t* vb, bf16* hilo, int tok0, int c, int nch, int s0, int s1,
                           bool writer, float* prt, uint32_t* cnt, uint8_t* wbuf) {
   const int g = cs.lane() / WL, u = cs.lane() % WL;
+  // own: the item applies the q/k norms + RoPE and writes the new K/V row itself, then takes that
+  // row from registers; with p.kv_pre the QKV epilogue did both, q is normed and every row,
+  // the new one included, is read from the cache
+  const bool own = writer && !p.kv_pre;
+  const int nown = own ? 1 : 0;   // trailing rows of the range taken from registers
   const bool staged = !CP && wbuf != nullptr && NT == 1;
-  const bool staged_cp = CP && wbuf != nullptr && NT == 1 && writer && p0 - s0 <= CPW_ROWS;
-  if (staged_cp) {   // cached rows [s0, p0), before the item's q/k/v loads
-    const int pieces = (p0 - s0) * (HD * 4 / 16);
+  const bool staged_cp = CP && wbuf != nullptr && NT == 1 && writer && p0 + 1 - nown - s0 <= CPW_ROWS;
+  if (staged_cp) {   // cached rows [s0, p0 + 1 - nown), before the item's q loads
+    const int pieces = (p0 + 1 - nown - s0) * (HD * 4 / 16);
     const size_t off = static_cast<size_t>(s0) * HD * 4;
     for (int e = cs.lane(); e < pieces; e += 32) {
       cp_async16(wbuf + e * 16, kb + off + e * 16);
@@ -1114,15 +1126,16 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
     float q0[WD], q1[WD], k[WD], v[WD];
     ld8_f32(qkv + t * QKV_ROWS + (2 * h) * HD + WD * u, q0);
     ld8_f32(qkv + t * QKV_ROWS + (2 * h + 1) * HD + WD * u, q1);
-    if (writer) {
+    if (own) {
       ld8_f32(qkv + t * QKV_ROWS + QSZ + h * HD + WD * u, k);
       ld8_f32(qkv + t * QKV_ROWS + QSZ + KVSZ + h * HD + WD * u, v);
     }
-    const uint4 c4 = *reinterpret_cast<const uint4*>(p.cos_tab + static_cast<size_t>(pos) * HD + WD * u);
-    const uint4 s4 = *reinterpret_cast<const uint4*>(p.sin_tab + static_cast<size_t>(pos) * HD + WD * u);
-    const uint4 wq = *reinterpret_cast<const uint4*>(L->q_norm + WD * u);
-    const uint4 wk = writer ? *reinterpret_cast<const uint4*>(L->k_norm + WD * u) : make_uint4(0, 0, 0, 0);
-    if (writer) {   // the token's new K/V row, read back below like every other row
+    const bool rope = !p.kv_pre;
+    const uint4 c4 = rope ? *reinterpret_cast<const uint4*>(p.cos_tab + static_cast<size_t>(pos) * HD + WD * u) : make_uint4(0, 0, 0, 0);
+    const uint4 s4 = rope ? *reinterpret_cast<const uint4*>(p.sin_tab + static_cast<size_t>(pos) * HD + WD * u) : make_uint4(0, 0, 0, 0);
+    const uint4 wq = rope ? *reinterpret_cast<const uint4*>(L->q_norm + WD * u) : make_uint4(0, 0, 0, 0);
+    const uint4 wk = own ? *reinterpret_cast<const uint4*>(L->k_norm + WD * u) : make_uint4(0, 0, 0, 0);
+    if (own) {   // the token's new K/V row, read back below like every other row
       w_norm_rope(k, wk, c4, s4, p.eps, u);
       if (g == 0) {
         const size_t row = static_cast<size_t>(pos) * HD + WD * u;
@@ -1148,21 +1161,23 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
       }
       __syncwarp();   // the row just stored is read back by the other lanes of this warp
     }
-    w_norm_rope(q0, wq, c4, s4, p.eps, u);
-    w_norm_rope(q1, wq, c4, s4, p.eps, u);
+    if (rope) {
+      w_norm_rope(q0, wq, c4, s4, p.eps, u);
+      w_norm_rope(q1, wq, c4, s4, p.eps, u);
+    }
     // Backbone items: the cached rows' copies go out once the item's own loads have returned.
     // Issued earlier, the stage's burst of cache reads (every warp of the grid at once, ~12 MB)
     // holds these L2 loads back by several microseconds. (The code predictor's few cached rows are
     // issued before its loads, at the top of the item.)
-    if (t == 0 && staged) w_stage_first(kb, vb, s0, writer ? min(s1, p0 + 1) - 1 : min(s1, p0 + 1), wbuf, cs.lane());
+    if (t == 0 && staged) w_stage_first(kb, vb, s0, min(s1, p0 + 1) - nown, wbuf, cs.lane());
     WSoft a0, a1;
     a0.init();
     a1.init();
     const int send = min(s1, p0 + t + 1);
     if (staged) {   // one token (frames): staged rows, then this token's own row
-      const int ce = writer ? send - 1 : send;
+      const int ce = send - nown;
       w_loop_staged(kb, vb, s0, ce, wbuf, q0, q1, p.attn_scale, cs.lane(), a0, a1);
-      if (writer) {   // position send - 1: the row just stored, from registers (bf16 as cached)
+      if (own) {   // position send - 1: the row just stored, from registers (bf16 as cached)
         WRow<false> kr[1], vr[1];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -1226,8 +1241,8 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
       a0.add_trip(d0, ok, vr);
       a1.add_trip(d1, ok, vr);
     }
-    } else if (staged_cp) {   // code predictor, one token: staged rows, then the own row
-      const int n = p0 - s0;
+    } else if (staged_cp) {   // code predictor, one token: staged rows, then (own) the new row
+      const int n = p0 + 1 - nown - s0;
       cp_async_wait<0>();
       __syncwarp();   // every lane's copies have landed
       for (int j = g; j - g < n; j += 2 * WG) {   // every lane runs the same trip count
@@ -1271,7 +1286,7 @@ __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const La
         a0.add_trip(d0, ok, vr);
         a1.add_trip(d1, ok, vr);
       }
-      {   // position p0: the row just stored, from registers (fp32 as cached)
+      if (own) {   // position p0: the row just stored, from registers (fp32 as cached)
         WRow<true> kr[1], vr[1];
 #pragma unroll
         for (int i = 0; i < WD; ++i) {
@@ -1386,9 +1401,10 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
     // one utterance in a dense prefill (row v at position p0 + v, all rows sharing its cache).
     const bool dense = p.mode == MODE_B_PREFILL_DENSE;
     const int NV = dense ? p.b_ntok : B, p0d = p.b_step;
-    if (dense) {
+    if (dense && !p.kv_pre) {
       // the chunk's new K/V rows first (q/k norm of k + RoPE, bf16), so that every row reads them
-      // from the cache after the barrier: item (token t, KV head h)
+      // from the cache after the barrier: item (token t, KV head h). (With p.kv_pre the QKV
+      // epilogue has written them.)
       const int g = cs.lane() / WL, u = cs.lane() % WL;
       for (int item = gw; item < NV * NKVH; item += NW) {
         const int t = item / NKVH, h = item - t * NKVH, pos = p0d + t;
@@ -1498,17 +1514,99 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
 // One decoder layer of the batch: QKV | attention | O | gate/up | down.
 // The four GEMM stages of a layer, each a function of its own: one epilogue's callbacks at a time
 // share the register budget, so the item loops run without spilling to local memory.
-__device__ __noinline__ bool b_qkv_stage(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, int T) {
+// QKV with p.kv_pre (clusters of 4: a row tile is one head): the epilogue also applies the q/k
+// RMSNorm and RoPE (the 16 items of a token's head row are 16 lanes of one warp, the layout of
+// w_norm_rope) and writes the token's new K and V rows into its cache (backbone bf16, code
+// predictor fp32), so that the attention items read every row from the cache.
+// Row of stack token t: its utterance, position and whether it is decoded (code predictor: pass
+// 0 holds two tokens per utterance at positions 0 and 1, pass g the token at position g + 1).
+struct BKvRow {
+  int s, pos;
+  bool on;
+};
+__device__ __forceinline__ BKvRow b_kv_row(const Params& p, const BState& bst, bool cp, int pass, int T, int t) {
+  BKvRow r;
+  if (cp) {
+    const int NT = T > p.nb ? 2 : 1;
+    r.s = t / NT;
+    r.pos = pass == 0 ? (t & 1) : pass + 1;
+    r.on = true;
+  } else if (p.mode == MODE_B_PREFILL_DENSE) {
+    r.s = 0;
+    r.pos = p.b_step + t;
+    r.on = true;
+  } else {
+    r.s = t;
+    r.pos = bst.pos[t];
+    r.on = bst.act[t] != 0;
+  }
+  return r;
+}
+__device__ __noinline__ bool b_qkv_stage(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int pass, int T) {
   const unsigned long long* ssq = b_ssq_cur(p, cs);
   const float eps = p.eps;
-  return b_gemm(
+  if (!p.kv_pre)
+    return b_gemm(
+        p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, false,
+        [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
+        [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
+          float v[EW];
+#pragma unroll
+          for (int i = 0; i < EW; ++i) v[i] = y[i] * st.rs;
+          stw_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
+        });
+  const BState bst = bstate(sm);
+  const LayerW* L = cp ? p.cp_layers + (li - p.n_bb) : p.bb_layers + li;
+  const bf16* const qn = L->q_norm;   // read once, before the stage's wait for D
+  const bf16* const kn = L->k_norm;
+  return b_gemm<true>(
       p, sm, cs, BGemm{BK_QKV, li, 0, T}, gn, false,
-      [&](int t, int r0, EpiSt& st) { st.rs = b_rstd(ssq, t, eps); },
+      [&](int t, int r0, EpiSt& st) {
+        st.rs = b_rstd(ssq, t, eps);
+        const int sec = r0 / HD, u = (r0 % HD) / WD;   // head row: q 0..15, k 16..23, v 24..31
+        const BKvRow kr = b_kv_row(p, bst, cp, pass, T, t);
+        const int pos = kr.on ? kr.pos : 0;
+        st.w4 = sec < NQH + NKVH ? *reinterpret_cast<const uint4*>((sec < NQH ? qn : kn) + WD * u) : make_uint4(0, 0, 0, 0);
+        st.c4 = *reinterpret_cast<const uint4*>(p.cos_tab + static_cast<size_t>(pos) * HD + WD * u);
+        st.s4 = *reinterpret_cast<const uint4*>(p.sin_tab + static_cast<size_t>(pos) * HD + WD * u);
+        st.kv = nullptr;
+        if (sec >= NQH && kr.on && st.valid) {
+          const int h = (sec - NQH) % NKVH;
+          const bool isv = sec >= NQH + NKVH;
+          void* const* base = sm.bkv + 4 * kr.s;   // the utterance's cache addresses (shared memory)
+          if (cp) {
+            const size_t off = ((static_cast<size_t>(li - p.n_bb) * NKVH + h) * p.cp_max_seq + pos) * HD + WD * u;
+            st.kv = static_cast<float*>(base[isv ? 3 : 2]) + off;
+          } else {
+            const size_t off = ((static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq + pos) * HD + WD * u;
+            st.kv = static_cast<bf16*>(base[isv ? 1 : 0]) + off;
+          }
+        }
+      },
       [&](int t, int r0, const float (&y)[EW], const float (&y2)[EW], const EpiSt& st) {
         float v[EW];
 #pragma unroll
         for (int i = 0; i < EW; ++i) v[i] = y[i] * st.rs;
-        stw_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
+        const int sec = r0 / HD, u = (r0 % HD) / WD;
+        // warp-uniform: the warp's 32 items are two tokens' rows of the same head
+        if (sec < NQH + NKVH) w_norm_rope(v, st.w4, st.c4, st.s4, eps, u);
+        if (!st.valid) return;
+        if (sec < NQH) {
+          stw_f32(p.bw.qkv + static_cast<size_t>(t) * QKV_ROWS + r0, v);
+        } else if (st.kv != nullptr) {
+          if (cp) {
+            float4* d = reinterpret_cast<float4*>(st.kv);
+            d[0] = make_float4(v[0], v[1], v[2], v[3]);
+            d[1] = make_float4(v[4], v[5], v[6], v[7]);
+          } else {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i]))) |
+                     (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1]))) << 16);
+            *reinterpret_cast<uint4*>(st.kv) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
       });
 }
 
@@ -1588,7 +1686,7 @@ __device__ __noinline__ bool b_d_stage(const Params& p, Smem& sm, Cons& cs, uint
 __device__ bool b_layer(const Params& p, Smem& sm, Cons& cs, uint32_t& gn, int li, bool cp, int pass, int T,
                         const float* hin, float* hout, const bf16* next_norm) {
   const LayerW* L = (cp ? p.cp_layers + (li - p.n_bb) : p.bb_layers + li);
-  if (!b_qkv_stage(p, sm, cs, gn, li, T)) return false;
+  if (!b_qkv_stage(p, sm, cs, gn, li, cp, pass, T)) return false;
   // attention -> A planes of o_proj
   if (!b_attention(p, sm, cs, li, cp, pass)) return false;
   if (!b_o_stage(p, sm, cs, gn, li, T, hin, L->post_norm)) return false;
@@ -1983,6 +2081,13 @@ extern "C" __global__ void __launch_bounds__(NTHREADS_B, 1) qtt_batch_kernel(con
         act = 1;
       if (p.mode == MODE_B_PREFILL || p.mode == MODE_B_PREFILL_DENSE) pos = p.b_step;
       if (g0 < 0 || g0 >= p.vocab) g0 = 0;
+    }
+    if (s < p.nb) {
+      const BStream& b = p.bs[s];
+      sm.bkv[4 * s] = b.k;
+      sm.bkv[4 * s + 1] = b.v;
+      sm.bkv[4 * s + 2] = b.cpk;
+      sm.bkv[4 * s + 3] = b.cpv;
     }
     sm.bstate[s] = pos;
     sm.bstate[BMAX + s] = step;

@@ -46,6 +46,7 @@ struct __align__(128) Smem {
   int bstate[4 * BMAX];              // per utterance: position, step, g0, active
   int bplan[257];                    // backbone attention plan of the launch (item offsets, chunks, count)
   int bplan_ok;                      // bplan holds the launch's plan
+  void* bkv[4 * BMAX];               // per utterance: backbone K, V and code-predictor K, V caches
 };
 
 size_t work_bytes() {

@@ -199,6 +199,7 @@ struct Params {
   const uint8_t* bmaps;
   int nb;                  // utterances of the batched launch
   int bcl;                 // CTAs per thread-block cluster of the batched launch (4 or 2)
+  int kv_pre;              // batched: the QKV epilogue applies the q/k norms + RoPE and writes the new K/V rows
   const BStream* bs;       // [nb]
   BWork bw;
   int b_step;              // MODE_B_PREFILL: context index of this step; DENSE: first position
