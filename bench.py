@@ -516,6 +516,7 @@ def run_c4(args, rank, world, local_rank, K, W):
     rows_d = torch.empty(B, 1024, dtype=torch.bfloat16, device="cuda")
     codes_devs = [eng.codes(s) for s in range(B)]
     codes_h = torch.empty(K, B, 16, dtype=torch.int32).pin_memory()
+    frame_codes_d = torch.empty(B, 16, dtype=torch.int32, device="cuda")
     sh = stream.cuda_stream
     spb = ctypes.byref(sp)
     no_trail = (ctypes.c_void_p * B)()
@@ -533,8 +534,11 @@ def run_c4(args, rank, world, local_rank, K, W):
         rc = lib.qtt_batch_frames(eng.h, B, 1, no_trail, zeros, row_ptrs, spb, sh)
         if rc != 0:
             raise _lib.QTTError(rc, "qtt_batch_frames")
-        for s in range(B):
-            codes_h[f, s].copy_(codes_devs[s][W + f], non_blocking=True)
+        # the frame's codes of all B utterances: one gather (qtt_batch_last_codes), one D2H copy
+        rc = lib.qtt_batch_last_codes(eng.h, B, frame_codes_d.data_ptr(), sh)
+        if rc != 0:
+            raise _lib.QTTError(rc, "qtt_batch_last_codes")
+        codes_h[f].copy_(frame_codes_d, non_blocking=True)
     # the run's codes of every rank to rank 0 (NCCL all-gather over NVLink; one rank: a copy)
     gathered = gather_codes(torch.stack([codes_devs[s][W:W + K] for s in range(B)]).reshape(-1, 16))
     e3.record(stream)
@@ -571,7 +575,8 @@ def run_c4(args, rank, world, local_rank, K, W):
                      "kernel": "qtt_batch_kernel (1 launch per frame of all utterances)"},
         "e2e": {"value": world * B * K / (ms_e2e / 1000.0), "unit": UNIT,
                 "h2d_bytes_per_step": B * 2048 + B * bstream_bytes, "d2h_bytes_per_step": B * 64,
-                "path": "qtt_batch_frames C-ABI per frame: pinned H2D of the B text rows, D2H of the B code rows; "
+                "path": "qtt_batch_frames C-ABI per frame: pinned H2D of the B text rows; the B code rows gathered "
+                        "by qtt_batch_last_codes and read back with one D2H copy; "
                         "the run's codes of all ranks gathered to rank 0 at the end (NCCL all-gather)"},
         "gpu_launches": K,
         "clocks": clocks.summary(t0, t1),

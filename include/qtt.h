@@ -271,6 +271,12 @@ qtt_status qtt_set_stream_params(qtt_engine* e, int s, int philox_stream, int fr
  * group-0 token of the next frame, done (EOS reached). Host array of 4 * B ints; synchronizes
  * `stream`. */
 qtt_status qtt_batch_states(qtt_engine* e, int B, int32_t* out, cudaStream_t stream);
+/* The codes of the latest frame of streams 0..B-1 in one device buffer (no counterpart in the
+ * reference, whose generate() returns the codes of one utterance at its end): out is device int32
+ * [B][16], row s = stream s's most recent frame (its 16 groups), or -1s if the stream has no frame
+ * yet. One small kernel on `stream`, asynchronous, so that a serving loop reads a whole batched
+ * frame with one device-to-host copy instead of one per utterance. */
+qtt_status qtt_batch_last_codes(qtt_engine* e, int B, int32_t* out, cudaStream_t stream);
 /* Diagnostics of the batched path (parity tests): the first n of its scratch device pointers,
  * in this order: GEMM operand planes 0 and 1 (bf16 [2][128][3072] each: plane 0 = hi, plane 1 =
  * lo, row = token), sampled-head logits (fp32 [64][3072]), frame tokens (int32 [64][16]), stack

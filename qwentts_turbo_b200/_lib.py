@@ -110,6 +110,7 @@ SIGNATURES = {
     "qtt_batch_states": (_I, [_P, _I, ctypes.POINTER(_I), _P]),
     "qtt_batch_frames": (_I, [_P, _I, _I, ctypes.POINTER(_P), ctypes.POINTER(_I), ctypes.POINTER(_P),
                               ctypes.POINTER(QttSampling), _P]),
+    "qtt_batch_last_codes": (_I, [_P, _I, _P, _P]),
     "qtt_batch_debug_buffers": (_I, [_P, ctypes.POINTER(_P), _I]),
     "qtt_batch_set_debug_outputs": (_I, [_P, _P, _P]),
     "qtt_backbone_step_noalloc": (_I, [_P, ctypes.POINTER(TTSLayerWeights), _P, _P, _P, _P, _P, _P, _P,

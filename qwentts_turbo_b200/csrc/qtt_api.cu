@@ -299,6 +299,7 @@ struct qtt_engine {
   qtt::BStream* d_bs = nullptr;
   float* d_cpkv = nullptr;
   qtt::StreamState** d_stptr = nullptr;   // qtt_batch_states: state pointers, gathered words, pinned copy
+  int32_t** d_codeptr = nullptr;          // qtt_batch_last_codes: each stream's code buffer
   int32_t* d_states = nullptr;
   int32_t* h_states = nullptr;
   std::vector<qtt::BStream> h_bs;
@@ -369,6 +370,7 @@ void engine_free(qtt_engine* e) {
   cudaFree(e->d_bs);
   cudaFree(e->d_cpkv);
   cudaFree(e->d_stptr);
+  cudaFree(e->d_codeptr);
   cudaFree(e->d_states);
   cudaFreeHost(e->h_states);
   cudaFree(e->d_work);
@@ -753,6 +755,11 @@ qtt_status ensure_batch(qtt_engine* e) {
   if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_stptr), sizeof(void*) * e->max_streams);
   if (ce == cudaSuccess)
     ce = cudaMemcpy(e->d_stptr, stp.data(), sizeof(void*) * e->max_streams, cudaMemcpyHostToDevice);
+  std::vector<int32_t*> cdp(e->max_streams);
+  for (int s = 0; s < e->max_streams; ++s) cdp[s] = e->streams[s].codes;
+  if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_codeptr), sizeof(void*) * e->max_streams);
+  if (ce == cudaSuccess)
+    ce = cudaMemcpy(e->d_codeptr, cdp.data(), sizeof(void*) * e->max_streams, cudaMemcpyHostToDevice);
   if (ce == cudaSuccess) ce = cudaMalloc(reinterpret_cast<void**>(&e->d_states), sizeof(int32_t) * 4 * e->max_streams);
   if (ce == cudaSuccess) ce = cudaMallocHost(reinterpret_cast<void**>(&e->h_states), sizeof(int32_t) * 4 * e->max_streams);
   if (ce != cudaSuccess) return from_cuda(ce);
@@ -933,6 +940,25 @@ extern "C" qtt_status qtt_batch_states(qtt_engine* e, int B, int32_t* out, cudaS
   if (ce != cudaSuccess) return from_cuda(ce);
   std::memcpy(out, e->h_states, sizeof(int32_t) * 4 * B);
   return QTT_OK;
+}
+
+// Row s of out: the 16 codes of stream s's latest frame (frame step - 1), or -1 without one.
+__global__ void batch_last_codes_kernel(qtt::StreamState* const* st, int32_t* const* codes, int B, int32_t* out) {
+  for (int i = threadIdx.x; i < qtt::NGROUPS * B; i += blockDim.x) {
+    const int s = i / qtt::NGROUPS, g = i - s * qtt::NGROUPS;
+    const int step = st[s]->step;
+    out[i] = step > 0 ? codes[s][(step - 1) * qtt::NGROUPS + g] : -1;
+  }
+}
+
+extern "C" qtt_status qtt_batch_last_codes(qtt_engine* e, int B, int32_t* out, cudaStream_t stream) {
+  if (!e || !out || B < 1 || B > e->max_streams) return QTT_ERR_INVALID_ARG;
+  qtt_status r = set_device(e);
+  if (r != QTT_OK) return r;
+  r = ensure_batch(e);
+  if (r != QTT_OK) return r;
+  batch_last_codes_kernel<<<1, 256, 0, stream>>>(e->d_stptr, e->d_codeptr, B, out);
+  return from_cuda(cudaGetLastError());
 }
 
 extern "C" qtt_status qtt_batch_set_debug_outputs(qtt_engine* e, float* cp_logits, float* g0_logits) {

@@ -253,6 +253,15 @@ class Engine:
         _lib.check(self.lib.qtt_batch_states(self.h, B, out, _stream_handle(stream)), "qtt_batch_states")
         return [list(out[4 * s:4 * s + 4]) for s in range(B)]
 
+    def batch_last_codes(self, B: int, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """int32 [B, 16] on the engine's GPU: the codes of each stream's latest frame (-1s if it has
+        none), gathered by one kernel on ``stream`` (asynchronous)."""
+        if out is None:
+            out = torch.empty(B, self.model.dims.n_groups, dtype=torch.int32, device=self.device)
+        assert out.is_cuda and out.dtype == torch.int32 and out.is_contiguous() and out.numel() >= 16 * B
+        _lib.check(self.lib.qtt_batch_last_codes(self.h, B, _ptr(out), _stream_handle(stream)), "qtt_batch_last_codes")
+        return out
+
     def batch_set_debug_outputs(self, cp_logits: torch.Tensor | None, g0_logits: torch.Tensor | None):
         """Parity tests: batched frames also write each head's logits into cp_logits fp32
         [B, 15, cp_vocab] and g0_logits fp32 [B, vocab]."""

@@ -193,6 +193,27 @@ def test_batch_matches_batch1_engine(dev_small):
     assert same >= 60, f"{same}/64 codes equal"
 
 
+def test_batch_last_codes(dev_small):
+    """qtt_batch_last_codes gathers each stream's latest frame (-1s before the first frame), the
+    rows a serving loop copies to the host once per batched frame."""
+    embeds, trailing, pads = _inputs([12, 25, 19], 4, 61)
+    sp = _greedy_sp()
+    eng = Engine(dev_small, max_streams=3, max_seq=512, max_frames=16)
+    try:
+        eng.batch_prefill([e.cuda() for e in embeds], sp)
+        assert torch.equal(eng.batch_last_codes(3).cpu(), torch.full((3, 16), -1, dtype=torch.int32))
+        tr, pd = [t.cuda() for t in trailing], [x.cuda() for x in pads]
+        for f in range(3):
+            eng.batch_frames(1, tr, pd, sp)
+            got = eng.batch_last_codes(3).cpu()
+            eng.check()
+            want = torch.stack([eng.codes(s)[f].cpu() for s in range(3)])
+            assert torch.equal(got, want), f
+        assert torch.equal(eng.batch_last_codes(2).cpu(), want[:2])   # a prefix of the streams
+    finally:
+        eng.close()
+
+
 def _batch_run(dev, embeds, trailing, pads, sp, n, debug):
     B = len(embeds)
     eng = Engine(dev, max_streams=B, max_seq=512, max_frames=16)
