@@ -1390,7 +1390,8 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
       const int s = item / NKVH, h = item - s * NKVH;
       const size_t off = (static_cast<size_t>(l) * NKVH + h) * p.cp_max_seq * HD;
       watt_item<true>(p, cs, L, p.bw.qkv + static_cast<size_t>(s * NT) * QKV_ROWS, NT, p0, h,
-                      reinterpret_cast<uint8_t*>(p.bs[s].cpk + off), reinterpret_cast<uint8_t*>(p.bs[s].cpv + off),
+                      reinterpret_cast<uint8_t*>(static_cast<float*>(sm.bkv[4 * s + 2]) + off),
+                      reinterpret_cast<uint8_t*>(static_cast<float*>(sm.bkv[4 * s + 3]) + off),
                       p.bw.abuf[1], s * NT, 0, 1, 0, p0 + NT, true, nullptr, nullptr, wb);
     }
   } else {
@@ -1501,7 +1502,8 @@ __device__ __noinline__ bool b_attention(const Params& p, Smem& sm, Cons& cs, in
       const int su = dense ? 0 : v;   // the utterance whose cache the row reads
       const size_t off = (static_cast<size_t>(li) * NKVH + h) * p.bb_max_seq * HD;
       watt_item<false>(p, cs, L, p.bw.qkv + static_cast<size_t>(v) * QKV_ROWS, 1, S - 1, h,
-                       reinterpret_cast<uint8_t*>(p.bs[su].k + off), reinterpret_cast<uint8_t*>(p.bs[su].v + off),
+                       reinterpret_cast<uint8_t*>(static_cast<bf16*>(sm.bkv[4 * su]) + off),
+                       reinterpret_cast<uint8_t*>(static_cast<bf16*>(sm.bkv[4 * su + 1]) + off),
                        p.bw.abuf[1], v, c, nch, s0, s1, !dense && s1 == S,
                        p.bw.prt + static_cast<size_t>(v) * NQH * MAX_ATT_CHUNKS * PRT_STRIDE,
                        p.bw.att_cnt + v * NKVH + h, wbuf);
