@@ -306,6 +306,11 @@ qtt_status qtt_set_debug_profile(qtt_engine* e, unsigned long long* marks, int n
  * early with the error word set; qtt_check then returns QTT_ERR_TIMEOUT and the engine stays
  * usable. barrier = 0 turns it off. */
 qtt_status qtt_set_debug_barrier_fault(qtt_engine* e, int barrier, unsigned long long wait_ns);
+/* Test hook (no counterpart in the reference): on = 1 makes the batched launches that follow apply
+ * the q/k norms and RoPE and write the new K/V rows in their attention stage, the path of GPUs
+ * whose thread-block clusters hold 2 CTAs, instead of in the QKV GEMM's epilogue (the default
+ * wherever a cluster holds 4 CTAs, a QKV row tile then being one whole head). 0 turns it off. */
+qtt_status qtt_set_debug_kv_in_attention(qtt_engine* e, int on);
 /* Weight-ring refill policy of the persistent kernel: 0 (default) refills a freed slot only
  * after the consumers' next grid barrier, keeping refill traffic out of the barrier; 1 refills
  * as soon as a slot is free. */

@@ -104,6 +104,7 @@ SIGNATURES = {
     "qtt_check": (_I, [_P, _P]),
     "qtt_set_refill_policy": (_I, [_P, _I]),
     "qtt_set_debug_barrier_fault": (_I, [_P, _I, ctypes.c_uint64]),
+    "qtt_set_debug_kv_in_attention": (_I, [_P, _I]),
     "qtt_batch_prefill": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_I), ctypes.POINTER(QttSampling), _P]),
     "qtt_prefill_tc": (_I, [_P, _I, _P, _I, ctypes.POINTER(QttSampling), _P]),
     "qtt_set_stream_params": (_I, [_P, _I, _I, _I]),

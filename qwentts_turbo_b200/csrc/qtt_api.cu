@@ -293,6 +293,7 @@ struct qtt_engine {
   const void* h_cp_head[qtt::NCPHEADS] = {};
   DevShape bshape;
   int bcl = 0;               // CTAs per cluster of the batched kernel
+  int dbg_kv_in_attention = 0;   // test hook: the batched attention stage writes the K/V rows
   bool b_ready = false;
   void* d_bwork = nullptr;
   void* d_bmaps = nullptr;
@@ -782,7 +783,8 @@ qtt::Params batch_params(qtt_engine* e, int B, const qtt_sampling* sp) {
   p.bmaps = static_cast<const uint8_t*>(e->d_bmaps);
   p.nb = B;
   p.bcl = e->bcl;
-  p.kv_pre = e->bcl == 4 ? 1 : 0;   // a QKV row tile is one head (N = 128) with clusters of 4
+  // a QKV row tile is one head (N = 128) with clusters of 4
+  p.kv_pre = (e->bcl == 4 && !e->dbg_kv_in_attention) ? 1 : 0;
   p.bs = e->d_bs;
   qtt::bwork_carve(e->d_bwork, &p.bw);
   p.sp = to_dev(sp);
@@ -1066,6 +1068,12 @@ extern "C" qtt_status qtt_set_debug_barrier_fault(qtt_engine* e, int barrier, un
   if (!e || barrier < 0) return QTT_ERR_INVALID_ARG;
   e->base.dbg_skip_barrier = barrier;
   e->base.dbg_wait_ns = wait_ns;
+  return QTT_OK;
+}
+
+extern "C" qtt_status qtt_set_debug_kv_in_attention(qtt_engine* e, int on) {
+  if (!e) return QTT_ERR_INVALID_ARG;
+  e->dbg_kv_in_attention = on ? 1 : 0;
   return QTT_OK;
 }
 

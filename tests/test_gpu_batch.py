@@ -131,6 +131,31 @@ def test_batch_small_teacher_forced(dev_small, orc_small):
         assert max(x["h_rel"] for x in r) <= HID_REL
 
 
+def test_batch_kv_in_attention_path(dev_small, orc_small):
+    """The path of GPUs whose clusters hold 2 CTAs (q/k norms, RoPE and the new K/V rows in the
+    attention stage rather than the QKV epilogue; forced by the qtt_set_debug_kv_in_attention test
+    hook): the same teacher-forced frames and a tensor-core prefill against the oracle."""
+    embeds, trailing, pads = _inputs([17, 30, 41], 5, 21)
+    eng = Engine(dev_small, max_streams=3, max_seq=512, max_frames=16)
+    try:
+        _lib.check(eng.lib.qtt_set_debug_kv_in_attention(eng.h, 1), "qtt_set_debug_kv_in_attention")
+        recs = run_teacher_forced_batch(eng, orc_small, embeds, trailing, pads, _greedy_sp(repetition_penalty=1.3), 6)
+        for s, r in enumerate(recs):
+            full, bad = _frame_stats(r)
+            assert not bad, (s, bad)
+            assert full >= len(r) - 1, (s, full)
+            assert max(x["h_rel"] for x in r) <= HID_REL
+        e = _inputs([150], 0, 61)[0][0]
+        eng.prefill_tc(0, e.cuda(), _greedy_sp())
+        eng.check()
+        ref = orc_small.prefill(e.to(F64))
+        got = eng.hidden(0).cpu().to(F64)
+        assert float((got - ref).norm() / ref.norm()) <= HID_REL
+    finally:
+        eng.lib.qtt_set_debug_kv_in_attention(eng.h, 0)
+        eng.close()
+
+
 def test_batch_sampling_teacher_forced(dev_small, orc_small):
     """Temperature / top-k / repetition penalty with per-utterance Philox streams, code predictor
     sampled too: each utterance's picks equal the oracle sampler's on the engine's logits."""
