@@ -1097,8 +1097,10 @@ __device__ __forceinline__ void w_loop_staged(const uint8_t* kb, const uint8_t* 
 }
 
 // One warp item: tokens t < NT of utterance rows qkv + t * QKV_ROWS at positions p0 + t, KV
-// head h, context positions [s0, s1) (chunk c of nch). The writer stores the new K/V rows of
-// the tokens first (q/k norm + RoPE), so every position is read from the cache.
+// head h, context positions [s0, s1) (chunk c of nch). writer: the item's range ends at the
+// tokens' own positions. With p.kv_pre the QKV epilogue has normed q and written the new K/V rows,
+// so every position is read from the cache; otherwise the writer item applies the q/k norms and
+// RoPE, stores the new rows and takes them from registers.
 template <bool CP>
 __device__ __noinline__ void watt_item(const Params& p, const Cons& cs, const LayerW* L, const float* qkv, int NT, int p0, int h,
                           uint8_t* kb, uint8_t* vb, bf16* hilo, int tok0, int c, int nch, int s0, int s1,
